@@ -1,0 +1,348 @@
+"""Decode throughput of the B200 resident Qwen2 FP32 path.
+
+Workload: 24-layer Qwen2.5-0.5B-architecture FP32 model,
+vocab 151936 (tied LM head), random-init weights N(0, 0.02) (seed 1), a
+32-token random prompt (seed 1 + rank), 128 greedy tokens per step at batch 1.
+One step = one resident launch that decodes the 128 tokens after the prompt
+(positions 31..158). The prompt is ingested before timing.
+
+Reported (one JSON line, rank 0):
+  value       tokens/s over all ranks, device-timed (CUDA events on the
+              runtime's default queue), inputs resident in HBM
+  e2e         the same through lrq_generate (host hidden in, host tokens out)
+  roofline    algorithmic weight + KV bytes per launch / launch time vs the
+              measured HBM copy bandwidth in MEASURED_PEAKS.json
+  cpu_baseline  the CPU oracle (reference algorithm restated) on the host
+              cores, bounded sample
+Weights (2 GB) exceed L2 (126 MB), so no flush is needed between steps.
+
+--impl reference times the reference's CPU implementation of the path (the
+oracle port; the reference's own code is HIP for AMD gfx1101 and cannot run
+here) on the same workload and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "light-rocm-runtime_b200"))
+
+LAYERS, VOCAB, PROMPT, NEW_TOKENS = 24, 151936, 32, 128
+SEED = 1
+KV_BYTES_PER_LAYER_POSITION = 128 * 4 * 2  # K and V rows of one position
+METRIC = "decode tokens/s, Qwen2.5-0.5B-arch FP32, batch 1 (config 2: 24 layers, 128 new tokens)"
+
+
+def parse_args():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=5)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--cpu-seconds", type=float, default=12.0,
+                        help="CPU baseline sample length")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    return parser.parse_args()
+
+
+def algorithmic_bytes_per_launch(weight_bytes: int, first_position: int, tokens: int) -> int:
+    """Weights once per token plus, per layer, the KV rows read (p+1) and the
+    row written at each position p."""
+    total = 0
+    for p in range(first_position, first_position + tokens):
+        total += weight_bytes + LAYERS * KV_BYTES_PER_LAYER_POSITION * (p + 2)
+    return total
+
+
+def measured_peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic_per_token():
+    """DRAM bytes per decode token of the compiled kernel from the committed
+    ncu summary (profiles/), or None when no capture has been summarised."""
+    path = REPO / "profiles" / "qwen_compiled_kernel_dram.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("dram_bytes_per_token:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.process = None
+
+    def __enter__(self):
+        try:
+            self.process = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.process = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.process is not None:
+            self.process.terminate()
+            try:
+                self.process.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.process.kill()
+
+    def summary(self):
+        self.file.flush()
+        rows = [line.split(",") for line in Path(self.file.name).read_text().splitlines()
+                if line.strip()]
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_weights(rank: int):
+    from lrrt_b200 import synthetic as S
+    weights, tail = S.model(SEED, LAYERS, VOCAB)
+    prompt = S.prompt(SEED + rank, PROMPT, VOCAB)
+    return weights, tail, prompt
+
+
+def cpu_tokens_per_second(weights, tail, prompt, seconds: float, threads: int):
+    """Times the CPU oracle decoding single tokens of the same model."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O
+    O.set_threads(threads)
+    model = O.OracleModel(weights, tail, PROMPT + NEW_TOKENS, 32, workers=148,
+                          max_tokens=1, keep_logits=False)
+    tokens, start = 0, time.perf_counter()
+    while True:
+        position = tokens % (PROMPT + NEW_TOKENS)
+        model.decode(model.embedding(int(prompt[position % PROMPT])), position, 1)
+        tokens += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds:
+            break
+    return tokens / elapsed, tokens, elapsed
+
+
+def reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return
+    weights, tail, prompt = make_weights(0)
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O
+    threads = O.max_threads()
+    O.set_threads(threads)
+    model = O.OracleModel(weights, tail, PROMPT + NEW_TOKENS, 32, workers=148,
+                          max_tokens=1, keep_logits=False)
+    per_step_tokens = 2
+
+    def step(i):
+        for k in range(per_step_tokens):
+            position = (i * per_step_tokens + k) % (PROMPT + NEW_TOKENS)
+            model.decode(model.embedding(int(prompt[position % PROMPT])), position, 1)
+
+    for i in range(args.warmup):
+        step(i)
+    start = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    elapsed = time.perf_counter() - start
+    value = per_step_tokens * args.steps / elapsed
+    sample = (f"{per_step_tokens} single-token decodes per step of the 24-layer model "
+              f"(positions cycling 0..159) on {threads} host threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * elapsed / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2: 24-layer Qwen2.5-0.5B-arch FP32 greedy decode, "
+                               "batch 1", "global_batch": 1, "seq_len": PROMPT + NEW_TOKENS},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference implementation of this path is HIP for AMD gfx1101; its "
+                "CPU restatement (oracle/) is timed instead",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def our_arm(args, rank: int, world: int, local_rank: int):
+    from lrrt_b200 import qwen as Q
+
+    weights, tail, prompt = make_weights(rank)
+    capacity = PROMPT + NEW_TOKENS
+    config = Q.ModelConfig(layer_count=LAYERS, vocab_size=VOCAB, cache_capacity=capacity,
+                           max_tokens_per_run=NEW_TOKENS)
+    model = Q.Model(config, device_index=local_rank)
+    for i, w in enumerate(weights):
+        model.set_layer(i, w)
+    model.set_tail(tail["final_norm"], tail["lm_head"])
+    model.ingest_prompt([int(t) for t in prompt])
+    start_position = PROMPT - 1
+    request = model.request(start_position, NEW_TOKENS)
+
+    def check(state):
+        if state.status != 2 or state.generated_tokens != NEW_TOKENS:
+            raise RuntimeError(f"decode run failed: status {state.status} error "
+                               f"{state.error_code}")
+
+    for _ in range(args.warmup):
+        model.launch(request)
+    model.synchronize()
+    check(model.read_state())
+    assert model.read_state().fused_path == 1
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_module
+        dist = dist_module
+        dist.barrier()
+    timer = Q.EventTimer(model.device)
+    per_launch = []
+    launch_timer = Q.EventTimer(model.device)
+    with ClockSampler(local_rank) as clocks:
+        model.synchronize()
+        timer.record_start()
+        for _ in range(args.steps):
+            model.launch(request)
+        timer.record_end()
+        model.synchronize()
+        total_ns = timer.elapsed_ns()
+        # Per-launch durations (separately bracketed) for the roofline.
+        for _ in range(min(args.steps, 3)):
+            launch_timer.record_start()
+            model.launch(request)
+            launch_timer.record_end()
+            model.synchronize()
+            per_launch.append(launch_timer.elapsed_ns())
+    check(model.read_state())
+    clock_summary = clocks.summary()
+
+    # End to end through the C ABI: host hidden in, host tokens out.
+    hidden_host = tail["lm_head"][int(prompt[-1])].copy()
+    tokens_host = np.zeros(NEW_TOKENS, np.uint32)
+    for _ in range(max(1, min(args.warmup, 2))):
+        model.generate(start_position, NEW_TOKENS, hidden=hidden_host, tokens=tokens_host)
+    e2e_start = time.perf_counter()
+    for _ in range(args.steps):
+        state, _ = model.generate(start_position, NEW_TOKENS, hidden=hidden_host,
+                                  tokens=tokens_host)
+        check(state)
+    e2e_seconds = time.perf_counter() - e2e_start
+
+    elapsed_s = total_ns / 1e9
+    if world > 1:
+        import torch
+        t = torch.tensor([elapsed_s, e2e_seconds], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_s, e2e_seconds = float(t[0]), float(t[1])
+
+    info = model.info
+    weight_bytes = int(info.weight_bytes_per_token)
+    algorithmic = algorithmic_bytes_per_launch(weight_bytes, start_position, NEW_TOKENS)
+    launch_s = statistics.median(per_launch) / 1e9
+    peak, peak_kind = measured_peaks()
+    achieved = algorithmic / launch_s / 1e9
+    traffic_per_token = profiled_traffic_per_token()
+    roofline = {
+        "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+        "frac": achieved / peak, "peak_source": peak_kind,
+        "traffic": traffic_per_token * NEW_TOKENS if traffic_per_token else None,
+        "algorithmic_bytes_per_launch": algorithmic,
+        "kernel": "qwen_stateful_graph_compiled_kernel",
+    }
+    tokens_total = world * NEW_TOKENS * args.steps
+    line = {
+        "metric": METRIC, "value": tokens_total / elapsed_s, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * elapsed_s / args.steps,
+        "ms_per_token": 1000.0 * elapsed_s / args.steps / NEW_TOKENS,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init weights N(0,0.02), seeded prompt)",
+        "config": {"workload": "config2: 24-layer Qwen2.5-0.5B-arch FP32 greedy decode, "
+                               "batch 1, 32-token prompt, 128 new tokens per step",
+                   "global_batch": world, "seq_len": PROMPT + NEW_TOKENS,
+                   "parallelism": f"dp{world} (independent replicas, no collective)",
+                   "l2": "weights 2 GB > L2 126 MB, no flush needed",
+                   "workers": info.worker_count},
+        "e2e": {"value": tokens_total / e2e_seconds, "unit": "tokens/s",
+                "h2d_bytes_per_step": 896 * 4, "d2h_bytes_per_step": NEW_TOKENS * 4},
+        "gpu_launches": args.steps,
+        "roofline": roofline,
+        "clocks": clock_summary,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import oracle as O
+        threads = O.max_threads()
+        tps, tokens, seconds = cpu_tokens_per_second(weights, tail, prompt, args.cpu_seconds,
+                                                     threads)
+        line["cpu_baseline"] = {
+            "value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{tokens} single-token decodes of the same 24-layer model "
+                      f"({seconds:.1f} s, OpenMP over rows, reference reduction order)"}
+    model.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and "RANK" in os.environ:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        if args.impl == "reference":
+            reference_arm(args, rank, world)
+        else:
+            our_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1 and "RANK" in os.environ:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

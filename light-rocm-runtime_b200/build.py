@@ -1,0 +1,103 @@
+"""Builds every native artefact of the package in-tree.
+
+Outputs (git-ignored, shipped with the working tree):
+  lib/liblrrt.so                  lr_* C ABI over the CUDA driver API
+  lib/liblrrt_qwen.so             Qwen decode driver (include/lrrt_qwen.h)
+  lib/qwen_stateful_graph.cubin   sm_100a decode megakernels
+  lib/stateful_graph_fixture.cubin  sm_100a scheduler fixture kernels
+  _build/tests/*                  C++ host tests (tests/cpp)
+
+Rebuilds a target only when one of its inputs is newer than it.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PACKAGE = Path(__file__).resolve().parent
+REPO = PACKAGE.parent
+INCLUDE = REPO / "include"
+LIB = PACKAGE / "lib"
+BUILD = PACKAGE / "_build"
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+NVCC = str(CUDA_HOME / "bin" / "nvcc")
+CXX = shutil.which("g++") or "g++"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CXXFLAGS = ["-std=c++17", "-O2", "-fPIC", "-Wall", "-Wextra", f"-I{INCLUDE}",
+            f"-I{CUDA_HOME / 'include'}"]
+NVCCFLAGS = ["-std=c++17", "-O3", *ARCH, "-lineinfo", f"-I{INCLUDE}"]
+
+
+def _headers() -> list[Path]:
+    return sorted(INCLUDE.rglob("*.h*")) + sorted(INCLUDE.rglob("*.cuh"))
+
+
+def _stale(target: Path, inputs: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    stamp = target.stat().st_mtime
+    return any(path.stat().st_mtime > stamp for path in inputs)
+
+
+def _run(command: list[str], verbose: bool) -> None:
+    if verbose:
+        print("+", " ".join(command), flush=True)
+    subprocess.run(command, check=True)
+
+
+def build(verbose: bool = False) -> dict[str, Path]:
+    LIB.mkdir(exist_ok=True)
+    BUILD.mkdir(exist_ok=True)
+    headers = _headers()
+    csrc = PACKAGE / "csrc"
+    outputs: dict[str, Path] = {}
+
+    runtime = LIB / "liblrrt.so"
+    runtime_sources = sorted((csrc / "runtime").glob("*.cpp"))
+    runtime_inputs = runtime_sources + sorted((csrc / "runtime").glob("*.hpp")) + headers
+    if _stale(runtime, runtime_inputs):
+        _run([CXX, *CXXFLAGS, "-shared", "-fvisibility=hidden",
+              *map(str, runtime_sources), "-o", str(runtime), "-ldl"], verbose)
+    outputs["runtime"] = runtime
+
+    driver = LIB / "liblrrt_qwen.so"
+    driver_sources = sorted((csrc / "qwen").glob("*.cpp"))
+    if _stale(driver, driver_sources + headers + [runtime]):
+        _run([CXX, *CXXFLAGS, "-shared", "-fvisibility=hidden",
+              *map(str, driver_sources), "-o", str(driver), f"-L{LIB}", "-llrrt",
+              "-Wl,-rpath,$ORIGIN"], verbose)
+    outputs["driver"] = driver
+
+    for name in ("qwen_stateful_graph", "stateful_graph_fixture"):
+        source = csrc / "kernels" / f"{name}.cu"
+        cubin = LIB / f"{name}.cubin"
+        if _stale(cubin, [source] + headers):
+            _run([NVCC, *NVCCFLAGS, "-cubin", str(source), "-o", str(cubin)], verbose)
+        outputs[name] = cubin
+
+    tests_dir = REPO / "tests" / "cpp"
+    test_build = BUILD / "tests"
+    test_build.mkdir(exist_ok=True)
+    for source in sorted(tests_dir.glob("*.cpp")):
+        binary = test_build / source.stem
+        if _stale(binary, [source] + headers + [runtime]):
+            _run([CXX, *CXXFLAGS, str(source), "-o", str(binary), f"-L{LIB}", "-llrrt",
+                  "-Wl,-rpath,$ORIGIN/../../lib"], verbose)
+        outputs[f"test:{source.stem}"] = binary
+    return outputs
+
+
+def build_oracle(verbose: bool = False) -> Path:
+    """Compiles the CPU oracle (test infrastructure) with its own Makefile."""
+    oracle = REPO / "oracle"
+    _run(["make", "-s", "-C", str(oracle)], verbose)
+    return oracle / "_build" / "liblrrt_oracle.so"
+
+
+if __name__ == "__main__":
+    for key, path in build(verbose="-v" in sys.argv).items():
+        print(f"{key}: {path}")
+    print("oracle:", build_oracle(verbose="-v" in sys.argv))

@@ -1,0 +1,200 @@
+"""Parity of the sm_100a decode kernels with the CPU oracle on identical
+seeded weights and inputs (tolerance: max relative logit error 1e-4, greedy
+tokens and integer state bit-exact)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import LOGIT_RTOL, build_pair, ingest_prompt, max_relative_error, prefill_kv
+from lrrt_b200 import native as N
+from lrrt_b200 import qwen as Q
+from lrrt_b200 import synthetic as S
+
+ACTIVATION_RTOL = 1.0e-4
+
+BUFFERS = ("hidden", "attention_normalized", "query", "key", "value", "mlp_normalized",
+           "activated", "projected", "final_normalized")
+
+
+def compare_run(model, oracle, state, tokens, check_buffers=True):
+    d = oracle.decode_state
+    assert state.status == 2, Q.STATUS_NAMES.get(state.status)
+    assert state.error_code == 0
+    assert tokens.tolist() == oracle.output_tokens[:d.generated_tokens].tolist()
+    assert (state.generated_tokens, state.token_position, state.kv_length,
+            state.stop_reason, state.sampled_token) == (
+        d.generated_tokens, d.token_position, d.kv_length, d.stop_reason, d.sampled_token)
+    assert abs(state.sampled_logit - d.sampled_logit) <= LOGIT_RTOL * max(1.0, abs(d.sampled_logit))
+    if not check_buffers:
+        return
+    for name in BUFFERS:
+        got = model.read(name)
+        want = getattr(oracle, name)
+        assert max_relative_error(got, want) <= ACTIVATION_RTOL, name
+    partials = model.read("partial_values")
+    assert max_relative_error(partials, oracle.partial_values[:len(partials)]) <= LOGIT_RTOL
+    assert model.read("partial_indices").tolist() == \
+        oracle.partial_indices[:len(partials)].tolist()
+    last = d.token_position + 1
+    for layer in range(oracle.layers):
+        for name, cache in (("key_cache", oracle.key_cache), ("value_cache", oracle.value_cache)):
+            got = model.read(name, layer).reshape(-1, 128)[:last]
+            assert max_relative_error(got, cache[layer][:last]) <= ACTIVATION_RTOL, (name, layer)
+
+
+@pytest.fixture(scope="module")
+def small(gpu):
+    """2 layers, vocab 4096, prompt of 6 tokens: fused path, every path."""
+    model, oracle, _, _ = build_pair(seed=7, layers=2, vocab=4096, capacity=64,
+                                     max_tokens=24)
+    prompt = S.prompt(7, 6, 4096)
+    ingest_prompt(model, oracle, prompt)
+    yield model, oracle, prompt
+    model.close()
+
+
+@pytest.mark.gpu
+def test_small_model_compiled_fused_matches_oracle(small):
+    model, oracle, prompt = small
+    start = len(prompt) - 1
+    oracle.decode(oracle.embedding(int(prompt[-1])), start, 24)
+    state, tokens = model.decode(start, 24)
+    assert state.fused_path == 1, "compiled run did not take the fused sm_100a path"
+    compare_run(model, oracle, state, tokens)
+    # executed task count and final phase as the reference verifies them
+    layers, steps, partitions = 2, 24, model.info.lm_head_partitions
+    assert state.executed_tasks == steps * layers * 79 + steps * (partitions + 3)
+    assert state.phase >> 8 == steps * (2 * layers + 1) - 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("path", [Q.PATH_DYNAMIC, Q.PATH_HOST_STEP, Q.PATH_STAGE_PROFILE])
+def test_small_model_other_paths_match_oracle(small, path):
+    model, oracle, prompt = small
+    start = len(prompt) - 1
+    oracle.decode(oracle.embedding(int(prompt[-1])), start, 12)
+    state, tokens = model.decode(start, 12, path=path)
+    compare_run(model, oracle, state, tokens)
+    if path == Q.PATH_STAGE_PROFILE:
+        ticks, counts = model.stage_profile()
+        assert sum(ticks) > 0 and sum(counts) > 0
+
+
+@pytest.mark.gpu
+def test_generic_compiled_path_matches_oracle(gpu):
+    model, oracle, _, _ = build_pair(seed=3, layers=2, vocab=1000, capacity=32,
+                                     max_tokens=8, partitions=7, fused=False)
+    hidden = S.hidden(3)
+    model.set_hidden(hidden)
+    oracle.decode(hidden, 0, 8)
+    state, tokens = model.decode(0, 8)
+    assert state.fused_path == 2
+    compare_run(model, oracle, state, tokens)
+    model.close()
+
+
+@pytest.mark.gpu
+def test_scheduler_profile_path_keeps_control_flow(small):
+    model, oracle, prompt = small
+    state, _ = model.decode(len(prompt) - 1, 4, path=Q.PATH_SCHEDULER_PROFILE)
+    assert state.status == 2 and state.step == 4 * 2 and state.generated_tokens == 4
+
+
+@pytest.mark.gpu
+def test_self_checks_chain_cycle_eos(small):
+    """Reference pre-timing self checks (qwen_stateful_graph.cpp:1272-1340)."""
+    model, oracle, prompt = small
+    chain = (N.Task * 64)(*[N.Task(9, (0 if i == 0 else 1 << (i - 1)) & 0xFFFFFFFF, 0, 1, 1, 0,
+                                   (0 if i == 0 else 1 << (i - 1)) >> 32, 0) for i in range(64)])
+    program = (N.Program * 1)(N.Program(0, 64, 0, 1 | 2, 0))
+    state = N.RunState()
+    N.check(N.driver().lrq_model_run_graph(model.handle, chain, 64, program, 1, Q.PATH_DYNAMIC,
+                                           0, 1, 64, 0, 1, C.byref(state)),
+            "lrq_model_run_graph")
+    assert (state.status, state.step, state.predicate_value, state.executed_tasks) == (2, 1, 64, 64)
+
+    tasks, programs = Q.program_table(4096, model.info.lm_head_partitions)
+    mask = 1 << 24
+    tasks[0].dependency_mask = mask & 0xFFFFFFFF
+    tasks[0].dependency_mask_high = mask >> 32
+    task_array = (N.Task * len(tasks))(*tasks)
+    program_array = (N.Program * len(programs))(*programs)
+    N.check(N.driver().lrq_model_run_graph(model.handle, task_array, len(tasks), program_array,
+                                           len(programs), Q.PATH_DYNAMIC, 0, 96, 1, 5, 24,
+                                           C.byref(state)), "lrq_model_run_graph")
+    assert (state.status, state.error_code) == (4, 1)
+
+    start = len(prompt) - 1
+    first_state, first = model.decode(start, 1)
+    eos_state, tokens = model.decode(start, 8, eos_token=int(first[0]))
+    assert eos_state.status == 2 and eos_state.step == 2
+    assert eos_state.generated_tokens == 1 and eos_state.stop_reason == 2
+    assert tokens.tolist() == first.tolist()
+
+
+@pytest.mark.gpu
+def test_barrier_wait_limit_reports_error_and_context_survives(small):
+    """Launching fewer blocks than State.worker_count leaves a grid barrier
+    that can never complete; the bounded wait ends the run with
+    invalid_program / error 3 instead of hanging, and the next run works."""
+    model, oracle, prompt = small
+    workers = model.info.worker_count
+    state, _ = model.decode(len(prompt) - 1, 2, wait_limit_ms=300, launch_workers=workers - 1)
+    assert state.status == 4 and state.error_code == 3
+    state, tokens = model.decode(len(prompt) - 1, 2)
+    assert state.status == 2 and len(tokens) == 2
+
+
+@pytest.mark.gpu
+def test_config1_single_layer_step(gpu):
+    """one decoder layer, KV pre-filled to 128 positions
+    ~ N(0,1), hidden ~ N(0,1), seed 0, full 151936-row tied LM head."""
+    model, oracle, _, _ = build_pair(seed=0, layers=1, vocab=151936, capacity=136,
+                                     max_tokens=4)
+    prefill_kv(model, oracle, 0, 1, 128)
+    hidden = S.hidden(0)
+    model.set_hidden(hidden)
+    oracle.decode(hidden, 128, 4)
+    state, tokens = model.decode(128, 4)
+    assert state.fused_path == 1
+    compare_run(model, oracle, state, tokens)
+    model.close()
+
+
+@pytest.mark.gpu
+def test_long_context_split_attention(gpu):
+    """4096 pre-filled positions: the attention stage runs split over the
+    resident blocks and combines partial softmax states."""
+    model, oracle, _, _ = build_pair(seed=5, layers=2, vocab=2048, capacity=4104,
+                                     max_tokens=8)
+    prefill_kv(model, oracle, 5, 2, 4096)
+    hidden = S.hidden(5)
+    model.set_hidden(hidden)
+    oracle.decode(hidden, 4096, 8)
+    state, tokens = model.decode(4096, 8)
+    assert state.fused_path == 1
+    compare_run(model, oracle, state, tokens)
+    model.close()
+
+
+@pytest.mark.gpu
+def test_config2_full_model_128_tokens(gpu):
+    """24 layers, vocab 151936, 32-token prompt (seed 1),
+    128 greedy tokens identical to the oracle."""
+    O.set_threads(O.max_threads())
+    model, oracle, _, tail = build_pair(seed=1, layers=24, vocab=151936, capacity=160,
+                                        max_tokens=128)
+    prompt = S.prompt(1, 32, 151936)
+    ingest_prompt(model, oracle, prompt)
+    start = len(prompt) - 1
+    oracle.decode(oracle.embedding(int(prompt[-1])), start, 128)
+    state, tokens = model.decode(start, 128)
+    assert state.fused_path == 1
+    gaps = oracle.top2_gaps[:128]
+    near_ties = int(np.sum(gaps < 1.0e-4 * np.abs(oracle.partial_values).max()))
+    assert near_ties == 0, "oracle reports near-tied greedy steps"
+    compare_run(model, oracle, state, tokens)
+    O.set_threads(1)
+    model.close()
