@@ -1,0 +1,185 @@
+// Work partition and weight-stream order of the fused resident decode path,
+// shared by the sm_100a kernel and host-side tests.
+//
+// Every block (worker w of W) owns a contiguous range of "units" of each
+// weight matrix; a unit is what one shared-memory ring slot holds:
+//   QKV   144 units: 8 rows = rows f..f+3 of one head and their rotary
+//                    partners f+32..f+35 (Q heads 0-13, K heads, then V)
+//   OUT   112 units: 8 consecutive o_proj rows
+//   GU   1216 units: gate rows 4u..4u+3 followed by up rows 4u..4u+3
+//   DOWN  896 units: one 4864-float down_proj row
+//   LM   ceil(V/8) units: 8 LM-head rows (the last may be shorter)
+// QKV, OUT, DOWN and LM units are split evenly; gate/up units are assigned so
+// that each block's bytes per layer (all four matrices) are balanced.
+//
+// A block's weight stream is the cyclic sequence
+//   [QKV(l), OUT(l), GU(l), DOWN(l)] for l = 0..L-1, then LM(0), repeat,
+// restricted to its own units. The producer issues it in this order; the
+// consumer walks the compiled stages, which visit the same units in the same
+// order, and checks each slot's tag.
+#ifndef LRRT_QWEN_RESIDENT_SCHEDULE_HPP_
+#define LRRT_QWEN_RESIDENT_SCHEDULE_HPP_
+
+#include "lrrt/persistent_graph/abi.hpp"
+#include "lrrt/qwen/resident_layout.hpp"
+#include "lrrt/qwen/stateful_graph_context.hpp"
+
+#include <cstdint>
+
+namespace lrrt::qwen::stateful_graph::resident {
+
+enum StreamKind : uint32_t { kNoKind = 0, kQkv = 1, kOut = 2, kGateUp = 3, kDown = 4,
+                             kLmHead = 5 };
+constexpr uint32_t kKinds = 6;
+
+constexpr uint32_t kQkvUnits = kPackedQkvSize / kSlotRows;     // 144
+constexpr uint32_t kQUnits = kQuerySize / kSlotRows;           // 112
+constexpr uint32_t kKUnits = kKvSize / kSlotRows;              // 16
+constexpr uint32_t kOUnits = kHiddenSize / kSlotRows;          // 112
+constexpr uint32_t kGuRowsPerUnit = kSlotRows / 2u;            // 4
+constexpr uint32_t kGuUnits = kIntermediateSize / kGuRowsPerUnit; // 1216
+constexpr uint32_t kDownUnits = kHiddenSize;                   // 896
+static_assert(kPackedQkvSize % kSlotRows == 0);
+static_assert(kIntermediateSize % kGuRowsPerUnit == 0);
+
+struct UnitRange {
+  uint32_t begin, end;
+};
+
+LRRT_HOST_DEVICE constexpr uint32_t lm_units_for(uint32_t vocab) {
+  return (vocab + kSlotRows - 1u) / kSlotRows;
+}
+
+// [w*U/W, (w+1)*U/W): contiguous, disjoint, covering [0, U).
+LRRT_HOST_DEVICE inline UnitRange even_range(uint32_t units, uint32_t worker,
+                                             uint32_t workers) {
+  return {static_cast<uint32_t>(uint64_t{units} * worker / workers),
+          static_cast<uint32_t>(uint64_t{units} * (worker + 1u) / workers)};
+}
+
+// Block holding unit `unit` of an even_range split (its inverse).
+LRRT_HOST_DEVICE inline uint32_t even_owner(uint32_t unit, uint32_t units,
+                                            uint32_t workers) {
+  return static_cast<uint32_t>((uint64_t{unit + 1u} * workers - 1u) / units);
+}
+
+LRRT_HOST_DEVICE inline uint64_t fixed_layer_bytes(uint32_t worker, uint32_t workers) {
+  const UnitRange q = even_range(kQkvUnits, worker, workers);
+  const UnitRange o = even_range(kOUnits, worker, workers);
+  const UnitRange d = even_range(kDownUnits, worker, workers);
+  return uint64_t{q.end - q.begin + o.end - o.begin} * kSlotBytes +
+         uint64_t{d.end - d.begin} * kDownRowBytes;
+}
+
+// Gate/up split by cumulative rounding of each block's remaining byte budget
+// (total layer bytes / W minus its QKV + OUT + DOWN bytes). Non-decreasing
+// boundaries, first block starts at 0, last ends at kGuUnits.
+LRRT_HOST_DEVICE inline uint32_t gate_up_boundary(uint32_t worker, uint32_t workers,
+                                                  uint64_t fixed_prefix) {
+  if (worker + 1u >= workers) {
+    return kGuUnits;
+  }
+  const uint64_t total = uint64_t{kQkvUnits + kOUnits + kGuUnits} * kSlotBytes +
+                         uint64_t{kDownUnits} * kDownRowBytes;
+  const int64_t want = static_cast<int64_t>(total * (worker + 1u) / workers) -
+                       static_cast<int64_t>(fixed_prefix);
+  const int64_t units = want <= 0 ? 0 : (want + kSlotBytes / 2) / kSlotBytes;
+  return units > static_cast<int64_t>(kGuUnits) ? kGuUnits : static_cast<uint32_t>(units);
+}
+
+LRRT_HOST_DEVICE inline UnitRange balanced_gate_up(uint32_t worker, uint32_t workers) {
+  uint64_t fixed_prefix = 0;
+  uint32_t previous = 0, current = 0;
+  for (uint32_t w = 0; w <= worker; ++w) {
+    fixed_prefix += fixed_layer_bytes(w, workers);
+    uint32_t boundary = gate_up_boundary(w, workers, fixed_prefix);
+    boundary = boundary < current ? current : boundary; // keep boundaries monotone
+    previous = current;
+    current = boundary;
+  }
+  return {previous, current};
+}
+
+struct UnitRanges {
+  UnitRange of[kKinds];
+};
+
+LRRT_HOST_DEVICE inline UnitRanges unit_ranges(uint32_t worker, uint32_t workers,
+                                               uint32_t vocab) {
+  UnitRanges r{};
+  r.of[kNoKind] = {0, 0};
+  r.of[kQkv] = even_range(kQkvUnits, worker, workers);
+  r.of[kOut] = even_range(kOUnits, worker, workers);
+  r.of[kGateUp] = balanced_gate_up(worker, workers);
+  r.of[kDown] = even_range(kDownUnits, worker, workers);
+  r.of[kLmHead] = even_range(lm_units_for(vocab), worker, workers);
+  return r;
+}
+
+// Tag of a unit in a ring slot: kind, layer (LM head uses layer 0), unit.
+LRRT_HOST_DEVICE constexpr uint32_t make_tag(uint32_t kind, uint32_t layer, uint32_t unit) {
+  return (kind << 28) | ((layer & 0xffu) << 20) | (unit & 0xfffffu);
+}
+
+struct StreamCursor {
+  uint32_t layer;
+  uint32_t kind;
+  uint32_t unit;
+};
+
+// Moves the cursor to the first existing unit at or after it, wrapping
+// layers and decode steps. `layers` >= 1; at least one unit must exist per
+// cycle (the caller checks) or the cursor stops after a bounded search.
+LRRT_HOST_DEVICE inline void normalize_cursor(const UnitRanges &r, uint32_t layers,
+                                              StreamCursor &c) {
+  for (uint32_t guard = 0; guard < 8u * (layers + 2u); ++guard) {
+    if (c.unit < r.of[c.kind].end) {
+      return;
+    }
+    if (c.kind == kLmHead) {
+      c.kind = kQkv;
+      c.layer = 0;
+    } else if (c.kind == kDown) {
+      if (c.layer + 1u >= layers) {
+        c.kind = kLmHead;
+        c.layer = 0;
+      } else {
+        c.kind = kQkv;
+        ++c.layer;
+      }
+    } else {
+      ++c.kind;
+    }
+    c.unit = r.of[c.kind].begin;
+  }
+}
+
+LRRT_HOST_DEVICE inline void advance_cursor(const UnitRanges &r, uint32_t layers,
+                                            StreamCursor &c) {
+  ++c.unit;
+  normalize_cursor(r, layers, c);
+}
+
+// Cursor at the start of the Program the launch begins with: program 0 at the
+// QKV units of layer `layer`, program 1 at its gate/up units, program 2 at the
+// LM head.
+LRRT_HOST_DEVICE inline StreamCursor start_cursor(const UnitRanges &r, uint32_t layers,
+                                                  uint32_t program, uint32_t layer) {
+  StreamCursor c{program == 2 ? 0u : layer,
+                 program == 0 ? kQkv : (program == 1 ? kGateUp : kLmHead), 0};
+  c.unit = r.of[c.kind].begin;
+  normalize_cursor(r, layers, c);
+  return c;
+}
+
+LRRT_HOST_DEVICE inline uint32_t units_per_cycle(const UnitRanges &r, uint32_t layers) {
+  uint32_t units = r.of[kLmHead].end - r.of[kLmHead].begin;
+  for (uint32_t k = kQkv; k <= kDown; ++k) {
+    units += layers * (r.of[k].end - r.of[k].begin);
+  }
+  return units;
+}
+
+} // namespace lrrt::qwen::stateful_graph::resident
+
+#endif // LRRT_QWEN_RESIDENT_SCHEDULE_HPP_

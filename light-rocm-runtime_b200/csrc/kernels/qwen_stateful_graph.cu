@@ -30,6 +30,7 @@
 #include "lrrt/persistent_graph/compiled_scheduler.cuh"
 #include "lrrt/persistent_graph/device_scheduler.cuh"
 #include "lrrt/qwen/resident_layout.hpp"
+#include "lrrt/qwen/resident_schedule.hpp"
 #include "lrrt/qwen/stateful_graph_context.hpp"
 
 #include <cstdint>
@@ -530,69 +531,8 @@ __device__ void generic_execute_stage(const sg::Stage &stage, const sg::Task *ta
 // ============================================================= fused path ==
 
 using namespace qd::resident;
-constexpr uint32_t kQkvUnits = qd::kPackedQkvSize / kSlotRows;      // 144
-constexpr uint32_t kQUnits = qd::kQuerySize / kSlotRows;            // 112
-constexpr uint32_t kKUnits = qd::kKvSize / kSlotRows;               // 16
-constexpr uint32_t kOUnits = qd::kHiddenSize / kSlotRows;           // 112
-constexpr uint32_t kGuUnits = qd::kIntermediateSize / 4u;           // 1216
-constexpr uint32_t kDownUnits = qd::kHiddenSize;                    // 896
 constexpr uint32_t kMaxAttentionChunks = 128;
 constexpr uint32_t kScoreTile = 64;
-static_assert(qd::kPackedQkvSize % kSlotRows == 0);
-
-enum StreamKind : uint32_t { kQkv = 1, kOut = 2, kGateUp = 3, kDown = 4, kLmHead = 5 };
-
-struct UnitRange {
-  uint32_t begin, end;
-};
-
-__device__ __forceinline__ UnitRange even_range(uint32_t units, uint32_t worker,
-                                                 uint32_t workers) {
-  return {static_cast<uint32_t>(uint64_t{units} * worker / workers),
-          static_cast<uint32_t>(uint64_t{units} * (worker + 1u) / workers)};
-}
-
-// Gate/up units are spread so that each block's total bytes per layer (QKV +
-// o_proj + gate/up + down) are balanced, using cumulative rounding of the
-// per-block remainder.
-__device__ UnitRange balanced_gate_up(uint32_t worker, uint32_t workers) {
-  auto fixed_bytes = [&](uint32_t w) -> uint64_t {
-    const UnitRange q = even_range(kQkvUnits, w, workers);
-    const UnitRange o = even_range(kOUnits, w, workers);
-    const UnitRange d = even_range(kDownUnits, w, workers);
-    return uint64_t{q.end - q.begin + o.end - o.begin} * kSlotBytes +
-           uint64_t{d.end - d.begin} * kDownRowBytes;
-  };
-  const uint64_t total = uint64_t{kQkvUnits + kOUnits + kGuUnits} * kSlotBytes +
-                         uint64_t{kDownUnits} * kDownRowBytes;
-  uint64_t fixed_prefix = 0;
-  uint32_t previous = 0, current = 0;
-  for (uint32_t w = 0; w <= worker; ++w) {
-    fixed_prefix += fixed_bytes(w);
-    const int64_t want = static_cast<int64_t>(total * (w + 1u) / workers) -
-                         static_cast<int64_t>(fixed_prefix);
-    int64_t units = want <= 0 ? 0 : (want + kSlotBytes / 2) / kSlotBytes;
-    if (w + 1u == workers) {
-      units = kGuUnits;
-    }
-    units = units < previous ? previous : units;
-    units = units > kGuUnits ? kGuUnits : units;
-    if (w == worker) {
-      current = static_cast<uint32_t>(units);
-    } else {
-      previous = static_cast<uint32_t>(units);
-    }
-  }
-  return {worker == 0 ? 0u : previous, current};
-}
-
-// Position in this block's cyclic weight stream:
-// [QKV, O, GU, DOWN] x layers, then LM head, repeated.
-struct StreamCursor {
-  uint32_t layer;
-  uint32_t kind;
-  uint32_t unit;
-};
 
 struct QwenBlock {
   bool fused;
@@ -600,7 +540,7 @@ struct QwenBlock {
   const qd::Context *contexts;
   qd::Workspace *workspace;
   uint32_t worker, workers, layers, vocab, lm_units;
-  UnitRange ranges[6]; // indexed by StreamKind
+  UnitRanges ranges;   // this block's units of each stream kind
   uint64_t policy;
   uint32_t limit_ms;
   uint32_t produced, consumed; // units issued / consumed by this block
@@ -608,43 +548,6 @@ struct QwenBlock {
   bool stream_empty;
   sg::Stage lm_stage;          // the tail Program's LM-head stage
 };
-
-__device__ __forceinline__ uint32_t make_tag(uint32_t kind, uint32_t layer, uint32_t unit) {
-  return (kind << 28) | ((layer & 0xffu) << 20) | (unit & 0xfffffu);
-}
-
-__device__ __forceinline__ uint32_t stream_next_kind(uint32_t kind) {
-  return kind == kDown ? kQkv : kind + 1u;
-}
-
-// Moves the cursor forward to the first unit at or after it that exists
-// (skipping empty ranges; wrapping layers and decode steps).
-__device__ void normalize_cursor(const QwenBlock &b, StreamCursor &cursor) {
-  for (uint32_t guard = 0; guard < 8u * (b.layers + 2u); ++guard) {
-    if (cursor.unit < b.ranges[cursor.kind].end) {
-      return;
-    }
-    if (cursor.kind == kLmHead) {
-      cursor.kind = kQkv;
-      cursor.layer = 0;
-    } else if (cursor.kind == kDown) {
-      if (cursor.layer + 1u == b.layers) {
-        cursor.kind = kLmHead;
-      } else {
-        cursor.kind = kQkv;
-        ++cursor.layer;
-      }
-    } else {
-      cursor.kind = stream_next_kind(cursor.kind);
-    }
-    cursor.unit = b.ranges[cursor.kind].begin;
-  }
-}
-
-__device__ __forceinline__ void advance_cursor(const QwenBlock &b, StreamCursor &cursor) {
-  ++cursor.unit;
-  normalize_cursor(b, cursor);
-}
 
 // Issues the bulk copies of the cursor's unit into the slot of unit number
 // b.produced (thread 0 only).
@@ -710,7 +613,7 @@ __device__ void issue_unit(QwenBlock &b) {
                              b.policy);
   }
   ++b.produced;
-  advance_cursor(b, b.cursor);
+  advance_cursor(b.ranges, b.layers, b.cursor);
 }
 
 // Waits for consumption number b.consumed, checks its tag. Returns the slot
@@ -831,7 +734,7 @@ __device__ bool consume_rows(QwenBlock &b, sg::State *state, uint32_t kind, uint
   const uint32_t warp = threadIdx.x >> 5u;
   float4 x[7];
   load_input_registers(b, x, lane);
-  const UnitRange range = b.ranges[kind];
+  const UnitRange range = b.ranges.of[kind];
   for (uint32_t u = range.begin; u < range.end; ++u) {
     const float *slot = slot_acquire(b, state, kind, layer, u);
     if (slot == nullptr) {
@@ -936,7 +839,7 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
     x[j] = index < kVectorsPerWarp ? input[warp * kVectorsPerWarp + index]
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  const UnitRange range = b.ranges[kDown];
+  const UnitRange range = b.ranges.of[kDown];
   for (uint32_t u = range.begin; u < range.end; ++u) {
     const float *slot = slot_acquire(b, state, kDown, layer, u);
     if (slot == nullptr) {
@@ -1158,7 +1061,7 @@ __device__ void fused_attention(QwenBlock &b, qd::Context *c) {
 // Program task it overlaps; candidate slot (worker + task) in the workspace.
 __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &stage,
                               const sg::Task *tasks) {
-  const UnitRange range = b.ranges[kLmHead];
+  const UnitRange range = b.ranges.of[kLmHead];
   if (range.begin == range.end) {
     return;
   }
@@ -1198,12 +1101,6 @@ __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &s
   }
 }
 
-// Block holding LM-head unit `unit` (inverse of even_range).
-__device__ __forceinline__ uint32_t lm_block_of_unit(uint32_t unit, uint32_t units,
-                                                     uint32_t workers) {
-  return static_cast<uint32_t>((uint64_t{unit + 1u} * workers - 1u) / units);
-}
-
 // Per-task top-1 over the candidate slots, then the reference reduce_top1.
 __device__ void fused_reduce_top1(QwenBlock &b, const sg::Stage &stage,
                                   const sg::Task *tasks, qd::Context *c) {
@@ -1211,9 +1108,9 @@ __device__ void fused_reduce_top1(QwenBlock &b, const sg::Stage &stage,
   qd::TailContext *tail = c->tail;
   if (threadIdx.x < stage.task_count) {
     const sg::Task &task = lm_tasks[threadIdx.x];
-    const uint32_t first = lm_block_of_unit(task.begin / kSlotRows, b.lm_units, b.workers);
+    const uint32_t first = even_owner(task.begin / kSlotRows, b.lm_units, b.workers);
     const uint32_t last =
-        lm_block_of_unit((task.end - 1u) / kSlotRows, b.lm_units, b.workers);
+        even_owner((task.end - 1u) / kSlotRows, b.lm_units, b.workers);
     float best_value = -INFINITY;
     uint32_t best_index = UINT32_MAX;
     for (uint32_t w = first; w <= last; ++w) {
@@ -1384,29 +1281,13 @@ template <bool kStageProfile> struct QwenWorkloadT {
     b.vocab = b.contexts[0].tail->vocab_size;
     b.lm_units = (b.vocab + kSlotRows - 1u) / kSlotRows;
     b.lm_stage = args.stages[args.compiled_programs[2].stage_offset + 1u];
-    b.ranges[0] = {0, 0};
-    b.ranges[kQkv] = even_range(kQkvUnits, b.worker, b.workers);
-    b.ranges[kOut] = even_range(kOUnits, b.worker, b.workers);
-    b.ranges[kGateUp] = balanced_gate_up(b.worker, b.workers);
-    b.ranges[kDown] = even_range(kDownUnits, b.worker, b.workers);
-    b.ranges[kLmHead] = even_range(b.lm_units, b.worker, b.workers);
+    b.ranges = unit_ranges(b.worker, b.workers, b.vocab);
     b.policy = dev::l2_evict_first_policy();
-    uint32_t units_per_cycle = b.ranges[kLmHead].end - b.ranges[kLmHead].begin;
-    for (uint32_t k = kQkv; k <= kDown; ++k) {
-      units_per_cycle += b.layers * (b.ranges[k].end - b.ranges[k].begin);
-    }
-    b.stream_empty = units_per_cycle == 0;
-    // The stream starts where the initial Program starts: program 0 at the
-    // QKV units of layer step % layers, program 1 at gate/up, program 2 at
-    // the LM head.
+    b.stream_empty = units_per_cycle(b.ranges, b.layers) == 0;
+    // The stream starts where the initial Program starts (see start_cursor).
     const uint32_t phase = dev::load_relaxed(&args.state->phase);
-    const uint32_t program = sg::phase_program(phase);
-    const uint32_t layer = dev::load_relaxed(&args.state->step) % b.layers;
-    b.cursor = {layer, program == 0 ? kQkv : (program == 1 ? kGateUp : kLmHead), 0};
-    b.cursor.unit = b.ranges[b.cursor.kind].begin;
-    if (!b.stream_empty) {
-      normalize_cursor(b, b.cursor);
-    }
+    b.cursor = start_cursor(b.ranges, b.layers, sg::phase_program(phase),
+                            dev::load_relaxed(&args.state->step) % b.layers);
     if (threadIdx.x == 0) {
       for (uint32_t s = 0; s < kSlots; ++s) {
         dev::mbarrier_init(&b.shared->full[s], 1);

@@ -89,3 +89,11 @@ def test_runtime_without_devices_reports_zero(built):
     # On a GPU-less host lr_init succeeds and reports no devices; on a GPU box
     # this still passes (count > 0).
     assert Q.Runtime.device_count() >= 0
+
+
+def test_cpp_resident_schedule_checks(built):
+    """Fused-path partition and weight-stream order (producer == consumer)."""
+    binary = built["test:resident_schedule_test"]
+    result = subprocess.run([str(binary)], capture_output=True, text=True, timeout=300)
+    assert result.returncode == 0, result.stderr
+    assert "ok" in result.stdout
