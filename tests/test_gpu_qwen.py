@@ -18,9 +18,15 @@ BUFFERS = ("hidden", "attention_normalized", "query", "key", "value", "mlp_norma
            "activated", "projected", "final_normalized")
 
 
-def compare_run(model, oracle, state, tokens, check_buffers=True):
+def compare_run(model, oracle, state, tokens, check_buffers=True, host_driven=False):
     d = oracle.decode_state
-    assert state.status == 2, Q.STATUS_NAMES.get(state.status)
+    if host_driven:
+        # The host-driven kernels never publish a status; the reference checks
+        # predicate and step instead (qwen_stateful_graph.cpp:1633-1638).
+        assert state.predicate_value == 1
+        assert state.step == d.generated_tokens * oracle.layers
+    else:
+        assert state.status == 2, Q.STATUS_NAMES.get(state.status)
     assert state.error_code == 0
     assert tokens.tolist() == oracle.output_tokens[:d.generated_tokens].tolist()
     assert (state.generated_tokens, state.token_position, state.kv_length,
@@ -76,7 +82,7 @@ def test_small_model_other_paths_match_oracle(small, path):
     start = len(prompt) - 1
     oracle.decode(oracle.embedding(int(prompt[-1])), start, 12)
     state, tokens = model.decode(start, 12, path=path)
-    compare_run(model, oracle, state, tokens)
+    compare_run(model, oracle, state, tokens, host_driven=path == Q.PATH_HOST_STEP)
     if path == Q.PATH_STAGE_PROFILE:
         ticks, counts = model.stage_profile()
         assert sum(ticks) > 0 and sum(counts) > 0
@@ -192,9 +198,16 @@ def test_config2_full_model_128_tokens(gpu):
     oracle.decode(oracle.embedding(int(prompt[-1])), start, 128)
     state, tokens = model.decode(start, 128)
     assert state.fused_path == 1
+    # Steps whose best and second-best logits are closer than the logit
+    # tolerance are reported; the token streams must still be identical.
     gaps = oracle.top2_gaps[:128]
-    near_ties = int(np.sum(gaps < 1.0e-4 * np.abs(oracle.partial_values).max()))
-    assert near_ties == 0, "oracle reports near-tied greedy steps"
+    want = oracle.output_tokens[:128]
+    near_ties = [int(i) for i in np.nonzero(gaps < 1.0e-4 * np.abs(state.sampled_logit))[0]]
+    print(f"config2: near-tied steps {near_ties}, min gap {float(gaps.min()):.3e}")
+    mismatch = np.nonzero(tokens != want)[0]
+    assert mismatch.size == 0, (
+        f"first differing step {int(mismatch[0])} (near-tied steps {near_ties}): "
+        f"gpu {int(tokens[mismatch[0]])} oracle {int(want[mismatch[0]])}")
     compare_run(model, oracle, state, tokens)
     O.set_threads(1)
     model.close()
