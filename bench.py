@@ -52,6 +52,8 @@ def parse_args():
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
                         help="CPU baseline sample length")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
+                        help="tokens per step (smaller only for profiler captures)")
     return parser.parse_args()
 
 
@@ -320,7 +322,9 @@ def our_arm(args, rank: int, world: int, local_rank: int):
 
 
 def main():
+    global NEW_TOKENS
     args = parse_args()
+    NEW_TOKENS = args.new_tokens
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

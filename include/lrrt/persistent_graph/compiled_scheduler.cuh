@@ -30,6 +30,9 @@
 //   end(Block&)                         // before the block returns
 //   initialize_profile(void*)
 //   complete_profile_stage(Block&, const Stage&, const Task*, void*)
+//   kTraceBarriers, trace_barrier(Block&, void* context, const Stage&,
+//                                 const Task*, arrive_ns, leave_ns)
+//                                       // optional per-block barrier trace
 #ifndef LRRT_PERSISTENT_GRAPH_COMPILED_SCHEDULER_CUH_
 #define LRRT_PERSISTENT_GRAPH_COMPILED_SCHEDULER_CUH_
 
@@ -85,27 +88,41 @@ __device__ bool validate_plan(const State *state, const Task *tasks,
   return true;
 }
 
-// Grid barrier number `index` (0-based within the generation). The last
-// arrival runs `on_last` (thread 0 of that block only) before releasing the
-// others. Returns false when the run failed or the wait limit passed.
+// Grid barrier number `index` (0-based within the generation); `workers`
+// blocks arrive. Arrivals accumulate in claimed_mask: a barrier inside a
+// Program is complete once claimed_mask reaches (index + 1) * workers. At a
+// Program's final barrier the last arrival first runs `on_last` (the Program
+// transition, on thread 0 of that block only) and then publishes
+// completed_mask = index + 1, which the other blocks wait for. Returns false
+// when the run failed or the wait limit passed.
+//
+// The block-wide __syncthreads before the arrival orders every thread's writes
+// before thread 0's release; thread 0's acquire and the __syncthreads after the
+// wait order every thread's later reads after the other blocks' writes.
 template <typename OnLast>
 __device__ bool grid_barrier(State *state, MaskState *barrier, uint32_t index,
-                             uint32_t workers, const Deadline &deadline,
+                             uint32_t workers, bool final, const Deadline &deadline,
                              OnLast on_last) {
   __shared__ uint32_t barrier_ok;
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     const uint32_t target = (index + 1u) * workers;
-    const uint32_t arrived = fetch_add_acq_rel(&barrier->claimed_mask, 1u) + 1u;
-    if (arrived == target) {
-      on_last();
-      __threadfence();
-      store_release(&barrier->completed_mask, index + 1u);
+    const uint32_t *watched = &barrier->claimed_mask;
+    uint32_t goal = target;
+    if (final) {
+      const uint32_t arrived = fetch_add_acq_rel(&barrier->claimed_mask, 1u) + 1u;
+      if (arrived == target) {
+        on_last();
+        store_release(&barrier->completed_mask, index + 1u);
+      }
+      watched = &barrier->completed_mask;
+      goal = index + 1u;
+    } else {
+      add_release(&barrier->claimed_mask, 1u);
     }
     uint32_t ok = 1;
     uint32_t spins = 0;
-    while (load_acquire(&barrier->completed_mask) < index + 1u) {
+    while (load_acquire(watched) < goal) {
       if ((++spins & 127u) == 0u) {
         if (load_status(state) != static_cast<uint32_t>(Status::running)) {
           ok = 0;
@@ -118,7 +135,6 @@ __device__ bool grid_barrier(State *state, MaskState *barrier, uint32_t index,
         }
       }
     }
-    __threadfence();
     barrier_ok = ok;
   }
   __syncthreads();
@@ -129,8 +145,13 @@ __device__ bool grid_barrier(State *state, MaskState *barrier, uint32_t index,
 
 // Default hooks for workloads without per-block state or fusion.
 struct CompiledWorkloadDefaults {
+  static constexpr bool kTraceBarriers = false;
   struct Block {};
+  __device__ static void trace_barrier(Block &, void *, const Stage &, const Task *,
+                                       uint64_t, uint64_t) {}
   __device__ static void begin(Block &, const ResidentArgs &) {}
+  __device__ static bool local_transitions(const Block &) { return false; }
+  __device__ static void program_begin(Block &, uint32_t) {}
   __device__ static bool barrier_after(Block &, const Stage &, const Stage &,
                                        const Task *) {
     return true;
@@ -141,6 +162,71 @@ struct CompiledWorkloadDefaults {
                                                 const Task *, void *) {}
 };
 
+namespace detail {
+
+// Program state a block tracks for itself in local-transition mode.
+struct LocalControl {
+  uint32_t phase;
+  uint32_t step;
+  uint32_t status;
+  uint32_t error_code;
+  uint64_t executed_tasks;
+};
+
+// The Program transition of finish_program computed from the block's own copy
+// of the control state; predicate_value and branch_value were written by the
+// Program's tasks before its final barrier.
+__device__ __forceinline__ void local_transition(LocalControl &c, const State *state,
+                                                 const Program &program,
+                                                 uint32_t generation,
+                                                 uint32_t phase_state_count,
+                                                 uint32_t max_steps, uint32_t stop_value) {
+  const uint32_t next_step =
+      c.step + ((program.flags & kProgramAdvancesStep) != 0 ? 1u : 0u);
+  c.step = next_step;
+  c.executed_tasks += program.task_count;
+  const bool predicate =
+      (program.flags & kProgramEvaluatesPredicate) != 0 &&
+      load_relaxed(&state->predicate_value) >= stop_value;
+  if (predicate) {
+    c.status = static_cast<uint32_t>(Status::complete);
+  } else if (next_step >= max_steps) {
+    c.status = static_cast<uint32_t>(Status::max_steps);
+  } else if (generation + 1u >= phase_state_count) {
+    c.status = static_cast<uint32_t>(Status::invalid_program);
+    c.error_code = kErrorPhaseSlots;
+  } else {
+    uint32_t next = program.next_program;
+    if ((program.flags & kProgramBranchesOnState) != 0 &&
+        load_relaxed(&state->branch_value) != 0) {
+      next = program.branch_program;
+    }
+    c.phase = make_phase(generation + 1u, next);
+  }
+}
+
+// Block 0 mirrors the local control state into State for the host.
+__device__ __forceinline__ void publish_control(State *state, const LocalControl &c) {
+  state->step = c.step;
+  state->executed_tasks = c.executed_tasks;
+  state->phase = c.phase;
+  if (c.status != static_cast<uint32_t>(Status::running)) {
+    if (c.error_code != 0) {
+      atomicCAS(&state->error_code, 0u, c.error_code);
+    }
+    __threadfence();
+    atomicCAS(&state->status, static_cast<uint32_t>(Status::running), c.status);
+  }
+}
+
+} // namespace detail
+
+// Workloads may opt into block-local Program transitions
+// (local_transitions(block) == true, the same answer in every block): each
+// block then evaluates the transition of a finished Program itself, every grid
+// barrier is a plain counting barrier, and block 0 mirrors the control state
+// into State. The workload must then take the step from program_begin()
+// instead of reading State during the run.
 template <typename Workload>
 __device__ void run_compiled_resident(const ResidentArgs &args) {
   State *state = args.state;
@@ -163,19 +249,36 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
   const uint32_t worker = blockIdx.x;
   typename Workload::Block block{};
   Workload::begin(block, args);
+  const bool local = Workload::local_transitions(block);
+  const uint32_t workers = load_relaxed(&state->worker_count);
   __shared__ uint32_t loop_phase, loop_running;
+  __shared__ detail::LocalControl shared_control;
+  detail::LocalControl control{};
+  if (threadIdx.x == 0) {
+    shared_control = {load_relaxed(&state->phase), load_relaxed(&state->step),
+                      static_cast<uint32_t>(Status::running), 0,
+                      static_cast<uint64_t>(atomicAdd(
+                          reinterpret_cast<unsigned long long *>(&state->executed_tasks),
+                          0ull))};
+  }
+  __syncthreads();
+  control = shared_control;
+  const uint32_t max_steps = load_relaxed(&state->max_steps);
+  const uint32_t stop_value = load_relaxed(&state->stop_value);
   while (true) {
-    if (threadIdx.x == 0) {
-      loop_phase = load_acquire(&state->phase);
+    if (!local) {
+      if (threadIdx.x == 0) {
+        loop_phase = load_acquire(&state->phase);
+      }
+      __syncthreads();
     }
-    __syncthreads();
-    const uint32_t phase = loop_phase;
+    const uint32_t phase = local ? control.phase : loop_phase;
     const uint32_t generation = phase_generation(phase);
     const Program program = args.programs[phase_program(phase)];
     const CompiledProgram compiled = args.compiled_programs[phase_program(phase)];
     MaskState *barrier = &args.phase_states[generation];
-    const uint32_t workers = load_relaxed(&state->worker_count);
     const Deadline deadline(limit_ms);
+    Workload::program_begin(block, control.step);
     uint32_t barrier_index = 0;
     bool ok = true;
     for (uint32_t s = 0; s < compiled.stage_count && ok; ++s) {
@@ -190,7 +293,8 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
                        args.tasks)) {
         continue;
       }
-      ok = detail::grid_barrier(state, barrier, barrier_index++, workers,
+      const uint64_t arrive_ns = Workload::kTraceBarriers ? global_timer_ns() : 0;
+      ok = detail::grid_barrier(state, barrier, barrier_index++, workers, last && !local,
                                 deadline, [&] {
                                   if (last) {
                                     detail::finish_program(state, program,
@@ -200,14 +304,35 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
                                   Workload::complete_profile_stage(
                                       block, stage, args.tasks, args.context);
                                 });
+      if (Workload::kTraceBarriers && threadIdx.x == 0) {
+        Workload::trace_barrier(block, args.context, stage, args.tasks, arrive_ns,
+                                global_timer_ns());
+      }
+      if (local && ok && worker == 0 && threadIdx.x == 0) {
+        // No block is elected as the last arrival in local mode; block 0
+        // records the stage profile after each barrier instead.
+        Workload::complete_profile_stage(block, stage, args.tasks, args.context);
+      }
     }
-    // One thread reads the status so every thread of the block takes the same
-    // branch even if another block fails the run concurrently.
+    // One thread decides whether to continue so every thread of the block
+    // takes the same branch even if another block fails the run concurrently.
     if (threadIdx.x == 0) {
-      loop_running = ok && detail::load_status(state) ==
-                               static_cast<uint32_t>(Status::running);
+      if (local && ok) {
+        detail::local_transition(shared_control, state, program, generation,
+                                 args.phase_state_count, max_steps, stop_value);
+        if (worker == 0) {
+          detail::publish_control(state, shared_control);
+        }
+      }
+      loop_running = ok &&
+                     (!local ||
+                      shared_control.status == static_cast<uint32_t>(Status::running)) &&
+                     detail::load_status(state) == static_cast<uint32_t>(Status::running);
     }
     __syncthreads();
+    if (local) {
+      control = shared_control;
+    }
     if (!loop_running) {
       break;
     }

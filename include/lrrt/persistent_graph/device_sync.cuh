@@ -54,6 +54,11 @@ __device__ __forceinline__ uint32_t fetch_add_acq_rel(uint32_t *address,
   return old;
 }
 
+__device__ __forceinline__ void add_release(uint32_t *address, uint32_t value) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(address), "r"(value)
+               : "memory");
+}
+
 // Wait limit helper: every spin in the resident kernels compares against a
 // deadline taken from the launch's wait limit.
 struct Deadline {

@@ -20,14 +20,18 @@ constexpr uint32_t kRingBytes = kSlots * kSlotBytes;
 constexpr uint32_t kInputFloats = kIntermediateSize; // largest GEMV input vector
 constexpr uint32_t kBlockThreads = lrrt::persistent_graph::kWorkerThreads;
 
+constexpr uint32_t kMaxFusedLayers = 48;  // layers covered by the pointer table
+constexpr uint32_t kLayerMatrices = 7;    // q, k, v, o, gate, up, down
+
 struct FusedShared {
   unsigned char ring[kRingBytes];
-  float input[kInputFloats];   // GEMV input vector; attention scratch
-  float hidden[kHiddenSize];
-  float results[2][kSlotRows]; // per-slot row results, double-buffered
-  float reduce[kBlockThreads];
-  uint64_t full[kSlots];       // one mbarrier per ring slot
-  uint32_t tags[kSlots];       // (kind, layer, unit) of the unit in each slot
+  float input[kInputFloats];   // GEMV input vector; attention and LM-head scratch
+  float reduce[kBlockThreads]; // block reductions, softmax running state
+  const float *layer_weights[kMaxFusedLayers][kLayerMatrices];
+  uint64_t full[kSlots];       // one mbarrier per ring slot (bytes landed)
+  uint32_t sequence[kSlots];   // stream sequence number of the unit in each slot
+  uint32_t unit_tag[kSlots];   // (kind, layer, unit) of that unit
+  uint32_t done[kSlots];       // consumer warps finished with the slot's unit
   uint32_t flag;
   uint32_t broadcast;
 };

@@ -180,6 +180,52 @@ LRRT_HOST_DEVICE inline uint32_t units_per_cycle(const UnitRanges &r, uint32_t l
   return units;
 }
 
+// Random access into the stream: the unit at sequence number `n` of a launch
+// whose stream starts at cycle offset `start` (see stream_start_offset).
+struct StreamMap {
+  uint32_t layers;
+  uint32_t per_layer;  // this block's QKV + OUT + GU + DOWN units per layer
+  uint32_t cycle;      // layers * per_layer + LM units
+  uint32_t start;      // cycle offset of sequence number 0
+  uint32_t first[kKinds];
+  uint32_t count[kKinds];
+};
+
+LRRT_HOST_DEVICE inline StreamMap make_stream_map(const UnitRanges &r, uint32_t layers,
+                                                  uint32_t program, uint32_t layer) {
+  StreamMap m{};
+  m.layers = layers;
+  for (uint32_t k = 0; k < kKinds; ++k) {
+    m.first[k] = r.of[k].begin;
+    m.count[k] = r.of[k].end - r.of[k].begin;
+  }
+  m.per_layer = m.count[kQkv] + m.count[kOut] + m.count[kGateUp] + m.count[kDown];
+  m.cycle = layers * m.per_layer + m.count[kLmHead];
+  // program 0 starts at the QKV units of `layer`, program 1 at its gate/up
+  // units, program 2 at the LM head.
+  const uint32_t layer_offset = layer * m.per_layer;
+  m.start = program == 0   ? layer_offset
+            : program == 1 ? layer_offset + m.count[kQkv] + m.count[kOut]
+                           : layers * m.per_layer;
+  return m;
+}
+
+LRRT_HOST_DEVICE inline StreamCursor stream_unit(const StreamMap &m, uint32_t n) {
+  uint32_t at = static_cast<uint32_t>((uint64_t{m.start} + n) % m.cycle);
+  const uint32_t decoder = m.layers * m.per_layer;
+  if (at >= decoder) {
+    return {0, kLmHead, m.first[kLmHead] + (at - decoder)};
+  }
+  const uint32_t layer = at / m.per_layer;
+  at -= layer * m.per_layer;
+  uint32_t kind = kQkv;
+  while (at >= m.count[kind]) {
+    at -= m.count[kind];
+    ++kind;
+  }
+  return {layer, kind, m.first[kind] + at};
+}
+
 } // namespace lrrt::qwen::stateful_graph::resident
 
 #endif // LRRT_QWEN_RESIDENT_SCHEDULE_HPP_

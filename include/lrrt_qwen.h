@@ -226,6 +226,14 @@ LRRT_API lr_status_t lrq_model_run_graph(lrq_model_t *model, const lrq_task_t *t
                                          uint32_t stop_value, uint32_t token_position,
                                          uint32_t maximum_tokens, lrq_run_state_t *state);
 
+/* Per-block barrier trace of LRQ_PATH_STAGE_PROFILE runs: with `entries` > 0
+ * every block records (arrive_ns, leave_ns) %globaltimer stamps of each grid
+ * barrier at entries[barrier * workers + worker]; 0 turns tracing off. */
+LRRT_API lr_status_t lrq_model_set_trace(lrq_model_t *model, uint32_t entries);
+/* Copies `capacity` (arrive, leave) pairs (2 x u64 each) of the last trace. */
+LRRT_API lr_status_t lrq_model_read_trace(lrq_model_t *model, uint64_t *entries,
+                                          uint32_t capacity);
+
 LRRT_API const char *lrq_last_error(void);
 
 #ifdef __cplusplus

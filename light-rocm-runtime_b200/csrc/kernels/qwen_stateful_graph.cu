@@ -401,15 +401,14 @@ __device__ void embedding_feedback(qd::Context *c, sg::State *state) {
 
 // Reference residual_advance default branch (:749-760).
 __device__ void residual_advance(const sg::Task &task, sg::State *state, qd::Context *c,
-                                 bool add_projected) {
+                                 bool add_projected, uint32_t step) {
   if (add_projected) {
     for (uint32_t i = task.begin + threadIdx.x; i < task.end; i += kThreads) {
       c->hidden[i] = dev::load_cg(c->hidden + i) + dev::load_cg(c->projected + i);
     }
   }
   if (threadIdx.x == 0) {
-    const bool boundary = task.argument1 == 0 ||
-                          (dev::load_relaxed(&state->step) + 1u) % c->layer_count == 0;
+    const bool boundary = task.argument1 == 0 || (step + 1u) % c->layer_count == 0;
     if (boundary && task.argument1 == 0) {
       state->predicate_value += task.argument0;
     }
@@ -493,7 +492,7 @@ __device__ void generic_execute(const sg::Task &task, sg::State *state, qd::Cont
     embedding_feedback(c, state);
     return;
   case qd::Opcode::residual_advance:
-    residual_advance(task, state, c, true);
+    residual_advance(task, state, c, true, dev::load_relaxed(&state->step));
     return;
   default:
     generic_rows(opcode, c, task.begin, task.end, threadIdx.x >> 5u, kWarps);
@@ -532,140 +531,239 @@ __device__ void generic_execute_stage(const sg::Stage &stage, const sg::Task *ta
 
 using namespace qd::resident;
 constexpr uint32_t kMaxAttentionChunks = 128;
-constexpr uint32_t kScoreTile = 64;
+constexpr uint32_t kKvTile = 32;                       // positions per attention tile
+constexpr uint32_t kKeyStride = qd::kHeadSize + 1u;    // padded K rows (bank-conflict free)
+constexpr uint32_t kGroupWarps = 4;                    // warps sharing one 8-row unit
+constexpr uint32_t kGroups = kWarps / kGroupWarps;     // units in flight per block
+constexpr uint32_t kLmScratch = 1024;                  // LM-head candidates (input floats)
+// Up to this many KV positions every block computes the attention output of
+// all 14 query heads itself, inside the o_proj stage, so the attention stage
+// needs no grid barrier; longer contexts use the split path.
+constexpr uint32_t kLocalAttentionLimit = 192;
+constexpr uint32_t kLocalAttentionBatch = 4;           // positions per warp per load batch
+enum Matrix : uint32_t { kMq, kMk, kMv, kMo, kMgate, kMup, kMdown };
 
-struct QwenBlock {
-  bool fused;
+// Block-uniform launch facts, written once by thread 0 in `begin` and kept in
+// shared memory: the fused path reads them on every stream unit, and a
+// per-thread copy would live in local memory, whose L1-missing loads wait
+// behind the weight stream for microseconds.
+struct QwenConfig {
+  bool stream_empty;
   FusedShared *shared;
   const qd::Context *contexts;
   qd::Workspace *workspace;
+  const float *lm_head;
   uint32_t worker, workers, layers, vocab, lm_units;
-  UnitRanges ranges;   // this block's units of each stream kind
-  uint64_t policy;
   uint32_t limit_ms;
-  uint32_t produced, consumed; // units issued / consumed by this block
-  StreamCursor cursor;         // next unit to issue (thread 0)
-  bool stream_empty;
-  sg::Stage lm_stage;          // the tail Program's LM-head stage
+  UnitRanges ranges;
+  StreamMap map;
+  uint64_t policy;
+  sg::Stage lm_stage;
+  qd::StageProfile *unit_trace; // stage-profile runs: block 0 unit timeline
+};
+__shared__ QwenConfig block_config;
+
+// Per-thread scheduler state of the Qwen workload (identical in every thread
+// of a block).
+struct QwenBlock {
+  bool fused;
+  bool attention_pending;   // block 0 owes the global query copy of attention
+  uint32_t consumed;        // stream sequence number of the next unit to consume
+  uint32_t traced_barriers; // stage-profile barrier trace position (thread 0)
+  uint32_t step;            // graph step of the current Program (local transitions)
 };
 
-// Issues the bulk copies of the cursor's unit into the slot of unit number
-// b.produced (thread 0 only).
-__device__ void issue_unit(QwenBlock &b) {
-  const uint32_t slot = b.produced % kSlots;
-  unsigned char *destination = b.shared->ring + size_t{slot} * kSlotBytes;
-  const StreamCursor cursor = b.cursor;
-  const qd::Context &c = b.contexts[cursor.layer];
-  const unsigned char *first = nullptr;
-  const unsigned char *second = nullptr;
-  uint32_t first_bytes = 0, second_bytes = 0;
-  const uint32_t u = cursor.unit;
-  switch (cursor.kind) {
-  case kQkv: {
-    // Rows f..f+3 of a head and their rotary partners f+32..f+35.
-    const float *weight = c.q_weight;
-    uint32_t local = u;
-    if (u >= kQUnits + kKUnits) {
-      weight = c.v_weight;
-      local = u - kQUnits - kKUnits;
-    } else if (u >= kQUnits) {
-      weight = c.k_weight;
-      local = u - kQUnits;
-    }
-    const uint32_t row = (local / 8u) * qd::kHeadSize + (local % 8u) * 4u;
-    first = reinterpret_cast<const unsigned char *>(weight + size_t{row} * qd::kHiddenSize);
-    second = first + size_t{qd::kRotarySize} * kRowBytes;
-    first_bytes = second_bytes = 4u * kRowBytes;
-    break;
+// Stage-profile runs record, for block 0, each warp's wait and compute times
+// per stream unit in the second half of StageProfile.entries.
+__shared__ uint32_t unit_trace_position;
+__device__ __forceinline__ void trace_unit(const QwenBlock &b, uint32_t n, uint64_t before,
+                                           uint64_t ready, uint64_t done) {
+  qd::StageProfile *p = block_config.unit_trace;
+  if (p == nullptr || p->entries == nullptr) {
+    return;
   }
-  case kOut:
-    first = reinterpret_cast<const unsigned char *>(c.out_weight +
-                                                    size_t{u} * kSlotRows * qd::kHiddenSize);
-    first_bytes = kSlotBytes;
-    break;
-  case kGateUp:
-    first = reinterpret_cast<const unsigned char *>(c.gate_weight +
-                                                    size_t{u} * 4u * qd::kHiddenSize);
-    second = reinterpret_cast<const unsigned char *>(c.up_weight +
-                                                     size_t{u} * 4u * qd::kHiddenSize);
-    first_bytes = second_bytes = 4u * kRowBytes;
-    break;
-  case kDown:
-    first = reinterpret_cast<const unsigned char *>(c.down_weight +
-                                                    size_t{u} * qd::kIntermediateSize);
-    first_bytes = kDownRowBytes;
-    break;
-  default: { // kLmHead
-    const uint32_t row = u * kSlotRows;
-    const uint32_t rows = min(kSlotRows, b.vocab - row);
-    first = reinterpret_cast<const unsigned char *>(b.contexts[0].tail->lm_head_weight +
-                                                    size_t{row} * qd::kHiddenSize);
-    first_bytes = rows * kRowBytes;
-    break;
+  const uint32_t slot = atomicAdd(&unit_trace_position, 2u); // shared: no global round trip
+  const uint32_t base = p->entry_count / 2u;
+  if (base + slot + 1u < p->entry_count) {
+    p->entries[base + slot] = {before, ready};
+    p->entries[base + slot + 1u] = {done, (uint64_t{n} << 8) | (threadIdx.x >> 5u)};
   }
-  }
-  uint64_t *barrier = &b.shared->full[slot];
-  b.shared->tags[slot] = make_tag(cursor.kind, cursor.layer, u);
-  dev::mbarrier_arrive_expect_tx(barrier, first_bytes + second_bytes);
-  dev::bulk_copy_to_shared(destination, first, first_bytes, barrier, b.policy);
-  if (second_bytes != 0) {
-    dev::bulk_copy_to_shared(destination + first_bytes, second, second_bytes, barrier,
-                             b.policy);
-  }
-  ++b.produced;
-  advance_cursor(b.ranges, b.layers, b.cursor);
 }
 
-// Waits for consumption number b.consumed, checks its tag. Returns the slot
-// pointer, or nullptr after failing the run (timeout / stream mismatch). All
-// threads of the block return the same result.
-__device__ const float *slot_acquire(QwenBlock &b, sg::State *state, uint32_t kind,
-                                     uint32_t layer, uint32_t unit) {
-  const uint32_t slot = b.consumed % kSlots;
-  const uint32_t parity = (b.consumed / kSlots) & 1u;
-  FusedShared *s = b.shared;
-  if (threadIdx.x == 0) {
-    uint32_t status = 0;
-    if (!dev::mbarrier_wait(&s->full[slot], parity, dev::Deadline(b.limit_ms))) {
-      status = sg::kErrorWaitTimeout;
-    } else if (s->tags[slot] != make_tag(kind, layer, unit)) {
-      status = sg::kErrorStreamMismatch;
+// Global source ranges of one stream unit (second part empty for
+// single-range units).
+struct UnitSource {
+  const float *first;
+  const float *second;
+  uint32_t first_bytes;
+  uint32_t second_bytes;
+};
+
+__device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
+  const float *const *w = block_config.shared->layer_weights[c.layer];
+  const uint32_t u = c.unit;
+  switch (c.kind) {
+  case kQkv: {
+    // Rows f..f+3 of a head and their rotary partners f+32..f+35.
+    const float *weight = w[kMq];
+    uint32_t local = u;
+    if (u >= kQUnits + kKUnits) {
+      weight = w[kMv];
+      local = u - kQUnits - kKUnits;
+    } else if (u >= kQUnits) {
+      weight = w[kMk];
+      local = u - kQUnits;
     }
-    if (status != 0) {
-      dev::detail::fail(state, status);
-    }
-    s->flag = status;
+    const float *first =
+        weight + size_t{(local / 8u) * qd::kHeadSize + (local % 8u) * 4u} * qd::kHiddenSize;
+    return {first, first + size_t{qd::kRotarySize} * qd::kHiddenSize, 4u * kRowBytes,
+            4u * kRowBytes};
   }
-  __syncthreads();
-  if (s->flag != 0) {
+  case kOut:
+    return {w[kMo] + size_t{u} * kSlotRows * qd::kHiddenSize, nullptr, kSlotBytes, 0};
+  case kGateUp:
+    return {w[kMgate] + size_t{u} * kGuRowsPerUnit * qd::kHiddenSize,
+            w[kMup] + size_t{u} * kGuRowsPerUnit * qd::kHiddenSize,
+            kGuRowsPerUnit * kRowBytes, kGuRowsPerUnit * kRowBytes};
+  case kDown:
+    return {w[kMdown] + size_t{u} * qd::kIntermediateSize, nullptr, kDownRowBytes, 0};
+  default: { // kLmHead
+    const uint32_t row = u * kSlotRows;
+    return {block_config.lm_head + size_t{row} * qd::kHiddenSize, nullptr,
+            min(kSlotRows, block_config.vocab - row) * kRowBytes, 0};
+  }
+  }
+}
+
+// Per-slot stream cursors: slot_cursor[s] is the next unit slot s will
+// receive. A slot receives units s, s + kSlots, ...; its cursor is touched
+// only by the lane refilling it, which is ordered after the previous refill
+// by the slot's mbarrier (release arrive, acquire wait) and the done counter.
+// (Advancing a cursor costs a few compares; recomputing a unit from its
+// sequence number takes 64-bit division on the refilling warp's critical path.)
+__shared__ StreamCursor slot_cursor[kSlots];
+
+__device__ __forceinline__ void advance_by_slots(StreamCursor &c) {
+#pragma unroll 1
+  for (uint32_t i = 0; i < kSlots; ++i) {
+    advance_cursor(block_config.ranges, block_config.layers, c);
+  }
+}
+
+// Issues the bulk copies of stream unit `n` into its ring slot (one lane).
+// The slot's previous unit (n - kSlots) has been released by its consumers.
+// (An L2 bulk prefetch of units further ahead was measured slower on B200.)
+__device__ void issue_unit(const QwenBlock &b, uint32_t n) {
+  FusedShared *s = block_config.shared;
+  const uint32_t slot = n % kSlots;
+  StreamCursor c = slot_cursor[slot];
+  const UnitSource src = unit_source(b, c);
+  unsigned char *destination = s->ring + size_t{slot} * kSlotBytes;
+  s->unit_tag[slot] = make_tag(c.kind, c.layer, c.unit);
+  __threadfence_block(); // tag before sequence number
+  *reinterpret_cast<volatile uint32_t *>(&s->sequence[slot]) = n;
+  dev::mbarrier_arrive_expect_tx(&s->full[slot], src.first_bytes + src.second_bytes);
+  dev::bulk_copy_to_shared(destination, src.first, src.first_bytes, &s->full[slot],
+                           block_config.policy);
+  if (src.second_bytes != 0) {
+    dev::bulk_copy_to_shared(destination + src.first_bytes, src.second, src.second_bytes,
+                             &s->full[slot], block_config.policy);
+  }
+  advance_by_slots(c);
+  slot_cursor[slot] = c;
+}
+
+// Lane 0's verdict, shared by the warp.
+__device__ __forceinline__ bool warp_uniform(bool lane0_value) {
+  return __shfl_sync(kFullMask, lane0_value ? 1u : 0u, 0) != 0u;
+}
+
+// Whole warp: waits until stream unit `n` is in its slot and its bytes have
+// landed, checks that it is the unit the caller expects, returns the slot.
+// nullptr (warp-uniform) after a timeout, a stream mismatch, or when another
+// block already failed the run.
+__device__ const float *wait_unit(const QwenBlock &b, sg::State *state, uint32_t n,
+                                  uint32_t tag) {
+  FusedShared *s = block_config.shared;
+  const uint32_t slot = n % kSlots;
+  const uint32_t parity = (n / kSlots) & 1u;
+  const volatile uint32_t *sequence = &s->sequence[slot];
+  uint32_t spins = 0;
+  uint64_t deadline_ns = 0; // taken at the first check: ready units skip the timer
+  auto give_up = [&]() {
+    if ((++spins & 63u) != 0u) {
+      return false;
+    }
+    bool stop = false;
+    if ((threadIdx.x & 31u) == 0u) {
+      const uint64_t now = dev::global_timer_ns();
+      if (deadline_ns == 0) {
+        deadline_ns = now + uint64_t{block_config.limit_ms} * 1000000ull;
+      }
+      if (dev::detail::load_status(state) != static_cast<uint32_t>(sg::Status::running)) {
+        stop = true;
+      } else if (now > deadline_ns) {
+        dev::detail::fail(state, sg::kErrorWaitTimeout);
+        stop = true;
+      }
+    }
+    return warp_uniform(stop);
+  };
+  while (__any_sync(kFullMask, *sequence != n)) { // issued (not a lap behind)
+    if (give_up()) {
+      return nullptr;
+    }
+  }
+  while (__any_sync(kFullMask, !dev::mbarrier_try_wait(&s->full[slot], parity))) {
+    if (give_up()) {
+      return nullptr;
+    }
+  }
+  if (!warp_uniform(s->unit_tag[slot] == tag)) {
+    if ((threadIdx.x & 31u) == 0u) {
+      dev::detail::fail(state, sg::kErrorStreamMismatch);
+    }
     return nullptr;
-  }
-  while (!dev::mbarrier_try_wait(&s->full[slot], parity)) {
   }
   return reinterpret_cast<const float *>(s->ring + size_t{slot} * kSlotBytes);
 }
 
-// After every thread finished reading the slot: refill it (thread 0).
-__device__ __forceinline__ void slot_release(QwenBlock &b) {
-  if (threadIdx.x == 0 && !b.stream_empty) {
-    dev::fence_proxy_async_shared();
-    issue_unit(b);
+// One lane per consumer warp: the last of `group` warps to finish with unit
+// `n` refills its slot with unit n + kSlots.
+__device__ __forceinline__ void release_unit(const QwenBlock &b, uint32_t n, uint32_t group) {
+  FusedShared *s = block_config.shared;
+  const uint32_t slot = n % kSlots;
+  __threadfence_block();
+  if (atomicAdd(&s->done[slot], 1u) + 1u == group) {
+    s->done[slot] = 0;
+    if (!block_config.stream_empty) {
+      dev::fence_proxy_async_shared();
+      issue_unit(b, n + kSlots);
+    }
   }
-  ++b.consumed;
 }
 
 // Block-wide RMSNorm of the hidden vector into shared input (every block
 // computes the same values in the same order).
-__device__ void fused_rmsnorm(QwenBlock &b, const qd::Context *c, const float *weight,
+__device__ void fused_rmsnorm(QwenBlock &b, qd::Context *c, const float *weight,
                               float epsilon, float *global_copy) {
-  FusedShared *s = b.shared;
+  FusedShared *s = block_config.shared;
   constexpr uint32_t kVectors = qd::kHiddenSize / 4u; // 224
-  float sum = 0.0f;
-  if (threadIdx.x < kVectors) {
-    const float4 h = dev::load_cg4(c->hidden + 4u * threadIdx.x);
-    reinterpret_cast<float4 *>(s->hidden)[threadIdx.x] = h;
-    sum = fmaf(h.x, h.x, fmaf(h.y, h.y, fmaf(h.z, h.z, h.w * h.w)));
+  if (b.attention_pending) {
+    // Block 0 publishes the attention output it computed in the o_proj stage
+    // now that every block has finished reading the query vectors.
+    if (threadIdx.x < kVectors) {
+      reinterpret_cast<float4 *>(c->query)[threadIdx.x] =
+          reinterpret_cast<const float4 *>(s->input)[threadIdx.x];
+    }
+    b.attention_pending = false;
+    __syncthreads();
   }
+  float4 h = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (threadIdx.x < kVectors) {
+    h = dev::load_cg4(c->hidden + 4u * threadIdx.x);
+  }
+  float sum = fmaf(h.x, h.x, fmaf(h.y, h.y, fmaf(h.z, h.z, h.w * h.w)));
   sum = warp_sum(sum);
   if ((threadIdx.x & 31u) == 0) {
     s->reduce[threadIdx.x >> 5u] = sum;
@@ -679,12 +777,11 @@ __device__ void fused_rmsnorm(QwenBlock &b, const qd::Context *c, const float *w
   const float inverse_rms =
       1.0f / sqrtf(total / static_cast<float>(qd::kHiddenSize) + epsilon);
   if (threadIdx.x < kVectors) {
-    const float4 h = reinterpret_cast<const float4 *>(s->hidden)[threadIdx.x];
     const float4 w = __ldg(reinterpret_cast<const float4 *>(weight) + threadIdx.x);
     const float4 x = make_float4(h.x * inverse_rms * w.x, h.y * inverse_rms * w.y,
                                  h.z * inverse_rms * w.z, h.w * inverse_rms * w.w);
     reinterpret_cast<float4 *>(s->input)[threadIdx.x] = x;
-    if (global_copy != nullptr && b.worker == 0) {
+    if (global_copy != nullptr && block_config.worker == 0) {
       reinterpret_cast<float4 *>(global_copy)[threadIdx.x] = x;
     }
   }
@@ -693,14 +790,15 @@ __device__ void fused_rmsnorm(QwenBlock &b, const qd::Context *c, const float *w
 
 // Copies a vector written by other blocks into shared input.
 __device__ void fused_load_input(QwenBlock &b, const float *source, uint32_t count) {
-  float4 *destination = reinterpret_cast<float4 *>(b.shared->input);
+  float4 *destination = reinterpret_cast<float4 *>(block_config.shared->input);
   for (uint32_t i = threadIdx.x; i < count / 4u; i += kThreads) {
     destination[i] = dev::load_cg4(source + 4u * i);
   }
   __syncthreads();
 }
 
-// Dot product of a 896-float shared-memory row with the register-held input.
+// Dot product of a 896-float shared-memory row with the register-held input,
+// summed into lane 0.
 __device__ __forceinline__ float row_dot(const float *row, const float4 (&x)[7],
                                          uint32_t lane) {
   const float4 *r = reinterpret_cast<const float4 *>(row);
@@ -716,232 +814,274 @@ __device__ __forceinline__ float row_dot(const float *row, const float4 (&x)[7],
   return warp_sum((a0 + a1) + (a2 + a3));
 }
 
-__device__ __forceinline__ void load_input_registers(const QwenBlock &b, float4 (&x)[7],
-                                                     uint32_t lane) {
-  const float4 *input = reinterpret_cast<const float4 *>(b.shared->input);
+// Consumes this block's units of an 8-row kind. Warps form kGroups groups of
+// four; group g takes units g, g + kGroups, ...; warp gw of a group computes
+// rows gw and gw + 4 of the unit (a rotary pair, a gate/up pair, or two plain
+// rows) and lane 0 runs `epilogue(unit, gw, row_a, row_b, rows)`.
+struct NoOperands {
+  __device__ float4 operator()(uint32_t, uint32_t) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+};
+
+template <typename Epilogue, typename Operands = NoOperands>
+__device__ bool consume_pairs(QwenBlock &b, sg::State *state, uint32_t kind,
+                              uint32_t layer, Epilogue epilogue,
+                              Operands operands = NoOperands{}) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = threadIdx.x >> 5u;
+  const uint32_t group = warp / kGroupWarps;
+  const uint32_t gw = warp % kGroupWarps;
+  float4 x[7];
+  const float4 *input = reinterpret_cast<const float4 *>(block_config.shared->input);
 #pragma unroll
   for (uint32_t j = 0; j < 7; ++j) {
     x[j] = input[lane + 32u * j];
   }
-}
-
-// Generic 8-row unit consumer for K = 896 streams; `epilogue(unit, results)`
-// runs after the block barrier that follows the dot products.
-template <typename Epilogue>
-__device__ bool consume_rows(QwenBlock &b, sg::State *state, uint32_t kind, uint32_t layer,
-                             Epilogue epilogue) {
-  const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t warp = threadIdx.x >> 5u;
-  float4 x[7];
-  load_input_registers(b, x, lane);
-  const UnitRange range = b.ranges.of[kind];
-  for (uint32_t u = range.begin; u < range.end; ++u) {
-    const float *slot = slot_acquire(b, state, kind, layer, u);
+  const UnitRange range = block_config.ranges.of[kind];
+  const uint32_t units = range.end - range.begin;
+  bool ok = true;
+  for (uint32_t i = group; i < units; i += kGroups) {
+    const uint32_t n = b.consumed + i;
+    const uint32_t u = range.begin + i;
+    // Epilogue operands (biases, RoPE factors, residual rows) are loaded
+    // before the wait so their latency overlaps it.
+    const float4 extra = lane == 0 ? operands(u, gw) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint64_t t_before = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
+    const float *slot = wait_unit(b, state, n, make_tag(kind, layer, u));
+    const uint64_t t_ready = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
     if (slot == nullptr) {
-      return false;
+      ok = false;
+      break;
     }
-    float *results = b.shared->results[b.consumed & 1u];
-    uint32_t rows = kSlotRows;
-    if (kind == kLmHead) {
-      rows = min(kSlotRows, b.vocab - u * kSlotRows);
-    }
-    if (warp < rows) {
-      const float value = row_dot(slot + warp * qd::kHiddenSize, x, lane);
-      if (lane == 0) {
-        results[warp] = value;
+    const uint32_t rows = kind == kLmHead ? min(kSlotRows, block_config.vocab - u * kSlotRows) : kSlotRows;
+    const float a = gw < rows ? row_dot(slot + gw * qd::kHiddenSize, x, lane) : 0.0f;
+    const float c = gw + 4u < rows ? row_dot(slot + (gw + 4u) * qd::kHiddenSize, x, lane) : 0.0f;
+    if (lane == 0) {
+      epilogue(u, gw, a, c, rows, extra);
+      release_unit(b, n, kGroupWarps);
+      if (block_config.unit_trace != nullptr) {
+        trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
       }
     }
-    __syncthreads();
-    epilogue(u, results, rows);
-    slot_release(b);
+    __syncwarp();
   }
-  return true;
+  b.consumed += units;
+  return ok;
+}
+
+// QKV unit geometry: which projection, and the first / rotary-partner rows.
+struct QkvRows {
+  uint32_t which; // 0 q, 1 k, 2 v
+  uint32_t first, second, frequency;
+};
+
+__device__ __forceinline__ QkvRows qkv_rows(uint32_t u, uint32_t gw) {
+  uint32_t which = 0, local = u;
+  if (u >= kQUnits + kKUnits) {
+    which = 2;
+    local = u - kQUnits - kKUnits;
+  } else if (u >= kQUnits) {
+    which = 1;
+    local = u - kQUnits;
+  }
+  const uint32_t f = (local % 8u) * 4u + gw;
+  const uint32_t first = (local / 8u) * qd::kHeadSize + f;
+  return {which, first, first + qd::kRotarySize, f};
 }
 
 __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
   const uint32_t position = decode_field(&c->tail->decode_state->token_position);
   const size_t rope = size_t{position} * qd::kRotarySize;
   const size_t cache_row = size_t{position} * qd::kKvSize;
-  consume_rows(b, state, kQkv, layer, [&](uint32_t u, const float *results, uint32_t) {
-    if (threadIdx.x >= 4u) {
-      return;
-    }
-    const uint32_t t = threadIdx.x;
-    const float *bias = c->q_bias;
-    float *out = c->query;
-    float *cache = nullptr;
-    bool rotate = true;
-    uint32_t local = u;
-    if (u >= kQUnits + kKUnits) {
-      bias = c->v_bias;
-      out = c->value;
-      cache = c->value_cache + cache_row;
-      rotate = false;
-      local = u - kQUnits - kKUnits;
-    } else if (u >= kQUnits) {
-      bias = c->k_bias;
-      out = c->key;
-      cache = c->key_cache + cache_row;
-      local = u - kQUnits;
-    }
-    const uint32_t f = (local % 8u) * 4u + t;
-    const uint32_t first = (local / 8u) * qd::kHeadSize + f;
-    const uint32_t second = first + qd::kRotarySize;
-    const float x0 = results[t] + bias[first];
-    const float x1 = results[t + 4u] + bias[second];
-    float r0 = x0, r1 = x1;
-    if (rotate) {
-      const float cosine = c->rope_cos[rope + f];
-      const float sine = c->rope_sin[rope + f];
-      r0 = x0 * cosine - x1 * sine;
-      r1 = x1 * cosine + x0 * sine;
-    }
-    out[first] = r0;
-    out[second] = r1;
-    if (cache != nullptr) {
-      cache[first] = r0;
-      cache[second] = r1;
-    }
-  });
+  consume_pairs(
+      b, state, kQkv, layer,
+      [&](uint32_t u, uint32_t gw, float first_dot, float second_dot, uint32_t,
+          float4 operand) {
+        const QkvRows r = qkv_rows(u, gw);
+        const float x0 = first_dot + operand.x;
+        const float x1 = second_dot + operand.y;
+        float r0 = x0, r1 = x1;
+        if (r.which != 2) {
+          r0 = x0 * operand.z - x1 * operand.w;
+          r1 = x1 * operand.z + x0 * operand.w;
+        }
+        float *out = r.which == 0 ? c->query : (r.which == 1 ? c->key : c->value);
+        out[r.first] = r0;
+        out[r.second] = r1;
+        if (r.which != 0) {
+          float *cache = (r.which == 1 ? c->key_cache : c->value_cache) + cache_row;
+          cache[r.first] = r0;
+          cache[r.second] = r1;
+        }
+      },
+      [&](uint32_t u, uint32_t gw) {
+        const QkvRows r = qkv_rows(u, gw);
+        const float *bias = r.which == 0 ? c->q_bias : (r.which == 1 ? c->k_bias : c->v_bias);
+        return make_float4(bias[r.first], bias[r.second], c->rope_cos[rope + r.frequency],
+                           c->rope_sin[rope + r.frequency]);
+      });
+}
+
+__device__ void local_attention(QwenBlock &b, const qd::Context *c, uint32_t positions);
+
+__device__ __forceinline__ bool use_local_attention(uint32_t positions) {
+  return positions <= kLocalAttentionLimit;
 }
 
 __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
-  fused_load_input(b, c->query, qd::kQuerySize);
-  consume_rows(b, state, kOut, layer, [&](uint32_t u, const float *results, uint32_t) {
-    if (threadIdx.x < kSlotRows) {
-      const uint32_t row = u * kSlotRows + threadIdx.x;
-      c->hidden[row] = dev::load_cg(c->hidden + row) + results[threadIdx.x];
-    }
-  });
+  const uint32_t positions = decode_field(&c->tail->decode_state->kv_length) + 1u;
+  if (use_local_attention(positions)) {
+    local_attention(b, c, positions);
+    b.attention_pending = block_config.worker == 0;
+  } else {
+    fused_load_input(b, c->query, qd::kQuerySize);
+  }
+  consume_pairs(
+      b, state, kOut, layer,
+      [&](uint32_t u, uint32_t gw, float a, float d, uint32_t, float4 residual) {
+        const uint32_t row = u * kSlotRows + gw;
+        c->hidden[row] = residual.x + a;
+        c->hidden[row + 4u] = residual.y + d;
+      },
+      [&](uint32_t u, uint32_t gw) {
+        const uint32_t row = u * kSlotRows + gw;
+        return make_float4(dev::load_cg(c->hidden + row), dev::load_cg(c->hidden + row + 4u),
+                           0.f, 0.f);
+      });
 }
 
 __device__ void fused_gate_up(QwenBlock &b, sg::State *state, qd::Context *c,
                               uint32_t layer) {
-  consume_rows(b, state, kGateUp, layer, [&](uint32_t u, const float *results, uint32_t) {
-    if (threadIdx.x < 4u) {
-      c->activated[u * 4u + threadIdx.x] =
-          silu_times(results[threadIdx.x], results[threadIdx.x + 4u]);
-    }
-  });
+  consume_pairs(b, state, kGateUp, layer,
+                [&](uint32_t u, uint32_t gw, float gate, float up, uint32_t, float4) {
+                  c->activated[u * kGuRowsPerUnit + gw] = silu_times(gate, up);
+                });
 }
 
-// Down projection: one 4864-float row per slot, split over the 8 warps.
+// Down projection: one 4864-float row per unit, one warp per unit.
 __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
   fused_load_input(b, c->activated, qd::kIntermediateSize);
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
-  constexpr uint32_t kVectorsPerWarp = qd::kIntermediateSize / 4u / kWarps; // 152
-  float4 x[5];
-  const float4 *input = reinterpret_cast<const float4 *>(b.shared->input);
-#pragma unroll
-  for (uint32_t j = 0; j < 5; ++j) {
-    const uint32_t index = lane + 32u * j;
-    x[j] = index < kVectorsPerWarp ? input[warp * kVectorsPerWarp + index]
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  const UnitRange range = b.ranges.of[kDown];
-  for (uint32_t u = range.begin; u < range.end; ++u) {
-    const float *slot = slot_acquire(b, state, kDown, layer, u);
+  constexpr uint32_t kVectors = qd::kIntermediateSize / 4u / 32u; // 38 per lane
+  const float4 *x = reinterpret_cast<const float4 *>(block_config.shared->input);
+  const UnitRange range = block_config.ranges.of[kDown];
+  const uint32_t units = range.end - range.begin;
+  for (uint32_t i = warp; i < units; i += kWarps) {
+    const uint32_t n = b.consumed + i;
+    const uint32_t u = range.begin + i;
+    const float residual = lane == 0 ? dev::load_cg(c->hidden + u) : 0.0f;
+    const uint64_t t_before = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
+    const float *slot = wait_unit(b, state, n, make_tag(kDown, layer, u));
+    const uint64_t t_ready = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
     if (slot == nullptr) {
-      return;
+      break;
     }
-    const float4 *row = reinterpret_cast<const float4 *>(slot) + warp * kVectorsPerWarp;
+    const float4 *row = reinterpret_cast<const float4 *>(slot);
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll
-    for (uint32_t j = 0; j < 5; ++j) {
-      const uint32_t index = lane + 32u * j;
-      if (index < kVectorsPerWarp) {
-        const float4 w = row[index];
-        a0 = fmaf(w.x, x[j].x, a0);
-        a1 = fmaf(w.y, x[j].y, a1);
-        a2 = fmaf(w.z, x[j].z, a2);
-        a3 = fmaf(w.w, x[j].w, a3);
-      }
+#pragma unroll 19
+    for (uint32_t j = 0; j < kVectors; ++j) {
+      const float4 w = row[lane + 32u * j];
+      const float4 v = x[lane + 32u * j];
+      a0 = fmaf(w.x, v.x, a0);
+      a1 = fmaf(w.y, v.y, a1);
+      a2 = fmaf(w.z, v.z, a2);
+      a3 = fmaf(w.w, v.w, a3);
     }
-    const float partial = warp_sum((a0 + a1) + (a2 + a3));
-    float *results = b.shared->results[b.consumed & 1u];
+    const float sum = warp_sum((a0 + a1) + (a2 + a3));
     if (lane == 0) {
-      results[warp] = partial;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float sum = 0.0f;
-#pragma unroll
-      for (uint32_t w = 0; w < kWarps; ++w) {
-        sum += results[w];
-      }
       c->projected[u] = sum;
-      c->hidden[u] = dev::load_cg(c->hidden + u) + sum;
+      c->hidden[u] = residual + sum;
+      release_unit(b, n, 1);
+      if (block_config.unit_trace != nullptr) {
+        trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
+      }
     }
-    slot_release(b);
+    __syncwarp();
   }
+  b.consumed += units;
 }
 
-// Split-position decode attention for one (kv head, chunk) item.
+// Split-position decode attention for one (kv head, chunk) item: K/V tiles
+// staged in shared memory, running softmax state per query head, partial
+// (acc, max, sum) written to the workspace; the last item of the kv head to
+// finish combines all chunks into the attention output (written over query).
 __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
                                uint32_t chunk, uint32_t chunks, uint32_t positions,
                                uint32_t item) {
-  FusedShared *s = b.shared;
+  FusedShared *s = block_config.shared;
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
   const uint32_t per_chunk = (positions + chunks - 1u) / chunks;
-  const uint32_t begin = chunk * per_chunk;
+  const uint32_t begin = min(positions, chunk * per_chunk);
   const uint32_t end = min(positions, begin + per_chunk);
-  float *scores = s->input;                        // [7][kScoreTile]
-  float *run_max = s->input + 7u * kScoreTile;      // [7]
-  float *run_sum = run_max + 8u;                    // [7]
-  float *scale = run_sum + 8u;                      // [7]
+  constexpr uint32_t kHeads = qd::kQueriesPerKvHead;
+  constexpr uint32_t kOutputs = kHeads * qd::kHeadSize; // 448
+  float *keys = s->input;                                // [32][65]
+  float *values = keys + kKvTile * kKeyStride;           // [32][64]
+  float *scores = values + kKvTile * qd::kHeadSize;      // [7][32]
+  float *query = scores + kHeads * kKvTile;              // [7][64]
+  float *run_max = s->reduce;                            // [7]
+  float *run_sum = s->reduce + 8;                        // [7]
+  float *scale = s->reduce + 16;                         // [7]
   const uint32_t kv_offset = group * qd::kHeadSize;
-  const uint32_t head0 = group * qd::kQueriesPerKvHead;
-  // Lane l keeps dims 2l, 2l+1 of the group's seven query heads.
-  float2 q[qd::kQueriesPerKvHead];
-#pragma unroll
-  for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
-    const float *row = c->query + (head0 + h) * qd::kHeadSize + 2u * lane;
-    q[h] = make_float2(dev::load_cg(row), dev::load_cg(row + 1));
+  const uint32_t head0 = group * kHeads;
+  for (uint32_t o = threadIdx.x; o < kOutputs; o += kThreads) {
+    query[o] = dev::load_cg(c->query + head0 * qd::kHeadSize + o);
   }
-  if (threadIdx.x < qd::kQueriesPerKvHead) {
+  if (threadIdx.x < kHeads) {
     run_max[threadIdx.x] = -INFINITY;
     run_sum[threadIdx.x] = 0.0f;
   }
-  // Thread t accumulates outputs t and t + 256 of the 7 x 64 (head, dim) grid.
   float acc[2] = {0.0f, 0.0f};
   __syncthreads();
-  for (uint32_t tile = begin; tile < end; tile += kScoreTile) {
-    const uint32_t count = min(kScoreTile, end - tile);
-    for (uint32_t p = warp; p < count; p += kWarps) {
-      const float *k = c->key_cache + size_t{tile + p} * qd::kKvSize + kv_offset + 2u * lane;
-      const float k0 = dev::load_cg(k), k1 = dev::load_cg(k + 1);
-#pragma unroll
-      for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
-        const float dot = warp_sum(q[h].x * k0 + q[h].y * k1);
-        if (lane == 0) {
-          scores[h * kScoreTile + p] = dot * 0.125f;
-        }
+  for (uint32_t tile = begin; tile < end; tile += kKvTile) {
+    const uint32_t count = min(kKvTile, end - tile);
+    // Stage K (padded rows) and V: 32 positions x 16 float4 each.
+    for (uint32_t v = threadIdx.x; v < kKvTile * 16u; v += kThreads) {
+      const uint32_t p = v / 16u, q4 = v % 16u;
+      float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = k4;
+      if (p < count) {
+        const size_t row = size_t{tile + p} * qd::kKvSize + kv_offset + 4u * q4;
+        k4 = dev::load_cg4(c->key_cache + row);
+        v4 = dev::load_cg4(c->value_cache + row);
       }
+      float *k = keys + p * kKeyStride + 4u * q4;
+      k[0] = k4.x;
+      k[1] = k4.y;
+      k[2] = k4.z;
+      k[3] = k4.w;
+      reinterpret_cast<float4 *>(values + p * qd::kHeadSize)[q4] = v4;
     }
     __syncthreads();
-    if (warp < qd::kQueriesPerKvHead) {
+    if (threadIdx.x < kHeads * kKvTile) {
+      const uint32_t h = threadIdx.x / kKvTile, p = threadIdx.x % kKvTile;
+      float dot = -INFINITY;
+      if (p < count) {
+        const float *q = query + h * qd::kHeadSize;
+        const float *k = keys + p * kKeyStride;
+        float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll 16
+        for (uint32_t d = 0; d < qd::kHeadSize; d += 2u) {
+          d0 = fmaf(q[d], k[d], d0);
+          d1 = fmaf(q[d + 1u], k[d + 1u], d1);
+        }
+        dot = (d0 + d1) * 0.125f; // 1/sqrt(head_dim)
+      }
+      scores[h * kKvTile + p] = dot;
+    }
+    __syncthreads();
+    if (warp < kHeads) {
       const uint32_t h = warp;
-      float tile_max = -INFINITY;
-      for (uint32_t p = lane; p < count; p += 32u) {
-        tile_max = fmaxf(tile_max, scores[h * kScoreTile + p]);
-      }
-      tile_max = warp_all_max(tile_max);
+      const float score = scores[h * kKvTile + lane];
       const float previous = run_max[h];
-      const float next = fmaxf(previous, tile_max);
-      float tile_sum = 0.0f;
-      for (uint32_t p = lane; p < count; p += 32u) {
-        const float e = expf(scores[h * kScoreTile + p] - next);
-        scores[h * kScoreTile + p] = e;
-        tile_sum += e;
-      }
-      tile_sum = warp_all_sum(tile_sum);
-      __syncwarp();
+      const float next = fmaxf(previous, warp_all_max(score));
+      const float e = lane < count ? expf(score - next) : 0.0f;
+      scores[h * kKvTile + lane] = e;
+      const float total = warp_all_sum(e);
       if (lane == 0) {
         const float alpha = expf(previous - next);
         scale[h] = alpha;
-        run_sum[h] = run_sum[h] * alpha + tile_sum;
+        run_sum[h] = run_sum[h] * alpha + total;
         run_max[h] = next;
       }
     }
@@ -949,72 +1089,66 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
 #pragma unroll
     for (uint32_t k = 0; k < 2; ++k) {
       const uint32_t o = threadIdx.x + k * kThreads;
-      if (o < qd::kQueriesPerKvHead * qd::kHeadSize) {
+      if (o < kOutputs) {
         const uint32_t h = o / qd::kHeadSize, d = o % qd::kHeadSize;
+        const float *e = scores + h * kKvTile;
         float value = acc[k] * scale[h];
         for (uint32_t p = 0; p < count; ++p) {
-          value = fmaf(scores[h * kScoreTile + p],
-                       dev::load_cg(c->value_cache + size_t{tile + p} * qd::kKvSize +
-                                    kv_offset + d),
-                       value);
+          value = fmaf(e[p], values[p * qd::kHeadSize + d], value);
         }
         acc[k] = value;
       }
     }
     __syncthreads();
   }
-  float *partial = b.workspace->attention_partials +
-                   size_t{item} * qd::kQueriesPerKvHead * qd::kAttentionPartialStride;
+  float *partial = block_config.workspace->attention_partials +
+                   size_t{item} * kHeads * qd::kAttentionPartialStride;
 #pragma unroll
   for (uint32_t k = 0; k < 2; ++k) {
     const uint32_t o = threadIdx.x + k * kThreads;
-    if (o < qd::kQueriesPerKvHead * qd::kHeadSize) {
-      const uint32_t h = o / qd::kHeadSize, d = o % qd::kHeadSize;
-      partial[h * qd::kAttentionPartialStride + d] = acc[k];
+    if (o < kOutputs) {
+      partial[(o / qd::kHeadSize) * qd::kAttentionPartialStride + o % qd::kHeadSize] = acc[k];
     }
   }
-  if (threadIdx.x < qd::kQueriesPerKvHead) {
+  if (threadIdx.x < kHeads) {
     partial[threadIdx.x * qd::kAttentionPartialStride + qd::kHeadSize] = run_max[threadIdx.x];
     partial[threadIdx.x * qd::kAttentionPartialStride + qd::kHeadSize + 1u] =
         run_sum[threadIdx.x];
   }
   __syncthreads();
-  // The last item of this kv head to finish combines all of its chunks.
   if (threadIdx.x == 0) {
-    __threadfence();
     const uint32_t arrived =
-        dev::fetch_add_acq_rel(&b.workspace->attention_arrivals[group], 1u) + 1u;
+        dev::fetch_add_acq_rel(&block_config.workspace->attention_arrivals[group], 1u) + 1u;
     s->broadcast = arrived == chunks ? 1u : 0u;
-    if (arrived == chunks) {
-      __threadfence();
-    }
   }
   __syncthreads();
   if (s->broadcast == 0) {
     return;
   }
-  const float *group_partials = b.workspace->attention_partials +
-                                size_t{group * chunks} * qd::kQueriesPerKvHead *
-                                    qd::kAttentionPartialStride;
-  float *weights = s->input; // [7][kMaxAttentionChunks]
-  if (warp < qd::kQueriesPerKvHead) {
+  // Last arrival: weights w_j = exp(m_j - M) / sum_j l_j exp(m_j - M) per head.
+  const float *group_partials = block_config.workspace->attention_partials +
+                                size_t{group * chunks} * kHeads * qd::kAttentionPartialStride;
+  float *maxima = s->input;                                  // [chunks][7]
+  float *sums = maxima + kMaxAttentionChunks * kHeads;       // [chunks][7]
+  float *weights = sums + kMaxAttentionChunks * kHeads;      // [7][chunks]
+  for (uint32_t t = threadIdx.x; t < chunks * kHeads; t += kThreads) {
+    const float *entry = group_partials + size_t{t} * qd::kAttentionPartialStride;
+    maxima[t] = dev::load_cg(entry + qd::kHeadSize);
+    sums[t] = dev::load_cg(entry + qd::kHeadSize + 1u);
+  }
+  __syncthreads();
+  if (warp < kHeads) {
     const uint32_t h = warp;
     float maximum = -INFINITY;
     for (uint32_t j = lane; j < chunks; j += 32u) {
-      maximum = fmaxf(maximum,
-                      dev::load_cg(group_partials +
-                                   (size_t{j} * qd::kQueriesPerKvHead + h) *
-                                       qd::kAttentionPartialStride +
-                                   qd::kHeadSize));
+      maximum = fmaxf(maximum, maxima[j * kHeads + h]);
     }
     maximum = warp_all_max(maximum);
     float denominator = 0.0f;
     for (uint32_t j = lane; j < chunks; j += 32u) {
-      const float *entry = group_partials +
-                           (size_t{j} * qd::kQueriesPerKvHead + h) * qd::kAttentionPartialStride;
-      const float e = expf(dev::load_cg(entry + qd::kHeadSize) - maximum);
+      const float e = expf(maxima[j * kHeads + h] - maximum);
       weights[h * kMaxAttentionChunks + j] = e;
-      denominator += e * dev::load_cg(entry + qd::kHeadSize + 1u);
+      denominator += e * sums[j * kHeads + h];
     }
     denominator = warp_all_sum(denominator);
     __syncwarp();
@@ -1026,106 +1160,269 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
 #pragma unroll
   for (uint32_t k = 0; k < 2; ++k) {
     const uint32_t o = threadIdx.x + k * kThreads;
-    if (o < qd::kQueriesPerKvHead * qd::kHeadSize) {
+    if (o < kOutputs) {
       const uint32_t h = o / qd::kHeadSize, d = o % qd::kHeadSize;
+      const float *w = weights + h * kMaxAttentionChunks;
+      const float *entry = group_partials + h * qd::kAttentionPartialStride + d;
+      const size_t stride = size_t{kHeads} * qd::kAttentionPartialStride;
       float value = 0.0f;
+#pragma unroll 8
       for (uint32_t j = 0; j < chunks; ++j) {
-        value = fmaf(weights[h * kMaxAttentionChunks + j],
-                     dev::load_cg(group_partials +
-                                  (size_t{j} * qd::kQueriesPerKvHead + h) *
-                                      qd::kAttentionPartialStride +
-                                  d),
-                     value);
+        value = fmaf(w[j], dev::load_cg(entry + j * stride), value);
       }
       c->query[(head0 + h) * qd::kHeadSize + d] = value;
     }
   }
   if (threadIdx.x == 0) {
-    b.workspace->attention_arrivals[group] = 0; // next use is after a barrier
+    block_config.workspace->attention_arrivals[group] = 0; // next use follows a grid barrier
+  }
+  __syncthreads();
+}
+
+// Attention output of all 14 query heads computed by this block alone into
+// shared input[0..895] ([head][dim]), for short contexts. Lane l of a warp
+// owns dims 4*(l%16)..+3 of kv head l/16 and that head's seven query heads;
+// warp w takes positions w, w+8, ...; each warp keeps an online softmax per
+// head, and the eight warps' states are merged pairwise at the end.
+__device__ void local_attention(QwenBlock &b, const qd::Context *c, uint32_t positions) {
+  FusedShared *s = block_config.shared;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = threadIdx.x >> 5u;
+  const uint32_t group = lane >> 4u;
+  const uint32_t dim = 4u * (lane & 15u);
+  constexpr uint32_t kHeads = qd::kQueriesPerKvHead;
+  float4 q[kHeads], acc[kHeads];
+  float maximum[kHeads], total[kHeads];
+#pragma unroll
+  for (uint32_t j = 0; j < kHeads; ++j) {
+    q[j] = dev::load_cg4(c->query + (group * kHeads + j) * qd::kHeadSize + dim);
+    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    maximum[j] = -INFINITY;
+    total[j] = 0.0f;
+  }
+  const float *keys = c->key_cache + 4u * lane;
+  const float *values = c->value_cache + 4u * lane;
+  for (uint32_t base = warp; base < positions; base += kWarps * kLocalAttentionBatch) {
+    float4 k4[kLocalAttentionBatch], v4[kLocalAttentionBatch];
+#pragma unroll
+    for (uint32_t i = 0; i < kLocalAttentionBatch; ++i) {
+      const uint32_t p = base + i * kWarps;
+      if (p < positions) {
+        k4[i] = dev::load_cg4(keys + size_t{p} * qd::kKvSize);
+        v4[i] = dev::load_cg4(values + size_t{p} * qd::kKvSize);
+      }
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < kLocalAttentionBatch; ++i) {
+      if (base + i * kWarps >= positions) {
+        break;
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < kHeads; ++j) {
+        float dot = q[j].x * k4[i].x + q[j].y * k4[i].y + q[j].z * k4[i].z + q[j].w * k4[i].w;
+        dot += __shfl_xor_sync(kFullMask, dot, 8);
+        dot += __shfl_xor_sync(kFullMask, dot, 4);
+        dot += __shfl_xor_sync(kFullMask, dot, 2);
+        dot += __shfl_xor_sync(kFullMask, dot, 1);
+        const float score = dot * 0.125f; // 1/sqrt(head_dim)
+        const float next = fmaxf(maximum[j], score);
+        const float alpha = expf(maximum[j] - next);
+        const float e = expf(score - next);
+        total[j] = total[j] * alpha + e;
+        acc[j].x = acc[j].x * alpha + e * v4[i].x;
+        acc[j].y = acc[j].y * alpha + e * v4[i].y;
+        acc[j].z = acc[j].z * alpha + e * v4[i].z;
+        acc[j].w = acc[j].w * alpha + e * v4[i].w;
+        maximum[j] = next;
+      }
+    }
+  }
+  // Pairwise merge of the warps' softmax states: half the remaining warps
+  // write theirs, the other half fold them in.
+  float *scratch = s->input + qd::kQuerySize;          // [4][896] accumulators
+  float *scratch_max = scratch + 4u * qd::kQuerySize;  // [4][14]
+  float *scratch_sum = scratch_max + 4u * qd::kAttentionHeads;
+  for (uint32_t active = kWarps / 2u; active >= 1u; active /= 2u) {
+    if (warp >= active && warp < 2u * active) {
+      const uint32_t slot = warp - active;
+#pragma unroll
+      for (uint32_t j = 0; j < kHeads; ++j) {
+        const uint32_t head = group * kHeads + j;
+        reinterpret_cast<float4 *>(scratch + slot * qd::kQuerySize + head * qd::kHeadSize +
+                                   dim)[0] = acc[j];
+        if ((lane & 15u) == 0u) {
+          scratch_max[slot * qd::kAttentionHeads + head] = maximum[j];
+          scratch_sum[slot * qd::kAttentionHeads + head] = total[j];
+        }
+      }
+    }
+    __syncthreads();
+    if (warp < active) {
+#pragma unroll
+      for (uint32_t j = 0; j < kHeads; ++j) {
+        const uint32_t head = group * kHeads + j;
+        const float other_max = scratch_max[warp * qd::kAttentionHeads + head];
+        if (other_max == -INFINITY) {
+          continue;
+        }
+        const float other_sum = scratch_sum[warp * qd::kAttentionHeads + head];
+        const float4 other = reinterpret_cast<const float4 *>(
+            scratch + warp * qd::kQuerySize + head * qd::kHeadSize + dim)[0];
+        const float next = fmaxf(maximum[j], other_max);
+        const float mine = maximum[j] == -INFINITY ? 0.0f : expf(maximum[j] - next);
+        const float theirs = expf(other_max - next);
+        total[j] = total[j] * mine + other_sum * theirs;
+        acc[j].x = acc[j].x * mine + other.x * theirs;
+        acc[j].y = acc[j].y * mine + other.y * theirs;
+        acc[j].z = acc[j].z * mine + other.z * theirs;
+        acc[j].w = acc[j].w * mine + other.w * theirs;
+        maximum[j] = next;
+      }
+    }
+    __syncthreads();
+  }
+  if (warp == 0) {
+#pragma unroll
+    for (uint32_t j = 0; j < kHeads; ++j) {
+      const float inverse = 1.0f / total[j];
+      reinterpret_cast<float4 *>(s->input + (group * kHeads + j) * qd::kHeadSize + dim)[0] =
+          make_float4(acc[j].x * inverse, acc[j].y * inverse, acc[j].z * inverse,
+                      acc[j].w * inverse);
+    }
   }
   __syncthreads();
 }
 
 __device__ void fused_attention(QwenBlock &b, qd::Context *c) {
   const uint32_t positions = decode_field(&c->tail->decode_state->kv_length) + 1u;
+  if (use_local_attention(positions)) {
+    return; // computed per block inside the o_proj stage
+  }
   uint32_t chunks = (positions + 15u) / 16u;
-  const uint32_t per_group = max(1u, min(b.workers / 2u, kMaxAttentionChunks));
-  chunks = min(chunks, per_group);
+  chunks = min(chunks, max(1u, min(block_config.workers / 2u, kMaxAttentionChunks)));
   const uint32_t items = qd::kKvHeads * chunks;
-  for (uint32_t item = b.worker; item < items; item += b.workers) {
+  for (uint32_t item = block_config.worker; item < items; item += block_config.workers) {
     attention_item(b, c, item / chunks, item % chunks, chunks, positions, item);
   }
 }
 
-// LM head: each block scans its rows, keeping the best (value, index) per
-// Program task it overlaps; candidate slot (worker + task) in the workspace.
+// LM head: lane 0 of each warp keeps its own best (value, index) per Program
+// task in shared memory; the block merges them per task and publishes
+// candidate slot (worker + task) in the workspace.
 __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &stage,
                               const sg::Task *tasks) {
-  const UnitRange range = b.ranges.of[kLmHead];
-  if (range.begin == range.end) {
-    return;
+  FusedShared *s = block_config.shared;
+  const uint32_t warp = threadIdx.x >> 5u;
+  const uint32_t task_count = stage.task_count;
+  float *best_values = s->input + kLmScratch;                     // [8][32]
+  uint32_t *best_indices =
+      reinterpret_cast<uint32_t *>(best_values + kWarps * qd::kMaximumLmHeadPartitions);
+  uint32_t *task_ends = best_indices + kWarps * qd::kMaximumLmHeadPartitions; // [32]
+  for (uint32_t t = threadIdx.x; t < kWarps * qd::kMaximumLmHeadPartitions; t += kThreads) {
+    best_values[t] = -INFINITY;
+    best_indices[t] = UINT32_MAX;
   }
-  const sg::Task *lm_tasks = tasks + stage.task_offset;
-  // Task containing the block's first row (tasks are contiguous, ascending).
-  uint32_t task = 0;
+  if (threadIdx.x < task_count) {
+    task_ends[threadIdx.x] = tasks[stage.task_offset + threadIdx.x].end;
+  }
+  __syncthreads();
+  const UnitRange range = block_config.ranges.of[kLmHead];
+  uint32_t task = 0; // lane 0's cursor: rows of a warp only increase
   const uint32_t first_row = range.begin * kSlotRows;
-  while (task + 1u < stage.task_count && lm_tasks[task].end <= first_row) {
+  while (task + 1u < task_count && task_ends[task] <= first_row) {
     ++task;
   }
-  float best_value = -INFINITY;
-  uint32_t best_index = UINT32_MAX;
-  qd::Workspace *workspace = b.workspace;
-  const uint32_t worker = b.worker;
-  consume_rows(b, state, kLmHead, 0, [&](uint32_t u, const float *results, uint32_t rows) {
-    if (threadIdx.x != 0) {
-      return;
+  float *mine = best_values + warp * qd::kMaximumLmHeadPartitions;
+  uint32_t *mine_index = best_indices + warp * qd::kMaximumLmHeadPartitions;
+  auto offer = [&](uint32_t row, float value) {
+    while (row >= task_ends[task]) {
+      ++task;
     }
-    for (uint32_t r = 0; r < rows; ++r) {
-      const uint32_t row = u * kSlotRows + r;
-      while (row >= lm_tasks[task].end) {
-        workspace->top1_values[worker + task] = best_value;
-        workspace->top1_indices[worker + task] = best_index;
-        best_value = -INFINITY;
-        best_index = UINT32_MAX;
-        ++task;
-      }
-      if (better_top1(results[r], row, best_value, best_index)) {
-        best_value = results[r];
-        best_index = row;
-      }
+    if (better_top1(value, row, mine[task], mine_index[task])) {
+      mine[task] = value;
+      mine_index[task] = row;
     }
-  });
-  if (threadIdx.x == 0) {
-    workspace->top1_values[worker + task] = best_value;
-    workspace->top1_indices[worker + task] = best_index;
+  };
+  consume_pairs(b, state, kLmHead, 0,
+                [&](uint32_t u, uint32_t gw, float a, float d, uint32_t rows, float4) {
+                  if (gw < rows) {
+                    offer(u * kSlotRows + gw, a);
+                  }
+                  if (gw + 4u < rows) {
+                    offer(u * kSlotRows + gw + 4u, d);
+                  }
+                });
+  __syncthreads();
+  if (threadIdx.x < task_count && range.begin < range.end) {
+    const uint32_t t = threadIdx.x;
+    const uint32_t task_begin = tasks[stage.task_offset + t].begin;
+    const uint32_t rows_end = min(range.end * kSlotRows, block_config.vocab);
+    if (task_begin < rows_end && task_ends[t] > first_row) {
+      float value = -INFINITY;
+      uint32_t index = UINT32_MAX;
+      for (uint32_t w = 0; w < kWarps; ++w) {
+        const uint32_t slot = w * qd::kMaximumLmHeadPartitions + t;
+        if (better_top1(best_values[slot], best_indices[slot], value, index)) {
+          value = best_values[slot];
+          index = best_indices[slot];
+        }
+      }
+      block_config.workspace->top1_values[block_config.worker + t] = value;
+      block_config.workspace->top1_indices[block_config.worker + t] = index;
+    }
   }
 }
 
-// Per-task top-1 over the candidate slots, then the reference reduce_top1.
+// Per-task top-1 over the candidate slots (loaded in one parallel pass), then
+// the reference reduce_top1 over the per-task partials.
 __device__ void fused_reduce_top1(QwenBlock &b, const sg::Stage &stage,
                                   const sg::Task *tasks, qd::Context *c) {
+  FusedShared *s = block_config.shared;
   const sg::Task *lm_tasks = tasks + stage.task_offset;
   qd::TailContext *tail = c->tail;
+  const uint32_t slots = block_config.workers + stage.task_count;
+  float *values = s->input;
+  uint32_t *indices = reinterpret_cast<uint32_t *>(s->input + 512);
+  float *partial_values = s->input + 1024;
+  uint32_t *partial_indices = reinterpret_cast<uint32_t *>(s->input + 1024 + 64);
+  for (uint32_t t = threadIdx.x; t < slots; t += kThreads) {
+    values[t] = dev::load_cg(block_config.workspace->top1_values + t);
+    indices[t] = dev::load_cg(block_config.workspace->top1_indices + t);
+  }
+  __syncthreads();
   if (threadIdx.x < stage.task_count) {
     const sg::Task &task = lm_tasks[threadIdx.x];
-    const uint32_t first = even_owner(task.begin / kSlotRows, b.lm_units, b.workers);
-    const uint32_t last =
-        even_owner((task.end - 1u) / kSlotRows, b.lm_units, b.workers);
+    const uint32_t first = even_owner(task.begin / kSlotRows, block_config.lm_units, block_config.workers);
+    const uint32_t last = even_owner((task.end - 1u) / kSlotRows, block_config.lm_units, block_config.workers);
     float best_value = -INFINITY;
     uint32_t best_index = UINT32_MAX;
     for (uint32_t w = first; w <= last; ++w) {
-      const float value = dev::load_cg(b.workspace->top1_values + w + threadIdx.x);
-      const uint32_t index = dev::load_cg(b.workspace->top1_indices + w + threadIdx.x);
-      if (better_top1(value, index, best_value, best_index)) {
-        best_value = value;
-        best_index = index;
+      if (better_top1(values[w + threadIdx.x], indices[w + threadIdx.x], best_value,
+                      best_index)) {
+        best_value = values[w + threadIdx.x];
+        best_index = indices[w + threadIdx.x];
       }
     }
     tail->partial_max_values[task.argument0] = best_value;
     tail->partial_max_indices[task.argument0] = best_index;
+    partial_values[task.argument0] = best_value;
+    partial_indices[task.argument0] = best_index;
   }
   __syncthreads();
-  generic_reduce_top1(c);
+  if (threadIdx.x == 0) {
+    // Reference reduce_top1 (:339-356) over the partials.
+    float best_value = partial_values[0];
+    uint32_t best_index = partial_indices[0];
+    for (uint32_t p = 1; p < tail->partition_count; ++p) {
+      if (better_top1(partial_values[p], partial_indices[p], best_value, best_index)) {
+        best_value = partial_values[p];
+        best_index = partial_indices[p];
+      }
+    }
+    tail->decode_state->sampled_logit = best_value;
+    tail->decode_state->sampled_token = best_index;
+  }
+  __syncthreads();
 }
 
 // Is the graph exactly the reference Qwen table (qwen_stateful_graph.cpp
@@ -1220,7 +1517,7 @@ __device__ bool fused_possible(const sg::ResidentArgs &args, uint32_t workers) {
   if (workspace == nullptr || workspace->magic != qd::kWorkspaceMagic ||
       workspace->worker_capacity < max(workers, 2u) ||
       dev::dynamic_shared_bytes() < kFusedSharedBytes || gridDim.x != workers ||
-      contexts[0].layer_count > 255u || tail->vocab_size >= (1u << 23) ||
+      contexts[0].layer_count > kMaxFusedLayers || tail->vocab_size >= (1u << 23) ||
       !aligned16(tail->lm_head_weight) || !aligned16(tail->final_norm_weight) ||
       !aligned16(tail->final_normalized)) {
     return false;
@@ -1243,6 +1540,24 @@ __device__ bool fused_possible(const sg::ResidentArgs &args, uint32_t workers) {
 
 template <bool kStageProfile> struct QwenWorkloadT {
   using Block = QwenBlock;
+  static constexpr bool kTraceBarriers = kStageProfile;
+
+  // Stage-profile runs: every block records when it arrived at and left each
+  // grid barrier into StageProfile.entries[barrier * workers + worker] when
+  // the host bound an entry array.
+  __device__ static void trace_barrier(QwenBlock &b, void *opaque, const sg::Stage &,
+                                       const sg::Task *, uint64_t arrive_ns,
+                                       uint64_t leave_ns) {
+    auto *contexts = static_cast<qd::Context *>(opaque);
+    qd::StageProfile *profile = contexts[0].tail->stage_profile;
+    if (profile != nullptr && profile->entries != nullptr) {
+      const uint64_t index = uint64_t{b.traced_barriers} * block_config.workers + block_config.worker;
+      if (index < profile->entry_count) {
+        profile->entries[index] = {arrive_ns, leave_ns};
+      }
+    }
+    ++b.traced_barriers;
+  }
 
   __device__ static bool valid_context(const sg::State *, void *opaque) {
     return valid_qwen_contexts(static_cast<qd::Context *>(opaque));
@@ -1255,57 +1570,81 @@ template <bool kStageProfile> struct QwenWorkloadT {
   }
 
   __device__ static void begin(QwenBlock &b, const sg::ResidentArgs &args) {
-    __shared__ uint32_t decision;
     b = QwenBlock{};
-    b.worker = blockIdx.x;
-    b.workers = dev::load_relaxed(&args.state->worker_count);
-    b.limit_ms = dev::detail::wait_limit_ms(args.reserved);
+    QwenConfig &k = block_config;
+    extern __shared__ __align__(128) unsigned char dynamic_shared[];
+    FusedShared *s = reinterpret_cast<FusedShared *>(dynamic_shared);
     if (threadIdx.x == 0) {
-      decision = fused_possible(args, b.workers) ? 1u : 0u;
-      qd::Workspace *workspace =
-          static_cast<const qd::Context *>(args.context)[0].tail->workspace;
-      if (blockIdx.x == 0 && workspace != nullptr) {
-        workspace->reserved[0] = decision != 0 ? 1u : 2u; // which path ran
+      k = QwenConfig{};
+      k.worker = blockIdx.x;
+      k.workers = dev::load_relaxed(&args.state->worker_count);
+      k.limit_ms = dev::detail::wait_limit_ms(args.reserved);
+      const bool fused = fused_possible(args, k.workers);
+      k.contexts = static_cast<const qd::Context *>(args.context);
+      k.workspace = k.contexts[0].tail->workspace;
+      if (blockIdx.x == 0 && k.workspace != nullptr) {
+        k.workspace->reserved[0] = fused ? 1u : 2u; // which path ran
+      }
+      if (fused) { // k.shared stays null on the generic path
+        k.shared = s;
+        k.lm_head = k.contexts[0].tail->lm_head_weight;
+        k.layers = k.contexts[0].layer_count;
+        k.vocab = k.contexts[0].tail->vocab_size;
+        k.lm_units = lm_units_for(k.vocab);
+        k.lm_stage = args.stages[args.compiled_programs[2].stage_offset + 1u];
+        k.ranges = unit_ranges(k.worker, k.workers, k.vocab);
+        k.policy = dev::l2_evict_first_policy();
+        // The stream starts where the initial Program starts (see make_stream_map).
+        k.unit_trace = kStageProfile && k.worker == 0 ? k.contexts[0].tail->stage_profile
+                                                     : nullptr;
+        unit_trace_position = 0;
+        k.map = make_stream_map(k.ranges, k.layers,
+                                sg::phase_program(dev::load_relaxed(&args.state->phase)),
+                                dev::load_relaxed(&args.state->step) % k.layers);
+        k.stream_empty = units_per_cycle(k.ranges, k.layers) == 0;
       }
     }
     __syncthreads();
-    b.fused = decision != 0;
+    b.fused = k.shared != nullptr;
     if (!b.fused) {
       return;
     }
-    extern __shared__ __align__(128) unsigned char dynamic_shared[];
-    b.shared = reinterpret_cast<FusedShared *>(dynamic_shared);
-    b.contexts = static_cast<const qd::Context *>(args.context);
-    b.workspace = b.contexts[0].tail->workspace;
-    b.layers = b.contexts[0].layer_count;
-    b.vocab = b.contexts[0].tail->vocab_size;
-    b.lm_units = (b.vocab + kSlotRows - 1u) / kSlotRows;
-    b.lm_stage = args.stages[args.compiled_programs[2].stage_offset + 1u];
-    b.ranges = unit_ranges(b.worker, b.workers, b.vocab);
-    b.policy = dev::l2_evict_first_policy();
-    b.stream_empty = units_per_cycle(b.ranges, b.layers) == 0;
-    // The stream starts where the initial Program starts (see start_cursor).
-    const uint32_t phase = dev::load_relaxed(&args.state->phase);
-    b.cursor = start_cursor(b.ranges, b.layers, sg::phase_program(phase),
-                            dev::load_relaxed(&args.state->step) % b.layers);
+    for (uint32_t i = threadIdx.x; i < block_config.layers * kLayerMatrices; i += kThreads) {
+      const qd::Context &layer = block_config.contexts[i / kLayerMatrices];
+      const float *pointers[kLayerMatrices] = {layer.q_weight,    layer.k_weight,
+                                               layer.v_weight,    layer.out_weight,
+                                               layer.gate_weight, layer.up_weight,
+                                               layer.down_weight};
+      s->layer_weights[i / kLayerMatrices][i % kLayerMatrices] = pointers[i % kLayerMatrices];
+    }
+    if (threadIdx.x < kSlots) {
+      s->sequence[threadIdx.x] = UINT32_MAX;
+      s->done[threadIdx.x] = 0;
+      s->unit_tag[threadIdx.x] = 0;
+    }
     if (threadIdx.x == 0) {
-      for (uint32_t s = 0; s < kSlots; ++s) {
-        dev::mbarrier_init(&b.shared->full[s], 1);
+      for (uint32_t slot = 0; slot < kSlots; ++slot) {
+        dev::mbarrier_init(&s->full[slot], 1);
       }
       dev::mbarrier_init_fence();
-      if (b.worker == 0) {
+      if (block_config.worker == 0) {
         // A launch that stopped early may have left arrivals behind. No block
         // reaches attention before passing the first barrier, which block 0
         // joins only after this reset.
         for (uint32_t g = 0; g < qd::kKvHeads; ++g) {
-          b.workspace->attention_arrivals[g] = 0;
+          block_config.workspace->attention_arrivals[g] = 0;
         }
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0 && !b.stream_empty) {
-      for (uint32_t s = 0; s < kSlots; ++s) {
-        issue_unit(b);
+    if (threadIdx.x == 0 && !block_config.stream_empty) {
+      StreamCursor c = stream_unit(block_config.map, 0);
+      for (uint32_t n = 0; n < kSlots; ++n) {
+        slot_cursor[n] = c;
+        advance_cursor(block_config.ranges, block_config.layers, c);
+      }
+      for (uint32_t n = 0; n < kSlots; ++n) {
+        issue_unit(b, n);
       }
     }
   }
@@ -1315,17 +1654,22 @@ template <bool kStageProfile> struct QwenWorkloadT {
       return;
     }
     // Wait for copies still in flight into this block's ring before exit.
+    __syncthreads();
     if (threadIdx.x == 0) {
-      const dev::Deadline deadline(b.limit_ms);
-      for (uint32_t n = b.consumed; n < b.produced; ++n) {
-        if (!dev::mbarrier_wait(&b.shared->full[n % kSlots], (n / kSlots) & 1u,
-                                deadline)) {
+      const dev::Deadline deadline(block_config.limit_ms);
+      for (uint32_t slot = 0; slot < kSlots; ++slot) {
+        const uint32_t n = block_config.shared->sequence[slot];
+        if (n != UINT32_MAX && n >= b.consumed &&
+            !dev::mbarrier_wait(&block_config.shared->full[slot], (n / kSlots) & 1u, deadline)) {
           break;
         }
       }
     }
     __syncthreads();
   }
+
+  __device__ static bool local_transitions(const QwenBlock &b) { return b.fused; }
+  __device__ static void program_begin(QwenBlock &b, uint32_t step) { b.step = step; }
 
   __device__ static bool barrier_after(QwenBlock &b, const sg::Stage &stage,
                                        const sg::Stage &next, const sg::Task *tasks) {
@@ -1344,6 +1688,11 @@ template <bool kStageProfile> struct QwenWorkloadT {
       return false;
     case qd::Opcode::rope_kv_cache_f32:
       return following != qd::Opcode::rope_kv_cache_f32;
+    case qd::Opcode::grouped_query_attention_f32: {
+      // Short contexts: attention runs per block inside the o_proj stage.
+      const qd::DecodeState *decode = block_config.contexts[0].tail->decode_state;
+      return !use_local_attention(decode_field(&decode->kv_length) + 1u);
+    }
     default:
       return true;
     }
@@ -1356,8 +1705,8 @@ template <bool kStageProfile> struct QwenWorkloadT {
       generic_execute_stage(stage, tasks, state, opaque, worker, workers);
       return;
     }
-    qd::Context *c = layer_context(opaque, state);
-    const uint32_t layer = dev::load_relaxed(&state->step) % b.layers;
+    const uint32_t layer = b.step % block_config.layers;
+    qd::Context *c = static_cast<qd::Context *>(opaque) + layer;
     const sg::Task &first = tasks[stage.task_offset];
     switch (opcode_of(first)) {
     case qd::Opcode::attention_rmsnorm_f32:
@@ -1387,7 +1736,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
       return;
     case qd::Opcode::residual_advance:
       if (worker == 0) {
-        residual_advance(first, state, c, false);
+        residual_advance(first, state, c, false, b.step);
       }
       return;
     case qd::Opcode::final_rmsnorm_f32:
@@ -1399,7 +1748,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
       return;
     case qd::Opcode::top1_reduce:
       if (worker == 0) {
-        fused_reduce_top1(b, b.lm_stage, tasks, c);
+        fused_reduce_top1(b, block_config.lm_stage, tasks, c);
       }
       return;
     case qd::Opcode::embedding_feedback_f32:
@@ -1487,7 +1836,7 @@ struct QwenSchedulerProfileWorkload : dev::CompiledWorkloadDefaults {
   __device__ static void execute(const sg::Task &task, sg::State *state, void *opaque) {
     qd::Context *c = layer_context(opaque, state);
     if (opcode_of(task) == qd::Opcode::residual_advance) {
-      residual_advance(task, state, c, true);
+      residual_advance(task, state, c, true, dev::load_relaxed(&state->step));
     } else if (opcode_of(task) == qd::Opcode::embedding_feedback_f32) {
       embedding_feedback(c, state);
     }

@@ -286,6 +286,8 @@ struct lrq_model_t {
   std::optional<sg::ResidentExecutor> compiled_executor, dynamic_executor,
       scheduler_profile_executor, stage_profile_executor;
 
+  std::optional<lrrt::DeviceBuffer> trace; // StageProfileEntry array, optional
+  uint32_t trace_capacity = 0;
   std::optional<std::array<uint32_t, 3>> staged_decode; // position, max, eos
   uint32_t last_path = 0;
   uint64_t device_bytes = 0;
@@ -586,7 +588,13 @@ void decode_launch(lrq_model_t &m, lrq_decode_request_t r) {
   }
   sg::ResidentExecutor &executor = executor_for(m, r.path);
   if (r.path == LRQ_PATH_STAGE_PROFILE) {
-    zero_fill(*m.profile);
+    qd::StageProfile header{};
+    if (m.trace) {
+      zero_fill(*m.trace);
+      header.entries = static_cast<qd::StageProfileEntry *>(m.trace->data());
+      header.entry_count = m.trace_capacity;
+    }
+    lrrt::copy_to_device(*m.profile, &header, sizeof(header));
   }
   executor.initialize_on_device(0, r.max_steps, r.stop_value);
   sg::ResidentArgs args = executor.arguments();
@@ -1079,6 +1087,31 @@ LRRT_API lr_status_t lrq_model_run_graph(lrq_model_t *model, const lrq_task_t *t
     executor.launch();
     m.last_path = path;
     read_state(m, state);
+  });
+}
+
+LRRT_API lr_status_t lrq_model_set_trace(lrq_model_t *model, uint32_t entries) {
+  return guarded("lrq_model_set_trace", [&] {
+    if (model == nullptr) {
+      throw std::invalid_argument("null model");
+    }
+    model->trace.reset();
+    model->trace_capacity = 0;
+    if (entries != 0) {
+      model->trace.emplace(model->device, size_t{entries} * sizeof(qd::StageProfileEntry));
+      model->trace_capacity = entries;
+    }
+  });
+}
+
+LRRT_API lr_status_t lrq_model_read_trace(lrq_model_t *model, uint64_t *entries,
+                                          uint32_t capacity) {
+  return guarded("lrq_model_read_trace", [&] {
+    if (model == nullptr || entries == nullptr || !model->trace ||
+        capacity > model->trace_capacity) {
+      throw std::invalid_argument("invalid trace read");
+    }
+    lrrt::copy_to_host(entries, *model->trace, size_t{capacity} * sizeof(qd::StageProfileEntry));
   });
 }
 

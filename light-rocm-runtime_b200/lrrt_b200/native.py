@@ -184,6 +184,8 @@ DRIVER_FUNCTIONS = {
     "lrq_model_stage_profile": (u32, [vp, P(u64), P(u64)]),
     "lrq_model_run_graph": (u32, [vp, P(Task), u32, P(Program), u32, u32, u32, u32, u32,
                                   u32, u32, P(RunState)]),
+    "lrq_model_set_trace": (u32, [vp, u32]),
+    "lrq_model_read_trace": (u32, [vp, P(u64), u32]),
     "lrq_last_error": (cp, []),
 }
 

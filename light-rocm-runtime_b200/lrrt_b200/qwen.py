@@ -262,6 +262,16 @@ class Model:
                 "lrq_model_stage_profile")
         return list(ticks), list(counts)
 
+    def set_trace(self, entries: int) -> None:
+        N.check(N.driver().lrq_model_set_trace(self.handle, entries), "lrq_model_set_trace")
+
+    def read_trace(self, entries: int) -> np.ndarray:
+        out = np.zeros((entries, 2), np.uint64)
+        N.check(N.driver().lrq_model_read_trace(
+            self.handle, out.ctypes.data_as(C.POINTER(C.c_uint64)), entries),
+            "lrq_model_read_trace")
+        return out
+
     def synchronize(self) -> None:
         N.check(N.runtime().lr_synchronize(self.device), "lr_synchronize")
 

@@ -111,9 +111,12 @@ int main() {
               continue;
             }
             r::StreamCursor c = r::start_cursor(ranges, layers, program, 0);
+            const r::StreamMap map = r::make_stream_map(ranges, layers, program, 0);
             for (size_t i = 0; i < want.size(); ++i) {
               const uint32_t got = r::make_tag(c.kind, c.layer, c.unit);
-              if (got != want[i]) {
+              const r::StreamCursor random = r::stream_unit(map, static_cast<uint32_t>(i));
+              if (got != want[i] ||
+                  r::make_tag(random.kind, random.layer, random.unit) != want[i]) {
                 expect(false, "stream order", workers, w, static_cast<uint32_t>(i));
                 break;
               }
