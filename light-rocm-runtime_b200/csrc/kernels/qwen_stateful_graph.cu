@@ -656,11 +656,17 @@ __device__ __forceinline__ void advance_by_slots(StreamCursor &c) {
 __device__ void issue_unit(const QwenBlock &b, uint32_t n) {
   FusedShared *s = block_config.shared;
   const uint32_t slot = n % kSlots;
-  StreamCursor c = slot_cursor[slot];
+  const StreamCursor c = slot_cursor[slot];
   const UnitSource src = unit_source(b, c);
   unsigned char *destination = s->ring + size_t{slot} * kSlotBytes;
+  // The slot's next cursor and this unit's tag are written before the unit is
+  // published: the lane that refills the slot next is a consumer of this unit
+  // and may run before this lane gets past the copies below.
+  StreamCursor next = c;
+  advance_by_slots(next);
+  slot_cursor[slot] = next;
   s->unit_tag[slot] = make_tag(c.kind, c.layer, c.unit);
-  __threadfence_block(); // tag before sequence number
+  __threadfence_block(); // cursor and tag before sequence number
   *reinterpret_cast<volatile uint32_t *>(&s->sequence[slot]) = n;
   dev::mbarrier_arrive_expect_tx(&s->full[slot], src.first_bytes + src.second_bytes);
   dev::bulk_copy_to_shared(destination, src.first, src.first_bytes, &s->full[slot],
@@ -669,8 +675,6 @@ __device__ void issue_unit(const QwenBlock &b, uint32_t n) {
     dev::bulk_copy_to_shared(destination + src.first_bytes, src.second, src.second_bytes,
                              &s->full[slot], block_config.policy);
   }
-  advance_by_slots(c);
-  slot_cursor[slot] = c;
 }
 
 // Lane 0's verdict, shared by the warp.
