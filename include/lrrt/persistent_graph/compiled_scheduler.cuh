@@ -151,7 +151,14 @@ struct CompiledWorkloadDefaults {
                                        uint64_t, uint64_t) {}
   __device__ static void begin(Block &, const ResidentArgs &) {}
   __device__ static bool local_transitions(const Block &) { return false; }
-  __device__ static void program_begin(Block &, uint32_t) {}
+  __device__ static void program_begin(Block &, uint32_t /*program*/, uint32_t /*step*/) {}
+  __device__ static void stage_begin(Block &, uint32_t /*stage index in program*/) {}
+  // Local-transition mode: the branch_value the finished Program's tasks
+  // wrote. A workload that can compute it from its own state (the same rule
+  // its task applies) avoids a global read.
+  __device__ static uint32_t branch_value(Block &, const State *state) {
+    return load_relaxed(&state->branch_value);
+  }
   __device__ static bool barrier_after(Block &, const Stage &, const Stage &,
                                        const Task *) {
     return true;
@@ -174,13 +181,14 @@ struct LocalControl {
 };
 
 // The Program transition of finish_program computed from the block's own copy
-// of the control state; predicate_value and branch_value were written by the
-// Program's tasks before its final barrier.
+// of the control state; predicate_value was written by the Program's tasks
+// before its final barrier, `branch` is the branch_value they produced.
 __device__ __forceinline__ void local_transition(LocalControl &c, const State *state,
                                                  const Program &program,
                                                  uint32_t generation,
                                                  uint32_t phase_state_count,
-                                                 uint32_t max_steps, uint32_t stop_value) {
+                                                 uint32_t max_steps, uint32_t stop_value,
+                                                 uint32_t branch) {
   const uint32_t next_step =
       c.step + ((program.flags & kProgramAdvancesStep) != 0 ? 1u : 0u);
   c.step = next_step;
@@ -197,8 +205,7 @@ __device__ __forceinline__ void local_transition(LocalControl &c, const State *s
     c.error_code = kErrorPhaseSlots;
   } else {
     uint32_t next = program.next_program;
-    if ((program.flags & kProgramBranchesOnState) != 0 &&
-        load_relaxed(&state->branch_value) != 0) {
+    if ((program.flags & kProgramBranchesOnState) != 0 && branch != 0) {
       next = program.branch_program;
     }
     c.phase = make_phase(generation + 1u, next);
@@ -247,6 +254,29 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
     Workload::initialize_profile(args.context);
   }
   const uint32_t worker = blockIdx.x;
+  // Small plans are copied into shared memory once: the loop reads a Program
+  // per transition and a Stage per stage, and a global read costs an L2 round
+  // trip behind whatever else the kernel streams.
+  constexpr uint32_t kCachedPrograms = 8;
+  constexpr uint32_t kCachedStages = 64;
+  __shared__ Program program_cache[kCachedPrograms];
+  __shared__ CompiledProgram compiled_cache[kCachedPrograms];
+  __shared__ Stage stage_cache[kCachedStages];
+  const bool cached =
+      args.program_count <= kCachedPrograms && args.stage_count <= kCachedStages;
+  if (cached) {
+    for (uint32_t i = threadIdx.x; i < args.program_count; i += blockDim.x) {
+      program_cache[i] = args.programs[i];
+      compiled_cache[i] = args.compiled_programs[i];
+    }
+    for (uint32_t i = threadIdx.x; i < args.stage_count; i += blockDim.x) {
+      stage_cache[i] = args.stages[i];
+    }
+  }
+  const Program *programs = cached ? program_cache : args.programs;
+  const CompiledProgram *compiled_programs =
+      cached ? compiled_cache : args.compiled_programs;
+  const Stage *stages = cached ? stage_cache : args.stages;
   typename Workload::Block block{};
   Workload::begin(block, args);
   const bool local = Workload::local_transitions(block);
@@ -254,6 +284,7 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
   __shared__ uint32_t loop_phase, loop_running;
   __shared__ detail::LocalControl shared_control;
   detail::LocalControl control{};
+  uint32_t status_seen = static_cast<uint32_t>(Status::running); // thread 0
   if (threadIdx.x == 0) {
     shared_control = {load_relaxed(&state->phase), load_relaxed(&state->step),
                       static_cast<uint32_t>(Status::running), 0,
@@ -274,23 +305,29 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
     }
     const uint32_t phase = local ? control.phase : loop_phase;
     const uint32_t generation = phase_generation(phase);
-    const Program program = args.programs[phase_program(phase)];
-    const CompiledProgram compiled = args.compiled_programs[phase_program(phase)];
+    const Program program = programs[phase_program(phase)];
+    const CompiledProgram compiled = compiled_programs[phase_program(phase)];
     MaskState *barrier = &args.phase_states[generation];
     const Deadline deadline(limit_ms);
-    Workload::program_begin(block, control.step);
+    if (local && threadIdx.x == 0) {
+      // Read now, used at the transition: a failure elsewhere is noticed one
+      // Program later (or by any wait), without a read on the critical path.
+      status_seen = load_relaxed(&state->status);
+    }
+    Workload::program_begin(block, phase_program(phase), control.step);
     uint32_t barrier_index = 0;
     bool ok = true;
     for (uint32_t s = 0; s < compiled.stage_count && ok; ++s) {
-      const Stage stage = args.stages[compiled.stage_offset + s];
+      const Stage stage = stages[compiled.stage_offset + s];
+      Workload::stage_begin(block, s);
       if (worker < workers) {
         Workload::execute_stage(block, stage, args.tasks, state, args.context,
                                 worker, workers);
       }
       const bool last = s + 1u == compiled.stage_count;
-      if (!last && !Workload::barrier_after(
-                       block, stage, args.stages[compiled.stage_offset + s + 1u],
-                       args.tasks)) {
+      if (!last && !Workload::barrier_after(block, stage,
+                                            stages[compiled.stage_offset + s + 1u],
+                                            args.tasks)) {
         continue;
       }
       const uint64_t arrive_ns = Workload::kTraceBarriers ? global_timer_ns() : 0;
@@ -318,16 +355,21 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
     // takes the same branch even if another block fails the run concurrently.
     if (threadIdx.x == 0) {
       if (local && ok) {
+        const uint32_t branch = (program.flags & kProgramBranchesOnState) != 0
+                                    ? Workload::branch_value(block, state)
+                                    : 0u;
         detail::local_transition(shared_control, state, program, generation,
-                                 args.phase_state_count, max_steps, stop_value);
+                                 args.phase_state_count, max_steps, stop_value, branch);
         if (worker == 0) {
           detail::publish_control(state, shared_control);
         }
       }
+      const uint32_t status =
+          local ? status_seen : detail::load_status(state);
       loop_running = ok &&
                      (!local ||
                       shared_control.status == static_cast<uint32_t>(Status::running)) &&
-                     detail::load_status(state) == static_cast<uint32_t>(Status::running);
+                     status == static_cast<uint32_t>(Status::running);
     }
     __syncthreads();
     if (local) {

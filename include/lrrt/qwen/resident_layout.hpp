@@ -39,7 +39,7 @@ struct FusedShared {
 // Dynamic shared memory a compiled launch needs for the fused path.
 constexpr uint32_t kFusedSharedBytes = sizeof(FusedShared);
 static_assert(kDownRowBytes <= kSlotBytes);
-static_assert(kFusedSharedBytes + 2048u <= 232448u,
+static_assert(kFusedSharedBytes + 4096u <= 232448u,
               "fused path plus static shared memory exceeds 227 KB");
 
 } // namespace lrrt::qwen::stateful_graph::resident

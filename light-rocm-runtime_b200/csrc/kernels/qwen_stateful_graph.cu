@@ -560,6 +560,14 @@ struct QwenConfig {
   uint64_t policy;
   sg::Stage lm_stage;
   qd::StageProfile *unit_trace; // stage-profile runs: block 0 unit timeline
+  // Token position / KV length at the launch's first decode step and the
+  // token index (step / layers, adjusted) they belong to: the fused path
+  // derives each step's values instead of reading DecodeState, which only
+  // embedding_feedback advances, by one per generated token.
+  uint32_t base_position, base_kv_length;
+  int32_t base_token;
+  float epsilon[3];               // attention, MLP and final RMSNorm tasks
+  uint32_t residual_argument[2];  // residual_advance task arguments
 };
 __shared__ QwenConfig block_config;
 
@@ -570,8 +578,39 @@ struct QwenBlock {
   bool attention_pending;   // block 0 owes the global query copy of attention
   uint32_t consumed;        // stream sequence number of the next unit to consume
   uint32_t traced_barriers; // stage-profile barrier trace position (thread 0)
+  uint32_t program;         // current Program and stage within it
+  uint32_t stage;
   uint32_t step;            // graph step of the current Program (local transitions)
+  uint32_t position;        // token position and KV length of that step
+  uint32_t kv_length;
 };
+
+// Stage opcodes of the canonical decode table the fused path requires
+// (checked by canonical_table).
+__device__ __forceinline__ qd::Opcode fused_opcode(uint32_t program, uint32_t stage) {
+  using O = qd::Opcode;
+  switch (program * 8u + stage) {
+  case 0: return O::attention_rmsnorm_f32;
+  case 1: return O::qkv_projection_f32;
+  case 2: return O::rope_kv_cache_f32;
+  case 3: return O::grouped_query_attention_f32;
+  case 4: return O::attention_output_residual_f32;
+  case 8: return O::mlp_rmsnorm_f32;
+  case 9: return O::gate_up_silu_f32;
+  case 10: return O::down_matvec_f32;
+  case 11: return O::residual_advance;
+  case 16: return O::final_rmsnorm_f32;
+  case 17: return O::lm_head_top1_partition_f32;
+  case 18: return O::top1_reduce;
+  default: return O::embedding_feedback_f32;
+  }
+}
+
+// residual_advance's branch rule (reference :749-760) for the fused path.
+__device__ __forceinline__ bool fused_layer_boundary(uint32_t step) {
+  return block_config.residual_argument[1] == 0 ||
+         (step + 1u) % block_config.layers == 0;
+}
 
 // Stage-profile runs record, for block 0, each warp's wait and compute times
 // per stream unit in the second half of StageProfile.entries.
@@ -893,7 +932,7 @@ __device__ __forceinline__ QkvRows qkv_rows(uint32_t u, uint32_t gw) {
 }
 
 __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
-  const uint32_t position = decode_field(&c->tail->decode_state->token_position);
+  const uint32_t position = b.position;
   const size_t rope = size_t{position} * qd::kRotarySize;
   const size_t cache_row = size_t{position} * qd::kKvSize;
   consume_pairs(
@@ -932,7 +971,7 @@ __device__ __forceinline__ bool use_local_attention(uint32_t positions) {
 }
 
 __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
-  const uint32_t positions = decode_field(&c->tail->decode_state->kv_length) + 1u;
+  const uint32_t positions = b.kv_length + 1u;
   if (use_local_attention(positions)) {
     local_attention(b, c, positions);
     b.attention_pending = block_config.worker == 0;
@@ -1298,7 +1337,7 @@ __device__ void local_attention(QwenBlock &b, const qd::Context *c, uint32_t pos
 }
 
 __device__ void fused_attention(QwenBlock &b, qd::Context *c) {
-  const uint32_t positions = decode_field(&c->tail->decode_state->kv_length) + 1u;
+  const uint32_t positions = b.kv_length + 1u;
   if (use_local_attention(positions)) {
     return; // computed per block inside the o_proj stage
   }
@@ -1602,9 +1641,24 @@ template <bool kStageProfile> struct QwenWorkloadT {
         k.unit_trace = kStageProfile && k.worker == 0 ? k.contexts[0].tail->stage_profile
                                                      : nullptr;
         unit_trace_position = 0;
-        k.map = make_stream_map(k.ranges, k.layers,
-                                sg::phase_program(dev::load_relaxed(&args.state->phase)),
-                                dev::load_relaxed(&args.state->step) % k.layers);
+        const uint32_t program = sg::phase_program(dev::load_relaxed(&args.state->phase));
+        const uint32_t step = dev::load_relaxed(&args.state->step);
+        k.map = make_stream_map(k.ranges, k.layers, program, step % k.layers);
+        // Program 2 of token t runs at step (t + 1) * layers, before the
+        // feedback that advances the decode state: a launch starting there is
+        // one token behind its step.
+        const qd::DecodeState *decode = k.contexts[0].tail->decode_state;
+        k.base_position = decode_field(&decode->token_position);
+        k.base_kv_length = decode_field(&decode->kv_length);
+        k.base_token = static_cast<int32_t>(step / k.layers) - (program == 2 ? 1 : 0);
+        const sg::Stage *stages = args.stages;
+        const sg::CompiledProgram *compiled = args.compiled_programs;
+        k.epsilon[0] = __uint_as_float(args.tasks[stages[compiled[0].stage_offset].task_offset].argument0);
+        k.epsilon[1] = __uint_as_float(args.tasks[stages[compiled[1].stage_offset].task_offset].argument0);
+        k.epsilon[2] = __uint_as_float(args.tasks[stages[compiled[2].stage_offset].task_offset].argument0);
+        const sg::Task &advance = args.tasks[stages[compiled[1].stage_offset + 3u].task_offset];
+        k.residual_argument[0] = advance.argument0;
+        k.residual_argument[1] = advance.argument1;
         k.stream_empty = units_per_cycle(k.ranges, k.layers) == 0;
       }
     }
@@ -1673,15 +1727,31 @@ template <bool kStageProfile> struct QwenWorkloadT {
   }
 
   __device__ static bool local_transitions(const QwenBlock &b) { return b.fused; }
-  __device__ static void program_begin(QwenBlock &b, uint32_t step) { b.step = step; }
+  __device__ static void program_begin(QwenBlock &b, uint32_t program, uint32_t step) {
+    b.program = program;
+    b.step = step;
+    if (b.fused) {
+      const int32_t tokens = static_cast<int32_t>(step / block_config.layers) -
+                             block_config.base_token;
+      b.position = block_config.base_position + static_cast<uint32_t>(tokens);
+      b.kv_length = block_config.base_kv_length + static_cast<uint32_t>(tokens);
+    }
+  }
+  __device__ static void stage_begin(QwenBlock &b, uint32_t stage) { b.stage = stage; }
+  __device__ static uint32_t branch_value(QwenBlock &b, const sg::State *state) {
+    if (b.fused) {
+      return fused_layer_boundary(b.step) ? 1u : 0u; // what residual_advance writes
+    }
+    return dev::load_relaxed(&state->branch_value);
+  }
 
   __device__ static bool barrier_after(QwenBlock &b, const sg::Stage &stage,
                                        const sg::Stage &next, const sg::Task *tasks) {
     if (!b.fused) {
       return true;
     }
-    const qd::Opcode op = opcode_of(tasks[stage.task_offset]);
-    const qd::Opcode following = opcode_of(tasks[next.task_offset]);
+    const qd::Opcode op = fused_opcode(b.program, b.stage);
+    const qd::Opcode following = fused_opcode(b.program, b.stage + 1u);
     switch (op) {
     case qd::Opcode::attention_rmsnorm_f32: // norm recomputed per block
     case qd::Opcode::mlp_rmsnorm_f32:
@@ -1692,11 +1762,9 @@ template <bool kStageProfile> struct QwenWorkloadT {
       return false;
     case qd::Opcode::rope_kv_cache_f32:
       return following != qd::Opcode::rope_kv_cache_f32;
-    case qd::Opcode::grouped_query_attention_f32: {
+    case qd::Opcode::grouped_query_attention_f32:
       // Short contexts: attention runs per block inside the o_proj stage.
-      const qd::DecodeState *decode = block_config.contexts[0].tail->decode_state;
-      return !use_local_attention(decode_field(&decode->kv_length) + 1u);
-    }
+      return !use_local_attention(b.kv_length + 1u);
     default:
       return true;
     }
@@ -1711,10 +1779,9 @@ template <bool kStageProfile> struct QwenWorkloadT {
     }
     const uint32_t layer = b.step % block_config.layers;
     qd::Context *c = static_cast<qd::Context *>(opaque) + layer;
-    const sg::Task &first = tasks[stage.task_offset];
-    switch (opcode_of(first)) {
+    switch (fused_opcode(b.program, b.stage)) {
     case qd::Opcode::attention_rmsnorm_f32:
-      fused_rmsnorm(b, c, c->attention_norm_weight, __uint_as_float(first.argument0),
+      fused_rmsnorm(b, c, c->attention_norm_weight, block_config.epsilon[0],
                     c->attention_normalized);
       return;
     case qd::Opcode::qkv_projection_f32:
@@ -1729,8 +1796,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
       fused_out(b, state, c, layer);
       return;
     case qd::Opcode::mlp_rmsnorm_f32:
-      fused_rmsnorm(b, c, c->mlp_norm_weight, __uint_as_float(first.argument0),
-                    c->mlp_normalized);
+      fused_rmsnorm(b, c, c->mlp_norm_weight, block_config.epsilon[1], c->mlp_normalized);
       return;
     case qd::Opcode::gate_up_silu_f32:
       fused_gate_up(b, state, c, layer);
@@ -1739,12 +1805,18 @@ template <bool kStageProfile> struct QwenWorkloadT {
       fused_down(b, state, c, layer);
       return;
     case qd::Opcode::residual_advance:
-      if (worker == 0) {
-        residual_advance(first, state, c, false, b.step);
+      // The residual was added in the down epilogue; what remains is the
+      // branch / predicate bookkeeping, which State carries for the host.
+      if (worker == 0 && threadIdx.x == 0) {
+        const bool boundary = fused_layer_boundary(b.step);
+        if (boundary && block_config.residual_argument[1] == 0) {
+          state->predicate_value += block_config.residual_argument[0];
+        }
+        state->branch_value = boundary ? 1u : 0u;
       }
       return;
     case qd::Opcode::final_rmsnorm_f32:
-      fused_rmsnorm(b, c, c->tail->final_norm_weight, __uint_as_float(first.argument0),
+      fused_rmsnorm(b, c, c->tail->final_norm_weight, block_config.epsilon[2],
                     c->tail->final_normalized);
       return;
     case qd::Opcode::lm_head_top1_partition_f32:
