@@ -533,8 +533,6 @@ using namespace qd::resident;
 constexpr uint32_t kMaxAttentionChunks = 128;
 constexpr uint32_t kKvTile = 32;                       // positions per attention tile
 constexpr uint32_t kKeyStride = qd::kHeadSize + 1u;    // padded K rows (bank-conflict free)
-constexpr uint32_t kGroupWarps = 4;                    // warps sharing one 8-row unit
-constexpr uint32_t kGroups = kWarps / kGroupWarps;     // units in flight per block
 constexpr uint32_t kLmScratch = 1024;                  // LM-head candidates (input floats)
 // Up to this many KV positions every block computes the attention output of
 // all 14 query heads itself, inside the o_proj stage, so the attention stage
@@ -840,39 +838,52 @@ __device__ void fused_load_input(QwenBlock &b, const float *source, uint32_t cou
   __syncthreads();
 }
 
-// Dot product of a 896-float shared-memory row with the register-held input,
-// summed into lane 0.
-__device__ __forceinline__ float row_dot(const float *row, const float4 (&x)[7],
-                                         uint32_t lane) {
-  const float4 *r = reinterpret_cast<const float4 *>(row);
-  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+// Sums eight per-lane partials across the warp with a transposed butterfly
+// (4 + 2 + 1 + 1 + 1 shuffles): afterwards lanes 4r..4r+3 hold row r's total,
+// r = (lane >> 2) & 7.
+__device__ __forceinline__ float reduce_rows8(const float (&a)[8], uint32_t lane) {
+  const bool high16 = (lane & 16u) != 0;
+  float q[4];
 #pragma unroll
-  for (uint32_t j = 0; j < 7; ++j) {
-    const float4 w = r[lane + 32u * j];
-    a0 = fmaf(w.x, x[j].x, a0);
-    a1 = fmaf(w.y, x[j].y, a1);
-    a2 = fmaf(w.z, x[j].z, a2);
-    a3 = fmaf(w.w, x[j].w, a3);
+  for (uint32_t i = 0; i < 4; ++i) {
+    const float send = high16 ? a[i] : a[i + 4];
+    const float keep = high16 ? a[i + 4] : a[i];
+    q[i] = keep + __shfl_xor_sync(kFullMask, send, 16);
   }
-  return warp_sum((a0 + a1) + (a2 + a3));
+  const bool high8 = (lane & 8u) != 0;
+  float p[2];
+#pragma unroll
+  for (uint32_t i = 0; i < 2; ++i) {
+    const float send = high8 ? q[i] : q[i + 2];
+    const float keep = high8 ? q[i + 2] : q[i];
+    p[i] = keep + __shfl_xor_sync(kFullMask, send, 8);
+  }
+  const bool high4 = (lane & 4u) != 0;
+  float v = (high4 ? p[1] : p[0]) + __shfl_xor_sync(kFullMask, high4 ? p[0] : p[1], 4);
+  v += __shfl_xor_sync(kFullMask, v, 2);
+  v += __shfl_xor_sync(kFullMask, v, 1);
+  return v;
 }
 
-// Consumes this block's units of an 8-row kind. Warps form kGroups groups of
-// four; group g takes units g, g + kGroups, ...; warp gw of a group computes
-// rows gw and gw + 4 of the unit (a rotary pair, a gate/up pair, or two plain
-// rows) and lane 0 runs `epilogue(unit, gw, row_a, row_b, rows)`.
+// Consumes this block's units of an 8-row kind, one whole unit per warp:
+// warp w takes units w, w + kWarps, ... Each lane accumulates its float4
+// columns of all eight rows (eight independent FMA chains against the
+// register-held input), reduce_rows8 leaves row r's dot product in lanes
+// 4r..4r+3, and every lane runs `epilogue(unit, row, value, rows, extra)`
+// with row = (lane >> 2) & 7; lanes with (lane & 3) == 0 own the row's
+// outputs. `operands(unit, row)` is loaded before the wait so its latency
+// overlaps it.
 struct NoOperands {
   __device__ float4 operator()(uint32_t, uint32_t) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
 };
 
 template <typename Epilogue, typename Operands = NoOperands>
-__device__ bool consume_pairs(QwenBlock &b, sg::State *state, uint32_t kind,
+__device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
                               uint32_t layer, Epilogue epilogue,
                               Operands operands = NoOperands{}) {
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
-  const uint32_t group = warp / kGroupWarps;
-  const uint32_t gw = warp % kGroupWarps;
+  const uint32_t row = (lane >> 2u) & 7u;
   float4 x[7];
   const float4 *input = reinterpret_cast<const float4 *>(block_config.shared->input);
 #pragma unroll
@@ -882,12 +893,10 @@ __device__ bool consume_pairs(QwenBlock &b, sg::State *state, uint32_t kind,
   const UnitRange range = block_config.ranges.of[kind];
   const uint32_t units = range.end - range.begin;
   bool ok = true;
-  for (uint32_t i = group; i < units; i += kGroups) {
+  for (uint32_t i = warp; i < units; i += kWarps) {
     const uint32_t n = b.consumed + i;
     const uint32_t u = range.begin + i;
-    // Epilogue operands (biases, RoPE factors, residual rows) are loaded
-    // before the wait so their latency overlaps it.
-    const float4 extra = lane == 0 ? operands(u, gw) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 extra = (lane & 3u) == 0u ? operands(u, row) : make_float4(0.f, 0.f, 0.f, 0.f);
     const uint64_t t_before = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
     const float *slot = wait_unit(b, state, n, make_tag(kind, layer, u));
     const uint64_t t_ready = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
@@ -895,15 +904,35 @@ __device__ bool consume_pairs(QwenBlock &b, sg::State *state, uint32_t kind,
       ok = false;
       break;
     }
-    const uint32_t rows = kind == kLmHead ? min(kSlotRows, block_config.vocab - u * kSlotRows) : kSlotRows;
-    const float a = gw < rows ? row_dot(slot + gw * qd::kHiddenSize, x, lane) : 0.0f;
-    const float c = gw + 4u < rows ? row_dot(slot + (gw + 4u) * qd::kHiddenSize, x, lane) : 0.0f;
-    if (lane == 0) {
-      epilogue(u, gw, a, c, rows, extra);
-      release_unit(b, n, kGroupWarps);
-      if (block_config.unit_trace != nullptr) {
-        trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
+    const uint32_t rows =
+        kind == kLmHead ? min(kSlotRows, block_config.vocab - u * kSlotRows) : kSlotRows;
+    // Rows past `rows` (the LM head's last unit) hold stale bytes; their sums
+    // stay in their own lanes and are ignored by the epilogue.
+    const float4 *w = reinterpret_cast<const float4 *>(slot);
+    float a[8];
+#pragma unroll
+    for (uint32_t r = 0; r < 8; ++r) {
+      a[r] = 0.0f;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 7; ++j) {
+#pragma unroll
+      for (uint32_t r = 0; r < 8; ++r) {
+        const float4 v = w[r * (qd::kHiddenSize / 4u) + lane + 32u * j];
+        a[r] = fmaf(v.x, x[j].x, a[r]);
+        a[r] = fmaf(v.y, x[j].y, a[r]);
+        a[r] = fmaf(v.z, x[j].z, a[r]);
+        a[r] = fmaf(v.w, x[j].w, a[r]);
       }
+    }
+    // The shuffles complete every lane's shared-memory reads of the slot.
+    const float value = reduce_rows8(a, lane);
+    if (lane == 0) {
+      release_unit(b, n, 1);
+    }
+    epilogue(u, row, value, rows, extra);
+    if (lane == 0 && block_config.unit_trace != nullptr) {
+      trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
     }
     __syncwarp();
   }
@@ -935,13 +964,18 @@ __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32
   const uint32_t position = b.position;
   const size_t rope = size_t{position} * qd::kRotarySize;
   const size_t cache_row = size_t{position} * qd::kKvSize;
-  consume_pairs(
+  consume_units(
       b, state, kQkv, layer,
-      [&](uint32_t u, uint32_t gw, float first_dot, float second_dot, uint32_t,
-          float4 operand) {
-        const QkvRows r = qkv_rows(u, gw);
-        const float x0 = first_dot + operand.x;
-        const float x1 = second_dot + operand.y;
+      [&](uint32_t u, uint32_t row, float value, uint32_t, float4 operand) {
+        // Rows 0-3 of a unit are f..f+3 of one head, rows 4-7 their rotary
+        // partners f+32..f+35: lane 4r (r < 4) rotates the pair (r, r + 4).
+        const float partner = __shfl_xor_sync(kFullMask, value, 16);
+        if (row >= 4u || (threadIdx.x & 3u) != 0u) {
+          return;
+        }
+        const QkvRows r = qkv_rows(u, row);
+        const float x0 = value + operand.x;
+        const float x1 = partner + operand.y;
         float r0 = x0, r1 = x1;
         if (r.which != 2) {
           r0 = x0 * operand.z - x1 * operand.w;
@@ -956,8 +990,11 @@ __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32
           cache[r.second] = r1;
         }
       },
-      [&](uint32_t u, uint32_t gw) {
-        const QkvRows r = qkv_rows(u, gw);
+      [&](uint32_t u, uint32_t row) {
+        if (row >= 4u) {
+          return make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const QkvRows r = qkv_rows(u, row);
         const float *bias = r.which == 0 ? c->q_bias : (r.which == 1 ? c->k_bias : c->v_bias);
         return make_float4(bias[r.first], bias[r.second], c->rope_cos[rope + r.frequency],
                            c->rope_sin[rope + r.frequency]);
@@ -978,25 +1015,27 @@ __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32
   } else {
     fused_load_input(b, c->query, qd::kQuerySize);
   }
-  consume_pairs(
+  consume_units(
       b, state, kOut, layer,
-      [&](uint32_t u, uint32_t gw, float a, float d, uint32_t, float4 residual) {
-        const uint32_t row = u * kSlotRows + gw;
-        c->hidden[row] = residual.x + a;
-        c->hidden[row + 4u] = residual.y + d;
+      [&](uint32_t u, uint32_t row, float value, uint32_t, float4 residual) {
+        if ((threadIdx.x & 3u) == 0u) {
+          c->hidden[u * kSlotRows + row] = residual.x + value;
+        }
       },
-      [&](uint32_t u, uint32_t gw) {
-        const uint32_t row = u * kSlotRows + gw;
-        return make_float4(dev::load_cg(c->hidden + row), dev::load_cg(c->hidden + row + 4u),
-                           0.f, 0.f);
+      [&](uint32_t u, uint32_t row) {
+        return make_float4(dev::load_cg(c->hidden + u * kSlotRows + row), 0.f, 0.f, 0.f);
       });
 }
 
 __device__ void fused_gate_up(QwenBlock &b, sg::State *state, qd::Context *c,
                               uint32_t layer) {
-  consume_pairs(b, state, kGateUp, layer,
-                [&](uint32_t u, uint32_t gw, float gate, float up, uint32_t, float4) {
-                  c->activated[u * kGuRowsPerUnit + gw] = silu_times(gate, up);
+  // Rows 0-3 of a unit are gate rows 4u..4u+3, rows 4-7 the matching up rows.
+  consume_units(b, state, kGateUp, layer,
+                [&](uint32_t u, uint32_t row, float value, uint32_t, float4) {
+                  const float up = __shfl_xor_sync(kFullMask, value, 16);
+                  if (row < 4u && (threadIdx.x & 3u) == 0u) {
+                    c->activated[u * kGuRowsPerUnit + row] = silu_times(value, up);
+                  }
                 });
 }
 
@@ -1386,15 +1425,47 @@ __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &s
       mine_index[task] = row;
     }
   };
-  consume_pairs(b, state, kLmHead, 0,
-                [&](uint32_t u, uint32_t gw, float a, float d, uint32_t rows, float4) {
-                  if (gw < rows) {
-                    offer(u * kSlotRows + gw, a);
-                  }
-                  if (gw + 4u < rows) {
-                    offer(u * kSlotRows + gw + 4u, d);
-                  }
-                });
+  consume_units(
+      b, state, kLmHead, 0,
+      [&](uint32_t u, uint32_t row, float value, uint32_t rows, float4) {
+        const uint32_t lane = threadIdx.x & 31u;
+        const uint32_t first = u * kSlotRows;
+        uint32_t task_end = 0;
+        if (lane == 0) {
+          while (first >= task_ends[task]) {
+            ++task;
+          }
+          task_end = task_ends[task];
+        }
+        task_end = __shfl_sync(kFullMask, task_end, 0);
+        if (first + rows <= task_end) {
+          // The whole unit lies in one task: warp top-1 (ties to the lower
+          // row), then one offer.
+          float best = row < rows ? value : -INFINITY;
+          uint32_t index = row < rows ? first + row : UINT32_MAX;
+#pragma unroll
+          for (uint32_t offset = 4; offset < 32; offset *= 2) {
+            const float other = __shfl_xor_sync(kFullMask, best, offset);
+            const uint32_t other_index = __shfl_xor_sync(kFullMask, index, offset);
+            if (better_top1(other, other_index, best, index)) {
+              best = other;
+              index = other_index;
+            }
+          }
+          if (lane == 0) {
+            offer(index, best);
+          }
+        } else {
+          // A task boundary inside the unit: offer row by row.
+#pragma unroll
+          for (uint32_t r = 0; r < kSlotRows; ++r) {
+            const float v = __shfl_sync(kFullMask, value, 4u * r);
+            if (lane == 0 && r < rows) {
+              offer(first + r, v);
+            }
+          }
+        }
+      });
   __syncthreads();
   if (threadIdx.x < task_count && range.begin < range.end) {
     const uint32_t t = threadIdx.x;
