@@ -145,12 +145,6 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return policy;
 }
 
-// Orders this thread's earlier generic-proxy shared-memory accesses before
-// later async-proxy (TMA) writes to the same buffer.
-__device__ __forceinline__ void fence_proxy_async_shared() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // L2-coherent loads for data other blocks wrote during this kernel.
 __device__ __forceinline__ float load_cg(const float *address) {
   return __ldcg(address);

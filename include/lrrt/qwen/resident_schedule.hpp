@@ -226,6 +226,57 @@ LRRT_HOST_DEVICE inline StreamCursor stream_unit(const StreamMap &m, uint32_t n)
   return {layer, kind, m.first[kind] + at};
 }
 
+// Incremental form of stream_unit for the lane that refills a ring slot:
+// (layer, index) with layer == layers meaning the LM-head region; advancing
+// by a ring's depth costs a compare and a subtraction per region crossed
+// instead of a division.
+struct StreamPosition {
+  uint32_t layer;
+  uint32_t index;
+};
+
+LRRT_HOST_DEVICE inline uint32_t region_units(const StreamMap &m, uint32_t layer) {
+  return layer < m.layers ? m.per_layer : m.count[kLmHead];
+}
+
+LRRT_HOST_DEVICE inline StreamPosition stream_position(const StreamMap &m, uint32_t n) {
+  const uint32_t at = static_cast<uint32_t>((uint64_t{m.start} + n) % m.cycle);
+  const uint32_t decoder = m.layers * m.per_layer;
+  if (at >= decoder) {
+    return {m.layers, at - decoder};
+  }
+  return {at / m.per_layer, at % m.per_layer};
+}
+
+// Moves `p` forward by `by` units (the stream must not be empty).
+LRRT_HOST_DEVICE inline void advance_position(const StreamMap &m, StreamPosition &p,
+                                              uint32_t by) {
+  p.index += by;
+  // Each pass leaves a region; m.layers + 1 regions form a cycle, and `by`
+  // is smaller than a cycle for every caller.
+  for (uint32_t guard = 0; guard < 2u * (m.layers + 1u) + by; ++guard) {
+    const uint32_t size = region_units(m, p.layer);
+    if (p.index < size) {
+      return;
+    }
+    p.index -= size;
+    p.layer = p.layer >= m.layers ? 0u : p.layer + 1u;
+  }
+}
+
+LRRT_HOST_DEVICE inline StreamCursor position_cursor(const StreamMap &m, StreamPosition p) {
+  if (p.layer >= m.layers) {
+    return {0, kLmHead, m.first[kLmHead] + p.index};
+  }
+  uint32_t at = p.index;
+  uint32_t kind = kQkv;
+  while (kind < kDown && at >= m.count[kind]) {
+    at -= m.count[kind];
+    ++kind;
+  }
+  return {p.layer, kind, m.first[kind] + at};
+}
+
 } // namespace lrrt::qwen::stateful_graph::resident
 
 #endif // LRRT_QWEN_RESIDENT_SCHEDULE_HPP_

@@ -672,20 +672,11 @@ __device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
   }
 }
 
-// Per-slot stream cursors: slot_cursor[s] is the next unit slot s will
-// receive. A slot receives units s, s + kSlots, ...; its cursor is touched
-// only by the lane refilling it, which is ordered after the previous refill
-// by the slot's mbarrier (release arrive, acquire wait) and the done counter.
-// (Advancing a cursor costs a few compares; recomputing a unit from its
-// sequence number takes 64-bit division on the refilling warp's critical path.)
-__shared__ StreamCursor slot_cursor[kSlots];
-
-__device__ __forceinline__ void advance_by_slots(StreamCursor &c) {
-#pragma unroll 1
-  for (uint32_t i = 0; i < kSlots; ++i) {
-    advance_cursor(block_config.ranges, block_config.layers, c);
-  }
-}
+// Per-slot stream positions: slot_position[s] is where the next unit slot s
+// receives sits in the block's stream. A slot receives units s, s + kSlots,
+// ...; its position is touched only by the lane refilling it, which is a
+// consumer of the slot's previous unit.
+__shared__ StreamPosition slot_position[kSlots];
 
 // Issues the bulk copies of stream unit `n` into its ring slot (one lane).
 // The slot's previous unit (n - kSlots) has been released by its consumers.
@@ -693,17 +684,20 @@ __device__ __forceinline__ void advance_by_slots(StreamCursor &c) {
 __device__ void issue_unit(const QwenBlock &b, uint32_t n) {
   FusedShared *s = block_config.shared;
   const uint32_t slot = n % kSlots;
-  const StreamCursor c = slot_cursor[slot];
+  const StreamPosition position = slot_position[slot];
+  const StreamCursor c = position_cursor(block_config.map, position);
   const UnitSource src = unit_source(b, c);
   unsigned char *destination = s->ring + size_t{slot} * kSlotBytes;
-  // The slot's next cursor and this unit's tag are written before the unit is
-  // published: the lane that refills the slot next is a consumer of this unit
-  // and may run before this lane gets past the copies below.
-  StreamCursor next = c;
-  advance_by_slots(next);
-  slot_cursor[slot] = next;
+  // The slot's next position and this unit's tag are written before the unit
+  // is published: the lane that refills the slot next is a consumer of this
+  // unit and may run before this lane gets past the copies below. Both reach
+  // other warps through the slot's mbarrier (this lane's arrive releases
+  // them, the consumers' wait acquires them); the sequence number only tells
+  // a consumer that the fill it waits for is the current one.
+  StreamPosition next = position;
+  advance_position(block_config.map, next, kSlots);
+  slot_position[slot] = next;
   s->unit_tag[slot] = make_tag(c.kind, c.layer, c.unit);
-  __threadfence_block(); // cursor and tag before sequence number
   *reinterpret_cast<volatile uint32_t *>(&s->sequence[slot]) = n;
   dev::mbarrier_arrive_expect_tx(&s->full[slot], src.first_bytes + src.second_bytes);
   dev::bulk_copy_to_shared(destination, src.first, src.first_bytes, &s->full[slot],
@@ -769,18 +763,14 @@ __device__ const float *wait_unit(const QwenBlock &b, sg::State *state, uint32_t
   return reinterpret_cast<const float *>(s->ring + size_t{slot} * kSlotBytes);
 }
 
-// One lane per consumer warp: the last of `group` warps to finish with unit
-// `n` refills its slot with unit n + kSlots.
-__device__ __forceinline__ void release_unit(const QwenBlock &b, uint32_t n, uint32_t group) {
-  FusedShared *s = block_config.shared;
-  const uint32_t slot = n % kSlots;
-  __threadfence_block();
-  if (atomicAdd(&s->done[slot], 1u) + 1u == group) {
-    s->done[slot] = 0;
-    if (!block_config.stream_empty) {
-      dev::fence_proxy_async_shared();
-      issue_unit(b, n + kSlots);
-    }
+// Lane 0 of the warp that consumed unit `n` (each unit has exactly one
+// consumer warp) refills its slot with unit n + kSlots. The warp's shuffles of
+// the unit's sums have completed every lane's reads of the slot, so the copy
+// may overwrite it: no fence is needed (a CTA fence here waits for the lane's
+// earlier global stores, about a microsecond while the weight stream runs).
+__device__ __forceinline__ void release_unit(const QwenBlock &b, uint32_t n) {
+  if (!block_config.stream_empty) {
+    issue_unit(b, n + kSlots);
   }
 }
 
@@ -928,7 +918,7 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
     // The shuffles complete every lane's shared-memory reads of the slot.
     const float value = reduce_rows8(a, lane);
     if (lane == 0) {
-      release_unit(b, n, 1);
+      release_unit(b, n);
     }
     epilogue(u, row, value, rows, extra);
     if (lane == 0 && block_config.unit_trace != nullptr) {
@@ -1073,7 +1063,7 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
     if (lane == 0) {
       c->projected[u] = sum;
       c->hidden[u] = residual + sum;
-      release_unit(b, n, 1);
+      release_unit(b, n);
       if (block_config.unit_trace != nullptr) {
         trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
       }
@@ -1748,7 +1738,6 @@ template <bool kStageProfile> struct QwenWorkloadT {
     }
     if (threadIdx.x < kSlots) {
       s->sequence[threadIdx.x] = UINT32_MAX;
-      s->done[threadIdx.x] = 0;
       s->unit_tag[threadIdx.x] = 0;
     }
     if (threadIdx.x == 0) {
@@ -1767,10 +1756,8 @@ template <bool kStageProfile> struct QwenWorkloadT {
     }
     __syncthreads();
     if (threadIdx.x == 0 && !block_config.stream_empty) {
-      StreamCursor c = stream_unit(block_config.map, 0);
       for (uint32_t n = 0; n < kSlots; ++n) {
-        slot_cursor[n] = c;
-        advance_cursor(block_config.ranges, block_config.layers, c);
+        slot_position[n] = stream_position(block_config.map, n);
       }
       for (uint32_t n = 0; n < kSlots; ++n) {
         issue_unit(b, n);

@@ -2,7 +2,8 @@
 // (include/lrrt/qwen/resident_schedule.hpp): every unit of every matrix has
 // exactly one owner, gate/up balancing keeps per-block layer bytes close to the
 // mean, even_owner inverts even_range, and the producer's cyclic stream visits
-// exactly the units the compiled stages consume, in the same order.
+// exactly the units the compiled stages consume, in the same order (also when
+// each ring slot advances its own stream position by the ring depth).
 #include "lrrt/qwen/resident_schedule.hpp"
 
 #include <algorithm>
@@ -112,15 +113,25 @@ int main() {
             }
             r::StreamCursor c = r::start_cursor(ranges, layers, program, 0);
             const r::StreamMap map = r::make_stream_map(ranges, layers, program, 0);
+            // Ring slots advance their position by the ring depth.
+            const uint32_t depth = 7;
+            std::vector<r::StreamPosition> slots;
+            for (uint32_t k = 0; k < depth; ++k) {
+              slots.push_back(r::stream_position(map, k));
+            }
             for (size_t i = 0; i < want.size(); ++i) {
               const uint32_t got = r::make_tag(c.kind, c.layer, c.unit);
               const r::StreamCursor random = r::stream_unit(map, static_cast<uint32_t>(i));
+              r::StreamPosition &slot = slots[i % depth];
+              const r::StreamCursor ring = r::position_cursor(map, slot);
               if (got != want[i] ||
-                  r::make_tag(random.kind, random.layer, random.unit) != want[i]) {
+                  r::make_tag(random.kind, random.layer, random.unit) != want[i] ||
+                  r::make_tag(ring.kind, ring.layer, ring.unit) != want[i]) {
                 expect(false, "stream order", workers, w, static_cast<uint32_t>(i));
                 break;
               }
               r::advance_cursor(ranges, layers, c);
+              r::advance_position(map, slot, depth);
             }
           }
         }
