@@ -31,6 +31,7 @@ struct FusedShared {
   uint64_t full[kSlots];       // one mbarrier per ring slot (bytes landed)
   uint32_t sequence[kSlots];   // stream sequence number of the unit in each slot
   uint32_t unit_tag[kSlots];   // (kind, layer, unit) of that unit
+  uint32_t pair_done[kSlots];  // warps done with a unit shared by four warps (mod 4)
   uint32_t flag;
   uint32_t broadcast;
 };

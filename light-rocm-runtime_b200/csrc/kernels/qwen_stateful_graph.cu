@@ -569,6 +569,22 @@ struct QwenConfig {
 };
 __shared__ QwenConfig block_config;
 
+// Shared-memory copies of layer Contexts, double-buffered by step parity:
+// layer_cache[s & 1] holds contexts[s % layers] while step s runs. Program 1
+// of step s fetches step s + 1's Context (the next Program always runs at
+// that step), so no stage chases a Context pointer through global memory.
+__shared__ __align__(16) qd::Context layer_cache[2];
+
+__device__ __forceinline__ void fetch_layer_context(uint32_t step) {
+  constexpr uint32_t kWords = sizeof(qd::Context) / sizeof(uint4);
+  static_assert(sizeof(qd::Context) % sizeof(uint4) == 0);
+  if (threadIdx.x < kWords) {
+    const uint4 *source =
+        reinterpret_cast<const uint4 *>(block_config.contexts + step % block_config.layers);
+    reinterpret_cast<uint4 *>(&layer_cache[step & 1u])[threadIdx.x] = __ldg(source + threadIdx.x);
+  }
+}
+
 // Per-thread scheduler state of the Qwen workload (identical in every thread
 // of a block).
 struct QwenBlock {
@@ -791,8 +807,10 @@ __device__ void fused_rmsnorm(QwenBlock &b, qd::Context *c, const float *weight,
     __syncthreads();
   }
   float4 h = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
   if (threadIdx.x < kVectors) {
     h = dev::load_cg4(c->hidden + 4u * threadIdx.x);
+    w = __ldg(reinterpret_cast<const float4 *>(weight) + threadIdx.x); // in flight with h
   }
   float sum = fmaf(h.x, h.x, fmaf(h.y, h.y, fmaf(h.z, h.z, h.w * h.w)));
   sum = warp_sum(sum);
@@ -808,7 +826,6 @@ __device__ void fused_rmsnorm(QwenBlock &b, qd::Context *c, const float *weight,
   const float inverse_rms =
       1.0f / sqrtf(total / static_cast<float>(qd::kHiddenSize) + epsilon);
   if (threadIdx.x < kVectors) {
-    const float4 w = __ldg(reinterpret_cast<const float4 *>(weight) + threadIdx.x);
     const float4 x = make_float4(h.x * inverse_rms * w.x, h.y * inverse_rms * w.y,
                                  h.z * inverse_rms * w.z, h.w * inverse_rms * w.w);
     reinterpret_cast<float4 *>(s->input)[threadIdx.x] = x;
@@ -855,17 +872,41 @@ __device__ __forceinline__ float reduce_rows8(const float (&a)[8], uint32_t lane
   return v;
 }
 
-// Consumes this block's units of an 8-row kind, one whole unit per warp:
-// warp w takes units w, w + kWarps, ... Each lane accumulates its float4
-// columns of all eight rows (eight independent FMA chains against the
-// register-held input), reduce_rows8 leaves row r's dot product in lanes
-// 4r..4r+3, and every lane runs `epilogue(unit, row, value, rows, extra)`
-// with row = (lane >> 2) & 7; lanes with (lane & 3) == 0 own the row's
-// outputs. `operands(unit, row)` is loaded before the wait so its latency
-// overlaps it.
+// Dot product of a 896-float shared-memory row with the register-held input;
+// every lane receives the total.
+__device__ __forceinline__ float row_dot(const float *row, const float4 (&x)[7],
+                                         uint32_t lane) {
+  const float4 *r = reinterpret_cast<const float4 *>(row);
+  float a = 0.0f;
+#pragma unroll
+  for (uint32_t j = 0; j < 7; ++j) {
+    const float4 w = r[lane + 32u * j];
+    a = fmaf(w.x, x[j].x, a);
+    a = fmaf(w.y, x[j].y, a);
+    a = fmaf(w.z, x[j].z, a);
+    a = fmaf(w.w, x[j].w, a);
+  }
+  return warp_all_sum(a);
+}
+
+// Consumes this block's units of an 8-row kind. Row r of a unit ends up in
+// lanes 4r..4r+3 of the warp that computed it, and every lane of that warp
+// runs `epilogue(unit, r, value, valid, extra)` with r = (lane >> 2) & 7;
+// `valid` says the lane holds row r's dot product (the LM head's last unit
+// is short, and a split unit gives each warp two rows), and lanes with
+// (lane & 3) == 0 own the row's outputs. `operands(unit, r)` is loaded before
+// the wait so its latency overlaps it.
+//  - Many units: one whole unit per warp (warp w takes units w, w + kWarps,
+//    ...); each lane accumulates its float4 columns of all eight rows
+//    (eight independent FMA chains) and reduce_rows8 sums them.
+//  - At most kWarps / 4 units (QKV, o_proj): four warps share a unit, warp g
+//    computing the row pair (g, g + 4), so a lone unit takes a quarter of
+//    the time.
 struct NoOperands {
   __device__ float4 operator()(uint32_t, uint32_t) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
 };
+
+constexpr uint32_t kPairWarps = 4; // warps sharing a split unit
 
 template <typename Epilogue, typename Operands = NoOperands>
 __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
@@ -882,8 +923,11 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
   }
   const UnitRange range = block_config.ranges.of[kind];
   const uint32_t units = range.end - range.begin;
+  const bool split = units * kPairWarps <= kWarps;
+  const uint32_t first_unit = split ? warp / kPairWarps : warp;
+  const uint32_t stride = split ? kWarps / kPairWarps : kWarps;
   bool ok = true;
-  for (uint32_t i = warp; i < units; i += kWarps) {
+  for (uint32_t i = first_unit; i < units; i += stride) {
     const uint32_t n = b.consumed + i;
     const uint32_t u = range.begin + i;
     const float4 extra = (lane & 3u) == 0u ? operands(u, row) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -896,31 +940,47 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
     }
     const uint32_t rows =
         kind == kLmHead ? min(kSlotRows, block_config.vocab - u * kSlotRows) : kSlotRows;
-    // Rows past `rows` (the LM head's last unit) hold stale bytes; their sums
-    // stay in their own lanes and are ignored by the epilogue.
-    const float4 *w = reinterpret_cast<const float4 *>(slot);
-    float a[8];
-#pragma unroll
-    for (uint32_t r = 0; r < 8; ++r) {
-      a[r] = 0.0f;
-    }
-#pragma unroll
-    for (uint32_t j = 0; j < 7; ++j) {
+    float value;
+    bool valid;
+    if (split) {
+      // Rows past `rows` are never split (only full 8-row kinds get here).
+      const uint32_t pair = warp % kPairWarps;
+      const float a = row_dot(slot + pair * qd::kHiddenSize, x, lane);
+      const float c = row_dot(slot + (pair + 4u) * qd::kHiddenSize, x, lane);
+      valid = row == pair || row == pair + 4u;
+      value = row == pair ? a : c;
+      if (lane == 0 && (atomicAdd(&block_config.shared->pair_done[n % kSlots], 1u) &
+                        (kPairWarps - 1u)) == kPairWarps - 1u) {
+        release_unit(b, n); // the unit's last warp refills the slot
+      }
+    } else {
+      // Rows past `rows` (the LM head's last unit) hold stale bytes; their
+      // sums stay in their own lanes and are flagged invalid.
+      const float4 *w = reinterpret_cast<const float4 *>(slot);
+      float a[8];
 #pragma unroll
       for (uint32_t r = 0; r < 8; ++r) {
-        const float4 v = w[r * (qd::kHiddenSize / 4u) + lane + 32u * j];
-        a[r] = fmaf(v.x, x[j].x, a[r]);
-        a[r] = fmaf(v.y, x[j].y, a[r]);
-        a[r] = fmaf(v.z, x[j].z, a[r]);
-        a[r] = fmaf(v.w, x[j].w, a[r]);
+        a[r] = 0.0f;
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < 7; ++j) {
+#pragma unroll
+        for (uint32_t r = 0; r < 8; ++r) {
+          const float4 v = w[r * (qd::kHiddenSize / 4u) + lane + 32u * j];
+          a[r] = fmaf(v.x, x[j].x, a[r]);
+          a[r] = fmaf(v.y, x[j].y, a[r]);
+          a[r] = fmaf(v.z, x[j].z, a[r]);
+          a[r] = fmaf(v.w, x[j].w, a[r]);
+        }
+      }
+      // The shuffles complete every lane's shared-memory reads of the slot.
+      value = reduce_rows8(a, lane);
+      valid = row < rows;
+      if (lane == 0) {
+        release_unit(b, n);
       }
     }
-    // The shuffles complete every lane's shared-memory reads of the slot.
-    const float value = reduce_rows8(a, lane);
-    if (lane == 0) {
-      release_unit(b, n);
-    }
-    epilogue(u, row, value, rows, extra);
+    epilogue(u, row, value, valid, extra);
     if (lane == 0 && block_config.unit_trace != nullptr) {
       trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
     }
@@ -956,11 +1016,12 @@ __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32
   const size_t cache_row = size_t{position} * qd::kKvSize;
   consume_units(
       b, state, kQkv, layer,
-      [&](uint32_t u, uint32_t row, float value, uint32_t, float4 operand) {
+      [&](uint32_t u, uint32_t row, float value, bool valid, float4 operand) {
         // Rows 0-3 of a unit are f..f+3 of one head, rows 4-7 their rotary
-        // partners f+32..f+35: lane 4r (r < 4) rotates the pair (r, r + 4).
+        // partners f+32..f+35: lane 4r (r < 4) rotates the pair (r, r + 4)
+        // (a warp holding row r also holds its partner).
         const float partner = __shfl_xor_sync(kFullMask, value, 16);
-        if (row >= 4u || (threadIdx.x & 3u) != 0u) {
+        if (row >= 4u || !valid || (threadIdx.x & 3u) != 0u) {
           return;
         }
         const QkvRows r = qkv_rows(u, row);
@@ -1007,8 +1068,8 @@ __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32
   }
   consume_units(
       b, state, kOut, layer,
-      [&](uint32_t u, uint32_t row, float value, uint32_t, float4 residual) {
-        if ((threadIdx.x & 3u) == 0u) {
+      [&](uint32_t u, uint32_t row, float value, bool valid, float4 residual) {
+        if (valid && (threadIdx.x & 3u) == 0u) {
           c->hidden[u * kSlotRows + row] = residual.x + value;
         }
       },
@@ -1021,54 +1082,98 @@ __device__ void fused_gate_up(QwenBlock &b, sg::State *state, qd::Context *c,
                               uint32_t layer) {
   // Rows 0-3 of a unit are gate rows 4u..4u+3, rows 4-7 the matching up rows.
   consume_units(b, state, kGateUp, layer,
-                [&](uint32_t u, uint32_t row, float value, uint32_t, float4) {
+                [&](uint32_t u, uint32_t row, float value, bool valid, float4) {
                   const float up = __shfl_xor_sync(kFullMask, value, 16);
-                  if (row < 4u && (threadIdx.x & 3u) == 0u) {
+                  if (row < 4u && valid && (threadIdx.x & 3u) == 0u) {
                     c->activated[u * kGuRowsPerUnit + row] = silu_times(value, up);
                   }
                 });
 }
 
-// Down projection: one 4864-float row per unit, one warp per unit.
+// Down projection: one 4864-float row per unit, every row computed by all
+// warps together. Warp w owns the float4 columns lane + 32k for k = w, w + 8,
+// ... (five or four per lane), loads that slice of the activated vector
+// straight into registers, and for a batch of up to kSlots rows reduces its
+// partial dot products with reduce_rows8; after a block sync threads 0..rows-1
+// add the eight warps' partials in warp order, write the row and refill its
+// slot.
 __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
-  fused_load_input(b, c->activated, qd::kIntermediateSize);
+  constexpr uint32_t kChunks = qd::kIntermediateSize / 4u / 32u; // 38 float4 per lane
+  constexpr uint32_t kMine = (kChunks + kWarps - 1u) / kWarps;    // 5
+  static_assert(kSlots < 8, "a batch of rows must fit reduce_rows8");
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
-  constexpr uint32_t kVectors = qd::kIntermediateSize / 4u / 32u; // 38 per lane
-  const float4 *x = reinterpret_cast<const float4 *>(block_config.shared->input);
+  const uint32_t row = (lane >> 2u) & 7u;
+  float4 x[kMine];
+#pragma unroll
+  for (uint32_t m = 0; m < kMine; ++m) {
+    const uint32_t k = warp + kWarps * m;
+    x[m] = k < kChunks ? dev::load_cg4(c->activated + 4u * (lane + 32u * k))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float *partial = block_config.shared->reduce; // [kWarps][kSlots]
   const UnitRange range = block_config.ranges.of[kDown];
   const uint32_t units = range.end - range.begin;
-  for (uint32_t i = warp; i < units; i += kWarps) {
-    const uint32_t n = b.consumed + i;
-    const uint32_t u = range.begin + i;
-    const float residual = lane == 0 ? dev::load_cg(c->hidden + u) : 0.0f;
-    const uint64_t t_before = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
-    const float *slot = wait_unit(b, state, n, make_tag(kDown, layer, u));
-    const uint64_t t_ready = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
-    if (slot == nullptr) {
-      break;
+  for (uint32_t batch = 0; batch < units; batch += kSlots) {
+    const uint32_t count = min(kSlots, units - batch);
+    const uint32_t mine = batch + threadIdx.x; // the row thread threadIdx.x finishes
+    const float residual = threadIdx.x < count ? dev::load_cg(c->hidden + range.begin + mine)
+                                               : 0.0f;
+    float a[8];
+#pragma unroll
+    for (uint32_t r = 0; r < 8; ++r) {
+      a[r] = 0.0f;
     }
-    const float4 *row = reinterpret_cast<const float4 *>(slot);
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 19
-    for (uint32_t j = 0; j < kVectors; ++j) {
-      const float4 w = row[lane + 32u * j];
-      const float4 v = x[lane + 32u * j];
-      a0 = fmaf(w.x, v.x, a0);
-      a1 = fmaf(w.y, v.y, a1);
-      a2 = fmaf(w.z, v.z, a2);
-      a3 = fmaf(w.w, v.w, a3);
-    }
-    const float sum = warp_sum((a0 + a1) + (a2 + a3));
-    if (lane == 0) {
-      c->projected[u] = sum;
-      c->hidden[u] = residual + sum;
-      release_unit(b, n);
-      if (block_config.unit_trace != nullptr) {
-        trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
+    bool ok = true;
+#pragma unroll
+    for (uint32_t r = 0; r < kSlots; ++r) {
+      if (r < count && ok) {
+        const uint32_t n = b.consumed + batch + r;
+        const uint64_t t_before = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
+        const float *slot =
+            wait_unit(b, state, n, make_tag(kDown, layer, range.begin + batch + r));
+        if (slot == nullptr) {
+          ok = false; // warp-uniform; the block agrees below
+          continue;
+        }
+        if (lane == 0 && warp == 0 && block_config.unit_trace != nullptr) {
+          trace_unit(b, n, t_before, dev::global_timer_ns(), dev::global_timer_ns());
+        }
+        const float4 *w = reinterpret_cast<const float4 *>(slot);
+#pragma unroll
+        for (uint32_t m = 0; m < kMine; ++m) {
+          const uint32_t k = warp + kWarps * m;
+          if (k < kChunks) {
+            const float4 v = w[lane + 32u * k];
+            a[r] = fmaf(v.x, x[m].x, a[r]);
+            a[r] = fmaf(v.y, x[m].y, a[r]);
+            a[r] = fmaf(v.z, x[m].z, a[r]);
+            a[r] = fmaf(v.w, x[m].w, a[r]);
+          }
+        }
       }
     }
-    __syncwarp();
+    const float value = reduce_rows8(a, lane);
+    if ((lane & 3u) == 0u && row < count) {
+      partial[warp * kSlots + row] = value;
+    }
+    // Every warp is done with the batch's slots; a failed wait in any warp
+    // (the run already carries the error) ends the stage for the whole block.
+    if (__syncthreads_or(ok ? 0 : 1) != 0) {
+      break;
+    }
+    if (threadIdx.x < count) {
+      float sum = 0.0f;
+#pragma unroll
+      for (uint32_t w = 0; w < kWarps; ++w) {
+        sum += partial[w * kSlots + threadIdx.x];
+      }
+      const uint32_t u = range.begin + mine;
+      c->projected[u] = sum;
+      c->hidden[u] = residual + sum;
+      release_unit(b, b.consumed + mine);
+    }
+    __syncthreads(); // partials are rewritten by the next batch
   }
   b.consumed += units;
 }
@@ -1417,9 +1522,10 @@ __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &s
   };
   consume_units(
       b, state, kLmHead, 0,
-      [&](uint32_t u, uint32_t row, float value, uint32_t rows, float4) {
+      [&](uint32_t u, uint32_t row, float value, bool valid, float4) {
         const uint32_t lane = threadIdx.x & 31u;
         const uint32_t first = u * kSlotRows;
+        const uint32_t rows = min(kSlotRows, block_config.vocab - first);
         uint32_t task_end = 0;
         if (lane == 0) {
           while (first >= task_ends[task]) {
@@ -1431,8 +1537,8 @@ __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &s
         if (first + rows <= task_end) {
           // The whole unit lies in one task: warp top-1 (ties to the lower
           // row), then one offer.
-          float best = row < rows ? value : -INFINITY;
-          uint32_t index = row < rows ? first + row : UINT32_MAX;
+          float best = valid ? value : -INFINITY;
+          uint32_t index = valid ? first + row : UINT32_MAX;
 #pragma unroll
           for (uint32_t offset = 4; offset < 32; offset *= 2) {
             const float other = __shfl_xor_sync(kFullMask, best, offset);
@@ -1736,7 +1842,9 @@ template <bool kStageProfile> struct QwenWorkloadT {
                                                layer.down_weight};
       s->layer_weights[i / kLayerMatrices][i % kLayerMatrices] = pointers[i % kLayerMatrices];
     }
+    fetch_layer_context(dev::load_relaxed(&args.state->step));
     if (threadIdx.x < kSlots) {
+      s->pair_done[threadIdx.x] = 0;
       s->sequence[threadIdx.x] = UINT32_MAX;
       s->unit_tag[threadIdx.x] = 0;
     }
@@ -1793,6 +1901,9 @@ template <bool kStageProfile> struct QwenWorkloadT {
                              block_config.base_token;
       b.position = block_config.base_position + static_cast<uint32_t>(tokens);
       b.kv_length = block_config.base_kv_length + static_cast<uint32_t>(tokens);
+      if (program == 1) {
+        fetch_layer_context(step + 1u); // read after this Program's block syncs
+      }
     }
   }
   __device__ static void stage_begin(QwenBlock &b, uint32_t stage) { b.stage = stage; }
@@ -1836,7 +1947,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
       return;
     }
     const uint32_t layer = b.step % block_config.layers;
-    qd::Context *c = static_cast<qd::Context *>(opaque) + layer;
+    qd::Context *c = &layer_cache[b.step & 1u];
     switch (fused_opcode(b.program, b.stage)) {
     case qd::Opcode::attention_rmsnorm_f32:
       fused_rmsnorm(b, c, c->attention_norm_weight, block_config.epsilon[0],
