@@ -234,6 +234,39 @@ LRRT_API lr_status_t lrq_model_set_trace(lrq_model_t *model, uint32_t entries);
 LRRT_API lr_status_t lrq_model_read_trace(lrq_model_t *model, uint64_t *entries,
                                           uint32_t capacity);
 
+/*
+ * Greedy LM-head top-1 that allocates no device memory. No counterpart in the
+ * reference: it is a variant of the LM-head partition + reduce tasks whose
+ * per-block candidates live in a file-scope static device array of
+ * LRQ_STATIC_TOP1_MAX_BLOCKS entries (8 KB) instead of partial buffers the
+ * caller allocates. It serves callers whose device memory belongs to another
+ * allocator (a serving stack that reserves HBM up front) and callers that
+ * cannot take cudaMalloc/cudaFree's implicit device-wide synchronisation on
+ * the decode path.
+ *
+ * token = argmax over rows r < `rows` of lm_head[r] . hidden (row-major
+ * [rows][columns], device pointers), ties to the lower row; logit = that dot
+ * product. Rows use the partitioned path's dot-product order, so both match
+ * it exactly.
+ *  - `blocks` is the grid size (0 = 2 x SMs); more than
+ *    LRQ_STATIC_TOP1_MAX_BLOCKS returns LR_ERROR_INVALID_ARGUMENT.
+ *  - Runs on `queue` (NULL = the device's default queue), waits for it and
+ *    writes token and logit to host memory.
+ *  - The first call on a device looks up the scratch address
+ *    (cudaGetSymbolAddress) and the SM count; make that first call before any
+ *    stream capture begins on the device.
+ *  - The scratch's arrival counter must be zero when a launch starts; every
+ *    call clears it on `queue` before launching.
+ *  - All calls on a device share the one scratch: calls that overlap in time
+ *    (other threads, other queues) race, and the caller must serialise them.
+ */
+#define LRQ_STATIC_TOP1_MAX_BLOCKS 1024u
+LRRT_API lr_status_t lrq_lm_head_top1_static(lr_device_t device, lr_queue_t *queue,
+                                             const float *lm_head, const float *hidden,
+                                             uint32_t rows, uint32_t columns,
+                                             uint32_t blocks, uint32_t *token,
+                                             float *logit);
+
 LRRT_API const char *lrq_last_error(void);
 
 #ifdef __cplusplus

@@ -65,10 +65,19 @@ def build(verbose: bool = False) -> dict[str, Path]:
 
     driver = LIB / "liblrrt_qwen.so"
     driver_sources = sorted((csrc / "qwen").glob("*.cpp"))
-    if _stale(driver, driver_sources + headers + [runtime]):
+    # CUDA runtime code of the driver (the static-scratch LM-head top-1),
+    # compiled to an object and linked with the static CUDA runtime.
+    static_top1 = csrc / "qwen" / "lm_head_top1_static.cu"
+    static_top1_object = BUILD / "lm_head_top1_static.o"
+    static_inputs = [static_top1, csrc / "qwen" / "lm_head_top1_static.hpp"] + headers
+    if _stale(static_top1_object, static_inputs):
+        _run([NVCC, *NVCCFLAGS, "-c", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+              str(static_top1), "-o", str(static_top1_object)], verbose)
+    if _stale(driver, driver_sources + static_inputs + [static_top1_object, runtime]):
         _run([CXX, *CXXFLAGS, "-shared", "-fvisibility=hidden",
-              *map(str, driver_sources), "-o", str(driver), f"-L{LIB}", "-llrrt",
-              "-Wl,-rpath,$ORIGIN"], verbose)
+              *map(str, driver_sources), str(static_top1_object), "-o", str(driver),
+              f"-L{LIB}", "-llrrt", f"-L{CUDA_HOME / 'lib64'}", "-lcudart_static",
+              "-lrt", "-ldl", "-lpthread", "-Wl,-rpath,$ORIGIN"], verbose)
     outputs["driver"] = driver
 
     for name in ("qwen_stateful_graph", "stateful_graph_fixture"):

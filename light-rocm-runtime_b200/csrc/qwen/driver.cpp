@@ -5,6 +5,8 @@
 // lr_* runtime, following light-rocm-runtime benchmarks/qwen_stateful_graph.cpp.
 #include "lrrt_qwen.h"
 
+#include "lm_head_top1_static.hpp"
+
 #include "lrrt/lrrt.hpp"
 #include "lrrt/persistent_graph.hpp"
 #include "lrrt/qwen/resident_layout.hpp"
@@ -1113,6 +1115,26 @@ LRRT_API lr_status_t lrq_model_read_trace(lrq_model_t *model, uint64_t *entries,
     }
     lrrt::copy_to_host(entries, *model->trace, size_t{capacity} * sizeof(qd::StageProfileEntry));
   });
+}
+
+LRRT_API lr_status_t lrq_lm_head_top1_static(lr_device_t device, lr_queue_t *queue,
+                                             const float *lm_head, const float *hidden,
+                                             uint32_t rows, uint32_t columns,
+                                             uint32_t blocks, uint32_t *token,
+                                             float *logit) {
+  void *stream = nullptr;
+  lr_status_t status = lr_queue_native_handle(device, queue, &stream);
+  if (status != LR_SUCCESS) {
+    set_error("lrq_lm_head_top1_static: lr_queue_native_handle failed");
+    return status;
+  }
+  std::string error;
+  status = lrq_static::lm_head_top1(device.index, stream, lm_head, hidden, rows, columns,
+                                    blocks, token, logit, error);
+  if (status != LR_SUCCESS) {
+    set_error("lrq_lm_head_top1_static: " + error);
+  }
+  return status;
 }
 
 LRRT_API const char *lrq_last_error(void) {
