@@ -90,6 +90,16 @@ def build(verbose: bool = False) -> dict[str, Path]:
     tests_dir = REPO / "tests" / "cpp"
     test_build = BUILD / "tests"
     test_build.mkdir(exist_ok=True)
+    # Test bundle for lrrt::Bundle: manifest + sm_100a cubin side by side.
+    bundle_dir = test_build / "bundle"
+    bundle_dir.mkdir(exist_ok=True)
+    bundle_cubin = bundle_dir / "bundle_kernels.cubin"
+    if _stale(bundle_cubin, [tests_dir / "bundle_kernels.cu"]):
+        _run([NVCC, *NVCCFLAGS, "-cubin", str(tests_dir / "bundle_kernels.cu"), "-o",
+              str(bundle_cubin)], verbose)
+    bundle_manifest = bundle_dir / "manifest.json"
+    shutil.copyfile(tests_dir / "bundle_manifest.json", bundle_manifest)
+    outputs["bundle_manifest"] = bundle_manifest
     for source in sorted(tests_dir.glob("*.cpp")):
         binary = test_build / source.stem
         if _stale(binary, [source] + headers + [runtime]):

@@ -97,3 +97,12 @@ def test_cpp_resident_schedule_checks(built):
     result = subprocess.run([str(binary)], capture_output=True, text=True, timeout=300)
     assert result.returncode == 0, result.stderr
     assert "ok" in result.stdout
+
+
+def test_cpp_bundle_checks(built):
+    """lrrt::bundle manifest parsing, launch configuration and kernarg packing
+    with the reference's error texts (no device needed)."""
+    binary = built["test:bundle_test"]
+    result = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
+    assert result.returncode == 0, result.stderr
+    assert "bundle checks: ok" in result.stdout
