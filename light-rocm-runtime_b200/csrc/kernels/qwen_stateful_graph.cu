@@ -585,6 +585,27 @@ __device__ __forceinline__ void fetch_layer_context(uint32_t step) {
   }
 }
 
+// The same copy without stalling the issuing threads (cp.async); it must be
+// completed with cp.async.wait_all by those threads before a block sync that
+// precedes the first read.
+__device__ __forceinline__ void prefetch_layer_context(uint32_t step) {
+  constexpr uint32_t kWords = sizeof(qd::Context) / sizeof(uint4);
+  if (threadIdx.x < kWords) {
+    const uint4 *source =
+        reinterpret_cast<const uint4 *>(block_config.contexts + step % block_config.layers);
+    const uint32_t destination =
+        dev::shared_address(reinterpret_cast<uint4 *>(&layer_cache[step & 1u]) + threadIdx.x);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n"
+                 "cp.async.commit_group;" ::"r"(destination),
+                 "l"(source + threadIdx.x)
+                 : "memory");
+  }
+}
+
+__device__ __forceinline__ void wait_prefetched_context() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // Per-thread scheduler state of the Qwen workload (identical in every thread
 // of a block).
 struct QwenBlock {
@@ -1092,18 +1113,20 @@ __device__ void fused_gate_up(QwenBlock &b, sg::State *state, qd::Context *c,
 
 // Down projection: one 4864-float row per unit, every row computed by all
 // warps together. Warp w owns the float4 columns lane + 32k for k = w, w + 8,
-// ... (five or four per lane), loads that slice of the activated vector
-// straight into registers, and for a batch of up to kSlots rows reduces its
-// partial dot products with reduce_rows8; after a block sync threads 0..rows-1
-// add the eight warps' partials in warp order, write the row and refill its
-// slot.
+// ... (five or four per lane) and loads that slice of the activated vector
+// straight into registers. For a batch of up to kSlots rows, warp r waits for
+// row r (the waits overlap), a block sync publishes the landed rows, every
+// warp accumulates its columns of all rows, reduce_rows8 sums lanes, and
+// threads 0..rows-1 add the eight warps' partials in warp order, write the
+// row and refill its slot.
 __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
   constexpr uint32_t kChunks = qd::kIntermediateSize / 4u / 32u; // 38 float4 per lane
   constexpr uint32_t kMine = (kChunks + kWarps - 1u) / kWarps;    // 5
-  static_assert(kSlots < 8, "a batch of rows must fit reduce_rows8");
+  static_assert(kSlots < 8 && kSlots <= kWarps, "a batch of rows must fit reduce_rows8");
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
   const uint32_t row = (lane >> 2u) & 7u;
+  FusedShared *shared = block_config.shared;
   float4 x[kMine];
 #pragma unroll
   for (uint32_t m = 0; m < kMine; ++m) {
@@ -1111,7 +1134,7 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
     x[m] = k < kChunks ? dev::load_cg4(c->activated + 4u * (lane + 32u * k))
                        : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  float *partial = block_config.shared->reduce; // [kWarps][kSlots]
+  float *partial = shared->reduce; // [kWarps][kSlots]
   const UnitRange range = block_config.ranges.of[kDown];
   const uint32_t units = range.end - range.begin;
   for (uint32_t batch = 0; batch < units; batch += kSlots) {
@@ -1119,27 +1142,36 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
     const uint32_t mine = batch + threadIdx.x; // the row thread threadIdx.x finishes
     const float residual = threadIdx.x < count ? dev::load_cg(c->hidden + range.begin + mine)
                                                : 0.0f;
+    bool ok = true;
+    if (warp < count) {
+      const uint32_t n = b.consumed + batch + warp;
+      const uint64_t t_before = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
+      ok = wait_unit(b, state, n, make_tag(kDown, layer, range.begin + batch + warp)) != nullptr;
+      if (lane == 0 && block_config.unit_trace != nullptr) {
+        trace_unit(b, n, t_before, dev::global_timer_ns(), dev::global_timer_ns());
+      }
+    }
+    // Every row of the batch has landed (its waiting warp checked the tag);
+    // a failed wait in any warp (the run already carries the error) ends the
+    // stage for the whole block.
+    if (__syncthreads_or(ok ? 0 : 1) != 0) {
+      break;
+    }
     float a[8];
 #pragma unroll
     for (uint32_t r = 0; r < 8; ++r) {
       a[r] = 0.0f;
     }
-    bool ok = true;
+    const dev::Deadline deadline(block_config.limit_ms);
 #pragma unroll
     for (uint32_t r = 0; r < kSlots; ++r) {
-      if (r < count && ok) {
+      if (r < count) {
         const uint32_t n = b.consumed + batch + r;
-        const uint64_t t_before = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
-        const float *slot =
-            wait_unit(b, state, n, make_tag(kDown, layer, range.begin + batch + r));
-        if (slot == nullptr) {
-          ok = false; // warp-uniform; the block agrees below
-          continue;
-        }
-        if (lane == 0 && warp == 0 && block_config.unit_trace != nullptr) {
-          trace_unit(b, n, t_before, dev::global_timer_ns(), dev::global_timer_ns());
-        }
-        const float4 *w = reinterpret_cast<const float4 *>(slot);
+        const uint32_t slot = n % kSlots;
+        // Acquire the slot's completed fill in this warp too: another warp saw
+        // it complete, so this returns at once (the deadline only bounds it).
+        dev::mbarrier_wait(&shared->full[slot], (n / kSlots) & 1u, deadline);
+        const float4 *w = reinterpret_cast<const float4 *>(shared->ring + size_t{slot} * kSlotBytes);
 #pragma unroll
         for (uint32_t m = 0; m < kMine; ++m) {
           const uint32_t k = warp + kWarps * m;
@@ -1157,11 +1189,7 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
     if ((lane & 3u) == 0u && row < count) {
       partial[warp * kSlots + row] = value;
     }
-    // Every warp is done with the batch's slots; a failed wait in any warp
-    // (the run already carries the error) ends the stage for the whole block.
-    if (__syncthreads_or(ok ? 0 : 1) != 0) {
-      break;
-    }
+    __syncthreads(); // partials written; every warp is done with the batch's slots
     if (threadIdx.x < count) {
       float sum = 0.0f;
 #pragma unroll
@@ -1878,6 +1906,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
       return;
     }
     // Wait for copies still in flight into this block's ring before exit.
+    wait_prefetched_context();
     __syncthreads();
     if (threadIdx.x == 0) {
       const dev::Deadline deadline(block_config.limit_ms);
@@ -1902,7 +1931,9 @@ template <bool kStageProfile> struct QwenWorkloadT {
       b.position = block_config.base_position + static_cast<uint32_t>(tokens);
       b.kv_length = block_config.base_kv_length + static_cast<uint32_t>(tokens);
       if (program == 1) {
-        fetch_layer_context(step + 1u); // read after this Program's block syncs
+        // Completed in this Program's residual_advance stage, read after the
+        // block syncs of its final barrier.
+        prefetch_layer_context(step + 1u);
       }
     }
   }
@@ -1974,6 +2005,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
       fused_down(b, state, c, layer);
       return;
     case qd::Opcode::residual_advance:
+      wait_prefetched_context(); // the next step's Context (program_begin)
       // The residual was added in the down epilogue; what remains is the
       // branch / predicate bookkeeping, which State carries for the host.
       if (worker == 0 && threadIdx.x == 0) {
