@@ -1117,8 +1117,9 @@ __device__ void fused_gate_up(QwenBlock &b, sg::State *state, qd::Context *c,
 // straight into registers. For a batch of up to kSlots rows, warp r waits for
 // row r (the waits overlap), a block sync publishes the landed rows, every
 // warp accumulates its columns of all rows, reduce_rows8 sums lanes, and
-// threads 0..rows-1 add the eight warps' partials in warp order, write the
-// row and refill its slot.
+// lane 0 of warp r adds the eight warps' partials of row r in warp order,
+// writes the row and refills its slot (one refill per warp, so they run in
+// parallel instead of as divergent lanes of one warp).
 __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
   constexpr uint32_t kChunks = qd::kIntermediateSize / 4u / 32u; // 38 float4 per lane
   constexpr uint32_t kMine = (kChunks + kWarps - 1u) / kWarps;    // 5
@@ -1139,9 +1140,9 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
   const uint32_t units = range.end - range.begin;
   for (uint32_t batch = 0; batch < units; batch += kSlots) {
     const uint32_t count = min(kSlots, units - batch);
-    const uint32_t mine = batch + threadIdx.x; // the row thread threadIdx.x finishes
-    const float residual = threadIdx.x < count ? dev::load_cg(c->hidden + range.begin + mine)
-                                               : 0.0f;
+    const bool finisher = lane == 0 && warp < count; // finishes row `warp` of the batch
+    const uint32_t mine = batch + warp;
+    const float residual = finisher ? dev::load_cg(c->hidden + range.begin + mine) : 0.0f;
     bool ok = true;
     if (warp < count) {
       const uint32_t n = b.consumed + batch + warp;
@@ -1190,11 +1191,11 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
       partial[warp * kSlots + row] = value;
     }
     __syncthreads(); // partials written; every warp is done with the batch's slots
-    if (threadIdx.x < count) {
+    if (finisher) {
       float sum = 0.0f;
 #pragma unroll
       for (uint32_t w = 0; w < kWarps; ++w) {
-        sum += partial[w * kSlots + threadIdx.x];
+        sum += partial[w * kSlots + warp];
       }
       const uint32_t u = range.begin + mine;
       c->projected[u] = sum;
