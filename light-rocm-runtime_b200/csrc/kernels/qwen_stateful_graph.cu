@@ -715,6 +715,15 @@ __device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
 // consumer of the slot's previous unit.
 __shared__ StreamPosition slot_position[kSlots];
 
+// Gate/up refills the down stage postpones: deferred_unit[s] is the sequence
+// number slot s is still to receive (UINT32_MAX: none). Every block releases
+// its down rows at the end of the stage, and issuing all those refills at
+// once puts the whole grid's next-layer gate/up bytes in front of the grid
+// barrier that follows (its release then takes three times as long). Gate/up
+// units are first needed in the next gate/up stage, so they are issued after
+// the next QKV barrier instead (issue_deferred_refills, attention stage).
+__shared__ uint32_t deferred_unit[kSlots];
+
 // Issues the bulk copies of stream unit `n` into its ring slot (one lane).
 // The slot's previous unit (n - kSlots) has been released by its consumers.
 // (An L2 bulk prefetch of units further ahead was measured slower on B200.)
@@ -742,6 +751,16 @@ __device__ void issue_unit(const QwenBlock &b, uint32_t n) {
   if (src.second_bytes != 0) {
     dev::bulk_copy_to_shared(destination + src.first_bytes, src.second, src.second_bytes,
                              &s->full[slot], block_config.policy);
+  }
+}
+
+// Lane 0 of warp s issues slot s's postponed refill, if any.
+__device__ __forceinline__ void issue_deferred_refills(const QwenBlock &b) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = threadIdx.x >> 5u;
+  if (lane == 0 && warp < kSlots && deferred_unit[warp] != UINT32_MAX) {
+    issue_unit(b, deferred_unit[warp]);
+    deferred_unit[warp] = UINT32_MAX;
   }
 }
 
@@ -1200,7 +1219,13 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
       const uint32_t u = range.begin + mine;
       c->projected[u] = sum;
       c->hidden[u] = residual + sum;
-      release_unit(b, b.consumed + mine);
+      const uint32_t n = b.consumed + mine;
+      if (!block_config.stream_empty &&
+          position_cursor(block_config.map, slot_position[n % kSlots]).kind == kGateUp) {
+        deferred_unit[n % kSlots] = n + kSlots; // see issue_deferred_refills
+      } else {
+        release_unit(b, n);
+      }
     }
     __syncthreads(); // partials are rewritten by the next batch
   }
@@ -1500,6 +1525,7 @@ __device__ void local_attention(QwenBlock &b, const qd::Context *c, uint32_t pos
 }
 
 __device__ void fused_attention(QwenBlock &b, qd::Context *c) {
+  issue_deferred_refills(b); // gate/up units the last down stage postponed
   const uint32_t positions = b.kv_length + 1u;
   if (use_local_attention(positions)) {
     return; // computed per block inside the o_proj stage
@@ -1873,6 +1899,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
     }
     fetch_layer_context(dev::load_relaxed(&args.state->step));
     if (threadIdx.x < kSlots) {
+      deferred_unit[threadIdx.x] = UINT32_MAX;
       s->pair_done[threadIdx.x] = 0;
       s->sequence[threadIdx.x] = UINT32_MAX;
       s->unit_tag[threadIdx.x] = 0;
