@@ -133,10 +133,28 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def max_over_ranks(values, dist):
+    """Element-wise maximum of per-rank timings (the job takes as long as its
+    slowest rank). The tensor lives where the process group's backend wants
+    it: on the rank's GPU for NCCL, on the host for gloo."""
+    import torch
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def rank_seeds(rank: int):
+    """(weight seed, prompt seed) of a replica: every rank holds the same
+    model and decodes its own prompt, so the replicas are independent streams."""
+    return SEED, SEED + rank
+
+
 def make_weights(rank: int):
     from lrrt_b200 import synthetic as S
-    weights, tail = S.model(SEED, LAYERS, VOCAB)
-    prompt = S.prompt(SEED + rank, PROMPT, VOCAB)
+    weight_seed, prompt_seed = rank_seeds(rank)
+    weights, tail = S.model(weight_seed, LAYERS, VOCAB)
+    prompt = S.prompt(prompt_seed, PROMPT, VOCAB)
     return weights, tail, prompt
 
 
@@ -267,10 +285,7 @@ def our_arm(args, rank: int, world: int, local_rank: int):
 
     elapsed_s = total_ns / 1e9
     if world > 1:
-        import torch
-        t = torch.tensor([elapsed_s, e2e_seconds], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_s, e2e_seconds = float(t[0]), float(t[1])
+        elapsed_s, e2e_seconds = max_over_ranks([elapsed_s, e2e_seconds], dist)
 
     info = model.info
     weight_bytes = int(info.weight_bytes_per_token)

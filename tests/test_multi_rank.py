@@ -1,0 +1,69 @@
+"""Host logic of bench.py's multi-GPU mode on CPU: two gloo ranks, as
+torchrun would start them (one process per rank, 127.0.0.1 rendezvous).
+Replicas are independent (same weights, own prompt per rank) and the job's
+time is the maximum over ranks. No device is used."""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import torch.multiprocessing as mp
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, results):
+    sys.path.insert(0, str(REPO))
+    sys.path.insert(0, str(REPO / "light-rocm-runtime_b200"))
+    import datetime
+
+    import torch.distributed as dist
+
+    import bench
+    from lrrt_b200 import synthetic as S
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        weight_seed, prompt_seed = bench.rank_seeds(rank)
+        prompt = S.prompt(prompt_seed, bench.PROMPT, bench.VOCAB)
+        # Rank r "took" 1 + r seconds of device time and 10 - r end to end.
+        elapsed, e2e = bench.max_over_ranks([1.0 + rank, 10.0 - rank], dist)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (weight_seed, prompt.tolist()))
+        results[rank] = (elapsed, e2e, gathered)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_reduce_max_and_keep_replicas_independent():
+    world = 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        port = _free_port()
+        processes = [ctx.Process(target=_rank_main, args=(r, world, port, results))
+                     for r in range(world)]
+        for p in processes:
+            p.start()
+        for p in processes:
+            p.join(timeout=120)
+        assert all(p.exitcode == 0 for p in processes), [p.exitcode for p in processes]
+        results = dict(results)
+    for rank in range(world):
+        elapsed, e2e, gathered = results[rank]
+        assert elapsed == 2.0 and e2e == 10.0  # max over ranks, on every rank
+        (seed0, prompt0), (seed1, prompt1) = gathered
+        assert seed0 == seed1                 # one model, replicated
+        assert prompt0 != prompt1             # independent streams
+        assert len(prompt0) == len(prompt1) == 32
