@@ -153,6 +153,15 @@ LRRT_API lr_status_t lrq_model_set_tail(lrq_model_t *model, const float *final_n
                                         const float *lm_head, const float *embeddings);
 /* Writes cache rows [first_position, first_position + positions) of one layer
  * from host arrays [positions][128]. */
+/* Loads one decoder layer / the model tail from the reference's FP32 weight
+ * bundles ("lrrt.mini_decoder_weights" v2, "lrrt.mini_model_tail_weights"
+ * v1; include/lrrt/qwen/weight_bundle.hpp) into the model: the manifests'
+ * shapes and rope_theta must match the model configuration (reference
+ * benchmarks/qwen_stateful_graph.cpp:760-880 reads the same files). */
+LRRT_API lr_status_t lrq_model_load_layer_bundle(lrq_model_t *model, uint32_t layer,
+                                                 const char *manifest_path);
+LRRT_API lr_status_t lrq_model_load_tail_bundle(lrq_model_t *model, const char *manifest_path);
+
 LRRT_API lr_status_t lrq_model_set_kv(lrq_model_t *model, uint32_t layer,
                                       uint32_t first_position, uint32_t positions,
                                       const float *keys, const float *values);

@@ -32,7 +32,8 @@ NVCCFLAGS = ["-std=c++17", "-O3", *ARCH, "-lineinfo", f"-I{INCLUDE}"]
 
 
 def _headers() -> list[Path]:
-    return sorted(INCLUDE.rglob("*.h*")) + sorted(INCLUDE.rglob("*.cuh"))
+    return (sorted(INCLUDE.rglob("*.h*")) + sorted(INCLUDE.rglob("*.cuh")) +
+            sorted((PACKAGE / "csrc" / "common").glob("*.hpp")))
 
 
 def _stale(target: Path, inputs: list[Path]) -> bool:
@@ -102,9 +103,9 @@ def build(verbose: bool = False) -> dict[str, Path]:
     outputs["bundle_manifest"] = bundle_manifest
     for source in sorted(tests_dir.glob("*.cpp")):
         binary = test_build / source.stem
-        if _stale(binary, [source] + headers + [runtime]):
-            _run([CXX, *CXXFLAGS, str(source), "-o", str(binary), f"-L{LIB}", "-llrrt",
-                  "-Wl,-rpath,$ORIGIN/../../lib"], verbose)
+        if _stale(binary, [source] + headers + [runtime, driver]):
+            _run([CXX, *CXXFLAGS, str(source), "-o", str(binary), f"-L{LIB}", "-llrrt_qwen",
+                  "-llrrt", "-Wl,-rpath,$ORIGIN/../../lib"], verbose)
         outputs[f"test:{source.stem}"] = binary
     return outputs
 

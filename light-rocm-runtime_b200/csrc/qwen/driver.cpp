@@ -6,6 +6,7 @@
 #include "lrrt_qwen.h"
 
 #include "lm_head_top1_static.hpp"
+#include "lrrt/qwen/weight_bundle.hpp"
 
 #include "lrrt/lrrt.hpp"
 #include "lrrt/persistent_graph.hpp"
@@ -842,6 +843,68 @@ LRRT_API lr_status_t lrq_model_set_tail(lrq_model_t *model, const float *final_n
       }
       lrrt::copy_to_device(*model->lm_head, lm_head, table);
       lrrt::copy_to_device(*model->embeddings, embeddings, table);
+    }
+  });
+}
+
+LRRT_API lr_status_t lrq_model_load_layer_bundle(lrq_model_t *model, uint32_t layer,
+                                                 const char *manifest_path) {
+  return guarded("lrq_model_load_layer_bundle", [&] {
+    if (model == nullptr || layer >= model->config.layer_count) {
+      throw std::invalid_argument("invalid layer");
+    }
+    namespace wb = lrrt::executor::qwen;
+    const wb::DecoderLayerWeights w = wb::load_decoder_layer_weights(manifest_path);
+    if (w.shape.hidden != qd::kHiddenSize || w.shape.heads != qd::kAttentionHeads ||
+        w.shape.kv_heads != qd::kKvHeads || w.shape.head_dim != qd::kHeadSize ||
+        w.shape.intermediate != qd::kIntermediateSize) {
+      throw std::invalid_argument(
+          "weight bundle shape does not match the model (hidden 896, 14/2 heads of 64, "
+          "intermediate 4864)");
+    }
+    if (w.rope_theta != model->config.rope_theta) {
+      throw std::invalid_argument("weight bundle rope_theta differs from the model's");
+    }
+    const lrq_layer_weights_t upload{
+        w.attention_norm_weight.data(), w.q_weight.data(), w.k_weight.data(),
+        w.v_weight.data(), w.q_bias.data(), w.k_bias.data(), w.v_bias.data(),
+        w.out_weight.data(), w.mlp_norm_weight.data(), w.gate_weight.data(),
+        w.up_weight.data(), w.down_weight.data()};
+    const lr_status_t status = lrq_model_set_layer(model, layer, &upload);
+    if (status != LR_SUCCESS) {
+      throw lrrt::Error(status, "lrq_model_set_layer");
+    }
+  });
+}
+
+LRRT_API lr_status_t lrq_model_load_tail_bundle(lrq_model_t *model, const char *manifest_path) {
+  return guarded("lrq_model_load_tail_bundle", [&] {
+    if (model == nullptr) {
+      throw std::invalid_argument("null model");
+    }
+    namespace wb = lrrt::executor::qwen;
+    const wb::ModelTailWeights w = wb::load_model_tail_weights(manifest_path);
+    if (w.hidden != qd::kHiddenSize || w.vocab != model->config.vocab_size) {
+      throw std::invalid_argument("tail bundle hidden size or vocabulary does not match the model");
+    }
+    // An untied model needs an embedding row for every token the decode can
+    // produce: the bundle's token_ids must then be 0..vocab-1 in order.
+    const float *embeddings = nullptr;
+    if (model->config.tied_embeddings == 0) {
+      bool complete = w.token_ids.size() == w.vocab;
+      for (uint32_t i = 0; complete && i < w.vocab; ++i) {
+        complete = w.token_ids[i] == i;
+      }
+      if (!complete) {
+        throw std::invalid_argument(
+            "untied model: the tail bundle must hold embeddings of token ids 0..vocab-1");
+      }
+      embeddings = w.token_embeddings.data();
+    }
+    const lr_status_t status = lrq_model_set_tail(model, w.final_norm_weight.data(),
+                                                  w.lm_head_weight.data(), embeddings);
+    if (status != LR_SUCCESS) {
+      throw lrrt::Error(status, "lrq_model_set_tail");
     }
   });
 }

@@ -170,6 +170,8 @@ DRIVER_FUNCTIONS = {
     "lrq_model_destroy": (u32, [vp]),
     "lrq_model_set_layer": (u32, [vp, u32, P(LayerWeights)]),
     "lrq_model_set_tail": (u32, [vp, vp, vp, vp]),
+    "lrq_model_load_layer_bundle": (u32, [vp, u32, cp]),
+    "lrq_model_load_tail_bundle": (u32, [vp, cp]),
     "lrq_model_set_kv": (u32, [vp, u32, u32, u32, vp, vp]),
     "lrq_model_replicate_layer": (u32, [vp, u32]),
     "lrq_model_set_hidden": (u32, [vp, vp]),

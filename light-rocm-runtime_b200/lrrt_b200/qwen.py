@@ -170,6 +170,19 @@ class Model:
         N.check(N.driver().lrq_model_replicate_layer(self.handle, source),
                 "lrq_model_replicate_layer")
 
+    def load_layer_bundle(self, layer: int, manifest: str) -> None:
+        """Uploads decoder layer `layer` from an FP32 weight bundle
+        ("lrrt.mini_decoder_weights" v2, see lrrt_b200.weight_bundle)."""
+        N.check(N.driver().lrq_model_load_layer_bundle(self.handle, layer,
+                                                       str(manifest).encode()),
+                "lrq_model_load_layer_bundle")
+
+    def load_tail_bundle(self, manifest: str) -> None:
+        """Uploads the final norm and LM head (and, for an untied model, the
+        embedding table) from a "lrrt.mini_model_tail_weights" v1 bundle."""
+        N.check(N.driver().lrq_model_load_tail_bundle(self.handle, str(manifest).encode()),
+                "lrq_model_load_tail_bundle")
+
     def set_tail(self, final_norm: np.ndarray, lm_head: np.ndarray,
                  embeddings: Optional[np.ndarray] = None) -> None:
         final_norm, lm_head = _f32(final_norm), _f32(lm_head)

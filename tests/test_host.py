@@ -106,3 +106,15 @@ def test_cpp_bundle_checks(built):
     result = subprocess.run([str(binary)], capture_output=True, text=True, timeout=60)
     assert result.returncode == 0, result.stderr
     assert "bundle checks: ok" in result.stdout
+
+
+def test_cpp_weight_bundle_checks(built, tmp_path):
+    """FP32 weight bundles: the fixture written by the reference's converter
+    loads, our writer round-trips, malformed manifests fail with the
+    reference's messages."""
+    binary = built["test:weight_bundle_test"]
+    fixture = Path(__file__).parent / "golden" / "weight_bundles"
+    result = subprocess.run([str(binary), str(fixture), str(tmp_path)], capture_output=True,
+                            text=True, timeout=60)
+    assert result.returncode == 0, result.stderr
+    assert "weight bundle checks: ok" in result.stdout
