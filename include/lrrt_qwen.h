@@ -76,7 +76,9 @@ typedef enum lrq_path_t {
   LRQ_PATH_DYNAMIC = 1,           /* dynamic-claim resident kernel */
   LRQ_PATH_HOST_STEP = 2,         /* 9 launches per layer + 4 per token */
   LRQ_PATH_SCHEDULER_PROFILE = 3, /* control-only compiled run */
-  LRQ_PATH_STAGE_PROFILE = 4      /* compiled run with per-stage ticks */
+  LRQ_PATH_STAGE_PROFILE = 4,     /* compiled run with per-stage ticks */
+  LRQ_PATH_GRAPH = 5              /* CUDA graph of one matched-step launch per compiled
+                                     stage, replayed per token (fixed count, no EOS) */
 } lrq_path_t;
 
 typedef struct lrq_decode_request_t {

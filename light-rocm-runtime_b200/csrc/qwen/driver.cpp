@@ -6,6 +6,8 @@
 #include "lrrt_qwen.h"
 
 #include "lm_head_top1_static.hpp"
+
+#include <cuda_runtime_api.h>
 #include "lrrt/qwen/weight_bundle.hpp"
 
 #include "lrrt/lrrt.hpp"
@@ -266,11 +268,12 @@ struct lrq_model_t {
         scheduler_profile(module.kernel("qwen_stateful_graph_scheduler_profile_kernel")),
         stage_profile(module.kernel("qwen_stateful_graph_stage_profile_kernel")),
         host_step(module.kernel("qwen_stateful_graph_host_step_kernel")),
+        matched_step(module.kernel("qwen_stateful_graph_matched_step_kernel")),
         config(config_), layout(layer_layout()) {}
 
   lrrt::Device device;
   lrrt::Module module;
-  lrrt::Kernel compiled, dynamic, scheduler_profile, stage_profile, host_step;
+  lrrt::Kernel compiled, dynamic, scheduler_profile, stage_profile, host_step, matched_step;
   lrq_model_config_t config;
   LayerLayout layout;
   uint32_t workers = 0;
@@ -290,6 +293,10 @@ struct lrq_model_t {
       scheduler_profile_executor, stage_profile_executor;
 
   std::optional<lrrt::DeviceBuffer> trace; // StageProfileEntry array, optional
+  // CUDA-graph comparator: one token of matched-step launches, captured once
+  // and replayed per token (LRQ_PATH_GRAPH).
+  cudaGraphExec_t token_graph = nullptr;
+  uint32_t token_graph_nodes = 0;
   uint32_t trace_capacity = 0;
   std::optional<std::array<uint32_t, 3>> staged_decode; // position, max, eos
   uint32_t last_path = 0;
@@ -533,7 +540,7 @@ void async_device_copy(lrq_model_t &m, lrrt::DeviceBuffer &dst, const lrrt::Devi
               "lr_memcpy_async");
 }
 
-void launch_host_steps(lrq_model_t &m, const lrq_decode_request_t &r) {
+void reset_host_state(lrq_model_t &m, const lrq_decode_request_t &r) {
   sg::State state{};
   state.abi_version = sg::kAbiVersion;
   state.status = static_cast<uint32_t>(sg::Status::ready);
@@ -544,6 +551,10 @@ void launch_host_steps(lrq_model_t &m, const lrq_decode_request_t &r) {
   lrrt::check(lr_memcpy(m.device.get(), m.host_state->data(), &state, sizeof(state),
                         LR_MEMCPY_HOST_TO_DEVICE),
               "lr_memcpy host state");
+}
+
+void launch_host_steps(lrq_model_t &m, const lrq_decode_request_t &r) {
+  reset_host_state(m, r);
   const auto *tasks = static_cast<const sg::Task *>(m.host_tasks->data());
   auto launch = [&](uint32_t first, uint32_t count) {
     const sg::HostStepArgs args{static_cast<sg::State *>(m.host_state->data()),
@@ -567,6 +578,81 @@ void launch_host_steps(lrq_model_t &m, const lrq_decode_request_t &r) {
   }
 }
 
+void check_cuda(cudaError_t status, const char *what) {
+  if (status != cudaSuccess) {
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(status));
+  }
+}
+
+void *default_stream(lrq_model_t &m) {
+  void *stream = nullptr;
+  lrrt::check(lr_queue_native_handle(m.device.get(), nullptr, &stream),
+              "lr_queue_native_handle");
+  return stream;
+}
+
+// Captures one token of the CUDA-graph comparator (reference
+// benchmarks/qwen_hip_graph.hpp: one matched-step node per compiled stage over
+// every worker block, in Program order: layers x (Program 0, Program 1), then
+// Program 2), via stream capture of the same lr_* launches on the device's
+// default queue.
+void build_token_graph(lrq_model_t &m) {
+  if (m.token_graph != nullptr) {
+    return;
+  }
+  check_cuda(cudaSetDevice(static_cast<int>(m.device.index())), "cudaSetDevice");
+  cudaStream_t stream = static_cast<cudaStream_t>(default_stream(m));
+  m.device.synchronize();
+  const auto *tasks = static_cast<const sg::Task *>(m.host_tasks->data());
+  const lr_launch_config_t config{{m.workers * sg::kWorkerThreads, 1, 1},
+                                  {sg::kWorkerThreads, 1, 1},
+                                  0};
+  uint32_t nodes = 0;
+  auto stage = [&](const sg::Stage &st) {
+    const sg::HostStepArgs args{static_cast<sg::State *>(m.host_state->data()),
+                                tasks + st.task_offset, st.task_count, 0, m.contexts->data()};
+    lrrt::launch(m.matched_step, config, args);
+    ++nodes;
+  };
+  check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal),
+             "cudaStreamBeginCapture");
+  cudaGraph_t graph = nullptr;
+  try {
+    for (uint32_t layer = 0; layer < m.config.layer_count; ++layer) {
+      for (uint32_t program = 0; program < 2; ++program) {
+        const sg::CompiledProgram &c = m.plan.programs[program];
+        for (uint32_t i = 0; i < c.stage_count; ++i) {
+          stage(m.plan.stages[c.stage_offset + i]);
+        }
+      }
+    }
+    const sg::CompiledProgram &tail = m.plan.programs[2];
+    for (uint32_t i = 0; i < tail.stage_count; ++i) {
+      stage(m.plan.stages[tail.stage_offset + i]);
+    }
+  } catch (...) {
+    cudaStreamEndCapture(stream, &graph);
+    if (graph != nullptr) {
+      cudaGraphDestroy(graph);
+    }
+    throw;
+  }
+  check_cuda(cudaStreamEndCapture(stream, &graph), "cudaStreamEndCapture");
+  const cudaError_t instantiated = cudaGraphInstantiate(&m.token_graph, graph, 0);
+  cudaGraphDestroy(graph);
+  check_cuda(instantiated, "cudaGraphInstantiate");
+  m.token_graph_nodes = nodes;
+}
+
+void launch_graph_steps(lrq_model_t &m, const lrq_decode_request_t &r) {
+  build_token_graph(m);
+  reset_host_state(m, r);
+  cudaStream_t stream = static_cast<cudaStream_t>(default_stream(m));
+  for (uint32_t token = 0; token < r.maximum_tokens; ++token) {
+    check_cuda(cudaGraphLaunch(m.token_graph, stream), "cudaGraphLaunch");
+  }
+}
+
 void decode_launch(lrq_model_t &m, lrq_decode_request_t r) {
   if (r.maximum_tokens == 0 || r.maximum_tokens > m.config.max_tokens_per_run ||
       uint64_t{r.token_position} + r.maximum_tokens > m.config.cache_capacity) {
@@ -578,8 +664,9 @@ void decode_launch(lrq_model_t &m, lrq_decode_request_t r) {
   if (r.stop_value == 0) {
     r.stop_value = 1;
   }
-  if (r.path == LRQ_PATH_HOST_STEP && r.eos_token != UINT32_MAX) {
-    throw std::invalid_argument("the host-step path runs a fixed token count (no EOS)");
+  if ((r.path == LRQ_PATH_HOST_STEP || r.path == LRQ_PATH_GRAPH) &&
+      r.eos_token != UINT32_MAX) {
+    throw std::invalid_argument("the host-step and graph paths run a fixed token count (no EOS)");
   }
   stage_decode_state(m, r.token_position, r.maximum_tokens, r.eos_token);
   async_device_copy(m, *m.decode_state, *m.decode_init, sizeof(qd::DecodeState));
@@ -587,6 +674,10 @@ void decode_launch(lrq_model_t &m, lrq_decode_request_t r) {
   m.last_path = r.path;
   if (r.path == LRQ_PATH_HOST_STEP) {
     launch_host_steps(m, r);
+    return;
+  }
+  if (r.path == LRQ_PATH_GRAPH) {
+    launch_graph_steps(m, r);
     return;
   }
   sg::ResidentExecutor &executor = executor_for(m, r.path);
@@ -612,7 +703,7 @@ void decode_launch(lrq_model_t &m, lrq_decode_request_t r) {
 void read_state(lrq_model_t &m, lrq_run_state_t *out) {
   m.device.synchronize();
   sg::State state{};
-  if (m.last_path == LRQ_PATH_HOST_STEP) {
+  if (m.last_path == LRQ_PATH_HOST_STEP || m.last_path == LRQ_PATH_GRAPH) {
     lrrt::copy_to_host(&state, *m.host_state, sizeof(state));
   } else {
     state = executor_for(m, m.last_path).read_state();
@@ -770,6 +861,10 @@ LRRT_API lr_status_t lrq_model_destroy(lrq_model_t *model) {
   return guarded("lrq_model_destroy", [&] {
     if (model == nullptr) {
       throw std::invalid_argument("null model");
+    }
+    if (model->token_graph != nullptr) {
+      model->device.synchronize();
+      cudaGraphExecDestroy(model->token_graph);
     }
     delete model;
   });

@@ -27,6 +27,7 @@ PATH_DYNAMIC = 1
 PATH_HOST_STEP = 2
 PATH_SCHEDULER_PROFILE = 3
 PATH_STAGE_PROFILE = 4
+PATH_GRAPH = 5
 
 BUFFERS = {
     "hidden": (0, HIDDEN, np.float32),

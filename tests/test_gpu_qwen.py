@@ -76,13 +76,15 @@ def test_small_model_compiled_fused_matches_oracle(small):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("path", [Q.PATH_DYNAMIC, Q.PATH_HOST_STEP, Q.PATH_STAGE_PROFILE])
+@pytest.mark.parametrize("path", [Q.PATH_DYNAMIC, Q.PATH_HOST_STEP, Q.PATH_STAGE_PROFILE,
+                                  Q.PATH_GRAPH])
 def test_small_model_other_paths_match_oracle(small, path):
     model, oracle, prompt = small
     start = len(prompt) - 1
     oracle.decode(oracle.embedding(int(prompt[-1])), start, 12)
     state, tokens = model.decode(start, 12, path=path)
-    compare_run(model, oracle, state, tokens, host_driven=path == Q.PATH_HOST_STEP)
+    compare_run(model, oracle, state, tokens,
+                host_driven=path in (Q.PATH_HOST_STEP, Q.PATH_GRAPH))
     if path == Q.PATH_STAGE_PROFILE:
         ticks, counts = model.stage_profile()
         assert sum(ticks) > 0 and sum(counts) > 0
