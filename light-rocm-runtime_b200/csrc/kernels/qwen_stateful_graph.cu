@@ -963,11 +963,14 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
   }
   const UnitRange range = block_config.ranges.of[kind];
   const uint32_t units = range.end - range.begin;
-  const bool split = units * kPairWarps <= kWarps;
-  const uint32_t first_unit = split ? warp / kPairWarps : warp;
-  const uint32_t stride = split ? kWarps / kPairWarps : kWarps;
-  bool ok = true;
-  for (uint32_t i = first_unit; i < units; i += stride) {
+  // Units whose slots must be reused within this stage (a stage of more
+  // units than ring slots) go first, four warps to a unit, so their refills
+  // are issued as early as possible; so do all units of stages with at most
+  // kWarps / kPairWarps units. The rest take one warp each.
+  const uint32_t early = units * kPairWarps <= kWarps                ? units
+                         : units > kSlots && units <= 2u * kSlots ? units - kSlots
+                                                                    : 0u;
+  auto process = [&](uint32_t i, bool split) -> bool {
     const uint32_t n = b.consumed + i;
     const uint32_t u = range.begin + i;
     const float4 extra = (lane & 3u) == 0u ? operands(u, row) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -975,8 +978,7 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
     const float *slot = wait_unit(b, state, n, make_tag(kind, layer, u));
     const uint64_t t_ready = block_config.unit_trace != nullptr ? dev::global_timer_ns() : 0;
     if (slot == nullptr) {
-      ok = false;
-      break;
+      return false;
     }
     const uint32_t rows =
         kind == kLmHead ? min(kSlotRows, block_config.vocab - u * kSlotRows) : kSlotRows;
@@ -1025,6 +1027,14 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
       trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
     }
     __syncwarp();
+    return true;
+  };
+  bool ok = true;
+  for (uint32_t i = warp / kPairWarps; ok && i < early; i += kWarps / kPairWarps) {
+    ok = process(i, true);
+  }
+  for (uint32_t i = early + warp; ok && i < units; i += kWarps) {
+    ok = process(i, false);
   }
   b.consumed += units;
   return ok;
