@@ -1,0 +1,158 @@
+// Kernel arguments of the prompt prefill module (qwen_prefill.cubin), shared
+// by the device code and the host driver. Every kernel takes one of these
+// structs by value, so the host launches them through lr_launch with the
+// struct as the packed argument blob.
+//
+// Prefill runs one chunk of prompt tokens through all layers at once: the
+// projections become GEMMs C[m][n] = A[m][k] . B[n][k] over the chunk's
+// token rows (B is an nn.Linear weight, row-major [out][in]). There is no
+// counterpart in light-rocm-runtime, whose prompts go through the decode step
+// one token at a time; the per-token arithmetic is the decode step's.
+//
+// 3xTF32 operands: for the tensor-core GEMM every operand x is stored as two
+// float arrays, hi = x rounded to TF32 and lo = (x - hi) rounded to TF32, and
+// C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi accumulates in FP32. Producers of
+// GEMM inputs write (hi, lo) pairs when `*_lo` is not null and plain FP32
+// otherwise.
+#ifndef LRRT_QWEN_PREFILL_HPP_
+#define LRRT_QWEN_PREFILL_HPP_
+
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define LRRT_PREFILL_HD __host__ __device__
+#else
+#define LRRT_PREFILL_HD
+#endif
+
+namespace lrrt::qwen::prefill {
+
+// hidden[t] = table[tokens[t]]
+struct EmbedArgs {
+  const uint32_t *tokens;
+  const float *table; // [rows][896]
+  float *hidden;      // [count][896]
+  uint32_t count;
+  uint32_t rows;      // table rows; out-of-range tokens write zeros
+};
+
+// out[t] = hidden[t] * rsqrt(mean(hidden[t]^2) + epsilon) * weight
+struct NormArgs {
+  const float *hidden;
+  const float *weight;
+  float *out;    // FP32, or the TF32 hi part when out_lo is set
+  float *out_lo; // optional TF32 lo part
+  uint32_t count;
+  float epsilon;
+};
+
+enum class GemmEpilogue : uint32_t {
+  bias = 0,     // c = acc + bias[n]                            (QKV)
+  residual = 1, // c += acc                                      (o_proj, down)
+  swiglu = 2,   // c = silu(acc(gate)) * acc(up)                 (gate/up)
+  partial = 3,  // c[split] = acc  (split-K partial sums, [splits][m][ldc])
+};
+
+// SIMT FP32 GEMM (mode bias, residual or swiglu): A [m][k] (lda),
+// B [n][k] (ldb), B2 the second weight for swiglu; c [m][ldc].
+struct GemmArgs {
+  const float *a;
+  const float *b;
+  const float *b2;
+  const float *bias;
+  float *c;
+  float *c_lo; // swiglu only: optional TF32 lo part of the output
+  uint32_t m, n, k, lda, ldb, ldc;
+};
+
+// Finishes split-K tiles of the tensor-core GEMM: for tiles
+// [tile_offset, tile_offset + tile_count) of the output's tile grid
+// (n_tiles per 128-row band), sums the `splits` compact partial
+// accumulators [split][tile][128][tile_columns] in split order and applies
+// the epilogue `mode` (bias, residual or swiglu) as the GEMM would have.
+struct ReduceArgs {
+  const float *partials;
+  const float *bias;
+  float *c;
+  float *c_lo;
+  uint32_t m, n, ldc;
+  uint32_t mode;          // GemmEpilogue (not partial)
+  uint32_t tile_offset, tile_count, n_tiles, splits;
+  uint32_t tile_columns;  // accumulator columns per tile (swiglu: gate + up)
+};
+
+// RoPE on the q and k parts of qkv rows [count][1152] at positions
+// first_position + t, then k and v appended to the cache rows.
+struct RopeArgs {
+  float *qkv;
+  const float *rope_cos; // [capacity][32]
+  const float *rope_sin;
+  float *key_cache;      // [capacity][128]
+  float *value_cache;
+  uint32_t count;
+  uint32_t first_position;
+};
+
+// Causal GQA attention: query row t attends to cache positions
+// 0..first_position + t. out [count][896] (hi part when out_lo is set).
+struct AttentionArgs {
+  const float *qkv;
+  const float *key_cache;
+  const float *value_cache;
+  float *out;
+  float *out_lo;
+  uint32_t count;
+  uint32_t first_position;
+};
+
+// hi[i] = tf32(x[i]), lo[i] = tf32(x[i] - hi[i]) for i < count.
+struct SplitArgs {
+  const float *x;
+  float *hi;
+  float *lo;
+  uint64_t count;
+};
+
+// Tensor-core 3xTF32 GEMM. Each CTA computes one 128 x N output tile
+// (N = 192, 224 or 256 accumulator columns, one kernel per width) over one
+// K slice: linear tile index tile_offset + blockIdx.x (n tile fastest),
+// K slice blockIdx.z of `splits`. A is [m][k], B is [rows][k]; the tensor maps
+// are 2-D fp32 maps with 64-byte swizzle and boxes of 16 columns x 128 rows
+// (A) or N / 2 rows (B: each B tile loads as two half boxes, so swiglu takes
+// N / 2 gate rows and N / 2 up rows starting at n_gate_offset).
+struct alignas(64) TensorMap {
+  uint64_t opaque[16];
+};
+
+struct TcGemmArgs {
+  TensorMap a_hi, a_lo, b_hi, b_lo;
+  const float *bias;
+  float *c;               // output, or the compact partials when mode == partial
+  float *c_lo;
+  uint32_t m, n, k, ldc;
+  uint32_t mode;          // GemmEpilogue
+  uint32_t tile_offset, n_tiles, tile_count, splits;
+  uint32_t n_gate_offset; // swiglu: row of the first up row in B
+  uint32_t wait_limit_ms; // per mbarrier wait
+  uint32_t *error;        // set to kTcErrorWaitTimeout when a wait gives up
+};
+
+constexpr uint32_t kTcTileM = 128;
+constexpr uint32_t kTcTileK = 16;   // one 64-byte swizzle row of fp32
+constexpr uint32_t kTcThreads = 128;
+constexpr uint32_t kTcMaximumN = 256;
+constexpr uint32_t kTcTmemColumns = 256;
+
+LRRT_PREFILL_HD constexpr uint32_t tc_stage_bytes(uint32_t n) { return 2u * (kTcTileM + n) * kTcTileK * 4u; }
+LRRT_PREFILL_HD constexpr uint32_t tc_stages(uint32_t n) {
+  return (200u * 1024u) / tc_stage_bytes(n) > 8u ? 8u : (200u * 1024u) / tc_stage_bytes(n);
+}
+LRRT_PREFILL_HD constexpr uint32_t tc_shared_bytes(uint32_t n) {
+  return tc_stages(n) * tc_stage_bytes(n) + 1024u /* alignment */ + 256u /* barriers */;
+}
+
+constexpr uint32_t kTcErrorWaitTimeout = 1;
+
+} // namespace lrrt::qwen::prefill
+
+#endif // LRRT_QWEN_PREFILL_HPP_

@@ -196,6 +196,63 @@ LRRT_API lr_status_t lrq_model_ingest_prompt(lrq_model_t *model, const uint32_t 
                                              uint32_t count);
 
 /*
+ * Batched prompt prefill (no counterpart in the reference, which ingests
+ * prompts one decode step at a time). The prefill kernels
+ * live in their own sm_100a module (qwen_prefill.cubin, built from
+ * light-rocm-runtime_b200/csrc/kernels/qwen_prefill.cu).
+ *
+ * lrq_model_enable_prefill loads that module and sizes its buffers for
+ * chunks of up to max_chunk_tokens tokens (0 = 512); longer prompts run in
+ * chunks. With LRQ_PREFILL_TF32X3 the first prefill after a weight upload
+ * also builds TF32 (hi, lo) copies of every layer's GEMM weights (2 x 59.6 MB
+ * per layer).
+ *
+ * lrq_model_prefill has lrq_model_ingest_prompt's contract: positions
+ * 0..count-2 are computed from prompt[0..count-2] (K/V rows written for
+ * every layer), then hidden is staged from prompt[count-1], so the next
+ * lrq_decode with token_position = count-1 produces the first new token.
+ * The projections run as GEMMs over all prompt rows:
+ *   LRQ_PREFILL_SIMT    FP32 FMA tiles on the CUDA cores;
+ *   LRQ_PREFILL_TF32X3  3xTF32 on the tcgen05 tensor cores (FP32 accuracy:
+ *                       each operand split into TF32 hi + lo, three products).
+ * Results match single-token ingestion to FP32 rounding (summation order
+ * differs), not bit for bit. Waits for the device before returning.
+ *
+ * lrq_model_prefill_at computes `count` tokens at positions
+ * first_position.. (K/V rows only, no hidden staging); positions before
+ * first_position must already hold the context's K/V rows.
+ */
+typedef enum lrq_prefill_path_t {
+  LRQ_PREFILL_SIMT = 0,
+  LRQ_PREFILL_TF32X3 = 1
+} lrq_prefill_path_t;
+
+LRRT_API lr_status_t lrq_model_enable_prefill(lrq_model_t *model, const void *module_image,
+                                              size_t module_image_size,
+                                              uint32_t max_chunk_tokens);
+LRRT_API lr_status_t lrq_model_prefill(lrq_model_t *model, const uint32_t *prompt,
+                                       uint32_t count, uint32_t path);
+LRRT_API lr_status_t lrq_model_prefill_at(lrq_model_t *model, const uint32_t *tokens,
+                                          uint32_t count, uint32_t first_position,
+                                          uint32_t path);
+
+/*
+ * Numerics check of one prefill GEMM on host matrices, through the prefill's
+ * own scheduler and kernels: c = epilogue(A . B^T) with A [m][k], B [n][k]
+ * row-major (mode 2, swiglu: B [2n][k], gate rows then up rows), c [m][n]
+ * read and written (mode 0: c = acc + bias; 1: c += acc; 2: c = silu(gate) *
+ * up). tile_columns 0 runs the FP32 SIMT kernels; 192, 224 or 256 runs the
+ * 3xTF32 tensor-core kernel of that accumulator width (k a multiple of 16,
+ * n of 32; swiglu: tile_columns 192 or 256 and n a multiple of half of it).
+ * Needs
+ * lrq_model_enable_prefill; waits for the device.
+ */
+LRRT_API lr_status_t lrq_prefill_gemm_check(lrq_model_t *model, uint32_t tile_columns,
+                                            uint32_t mode, uint32_t m, uint32_t n, uint32_t k,
+                                            const float *a, const float *b, const float *bias,
+                                            float *c);
+
+/*
  * End-to-end generate from host memory: copies the host hidden vector (or,
  * when hidden is NULL, stages the embedding of start_token) to the device,
  * runs the compiled path and copies the generated tokens back into `tokens`.

@@ -4,6 +4,7 @@ Outputs (git-ignored, shipped with the working tree):
   lib/liblrrt.so                  lr_* C ABI over the CUDA driver API
   lib/liblrrt_qwen.so             Qwen decode driver (include/lrrt_qwen.h)
   lib/qwen_stateful_graph.cubin   sm_100a decode megakernels
+  lib/qwen_prefill.cubin          sm_100a prompt prefill kernels
   lib/stateful_graph_fixture.cubin  sm_100a scheduler fixture kernels
   _build/tests/*                  C++ host tests (tests/cpp)
 
@@ -66,6 +67,7 @@ def build(verbose: bool = False) -> dict[str, Path]:
 
     driver = LIB / "liblrrt_qwen.so"
     driver_sources = sorted((csrc / "qwen").glob("*.cpp"))
+    driver_headers = sorted((csrc / "qwen").glob("*.hpp"))
     # CUDA runtime code of the driver (the static-scratch LM-head top-1),
     # compiled to an object and linked with the static CUDA runtime.
     static_top1 = csrc / "qwen" / "lm_head_top1_static.cu"
@@ -74,14 +76,15 @@ def build(verbose: bool = False) -> dict[str, Path]:
     if _stale(static_top1_object, static_inputs):
         _run([NVCC, *NVCCFLAGS, "-c", "-Xcompiler", "-fPIC,-fvisibility=hidden",
               str(static_top1), "-o", str(static_top1_object)], verbose)
-    if _stale(driver, driver_sources + static_inputs + [static_top1_object, runtime]):
+    if _stale(driver, driver_sources + driver_headers + static_inputs +
+              [static_top1_object, runtime]):
         _run([CXX, *CXXFLAGS, "-shared", "-fvisibility=hidden",
               *map(str, driver_sources), str(static_top1_object), "-o", str(driver),
               f"-L{LIB}", "-llrrt", f"-L{CUDA_HOME / 'lib64'}", "-lcudart_static",
               "-lrt", "-ldl", "-lpthread", "-Wl,-rpath,$ORIGIN"], verbose)
     outputs["driver"] = driver
 
-    for name in ("qwen_stateful_graph", "stateful_graph_fixture"):
+    for name in ("qwen_stateful_graph", "qwen_prefill", "stateful_graph_fixture"):
         source = csrc / "kernels" / f"{name}.cu"
         cubin = LIB / f"{name}.cubin"
         if _stale(cubin, [source] + headers):

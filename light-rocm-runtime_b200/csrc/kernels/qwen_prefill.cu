@@ -1,0 +1,794 @@
+// Prompt prefill of the Qwen2 FP32 decode path on sm_100a (module
+// qwen_prefill.cubin). All tokens of a prompt chunk go through each layer
+// together, so the projections become GEMMs over the chunk's rows:
+// [T x 896].[896 x 1152] (QKV), [T x 896].[896 x 896] (o_proj),
+// [T x 896].[896 x 2 x 4864] (gate/up), [T x 4864].[4864 x 896] (down).
+// The results fill the KV cache the way single-token decode steps do (same
+// token-major cache layout, same RoPE tables), after which decoding
+// continues from the last prompt token.
+//
+// light-rocm-runtime has no prefill: its prompts run through the decode step
+// one token at a time. The per-token arithmetic here follows that step
+// (benchmarks/qwen_stateful_graph_kernel.cpp: RMSNorm :665-701, QKV + bias
+// :392-427, RoPE + KV append :517-552, GQA :554-600, o_proj + residual
+// :602-620, SwiGLU :494-515, down + residual :158-176).
+//
+// Two GEMM implementations share the per-token kernels:
+//  * prefill_gemm_{bias,residual,swiglu}: FP32 FMA tiles on the CUDA cores
+//    (exact FP32 products, the comparator);
+//  * prefill_tc_gemm: 3xTF32 on the tcgen05 tensor cores. Operands are stored
+//    as TF32 (hi, lo) pairs (include/lrrt/qwen/prefill.hpp), TMA moves
+//    128-byte-swizzled tiles into shared memory, one thread issues
+//    tcgen05.mma into a TMEM accumulator (hi.hi + hi.lo + lo.hi per K step)
+//    and four warps read it back with tcgen05.ld for the epilogue.
+#include "lrrt/persistent_graph/device_sync.cuh"
+#include "lrrt/qwen/prefill.hpp"
+#include "lrrt/qwen/stateful_graph_context.hpp"
+
+#include <cstdint>
+
+namespace qd = lrrt::qwen::stateful_graph;
+namespace pf = lrrt::qwen::prefill;
+namespace dev = lrrt::persistent_graph::device;
+
+namespace {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// Round to TF32 (10 explicit mantissa bits), nearest with ties away from zero.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t bits;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(bits) : "f"(x));
+  return __uint_as_float(bits);
+}
+
+// Writes v, or its (hi, lo) TF32 pair when lo is not null.
+__device__ __forceinline__ void store_operand(float *out, float *lo, size_t index, float v) {
+  if (lo == nullptr) {
+    out[index] = v;
+  } else {
+    const float hi = to_tf32(v);
+    out[index] = hi;
+    lo[index] = to_tf32(v - hi);
+  }
+}
+
+__device__ __forceinline__ float silu_times(float gate, float up) {
+  return (gate / (1.0f + expf(-gate))) * up;
+}
+
+// ------------------------------------------------------------ SIMT GEMM --
+//
+// C[m][n] = sum_k A[m][k] * B[n][k]: A [M][K] (lda), B [N][K] (ldb), both
+// K-contiguous. 128 x 128 output tiles per 256-thread block, K in steps of
+// 16 staged in shared memory transposed to [k][m] / [k][n], 8 x 8 outputs
+// per thread; the next K step is loaded into registers while the current
+// one is multiplied. Requires K % 16 == 0 and lda, ldb % 4 == 0.
+
+constexpr uint32_t kTileM = 128, kTileN = 128, kTileK = 16, kGemmThreads = 256;
+
+template <pf::GemmEpilogue kMode>
+__device__ __forceinline__ void simt_gemm(const pf::GemmArgs &p) {
+  constexpr bool kTwo = kMode == pf::GemmEpilogue::swiglu;
+  __shared__ __align__(16) float as[kTileK][kTileM + 4];
+  __shared__ __align__(16) float bs[kTileK][kTileN + 4];
+  __shared__ __align__(16) float b2s[kTwo ? kTileK : 1][kTwo ? kTileN + 4 : 4];
+  const uint32_t tid = threadIdx.x;
+  const uint32_t tx = tid % 16u, ty = tid / 16u;
+  const uint32_t m0 = blockIdx.y * kTileM, n0 = blockIdx.x * kTileN;
+  const uint32_t load_row = tid / 4u, load_k = (tid % 4u) * 4u;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 a_next[2], b_next[2], b2_next[2];
+  auto fetch = [&](uint32_t k0) {
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+      const uint32_t m = m0 + load_row + 64u * h;
+      const uint32_t n = n0 + load_row + 64u * h;
+      a_next[h] = m < p.m ? __ldg(reinterpret_cast<const float4 *>(p.a + size_t{m} * p.lda + k0 + load_k))
+                          : zero;
+      b_next[h] = n < p.n ? __ldg(reinterpret_cast<const float4 *>(p.b + size_t{n} * p.ldb + k0 + load_k))
+                          : zero;
+      if constexpr (kTwo) {
+        b2_next[h] = n < p.n ? __ldg(reinterpret_cast<const float4 *>(p.b2 + size_t{n} * p.ldb + k0 +
+                                                                      load_k))
+                             : zero;
+      }
+    }
+  };
+  auto stage = [&]() {
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+      const uint32_t r = load_row + 64u * h;
+      as[load_k + 0][r] = a_next[h].x;
+      as[load_k + 1][r] = a_next[h].y;
+      as[load_k + 2][r] = a_next[h].z;
+      as[load_k + 3][r] = a_next[h].w;
+      bs[load_k + 0][r] = b_next[h].x;
+      bs[load_k + 1][r] = b_next[h].y;
+      bs[load_k + 2][r] = b_next[h].z;
+      bs[load_k + 3][r] = b_next[h].w;
+      if constexpr (kTwo) {
+        b2s[load_k + 0][r] = b2_next[h].x;
+        b2s[load_k + 1][r] = b2_next[h].y;
+        b2s[load_k + 2][r] = b2_next[h].z;
+        b2s[load_k + 3][r] = b2_next[h].w;
+      }
+    }
+  };
+  float acc[8][8];
+  float acc2[kTwo ? 8 : 1][kTwo ? 8 : 1];
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      acc[i][j] = 0.0f;
+      if constexpr (kTwo) {
+        acc2[i][j] = 0.0f;
+      }
+    }
+  }
+  fetch(0);
+  for (uint32_t k0 = 0; k0 < p.k; k0 += kTileK) {
+    __syncthreads(); // the previous step's shared reads are done
+    stage();
+    __syncthreads();
+    if (k0 + kTileK < p.k) {
+      fetch(k0 + kTileK);
+    }
+#pragma unroll
+    for (uint32_t kk = 0; kk < kTileK; ++kk) {
+      float av[8], bv[8], b2v[kTwo ? 8 : 1];
+      const float4 a0 = *reinterpret_cast<const float4 *>(&as[kk][ty * 4u]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&as[kk][64u + ty * 4u]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&bs[kk][tx * 4u]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&bs[kk][64u + tx * 4u]);
+      av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+      av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+      bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+      bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+      if constexpr (kTwo) {
+        const float4 c0 = *reinterpret_cast<const float4 *>(&b2s[kk][tx * 4u]);
+        const float4 c1 = *reinterpret_cast<const float4 *>(&b2s[kk][64u + tx * 4u]);
+        b2v[0] = c0.x; b2v[1] = c0.y; b2v[2] = c0.z; b2v[3] = c0.w;
+        b2v[4] = c1.x; b2v[5] = c1.y; b2v[6] = c1.z; b2v[7] = c1.w;
+      }
+#pragma unroll
+      for (uint32_t i = 0; i < 8; ++i) {
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) {
+          acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+          if constexpr (kTwo) {
+            acc2[i][j] = fmaf(av[i], b2v[j], acc2[i][j]);
+          }
+        }
+      }
+    }
+  }
+  // Thread (ty, tx) owns tile rows ty*4 + {0..3}, 64 + ty*4 + {0..3} and
+  // columns tx*4 + {0..3}, 64 + tx*4 + {0..3}.
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+    const uint32_t m = m0 + (i < 4 ? ty * 4u + i : 64u + ty * 4u + (i - 4u));
+    if (m >= p.m) {
+      continue;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      const uint32_t n = n0 + (j < 4 ? tx * 4u + j : 64u + tx * 4u + (j - 4u));
+      if (n >= p.n) {
+        continue;
+      }
+      const size_t at = size_t{m} * p.ldc + n;
+      if constexpr (kMode == pf::GemmEpilogue::bias) {
+        p.c[at] = acc[i][j] + p.bias[n];
+      } else if constexpr (kMode == pf::GemmEpilogue::residual) {
+        p.c[at] = p.c[at] + acc[i][j];
+      } else {
+        store_operand(p.c, p.c_lo, at, silu_times(acc[i][j], acc2[i][j]));
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------ tcgen05 3xTF32 --
+
+__device__ __forceinline__ void tma_load_2d(void *destination, const pf::TensorMap *map,
+                                            uint32_t x, uint32_t y, uint64_t *barrier) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dev::shared_address(destination)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(dev::shared_address(barrier))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile stored as 64-byte rows
+// with the 64-byte swizzle (the layout a TMA box of 16 fp32 x rows writes):
+// 8-row atoms of 512 bytes, stride byte offset 512, descriptor version 1,
+// layout type 4 (SWIZZLE_64B). Tiles start on 512-byte boundaries.
+__device__ __forceinline__ uint64_t sw64_descriptor(const void *tile) {
+  const uint64_t address = dev::shared_address(tile);
+  return ((address & 0x3ffffu) >> 4) | (uint64_t{1} << 16) | (uint64_t{512 >> 4} << 32) |
+         (uint64_t{1} << 46) | (uint64_t{4} << 61);
+}
+
+// Instruction descriptor: kind::tf32, FP32 accumulator, A and B K-major,
+// M = 128, N = kN.
+template <uint32_t kN> __host__ __device__ constexpr uint32_t tc_instruction() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((kN >> 3) << 17) | ((pf::kTcTileM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t instruction,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(instruction), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *barrier) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          dev::shared_address(barrier))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_load32(uint32_t address, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(address));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (uint32_t i = 0; i < 32; ++i) {
+    v[i] = __uint_as_float(r[i]);
+  }
+}
+
+template <uint32_t kStages> struct TcShared {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t done;
+  uint32_t tmem;
+  uint32_t abort;
+};
+
+// Epilogue of one output element, shared by the GEMM and the split-K reduce.
+__device__ __forceinline__ void finish_element(const float *bias, float *c, float *c_lo,
+                                               size_t at, uint32_t column, uint32_t mode,
+                                               float value, float up) {
+  if (mode == static_cast<uint32_t>(pf::GemmEpilogue::bias)) {
+    c[at] = value + bias[column];
+  } else if (mode == static_cast<uint32_t>(pf::GemmEpilogue::residual)) {
+    c[at] = c[at] + value;
+  } else {
+    store_operand(c, c_lo, at, silu_times(value, up));
+  }
+}
+
+} // namespace
+
+// ------------------------------------------------------------- kernels --
+
+extern "C" __global__ void __launch_bounds__(kGemmThreads) prefill_gemm_bias(pf::GemmArgs p) {
+  simt_gemm<pf::GemmEpilogue::bias>(p);
+}
+
+extern "C" __global__ void __launch_bounds__(kGemmThreads) prefill_gemm_residual(pf::GemmArgs p) {
+  simt_gemm<pf::GemmEpilogue::residual>(p);
+}
+
+// c = silu(a . b^T) * (a . b2^T)
+extern "C" __global__ void __launch_bounds__(kGemmThreads) prefill_gemm_swiglu(pf::GemmArgs p) {
+  simt_gemm<pf::GemmEpilogue::swiglu>(p);
+}
+
+// One block per token; out-of-range token ids write a zero row (the host
+// rejects them before launching).
+extern "C" __global__ void __launch_bounds__(256) prefill_embed(pf::EmbedArgs p) {
+  const uint32_t t = blockIdx.x;
+  if (t >= p.count) {
+    return;
+  }
+  const uint32_t token = p.tokens[t];
+  float *out = p.hidden + size_t{t} * qd::kHiddenSize;
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += blockDim.x) {
+    out[i] = token < p.rows ? p.table[size_t{token} * qd::kHiddenSize + i] : 0.0f;
+  }
+}
+
+// One block per token: the decode step's RMSNorm (per-thread strided sum of
+// squares, shared-memory tree, 1/sqrt(mean + eps), x * inverse * weight).
+extern "C" __global__ void __launch_bounds__(256) prefill_rmsnorm(pf::NormArgs p) {
+  __shared__ float partial[256];
+  const uint32_t t = blockIdx.x;
+  if (t >= p.count) {
+    return;
+  }
+  const float *x = p.hidden + size_t{t} * qd::kHiddenSize;
+  float sum = 0.0f;
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+    sum = fmaf(x[i], x[i], sum);
+  }
+  partial[threadIdx.x] = sum;
+  __syncthreads();
+  for (uint32_t stride = 128; stride != 0; stride >>= 1u) {
+    if (threadIdx.x < stride) {
+      partial[threadIdx.x] += partial[threadIdx.x + stride];
+    }
+    __syncthreads();
+  }
+  const float inverse = 1.0f / sqrtf(partial[0] / static_cast<float>(qd::kHiddenSize) + p.epsilon);
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+    store_operand(p.out, p.out_lo, size_t{t} * qd::kHiddenSize + i, x[i] * inverse * p.weight[i]);
+  }
+}
+
+// RoPE (pairs f and f + 32 of each head) on q and k of every chunk token at
+// position first_position + t, then the cache append of k and v; one block
+// per token.
+extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p) {
+  const uint32_t t = blockIdx.x;
+  if (t >= p.count) {
+    return;
+  }
+  const uint32_t position = p.first_position + t;
+  float *row = p.qkv + size_t{t} * qd::kPackedQkvSize;
+  const float *cos_row = p.rope_cos + size_t{position} * qd::kRotarySize;
+  const float *sin_row = p.rope_sin + size_t{position} * qd::kRotarySize;
+  float *key_row = p.key_cache + size_t{position} * qd::kKvSize;
+  float *value_row = p.value_cache + size_t{position} * qd::kKvSize;
+  for (uint32_t i = threadIdx.x; i < qd::kRotaryHeads * qd::kRotarySize; i += 256u) {
+    const uint32_t head = i / qd::kRotarySize, f = i % qd::kRotarySize;
+    float *base = row + head * qd::kHeadSize;
+    const float x0 = base[f], x1 = base[f + qd::kRotarySize];
+    const float r0 = x0 * cos_row[f] - x1 * sin_row[f];
+    const float r1 = x1 * cos_row[f] + x0 * sin_row[f];
+    base[f] = r0;
+    base[f + qd::kRotarySize] = r1;
+    if (head >= qd::kAttentionHeads) {
+      const uint32_t local = (head - qd::kAttentionHeads) * qd::kHeadSize;
+      key_row[local + f] = r0;
+      key_row[local + f + qd::kRotarySize] = r1;
+    }
+  }
+  const float *value = row + qd::kQuerySize + qd::kKvSize;
+  for (uint32_t i = threadIdx.x; i < qd::kKvSize; i += 256u) {
+    value_row[i] = value[i];
+  }
+}
+
+// Causal GQA attention, register-blocked. Block (x, y) serves 32 query rows
+// of head y (the heaviest row tiles get the lowest block indices) over cache
+// positions 0..first_position + row, in 64-position tiles staged in shared
+// memory. Thread (ty, tx) = (tid / 16, tid % 16) owns query rows
+// 4ty..4ty+3 and, per tile, keys 4tx..4tx+3 of S = Q.K^T / 8 and output dims
+// 4tx..4tx+3 of O; a row's sixteen threads reduce with shuffles. Q and K are
+// stored transposed ([dim][row], [dim][key]) so that both inner loops read
+// broadcast or contiguous float4 values. The softmax is the decode step's
+// online softmax (expf) applied per tile. out[t][head * 64 + d].
+constexpr uint32_t kAttentionRows = 32, kAttentionKeys = 64, kAttentionThreads = 128;
+
+extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attention(pf::AttentionArgs p) {
+  __shared__ __align__(16) float qt[qd::kHeadSize][kAttentionRows];   // [d][row]
+  __shared__ __align__(16) float kt[qd::kHeadSize][kAttentionKeys];   // [d][key]
+  __shared__ __align__(16) float vs[kAttentionKeys][qd::kHeadSize];   // [key][d]
+  __shared__ __align__(16) float ps[kAttentionRows][kAttentionKeys];  // [row][key]
+  const uint32_t tid = threadIdx.x;
+  const uint32_t ty = tid / 16u, tx = tid % 16u;
+  const uint32_t head = blockIdx.y, group = head / qd::kQueriesPerKvHead;
+  const uint32_t t0 = (gridDim.x - 1u - blockIdx.x) * kAttentionRows;
+  if (t0 >= p.count) {
+    return;
+  }
+  const uint32_t rows = min(kAttentionRows, p.count - t0);
+  for (uint32_t i = tid; i < kAttentionRows * qd::kHeadSize / 4u; i += kAttentionThreads) {
+    const uint32_t row = i % kAttentionRows, d = (i / kAttentionRows) * 4u;
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < rows) {
+      q = *reinterpret_cast<const float4 *>(p.qkv + size_t{t0 + row} * qd::kPackedQkvSize +
+                                            head * qd::kHeadSize + d);
+    }
+    qt[d][row] = q.x;
+    qt[d + 1][row] = q.y;
+    qt[d + 2][row] = q.z;
+    qt[d + 3][row] = q.w;
+  }
+  const uint32_t last = p.first_position + t0 + rows - 1u;
+  uint32_t position[4];
+  float maximum[4], denominator[4], acc[4][4];
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) {
+    position[i] = p.first_position + t0 + 4u * ty + i;
+    maximum[i] = -INFINITY;
+    denominator[i] = 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      acc[i][j] = 0.0f;
+    }
+  }
+  const size_t kv_offset = size_t{group} * qd::kHeadSize;
+  for (uint32_t base = 0; base <= last; base += kAttentionKeys) {
+    __syncthreads(); // the previous tile's reads are done (and qt is written)
+    for (uint32_t i = tid; i < kAttentionKeys * qd::kHeadSize / 4u; i += kAttentionThreads) {
+      const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
+      float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+      if (base + key <= last) {
+        const size_t at = size_t{base + key} * qd::kKvSize + kv_offset + d;
+        k = *reinterpret_cast<const float4 *>(p.key_cache + at);
+        v = *reinterpret_cast<const float4 *>(p.value_cache + at);
+      }
+      kt[d][key] = k.x;
+      kt[d + 1][key] = k.y;
+      kt[d + 2][key] = k.z;
+      kt[d + 3][key] = k.w;
+      *reinterpret_cast<float4 *>(&vs[key][d]) = v;
+    }
+    __syncthreads();
+    float score[4][4];
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        score[i][j] = 0.0f;
+      }
+    }
+#pragma unroll 8
+    for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
+      const float4 q = *reinterpret_cast<const float4 *>(&qt[d][4u * ty]);
+      const float4 k = *reinterpret_cast<const float4 *>(&kt[d][4u * tx]);
+      const float qv[4] = {q.x, q.y, q.z, q.w}, kv[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+      for (uint32_t i = 0; i < 4; ++i) {
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          score[i][j] = fmaf(qv[i], kv[j], score[i][j]);
+        }
+      }
+    }
+    float scale[4];
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+      float tile_maximum = -INFINITY;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        score[i][j] = base + 4u * tx + j <= position[i] ? score[i][j] * 0.125f : -INFINITY;
+        tile_maximum = fmaxf(tile_maximum, score[i][j]);
+      }
+#pragma unroll
+      for (uint32_t offset = 1; offset < 16; offset <<= 1u) {
+        tile_maximum = fmaxf(tile_maximum, __shfl_xor_sync(kFullMask, tile_maximum, offset));
+      }
+      // A row whose positions all lie after this tile keeps a -inf maximum
+      // only before its first key; then its scale is 1 and its weights 0.
+      const float next = fmaxf(maximum[i], tile_maximum);
+      const bool live = next != -INFINITY;
+      scale[i] = live ? expf(maximum[i] - next) : 1.0f;
+      float weights[4], sum = 0.0f;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        weights[j] = live ? expf(score[i][j] - next) : 0.0f;
+        sum += weights[j];
+      }
+#pragma unroll
+      for (uint32_t offset = 1; offset < 16; offset <<= 1u) {
+        sum += __shfl_xor_sync(kFullMask, sum, offset);
+      }
+      denominator[i] = denominator[i] * scale[i] + sum;
+      maximum[i] = next;
+      *reinterpret_cast<float4 *>(&ps[4u * ty + i][4u * tx]) =
+          make_float4(weights[0], weights[1], weights[2], weights[3]);
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        acc[i][j] *= scale[i];
+      }
+    }
+    __syncwarp(); // a row's weights come from the sixteen threads of its warp half
+#pragma unroll 2
+    for (uint32_t key = 0; key < kAttentionKeys; key += 4) {
+      float pv[4][4];
+#pragma unroll
+      for (uint32_t i = 0; i < 4; ++i) {
+        const float4 w = *reinterpret_cast<const float4 *>(&ps[4u * ty + i][key]);
+        pv[i][0] = w.x;
+        pv[i][1] = w.y;
+        pv[i][2] = w.z;
+        pv[i][3] = w.w;
+      }
+#pragma unroll
+      for (uint32_t e = 0; e < 4; ++e) {
+        const float4 v = *reinterpret_cast<const float4 *>(&vs[key + e][4u * tx]);
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (uint32_t i = 0; i < 4; ++i) {
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) {
+            acc[i][j] = fmaf(pv[i][e], vv[j], acc[i][j]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) {
+    const uint32_t row = 4u * ty + i;
+    if (row < rows) {
+      const size_t at = size_t{t0 + row} * qd::kQuerySize + head * qd::kHeadSize + 4u * tx;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        store_operand(p.out, p.out_lo, at + j, acc[i][j] / denominator[i]);
+      }
+    }
+  }
+}
+
+// Finishes split-K tiles: one thread per output element of tiles
+// [tile_offset, tile_offset + tile_count); partial sums are added in split
+// order, so the result does not depend on which CTA finished first.
+extern "C" __global__ void __launch_bounds__(256) prefill_reduce(pf::ReduceArgs p) {
+  const bool swiglu = p.mode == static_cast<uint32_t>(pf::GemmEpilogue::swiglu);
+  const uint32_t out_columns = swiglu ? p.tile_columns / 2u : p.tile_columns;
+  const uint64_t i = uint64_t{blockIdx.x} * blockDim.x + threadIdx.x;
+  if (i >= uint64_t{p.tile_count} * pf::kTcTileM * out_columns) {
+    return;
+  }
+  const uint32_t local = static_cast<uint32_t>(i / (uint64_t{pf::kTcTileM} * out_columns));
+  const uint32_t r = static_cast<uint32_t>((i / out_columns) % pf::kTcTileM);
+  const uint32_t column_in_tile = static_cast<uint32_t>(i % out_columns);
+  const uint32_t tile = p.tile_offset + local;
+  const uint32_t row = (tile / p.n_tiles) * pf::kTcTileM + r;
+  const uint32_t column = (tile % p.n_tiles) * out_columns + column_in_tile;
+  if (row >= p.m || column >= p.n) {
+    return;
+  }
+  const size_t tile_floats = size_t{pf::kTcTileM} * p.tile_columns;
+  const float *partial = p.partials + local * tile_floats + size_t{r} * p.tile_columns +
+                         column_in_tile;
+  const size_t split_stride = size_t{p.tile_count} * tile_floats;
+  float value = partial[0];
+  float up = swiglu ? partial[out_columns] : 0.0f;
+  for (uint32_t s = 1; s < p.splits; ++s) {
+    value += partial[s * split_stride];
+    if (swiglu) {
+      up += partial[s * split_stride + out_columns];
+    }
+  }
+  finish_element(p.bias, p.c, p.c_lo, size_t{row} * p.ldc + column, column, p.mode, value, up);
+}
+
+// TF32 (hi, lo) split of an FP32 array (weights, once per weight change).
+extern "C" __global__ void __launch_bounds__(256) prefill_split(pf::SplitArgs p) {
+  const uint64_t stride = uint64_t{gridDim.x} * blockDim.x;
+  for (uint64_t i = uint64_t{blockIdx.x} * blockDim.x + threadIdx.x; i < p.count; i += stride) {
+    const float x = p.x[i];
+    const float hi = to_tf32(x);
+    p.hi[i] = hi;
+    p.lo[i] = to_tf32(x - hi);
+  }
+}
+
+// 3xTF32 GEMM tile on the tensor cores: CTA (x, 0, z) computes output tile
+// tile_offset + x (n tile fastest: 128 rows x kN accumulator columns, which
+// are kN output columns, or kN / 2 for swiglu with gate in the first half and
+// up in the second) over K slice z. Warp 0 lane 0 issues the TMA loads into a
+// ring of kStages (A_hi, A_lo, B_hi, B_lo) stages, warp 1 owns the TMEM
+// allocation and its lane 0 issues the MMAs, then all four warps run the
+// epilogue, one accumulator row per thread. Every mbarrier wait is bounded;
+// on expiry the kernel records kTcErrorWaitTimeout, skips its stores, waits
+// (bounded) for its copies and MMAs in flight, frees TMEM and returns.
+template <uint32_t kN>
+__device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
+  constexpr uint32_t kStages = pf::tc_stages(kN);
+  constexpr uint32_t kStageBytes = pf::tc_stage_bytes(kN);
+  constexpr uint32_t kBytesA = pf::kTcTileM * pf::kTcTileK * 4u;
+  constexpr uint32_t kBytesB = kN * pf::kTcTileK * 4u;
+  constexpr uint32_t kInstruction = tc_instruction<kN>();
+  static_assert(kN % 32 == 0 && kN <= pf::kTcMaximumN, "accumulator width");
+  // The swiglu epilogue reads gate/up column pairs in chunks of 32; widths
+  // whose halves are not multiples of 32 (224) serve only the other modes.
+  static_assert(kBytesA % 512 == 0 && (kBytesB / 2) % 512 == 0, "swizzle atom alignment");
+  extern __shared__ __align__(1024) unsigned char raw_shared[];
+  unsigned char *tiles = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(raw_shared) + 1023u) & ~uintptr_t{1023});
+  auto &s = *reinterpret_cast<TcShared<kStages> *>(tiles + kStages * kStageBytes);
+  auto a_hi = [&](uint32_t st) { return tiles + st * kStageBytes; };
+  auto a_lo = [&](uint32_t st) { return a_hi(st) + kBytesA; };
+  auto b_hi = [&](uint32_t st) { return a_lo(st) + kBytesA; };
+  auto b_lo = [&](uint32_t st) { return b_hi(st) + kBytesB; };
+
+  const uint32_t warp = threadIdx.x >> 5u, lane = threadIdx.x & 31u;
+  const bool swiglu = p.mode == static_cast<uint32_t>(pf::GemmEpilogue::swiglu);
+  const uint32_t tile = p.tile_offset + blockIdx.x;
+  const uint32_t m0 = (tile / p.n_tiles) * pf::kTcTileM;
+  const uint32_t n_tile = tile % p.n_tiles;
+  const uint32_t k_tiles = p.k / pf::kTcTileK;
+  const uint32_t first_tile = blockIdx.z * k_tiles / p.splits;
+  const uint32_t count = (blockIdx.z + 1u) * k_tiles / p.splits - first_tile;
+  const dev::Deadline deadline(p.wait_limit_ms);
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < kStages; ++i) {
+      dev::mbarrier_init(&s.full[i], 1);
+      dev::mbarrier_init(&s.empty[i], 1);
+    }
+    dev::mbarrier_init(&s.done, 1);
+    s.abort = 0;
+    dev::mbarrier_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     dev::shared_address(&s.tmem)),
+                 "r"(pf::kTcTmemColumns)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem;
+
+  auto fail = [&]() {
+    s.abort = 1;
+    atomicExch(p.error, pf::kTcErrorWaitTimeout);
+  };
+
+  if (warp == 0 && lane == 0) {
+    // Producer. B rows: [n0, n0 + kN/2) and the next half, or, for a gate/up
+    // pair (n_gate_offset set; also in split mode, whose epilogue is
+    // `partial`), kN/2 gate rows and the matching kN/2 up rows.
+    const uint32_t half = kN / 2u;
+    const bool paired = p.n_gate_offset != 0;
+    const uint32_t n_first = paired ? n_tile * half : n_tile * kN;
+    const uint32_t n_second = paired ? p.n_gate_offset + n_tile * half : n_first + half;
+    uint32_t issued = 0;
+    for (uint32_t i = 0; i < count && s.abort == 0; ++i) {
+      const uint32_t st = i % kStages;
+      if (i >= kStages && !dev::mbarrier_wait(&s.empty[st], ((i / kStages) + 1u) & 1u, deadline)) {
+        fail();
+        break;
+      }
+      const uint32_t k0 = (first_tile + i) * pf::kTcTileK;
+      dev::mbarrier_arrive_expect_tx(&s.full[st], kStageBytes);
+      tma_load_2d(a_hi(st), &p.a_hi, k0, m0, &s.full[st]);
+      tma_load_2d(a_lo(st), &p.a_lo, k0, m0, &s.full[st]);
+      tma_load_2d(b_hi(st), &p.b_hi, k0, n_first, &s.full[st]);
+      tma_load_2d(b_hi(st) + kBytesB / 2u, &p.b_hi, k0, n_second, &s.full[st]);
+      tma_load_2d(b_lo(st), &p.b_lo, k0, n_first, &s.full[st]);
+      tma_load_2d(b_lo(st) + kBytesB / 2u, &p.b_lo, k0, n_second, &s.full[st]);
+      ++issued;
+    }
+    // Wait for the newest load of every stage (already consumed when
+    // nothing failed) so that no copy lands after the exit.
+    const dev::Deadline drain(p.wait_limit_ms);
+    for (uint32_t i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+      if (!dev::mbarrier_wait(&s.full[i % kStages], (i / kStages) & 1u, drain)) {
+        fail();
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: per stage two K = 8 steps, three products each.
+    for (uint32_t i = 0; i < count; ++i) {
+      const uint32_t st = i % kStages;
+      if (!dev::mbarrier_wait(&s.full[st], (i / kStages) & 1u, deadline)) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const uint64_t ah = sw64_descriptor(a_hi(st)), al = sw64_descriptor(a_lo(st));
+      const uint64_t bh = sw64_descriptor(b_hi(st)), bl = sw64_descriptor(b_lo(st));
+#pragma unroll
+      for (uint32_t kk = 0; kk < pf::kTcTileK / 8u; ++kk) {
+        const uint64_t step = kk * 2u; // 32 bytes, in 16-byte descriptor units
+        tc_mma(tmem, ah + step, bh + step, kInstruction, (i | kk) != 0 ? 1u : 0u);
+        tc_mma(tmem, ah + step, bl + step, kInstruction, 1u);
+        tc_mma(tmem, al + step, bh + step, kInstruction, 1u);
+      }
+      tc_commit(&s.empty[st]);
+    }
+    tc_commit(&s.done);
+  }
+  __syncwarp();
+
+  // Epilogue: thread (warp, lane) holds tile row 32 * warp + lane.
+  const dev::Deadline finish(p.wait_limit_ms);
+  const bool ready = dev::mbarrier_wait(&s.done, 0, finish);
+  if (!ready) {
+    fail();
+  }
+  tc_fence_after();
+  const uint32_t r = warp * 32u + lane;
+  const uint32_t row = m0 + r;
+  const uint32_t lane_address = tmem + ((warp * 32u) << 16);
+  const bool store = ready && s.abort == 0 && count != 0;
+  if (p.mode == static_cast<uint32_t>(pf::GemmEpilogue::partial)) {
+    float *out = p.c + (size_t{blockIdx.z} * p.tile_count + blockIdx.x) * pf::kTcTileM * kN +
+                 size_t{r} * kN;
+#pragma unroll 1
+    for (uint32_t chunk = 0; chunk < kN / 32u; ++chunk) {
+      float v[32];
+      tc_load32(lane_address + chunk * 32u, v);
+      if (store) {
+        float4 *o = reinterpret_cast<float4 *>(out + chunk * 32u);
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) {
+          o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+      }
+    }
+  } else if (swiglu) {
+#pragma unroll 1
+    for (uint32_t chunk = 0; chunk < kN / 64u; ++chunk) {
+      float gate[32], up[32];
+      tc_load32(lane_address + chunk * 32u, gate);
+      tc_load32(lane_address + kN / 2u + chunk * 32u, up);
+      const uint32_t column = n_tile * (kN / 2u) + chunk * 32u;
+      if (store && row < p.m && column < p.n) {
+        const size_t at = size_t{row} * p.ldc + column;
+#pragma unroll
+        for (uint32_t j = 0; j < 32; ++j) {
+          store_operand(p.c, p.c_lo, at + j, silu_times(gate[j], up[j]));
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (uint32_t chunk = 0; chunk < kN / 32u; ++chunk) {
+      float v[32];
+      tc_load32(lane_address + chunk * 32u, v);
+      const uint32_t column = n_tile * kN + chunk * 32u;
+      if (store && row < p.m && column < p.n) {
+        const size_t at = size_t{row} * p.ldc + column;
+#pragma unroll
+        for (uint32_t j = 0; j < 32; ++j) {
+          finish_element(p.bias, p.c, p.c_lo, at + j, column + j, p.mode, v[j], 0.0f);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(pf::kTcTmemColumns)
+                 : "memory");
+  }
+}
+
+extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
+    prefill_tc_gemm_n192(const __grid_constant__ pf::TcGemmArgs p) {
+  tc_gemm<192>(p);
+}
+
+extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
+    prefill_tc_gemm_n224(const __grid_constant__ pf::TcGemmArgs p) {
+  tc_gemm<224>(p);
+}
+
+extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
+    prefill_tc_gemm_n256(const __grid_constant__ pf::TcGemmArgs p) {
+  tc_gemm<256>(p);
+}

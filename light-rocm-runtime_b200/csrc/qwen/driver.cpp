@@ -6,6 +6,7 @@
 #include "lrrt_qwen.h"
 
 #include "lm_head_top1_static.hpp"
+#include "prefill.hpp"
 
 #include <cuda_runtime_api.h>
 #include "lrrt/qwen/weight_bundle.hpp"
@@ -301,6 +302,10 @@ struct lrq_model_t {
   std::optional<std::array<uint32_t, 3>> staged_decode; // position, max, eos
   uint32_t last_path = 0;
   uint64_t device_bytes = 0;
+  // Prompt prefill (optional module); weights_generation counts layer-weight
+  // uploads so the prefill's TF32 weight copies know when to refresh.
+  std::unique_ptr<lrrt::qwen::prefill::Prefill> prefill;
+  uint64_t weights_generation = 0;
 
   float *layer_weight(uint32_t layer, size_t offset) const {
     return static_cast<float *>(weights->data()) + size_t{layer} * layout.floats + offset;
@@ -893,6 +898,7 @@ LRRT_API lr_status_t lrq_model_set_layer(lrq_model_t *model, uint32_t layer,
                  {w->gate, l.gate, i * h},
                  {w->up, l.up, i * h},
                  {w->down, l.down, h * i}};
+    ++model->weights_generation;
     for (const auto &part : parts) {
       if (part.source == nullptr) {
         throw std::invalid_argument("missing layer weight");
@@ -911,6 +917,7 @@ LRRT_API lr_status_t lrq_model_replicate_layer(lrq_model_t *model, uint32_t sour
       throw std::invalid_argument("invalid layer");
     }
     const size_t bytes = model->layout.floats * sizeof(float);
+    ++model->weights_generation;
     for (uint32_t layer = 0; layer < model->config.layer_count; ++layer) {
       if (layer != source_layer) {
         lrrt::check(lr_memcpy(model->device.get(), model->layer_weight(layer, 0),
@@ -1103,6 +1110,108 @@ LRRT_API lr_status_t lrq_model_ingest_prompt(lrq_model_t *model, const uint32_t 
       throw std::invalid_argument("prompt token out of range");
     }
     model->device.synchronize();
+    lrrt::check(static_cast<lr_status_t>(
+                    lrq_model_set_hidden_from_token(model, prompt[count - 1u])),
+                "stage last prompt token");
+  });
+}
+
+namespace {
+
+lrrt::qwen::prefill::ModelView prefill_view(lrq_model_t &m) {
+  lrrt::qwen::prefill::ModelView view{};
+  view.vocab = m.config.vocab_size;
+  view.capacity = m.config.cache_capacity;
+  view.epsilon = m.config.rms_epsilon;
+  view.embeddings = static_cast<const float *>(m.embeddings->data());
+  view.rope_cos = static_cast<const float *>(m.rope_cos->data());
+  view.rope_sin = static_cast<const float *>(m.rope_sin->data());
+  const LayerLayout &l = m.layout;
+  for (uint32_t layer = 0; layer < m.config.layer_count; ++layer) {
+    view.layers.push_back({m.layer_weight(layer, l.attention_norm), m.layer_weight(layer, l.q),
+                           m.layer_weight(layer, l.q_bias), m.layer_weight(layer, l.o),
+                           m.layer_weight(layer, l.mlp_norm), m.layer_weight(layer, l.gate),
+                           m.layer_weight(layer, l.down),
+                           static_cast<float *>(m.key_cache->data()) + layer * m.cache_floats(),
+                           static_cast<float *>(m.value_cache->data()) + layer * m.cache_floats()});
+  }
+  return view;
+}
+
+void prefill_tokens(lrq_model_t &m, const uint32_t *tokens, uint32_t count,
+                    uint32_t first_position, uint32_t path) {
+  if (!m.prefill) {
+    throw std::logic_error("prefill is not enabled on this model");
+  }
+  if (path != LRQ_PREFILL_SIMT && path != LRQ_PREFILL_TF32X3) {
+    throw std::invalid_argument("unknown prefill path");
+  }
+  m.prefill->run(prefill_view(m), tokens, count, first_position,
+                 static_cast<lrrt::qwen::prefill::Path>(path), m.weights_generation);
+}
+
+} // namespace
+
+LRRT_API lr_status_t lrq_model_enable_prefill(lrq_model_t *model, const void *module_image,
+                                              size_t module_image_size,
+                                              uint32_t max_chunk_tokens) {
+  return guarded("lrq_model_enable_prefill", [&] {
+    if (model == nullptr || module_image == nullptr || module_image_size == 0) {
+      throw std::invalid_argument("null argument");
+    }
+    // q, k, v (and their biases) and gate, up must be contiguous: the prefill
+    // multiplies them as single [1152][896] and [9728][896] matrices.
+    const LayerLayout &l = model->layout;
+    const size_t h = qd::kHiddenSize, kv = qd::kKvSize, i = qd::kIntermediateSize;
+    if (l.k != l.q + h * h || l.v != l.k + kv * h || l.k_bias != l.q_bias + h ||
+        l.v_bias != l.k_bias + kv || l.up != l.gate + i * h) {
+      throw std::logic_error("layer layout does not keep QKV and gate/up contiguous");
+    }
+    model->prefill.reset();
+    model->prefill = std::make_unique<lrrt::qwen::prefill::Prefill>(
+        model->device, module_image, module_image_size,
+        max_chunk_tokens == 0 ? 512u : max_chunk_tokens);
+  });
+}
+
+LRRT_API lr_status_t lrq_model_prefill_at(lrq_model_t *model, const uint32_t *tokens,
+                                          uint32_t count, uint32_t first_position,
+                                          uint32_t path) {
+  return guarded("lrq_model_prefill_at", [&] {
+    if (model == nullptr || (tokens == nullptr && count != 0)) {
+      throw std::invalid_argument("null argument");
+    }
+    prefill_tokens(*model, tokens, count, first_position, path);
+  });
+}
+
+LRRT_API lr_status_t lrq_prefill_gemm_check(lrq_model_t *model, uint32_t tile_columns,
+                                            uint32_t mode, uint32_t m, uint32_t n, uint32_t k,
+                                            const float *a, const float *b, const float *bias,
+                                            float *c) {
+  return guarded("lrq_prefill_gemm_check", [&] {
+    if (model == nullptr || a == nullptr || b == nullptr || c == nullptr || mode > 2) {
+      throw std::invalid_argument("invalid GEMM check");
+    }
+    if (!model->prefill) {
+      throw std::logic_error("prefill is not enabled on this model");
+    }
+    model->prefill->gemm_check(tile_columns, static_cast<lrrt::qwen::prefill::GemmEpilogue>(mode),
+                               m, n, k, a, b, bias, c);
+  });
+}
+
+LRRT_API lr_status_t lrq_model_prefill(lrq_model_t *model, const uint32_t *prompt,
+                                       uint32_t count, uint32_t path) {
+  return guarded("lrq_model_prefill", [&] {
+    if (model == nullptr || prompt == nullptr || count == 0 ||
+        count > model->config.cache_capacity) {
+      throw std::invalid_argument("invalid prompt");
+    }
+    if (prompt[count - 1u] >= model->config.vocab_size) {
+      throw std::invalid_argument("prompt token out of range");
+    }
+    prefill_tokens(*model, prompt, count - 1u, 0, path);
     lrrt::check(static_cast<lr_status_t>(
                     lrq_model_set_hidden_from_token(model, prompt[count - 1u])),
                 "stage last prompt token");

@@ -1,0 +1,428 @@
+// Host side of the prompt prefill: chunk buffers, the 3xTF32 operand copies
+// and tensor maps, and the launch sequence of one chunk through all layers.
+#include "prefill.hpp"
+
+#include "lrrt/qwen/stateful_graph_context.hpp"
+
+#include <cuda.h>
+#include <cuda_runtime_api.h>
+
+#include <algorithm>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+namespace lrrt::qwen::prefill {
+namespace {
+
+namespace qd = lrrt::qwen::stateful_graph;
+
+constexpr uint32_t kHidden = qd::kHiddenSize;
+constexpr uint32_t kQkv = qd::kPackedQkvSize;
+constexpr uint32_t kIntermediate = qd::kIntermediateSize;
+constexpr uint32_t kSms = 148;           // B200 SM count: one TC GEMM CTA per SM
+constexpr uint32_t kWaitLimitMs = 2000;  // per mbarrier wait of the TC GEMM
+// Accumulator columns per tensor-core tile of each GEMM: output widths 1152
+// (QKV) = 6 x 192, 896 (o_proj, down) = 4 x 224, gate/up = 38 x (128 gate +
+// 128 up).
+constexpr uint32_t kQkvTile = 192, kHiddenTile = 224, kGateUpTile = 256;
+
+// Floats of one layer's GEMM weights: QKV, o_proj, gate/up, down.
+constexpr size_t kQkvFloats = size_t{kQkv} * kHidden;
+constexpr size_t kOFloats = size_t{kHidden} * kHidden;
+constexpr size_t kGateUpFloats = size_t{2} * kIntermediate * kHidden;
+constexpr size_t kDownFloats = size_t{kHidden} * kIntermediate;
+constexpr size_t kLayerFloats = kQkvFloats + kOFloats + kGateUpFloats + kDownFloats;
+
+static_assert(sizeof(CUtensorMap) == sizeof(TensorMap), "TensorMap must hold a CUtensorMap");
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                 const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                 const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_tiled() {
+  static const EncodeTiled function = [] {
+    void *entry = nullptr;
+    cudaDriverEntryPointQueryResult found{};
+    const cudaError_t status = cudaGetDriverEntryPointByVersion(
+        "cuTensorMapEncodeTiled", &entry, 12000, cudaEnableDefault, &found);
+    if (status != cudaSuccess || found != cudaDriverEntryPointSuccess || entry == nullptr) {
+      throw std::runtime_error("cuTensorMapEncodeTiled is not available");
+    }
+    return reinterpret_cast<EncodeTiled>(entry);
+  }();
+  return function;
+}
+
+// 2-D fp32 map over a row-major [rows][columns] array: box of 16 columns
+// (one 64-byte swizzle row) x box_rows rows, 64-byte swizzle, zero fill
+// outside the array.
+TensorMap map_2d(const float *base, uint64_t rows, uint64_t columns, uint32_t box_rows) {
+  CUtensorMap map{};
+  const cuuint64_t dims[2] = {columns, rows};
+  const cuuint64_t strides[1] = {columns * sizeof(float)};
+  const cuuint32_t box[2] = {kTcTileK, box_rows};
+  const cuuint32_t element_strides[2] = {1, 1};
+  const CUresult status = encode_tiled()(
+      &map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
+      element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (status != CUDA_SUCCESS) {
+    throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(status) + ")");
+  }
+  TensorMap out{};
+  std::memcpy(&out, &map, sizeof(out));
+  return out;
+}
+
+lr_launch_config_t rows_config(uint32_t blocks, uint32_t threads) {
+  return lr_launch_config_t{{blocks * threads, 1, 1}, {threads, 1, 1}, 0};
+}
+
+uint32_t ceil_div(uint64_t a, uint64_t b) { return static_cast<uint32_t>((a + b - 1) / b); }
+
+} // namespace
+
+Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t max_chunk_tokens)
+    : device_(device), module_(device, image, image_size), embed_(module_.kernel("prefill_embed")),
+      rmsnorm_(module_.kernel("prefill_rmsnorm")), rope_kv_(module_.kernel("prefill_rope_kv")),
+      attend_(module_.kernel("prefill_attention")), reduce_(module_.kernel("prefill_reduce")),
+      split_(module_.kernel("prefill_split")), gemm_bias_(module_.kernel("prefill_gemm_bias")),
+      gemm_residual_(module_.kernel("prefill_gemm_residual")),
+      gemm_swiglu_(module_.kernel("prefill_gemm_swiglu")),
+      tc_n192_(module_.kernel("prefill_tc_gemm_n192")),
+      tc_n224_(module_.kernel("prefill_tc_gemm_n224")),
+      tc_n256_(module_.kernel("prefill_tc_gemm_n256")), chunk_(max_chunk_tokens) {
+  if (chunk_ == 0 || chunk_ > 8192) {
+    throw std::invalid_argument("prefill chunk must be 1..8192 tokens");
+  }
+  const size_t c = chunk_;
+  hidden_.emplace(allocate(sizeof(float) * c * kHidden));
+  normalized_.emplace(allocate(sizeof(float) * c * kHidden));
+  normalized_lo_.emplace(allocate(sizeof(float) * c * kHidden));
+  qkv_.emplace(allocate(sizeof(float) * c * kQkv));
+  attention_.emplace(allocate(sizeof(float) * c * kHidden));
+  attention_lo_.emplace(allocate(sizeof(float) * c * kHidden));
+  activated_.emplace(allocate(sizeof(float) * c * kIntermediate));
+  activated_lo_.emplace(allocate(sizeof(float) * c * kIntermediate));
+  // Split-K partials: at most one 128 x 256 tile per SM in flight.
+  partials_.emplace(allocate(sizeof(float) * kSms * kTcTileM * kTcMaximumN));
+  error_.emplace(allocate(sizeof(uint32_t)));
+}
+
+DeviceBuffer Prefill::allocate(size_t bytes) {
+  device_bytes_ += bytes;
+  return DeviceBuffer(device_, std::max<size_t>(bytes, 16));
+}
+
+// (Re)builds the TF32 (hi, lo) weight copies when the weights changed since
+// the last split, and the tensor maps over them and the chunk operands.
+void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_generation) {
+  const size_t layers = model.layers.size();
+  if (!split_weights_ || split_weights_->size() < sizeof(float) * 2 * kLayerFloats * layers) {
+    split_weights_.reset();
+    split_weights_.emplace(allocate(sizeof(float) * 2 * kLayerFloats * layers));
+    split_generation_ = UINT64_MAX;
+  }
+  if (split_generation_ == weights_generation && split_source_ == model.layers[0].qkv &&
+      layer_maps_.size() == layers) {
+    return;
+  }
+  if (cudaSetDevice(static_cast<int>(device_.index())) != cudaSuccess) {
+    throw std::runtime_error("cudaSetDevice failed");
+  }
+  const size_t c = chunk_;
+  auto *hi_lo = static_cast<float *>(split_weights_->data());
+  normalized_maps_[0] = map_2d(static_cast<float *>(normalized_->data()), c, kHidden, kTcTileM);
+  normalized_maps_[1] = map_2d(static_cast<float *>(normalized_lo_->data()), c, kHidden, kTcTileM);
+  attention_maps_[0] = map_2d(static_cast<float *>(attention_->data()), c, kHidden, kTcTileM);
+  attention_maps_[1] = map_2d(static_cast<float *>(attention_lo_->data()), c, kHidden, kTcTileM);
+  activated_maps_[0] = map_2d(static_cast<float *>(activated_->data()), c, kIntermediate, kTcTileM);
+  activated_maps_[1] =
+      map_2d(static_cast<float *>(activated_lo_->data()), c, kIntermediate, kTcTileM);
+  layer_maps_.assign(layers, LayerMaps{});
+  for (size_t layer = 0; layer < layers; ++layer) {
+    const LayerView &w = model.layers[layer];
+    float *hi = hi_lo + layer * 2 * kLayerFloats;
+    float *lo = hi + kLayerFloats;
+    const struct {
+      const float *source;
+      size_t offset, floats;
+    } parts[] = {{w.qkv, 0, kQkvFloats},
+                 {w.o, kQkvFloats, kOFloats},
+                 {w.gate_up, kQkvFloats + kOFloats, kGateUpFloats},
+                 {w.down, kQkvFloats + kOFloats + kGateUpFloats, kDownFloats}};
+    for (const auto &part : parts) {
+      const SplitArgs args{part.source, hi + part.offset, lo + part.offset, part.floats};
+      launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(part.floats, 256), kSms * 8), 256),
+             args);
+    }
+    LayerMaps &maps = layer_maps_[layer];
+    const float *gate_up = hi + kQkvFloats + kOFloats;
+    const float *down = gate_up + kGateUpFloats;
+    for (uint32_t part = 0; part < 2; ++part) {
+      const float *base = part == 0 ? hi : lo;
+      const size_t shift = base - hi;
+      maps.qkv[part] = map_2d(base, kQkv, kHidden, kQkvTile / 2u);
+      maps.o[part] = map_2d(base + kQkvFloats, kHidden, kHidden, kHiddenTile / 2u);
+      maps.gate_up[part] = map_2d(gate_up + shift, 2 * kIntermediate, kHidden, kGateUpTile / 2u);
+      maps.down[part] = map_2d(down + shift, kHidden, kIntermediate, kHiddenTile / 2u);
+    }
+  }
+  split_generation_ = weights_generation;
+  split_source_ = model.layers[0].qkv;
+}
+
+// One 3xTF32 GEMM C = A . B^T over m chunk rows with tile_columns-wide
+// tensor-core tiles. Whole waves of kSms tiles run data-parallel with the
+// epilogue in the GEMM; the tiles of a last partial wave (or all tiles, when
+// there are fewer than kSms) are split along K so that the launch fills the
+// SMs, and prefill_reduce sums their partials in split order.
+void Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b, uint32_t m,
+                      uint32_t n, uint32_t k, GemmEpilogue mode, float *c, float *c_lo,
+                      uint32_t ldc, const float *bias) {
+  const bool swiglu = mode == GemmEpilogue::swiglu;
+  const uint32_t out_columns = swiglu ? tile_columns / 2u : tile_columns;
+  const uint32_t n_tiles = ceil_div(n, out_columns);
+  const uint32_t tiles = n_tiles * ceil_div(m, kTcTileM);
+  const uint32_t k_tiles = k / kTcTileK;
+  const Kernel &kernel = tile_columns == 192 ? tc_n192_ : tile_columns == 224 ? tc_n224_ : tc_n256_;
+  TcGemmArgs args{};
+  args.a_hi = a[0];
+  args.a_lo = a[1];
+  args.b_hi = b[0];
+  args.b_lo = b[1];
+  args.m = m;
+  args.n = n;
+  args.k = k;
+  args.ldc = ldc;
+  args.n_tiles = n_tiles;
+  args.n_gate_offset = swiglu ? n : 0u;
+  args.wait_limit_ms = kWaitLimitMs;
+  args.error = static_cast<uint32_t *>(error_->data());
+  auto run = [&](uint32_t offset, uint32_t count, uint32_t splits) {
+    args.tile_offset = offset;
+    args.tile_count = count;
+    args.splits = splits;
+    args.mode = static_cast<uint32_t>(splits > 1 ? GemmEpilogue::partial : mode);
+    args.c = splits > 1 ? static_cast<float *>(partials_->data()) : c;
+    args.c_lo = splits > 1 ? nullptr : c_lo;
+    args.bias = bias;
+    const lr_launch_config_t config{
+        {count * kTcThreads, 1, splits}, {kTcThreads, 1, 1}, tc_shared_bytes(tile_columns)};
+    launch(kernel.get(), config, args);
+    if (splits > 1) {
+      const ReduceArgs reduce{static_cast<const float *>(partials_->data()),
+                              bias,
+                              c,
+                              c_lo,
+                              m,
+                              n,
+                              ldc,
+                              static_cast<uint32_t>(mode),
+                              offset,
+                              count,
+                              n_tiles,
+                              splits,
+                              tile_columns};
+      launch(reduce_.get(),
+             rows_config(ceil_div(uint64_t{count} * kTcTileM * out_columns, 256), 256), reduce);
+    }
+  };
+  if (tiles >= kSms) {
+    const uint32_t full = tiles / kSms * kSms;
+    run(0, full, 1);
+    if (tiles > full) {
+      const uint32_t rest = tiles - full;
+      run(full, rest, std::max(1u, std::min(kSms / rest, k_tiles / 2u)));
+    }
+  } else {
+    run(0, tiles, std::max(1u, std::min({kSms / tiles, k_tiles / 4u, 16u})));
+  }
+}
+
+void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_position,
+                        Path path) {
+  const bool tc = path == Path::tf32x3;
+  auto *hidden = static_cast<float *>(hidden_->data());
+  auto *normalized = static_cast<float *>(normalized_->data());
+  auto *normalized_lo = tc ? static_cast<float *>(normalized_lo_->data()) : nullptr;
+  auto *qkv = static_cast<float *>(qkv_->data());
+  auto *attention = static_cast<float *>(attention_->data());
+  auto *attention_lo = tc ? static_cast<float *>(attention_lo_->data()) : nullptr;
+  auto *activated = static_cast<float *>(activated_->data());
+  auto *activated_lo = tc ? static_cast<float *>(activated_lo_->data()) : nullptr;
+  const uint32_t m_tiles = ceil_div(count, 128);
+  auto simt = [&](const Kernel &kernel, const GemmArgs &args, uint32_t n_tiles) {
+    const lr_launch_config_t config{{n_tiles * 256u, m_tiles, 1}, {256, 1, 1}, 0};
+    launch(kernel.get(), config, args);
+  };
+
+  for (size_t layer = 0; layer < model.layers.size(); ++layer) {
+    const LayerView &w = model.layers[layer];
+    launch(rmsnorm_.get(), rows_config(count, 256),
+           NormArgs{hidden, w.attention_norm, normalized, normalized_lo, count, model.epsilon});
+    if (tc) {
+      const LayerMaps &maps = layer_maps_[layer];
+      tc_gemm(kQkvTile, normalized_maps_, maps.qkv, count, kQkv, kHidden, GemmEpilogue::bias, qkv,
+              nullptr, kQkv, w.qkv_bias);
+    } else {
+      simt(gemm_bias_,
+           GemmArgs{normalized, w.qkv, nullptr, w.qkv_bias, qkv, nullptr, count, kQkv, kHidden,
+                    kHidden, kHidden, kQkv},
+           ceil_div(kQkv, 128));
+    }
+    launch(rope_kv_.get(), rows_config(count, 256),
+           RopeArgs{qkv, model.rope_cos, model.rope_sin, w.key_cache, w.value_cache, count,
+                    first_position});
+    // Attention blocks: 32 query rows x one head each, 128 threads.
+    const lr_launch_config_t attention_config{
+        {ceil_div(count, 32) * 128u, qd::kAttentionHeads, 1}, {128, 1, 1}, 0};
+    launch(attend_.get(), attention_config,
+           AttentionArgs{qkv, w.key_cache, w.value_cache, attention, attention_lo, count,
+                         first_position});
+    if (tc) {
+      const LayerMaps &maps = layer_maps_[layer];
+      tc_gemm(kHiddenTile, attention_maps_, maps.o, count, kHidden, kHidden,
+              GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr);
+    } else {
+      simt(gemm_residual_,
+           GemmArgs{attention, w.o, nullptr, nullptr, hidden, nullptr, count, kHidden, kHidden,
+                    kHidden, kHidden, kHidden},
+           ceil_div(kHidden, 128));
+    }
+    launch(rmsnorm_.get(), rows_config(count, 256),
+           NormArgs{hidden, w.mlp_norm, normalized, normalized_lo, count, model.epsilon});
+    if (tc) {
+      const LayerMaps &maps = layer_maps_[layer];
+      tc_gemm(kGateUpTile, normalized_maps_, maps.gate_up, count, kIntermediate, kHidden,
+              GemmEpilogue::swiglu, activated, activated_lo, kIntermediate, nullptr);
+      tc_gemm(kHiddenTile, activated_maps_, maps.down, count, kHidden, kIntermediate,
+              GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr);
+    } else {
+      const float *up = w.gate_up + size_t{kIntermediate} * kHidden;
+      simt(gemm_swiglu_,
+           GemmArgs{normalized, w.gate_up, up, nullptr, activated, nullptr, count, kIntermediate,
+                    kHidden, kHidden, kHidden, kIntermediate},
+           ceil_div(kIntermediate, 128));
+      simt(gemm_residual_,
+           GemmArgs{activated, w.down, nullptr, nullptr, hidden, nullptr, count, kHidden,
+                    kIntermediate, kIntermediate, kIntermediate, kHidden},
+           ceil_div(kHidden, 128));
+    }
+  }
+}
+
+void Prefill::gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, uint32_t n,
+                         uint32_t k, const float *a, const float *b, const float *bias,
+                         float *c) {
+  const bool swiglu = mode == GemmEpilogue::swiglu;
+  if (m == 0 || n == 0 || k == 0 || k % kTcTileK != 0 || n % 32 != 0 || mode == GemmEpilogue::partial ||
+      (tile_columns != 0 && tile_columns != 192 && tile_columns != 224 && tile_columns != 256) ||
+      (swiglu && tile_columns != 0 &&
+       (n % (tile_columns / 2u) != 0 || (tile_columns / 2u) % 32u != 0))) {
+    throw std::invalid_argument("unsupported GEMM check shape");
+  }
+  const uint64_t rows_b = swiglu ? 2ull * n : n;
+  DeviceBuffer a_dev(device_, sizeof(float) * m * k), b_dev(device_, sizeof(float) * rows_b * k);
+  DeviceBuffer c_dev(device_, sizeof(float) * m * n);
+  DeviceBuffer bias_dev(device_, sizeof(float) * n);
+  copy_to_device(a_dev, a, a_dev.size());
+  copy_to_device(b_dev, b, b_dev.size());
+  copy_to_device(c_dev, c, c_dev.size());
+  if (bias != nullptr) {
+    copy_to_device(bias_dev, bias, bias_dev.size());
+  }
+  auto *bias_ptr = bias != nullptr ? static_cast<const float *>(bias_dev.data()) : nullptr;
+  auto *cd = static_cast<float *>(c_dev.data());
+  const uint32_t zero = 0;
+  check(lr_memcpy(device_.get(), error_->data(), &zero, sizeof(zero), LR_MEMCPY_HOST_TO_DEVICE),
+        "lr_memcpy gemm error");
+  if (tile_columns == 0) {
+    const auto *ad = static_cast<const float *>(a_dev.data());
+    const auto *bd = static_cast<const float *>(b_dev.data());
+    const GemmArgs args{ad, bd, swiglu ? bd + size_t{n} * k : nullptr, bias_ptr, cd, nullptr,
+                        m, n, k, k, k, n};
+    const Kernel &kernel = mode == GemmEpilogue::bias       ? gemm_bias_
+                           : mode == GemmEpilogue::residual ? gemm_residual_
+                                                            : gemm_swiglu_;
+    const lr_launch_config_t config{{ceil_div(n, 128) * 256u, ceil_div(m, 128), 1}, {256, 1, 1}, 0};
+    launch(kernel.get(), config, args);
+  } else {
+    if (cudaSetDevice(static_cast<int>(device_.index())) != cudaSuccess) {
+      throw std::runtime_error("cudaSetDevice failed");
+    }
+    DeviceBuffer a_split(device_, 2 * a_dev.size()), b_split(device_, 2 * b_dev.size());
+    auto *ah = static_cast<float *>(a_split.data());
+    auto *bh = static_cast<float *>(b_split.data());
+    const uint64_t a_floats = uint64_t{m} * k, b_floats = rows_b * k;
+    launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(a_floats, 256), kSms * 8), 256),
+           SplitArgs{static_cast<const float *>(a_dev.data()), ah, ah + a_floats, a_floats});
+    launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(b_floats, 256), kSms * 8), 256),
+           SplitArgs{static_cast<const float *>(b_dev.data()), bh, bh + b_floats, b_floats});
+    const TensorMap a_maps[2] = {map_2d(ah, m, k, kTcTileM), map_2d(ah + a_floats, m, k, kTcTileM)};
+    const TensorMap b_maps[2] = {map_2d(bh, rows_b, k, tile_columns / 2u),
+                                 map_2d(bh + b_floats, rows_b, k, tile_columns / 2u)};
+    tc_gemm(tile_columns, a_maps, b_maps, m, n, k, mode, cd, nullptr, n, bias_ptr);
+  }
+  device_.synchronize();
+  copy_to_host(c, c_dev, c_dev.size());
+  uint32_t error = 0;
+  check(lr_memcpy(device_.get(), &error, error_->data(), sizeof(error), LR_MEMCPY_DEVICE_TO_HOST),
+        "lr_memcpy gemm error");
+  if (error != 0) {
+    throw std::runtime_error("prefill tensor-core GEMM gave up waiting (code " +
+                             std::to_string(error) + ")");
+  }
+}
+
+void Prefill::run(const ModelView &model, const uint32_t *tokens, uint32_t count,
+                  uint32_t first_position, Path path, uint64_t weights_generation) {
+  if (count == 0) {
+    return;
+  }
+  if (uint64_t{first_position} + count > model.capacity) {
+    throw std::invalid_argument("prefill exceeds the KV-cache capacity");
+  }
+  if (path != Path::simt && path != Path::tf32x3) {
+    throw std::invalid_argument("unknown prefill path");
+  }
+  for (uint32_t i = 0; i < count; ++i) {
+    if (tokens[i] >= model.vocab) {
+      throw std::invalid_argument("prompt token out of range");
+    }
+  }
+  if (!tokens_ || tokens_->size() < sizeof(uint32_t) * count) {
+    tokens_.reset();
+    tokens_.emplace(allocate(sizeof(uint32_t) * std::max<uint32_t>(count, chunk_)));
+  }
+  // The queue may still run an earlier prefill reading these buffers.
+  device_.synchronize();
+  check(lr_memcpy(device_.get(), tokens_->data(), tokens, sizeof(uint32_t) * count,
+                  LR_MEMCPY_HOST_TO_DEVICE),
+        "lr_memcpy prompt");
+  const uint32_t zero = 0;
+  check(lr_memcpy(device_.get(), error_->data(), &zero, sizeof(zero), LR_MEMCPY_HOST_TO_DEVICE),
+        "lr_memcpy prefill error");
+  if (path == Path::tf32x3) {
+    prepare_tensor_cores(model, weights_generation);
+  }
+  for (uint32_t start = 0; start < count; start += chunk_) {
+    const uint32_t n = std::min(chunk_, count - start);
+    launch(embed_.get(), rows_config(n, 256),
+           EmbedArgs{static_cast<const uint32_t *>(tokens_->data()) + start, model.embeddings,
+                     static_cast<float *>(hidden_->data()), n, model.vocab});
+    run_chunk(model, n, first_position + start, path);
+  }
+  device_.synchronize();
+  uint32_t error = 0;
+  check(lr_memcpy(device_.get(), &error, error_->data(), sizeof(error), LR_MEMCPY_DEVICE_TO_HOST),
+        "lr_memcpy prefill error");
+  if (error != 0) {
+    throw std::runtime_error("prefill tensor-core GEMM gave up waiting (code " +
+                             std::to_string(error) + ")");
+  }
+}
+
+} // namespace lrrt::qwen::prefill

@@ -963,10 +963,18 @@ LRRT_API lr_status_t lr_memcpy(lr_device_t device, void *dst, const void *src,
   if (size == 0) {
     return LR_SUCCESS;
   }
+  // Synchronous in the full sense: earlier work is drained, the copy runs on
+  // the device's (non-blocking) queue and has landed when this returns. A
+  // plain cuMemcpy would run on the legacy stream, which the queues do not
+  // wait for, and may return before a pageable host-to-device DMA or a
+  // device-to-device copy has completed; queue work issued next (a decode
+  // that re-arms its state from a freshly written image) could then read
+  // the old bytes.
   LR_TRY(drain(*state));
-  LR_TRY(cu(g_driver.cuMemcpy_(reinterpret_cast<CUdeviceptr>(dst),
-                               reinterpret_cast<CUdeviceptr>(src), size),
-            "cuMemcpy"));
+  LR_TRY(cu(g_driver.cuMemcpyAsync_(reinterpret_cast<CUdeviceptr>(dst),
+                                    reinterpret_cast<CUdeviceptr>(src), size, state->stream),
+            "cuMemcpyAsync"));
+  LR_TRY(drain(*state));
   count_copy(*state, size, kind);
   return LR_SUCCESS;
 }

@@ -16,6 +16,7 @@ LIB = PACKAGE / "lib"
 RUNTIME_PATH = LIB / "liblrrt.so"
 DRIVER_PATH = LIB / "liblrrt_qwen.so"
 QWEN_CUBIN = LIB / "qwen_stateful_graph.cubin"
+PREFILL_CUBIN = LIB / "qwen_prefill.cubin"
 FIXTURE_CUBIN = LIB / "stateful_graph_fixture.cubin"
 
 u32, u64, f32, vp, cp, sz = C.c_uint32, C.c_uint64, C.c_float, C.c_void_p, C.c_char_p, C.c_size_t
@@ -180,6 +181,10 @@ DRIVER_FUNCTIONS = {
     "lrq_decode": (u32, [vp, P(DecodeRequest), P(RunState), P(u32), u32]),
     "lrq_model_read_state": (u32, [vp, P(RunState)]),
     "lrq_model_ingest_prompt": (u32, [vp, P(u32), u32]),
+    "lrq_model_enable_prefill": (u32, [vp, vp, sz, u32]),
+    "lrq_model_prefill": (u32, [vp, P(u32), u32, u32]),
+    "lrq_model_prefill_at": (u32, [vp, P(u32), u32, u32, u32]),
+    "lrq_prefill_gemm_check": (u32, [vp, u32, u32, u32, u32, u32, vp, vp, vp, vp]),
     "lrq_generate": (u32, [vp, vp, u32, u32, u32, u32, P(u32), P(RunState)]),
     "lrq_model_read": (u32, [vp, u32, u32, vp, sz]),
     "lrq_model_info": (u32, [vp, P(ModelInfo)]),

@@ -29,6 +29,9 @@ PATH_SCHEDULER_PROFILE = 3
 PATH_STAGE_PROFILE = 4
 PATH_GRAPH = 5
 
+PREFILL_SIMT = 0    # FP32 FMA GEMM tiles on the CUDA cores
+PREFILL_TF32X3 = 1  # 3xTF32 tcgen05 tensor-core GEMMs
+
 BUFFERS = {
     "hidden": (0, HIDDEN, np.float32),
     "attention_normalized": (1, HIDDEN, np.float32),
@@ -212,6 +215,42 @@ class Model:
         tokens = (C.c_uint32 * len(prompt))(*prompt)
         N.check(N.driver().lrq_model_ingest_prompt(self.handle, tokens, len(prompt)),
                 "lrq_model_ingest_prompt")
+
+    def enable_prefill(self, max_chunk_tokens: int = 512,
+                       cubin: Optional[bytes] = None) -> None:
+        """Loads the prefill module (lib/qwen_prefill.cubin) into the model."""
+        image = cubin if cubin is not None else N.PREFILL_CUBIN.read_bytes()
+        self._prefill_image = C.create_string_buffer(image, len(image))
+        N.check(N.driver().lrq_model_enable_prefill(self.handle, self._prefill_image,
+                                                    len(image), max_chunk_tokens),
+                "lrq_model_enable_prefill")
+
+    def prefill(self, prompt, path: int = PREFILL_TF32X3) -> None:
+        """Batched prompt ingestion, same contract as ingest_prompt."""
+        tokens = (C.c_uint32 * len(prompt))(*[int(t) for t in prompt])
+        N.check(N.driver().lrq_model_prefill(self.handle, tokens, len(prompt), path),
+                "lrq_model_prefill")
+
+    def prefill_at(self, tokens, first_position: int, path: int = PREFILL_TF32X3) -> None:
+        """K/V rows of `tokens` at positions first_position.. (no hidden staging)."""
+        array = (C.c_uint32 * max(len(tokens), 1))(*[int(t) for t in tokens])
+        N.check(N.driver().lrq_model_prefill_at(self.handle, array, len(tokens),
+                                                first_position, path),
+                "lrq_model_prefill_at")
+
+    def prefill_gemm_check(self, tile_columns: int, mode: int, a: np.ndarray, b: np.ndarray,
+                           c: np.ndarray, bias: Optional[np.ndarray] = None) -> np.ndarray:
+        """One prefill GEMM on host arrays (see lrq_prefill_gemm_check)."""
+        a, b = _f32(a), _f32(b)
+        out = _f32(c).copy()
+        m, k = a.shape
+        n = out.shape[1]
+        bias_array = _f32(bias) if bias is not None else None
+        N.check(N.driver().lrq_prefill_gemm_check(
+            self.handle, tile_columns, mode, m, n, k, _ptr(a), _ptr(b),
+            _ptr(bias_array) if bias_array is not None else None, _ptr(out)),
+            "lrq_prefill_gemm_check")
+        return out
 
     # ---- runs --------------------------------------------------------------
     @staticmethod
