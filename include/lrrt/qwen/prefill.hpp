@@ -81,8 +81,18 @@ struct ReduceArgs {
   uint32_t tile_columns;  // accumulator columns per tile (swiglu: gate + up)
 };
 
+// Split-K partial accumulators of a tensor-core GEMM whose finish is left
+// to the next row kernel: tiles [0, tile_count) of the output's tile grid
+// (n_tiles per 128-row band), [split][tile][128][tile_columns].
+struct PartialTiles {
+  const float *partials; // null: the GEMM wrote its output directly
+  uint32_t splits, n_tiles, tile_count, tile_columns;
+};
+
 // RoPE on the q and k parts of qkv rows [count][1152] at positions
-// first_position + t, then k and v appended to the cache rows.
+// first_position + t, then k and v appended to the cache rows. With
+// qkv_partials set, each row is first finished from the QKV GEMM's partial
+// sums plus qkv_bias and written to qkv.
 struct RopeArgs {
   float *qkv;
   const float *rope_cos; // [capacity][32]
@@ -91,10 +101,27 @@ struct RopeArgs {
   float *value_cache;
   uint32_t count;
   uint32_t first_position;
+  PartialTiles qkv_partials;
+  const float *qkv_bias;
+};
+
+// Row finish of a residual GEMM: hidden[t] += (partial sums of row t), then,
+// when norm_weight is set, out[t] = RMSNorm(hidden[t]) * norm_weight (TF32
+// hi/lo pair when out_lo is set). One block per row.
+struct FinishArgs {
+  PartialTiles partials;
+  float *hidden; // [count][896]
+  uint32_t count;
+  float epsilon;
+  const float *norm_weight;
+  float *out;
+  float *out_lo;
 };
 
 // Causal GQA attention: query row t attends to cache positions
 // 0..first_position + t. out [count][896] (hi part when out_lo is set).
+// Launch: blocks of kAttentionThreads threads over (ceil(count / 32), 14)
+// with kAttentionSharedBytes of dynamic shared memory.
 struct AttentionArgs {
   const float *qkv;
   const float *key_cache;
@@ -104,6 +131,10 @@ struct AttentionArgs {
   uint32_t count;
   uint32_t first_position;
 };
+
+constexpr uint32_t kAttentionThreads = 512;
+constexpr uint32_t kAttentionSharedBytes =
+    4u * (64u * 32u + 4u * (64u * 64u * 2u + 32u * 64u) + 2u * 4u * 32u);
 
 // hi[i] = tf32(x[i]), lo[i] = tf32(x[i] - hi[i]) for i < count.
 struct SplitArgs {

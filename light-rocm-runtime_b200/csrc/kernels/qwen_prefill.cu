@@ -344,76 +344,172 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rmsnorm(pf::NormArgs p
   }
 }
 
+// Sum over splits of one element of a deferred GEMM's partial tiles: row t,
+// column c of the output.
+__device__ __forceinline__ float partial_sum(const pf::PartialTiles &tiles, uint32_t t,
+                                             uint32_t column) {
+  const uint32_t tile = (t / pf::kTcTileM) * tiles.n_tiles + column / tiles.tile_columns;
+  const size_t tile_floats = size_t{pf::kTcTileM} * tiles.tile_columns;
+  const float *at = tiles.partials + size_t{tile} * tile_floats +
+                    size_t{t % pf::kTcTileM} * tiles.tile_columns + column % tiles.tile_columns;
+  const size_t split_stride = size_t{tiles.tile_count} * tile_floats;
+  float sum = at[0];
+  for (uint32_t s = 1; s < tiles.splits; ++s) {
+    sum += at[s * split_stride];
+  }
+  return sum;
+}
+
+// The decode step's RMSNorm of one 896-float row held in shared memory
+// (per-thread strided sum of squares, shared tree, 1/sqrt(mean + eps)).
+__device__ __forceinline__ void row_rmsnorm(const float *x, const float *weight, float epsilon,
+                                            float *out, float *out_lo, size_t at,
+                                            float *partial) {
+  float sum = 0.0f;
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+    sum = fmaf(x[i], x[i], sum);
+  }
+  partial[threadIdx.x] = sum;
+  __syncthreads();
+  for (uint32_t stride = 128; stride != 0; stride >>= 1u) {
+    if (threadIdx.x < stride) {
+      partial[threadIdx.x] += partial[threadIdx.x + stride];
+    }
+    __syncthreads();
+  }
+  const float inverse = 1.0f / sqrtf(partial[0] / static_cast<float>(qd::kHiddenSize) + epsilon);
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+    store_operand(out, out_lo, at + i, x[i] * inverse * weight[i]);
+  }
+}
+
 // RoPE (pairs f and f + 32 of each head) on q and k of every chunk token at
 // position first_position + t, then the cache append of k and v; one block
-// per token.
+// per token. The row is first finished from the QKV GEMM's partial sums when
+// those are given.
 extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p) {
+  __shared__ float row[qd::kPackedQkvSize];
   const uint32_t t = blockIdx.x;
   if (t >= p.count) {
     return;
   }
   const uint32_t position = p.first_position + t;
-  float *row = p.qkv + size_t{t} * qd::kPackedQkvSize;
+  float *qkv = p.qkv + size_t{t} * qd::kPackedQkvSize;
+  for (uint32_t i = threadIdx.x; i < qd::kPackedQkvSize; i += 256u) {
+    row[i] = p.qkv_partials.partials != nullptr ? partial_sum(p.qkv_partials, t, i) + p.qkv_bias[i]
+                                                : qkv[i];
+  }
+  __syncthreads();
   const float *cos_row = p.rope_cos + size_t{position} * qd::kRotarySize;
   const float *sin_row = p.rope_sin + size_t{position} * qd::kRotarySize;
   float *key_row = p.key_cache + size_t{position} * qd::kKvSize;
   float *value_row = p.value_cache + size_t{position} * qd::kKvSize;
   for (uint32_t i = threadIdx.x; i < qd::kRotaryHeads * qd::kRotarySize; i += 256u) {
     const uint32_t head = i / qd::kRotarySize, f = i % qd::kRotarySize;
-    float *base = row + head * qd::kHeadSize;
-    const float x0 = base[f], x1 = base[f + qd::kRotarySize];
+    const uint32_t first = head * qd::kHeadSize + f;
+    const float x0 = row[first], x1 = row[first + qd::kRotarySize];
     const float r0 = x0 * cos_row[f] - x1 * sin_row[f];
     const float r1 = x1 * cos_row[f] + x0 * sin_row[f];
-    base[f] = r0;
-    base[f + qd::kRotarySize] = r1;
-    if (head >= qd::kAttentionHeads) {
-      const uint32_t local = (head - qd::kAttentionHeads) * qd::kHeadSize;
-      key_row[local + f] = r0;
-      key_row[local + f + qd::kRotarySize] = r1;
+    if (head < qd::kAttentionHeads) {
+      qkv[first] = r0;
+      qkv[first + qd::kRotarySize] = r1;
+    } else {
+      const uint32_t local = (head - qd::kAttentionHeads) * qd::kHeadSize + f;
+      key_row[local] = r0;
+      key_row[local + qd::kRotarySize] = r1;
     }
   }
-  const float *value = row + qd::kQuerySize + qd::kKvSize;
   for (uint32_t i = threadIdx.x; i < qd::kKvSize; i += 256u) {
-    value_row[i] = value[i];
+    value_row[i] = row[qd::kQuerySize + qd::kKvSize + i];
+  }
+}
+
+// Residual finish of o_proj / down from their partial sums, then the next
+// RMSNorm of the same row (mlp norm, or the next layer's attention norm).
+extern "C" __global__ void __launch_bounds__(256) prefill_finish_rows(pf::FinishArgs p) {
+  __shared__ float row[qd::kHiddenSize];
+  __shared__ float partial[256];
+  const uint32_t t = blockIdx.x;
+  if (t >= p.count) {
+    return;
+  }
+  float *hidden = p.hidden + size_t{t} * qd::kHiddenSize;
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+    const float value = p.partials.partials != nullptr
+                            ? hidden[i] + partial_sum(p.partials, t, i)
+                            : hidden[i];
+    hidden[i] = value;
+    row[i] = value;
+  }
+  __syncthreads();
+  if (p.norm_weight != nullptr) {
+    row_rmsnorm(row, p.norm_weight, p.epsilon, p.out, p.out_lo, size_t{t} * qd::kHiddenSize,
+                partial);
   }
 }
 
 // Causal GQA attention, register-blocked. Block (x, y) serves 32 query rows
 // of head y (the heaviest row tiles get the lowest block indices) over cache
-// positions 0..first_position + row, in 64-position tiles staged in shared
-// memory. Thread (ty, tx) = (tid / 16, tid % 16) owns query rows
-// 4ty..4ty+3 and, per tile, keys 4tx..4tx+3 of S = Q.K^T / 8 and output dims
-// 4tx..4tx+3 of O; a row's sixteen threads reduce with shuffles. Q and K are
-// stored transposed ([dim][row], [dim][key]) so that both inner loops read
-// broadcast or contiguous float4 values. The softmax is the decode step's
-// online softmax (expf) applied per tile. out[t][head * 64 + d].
-constexpr uint32_t kAttentionRows = 32, kAttentionKeys = 64, kAttentionThreads = 128;
+// positions 0..first_position + row, in 64-position key tiles. Four groups
+// of four warps take every fourth key tile, each with its own shared K/V/P
+// buffers and a named barrier, and their softmax states are merged at the
+// end. In a group, thread (ty, tx) = (tid / 16, tid % 16) owns query rows
+// 4ty..4ty+3 and, per tile, keys 4tx..4tx+3 of S = Q.K^T / 8 and output
+// dims 4tx..4tx+3 of O; a row's sixteen threads reduce with shuffles. Q and
+// K are stored transposed ([dim][row], [dim][key]) so that both inner loops
+// read broadcast or contiguous float4 values. Each group runs the decode
+// step's online softmax (expf) per tile; the merge rescales the groups'
+// partial sums to the common maximum. out[t][head * 64 + d].
+constexpr uint32_t kAttentionRows = 32, kAttentionKeys = 64, kAttentionGroups = 4;
+constexpr uint32_t kAttentionGroupThreads = 128;
+static_assert(kAttentionGroups * kAttentionGroupThreads == pf::kAttentionThreads, "block size");
 
-extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attention(pf::AttentionArgs p) {
-  __shared__ __align__(16) float qt[qd::kHeadSize][kAttentionRows];   // [d][row]
-  __shared__ __align__(16) float kt[qd::kHeadSize][kAttentionKeys];   // [d][key]
-  __shared__ __align__(16) float vs[kAttentionKeys][qd::kHeadSize];   // [key][d]
-  __shared__ __align__(16) float ps[kAttentionRows][kAttentionKeys];  // [row][key]
-  const uint32_t tid = threadIdx.x;
+struct AttentionGroupShared {
+  float kt[qd::kHeadSize][kAttentionKeys];  // [d][key]
+  float vs[kAttentionKeys][qd::kHeadSize];  // [key][d]
+  float ps[kAttentionRows][kAttentionKeys]; // [row][key]
+};
+
+struct AttentionShared {
+  float qt[qd::kHeadSize][kAttentionRows];  // [d][row]
+  AttentionGroupShared group[kAttentionGroups];
+  float maximum[kAttentionGroups][kAttentionRows];
+  float denominator[kAttentionGroups][kAttentionRows];
+};
+
+__device__ __forceinline__ void group_barrier(uint32_t group) {
+  asm volatile("bar.sync %0, %1;" ::"r"(group + 1u), "r"(kAttentionGroupThreads) : "memory");
+}
+
+static_assert(sizeof(AttentionShared) == pf::kAttentionSharedBytes, "shared layout");
+
+extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
+    prefill_attention(pf::AttentionArgs p) {
+  extern __shared__ __align__(16) unsigned char attention_raw[];
+  AttentionShared &sh = *reinterpret_cast<AttentionShared *>(attention_raw);
+  const uint32_t g = threadIdx.x / kAttentionGroupThreads;
+  const uint32_t tid = threadIdx.x % kAttentionGroupThreads;
   const uint32_t ty = tid / 16u, tx = tid % 16u;
-  const uint32_t head = blockIdx.y, group = head / qd::kQueriesPerKvHead;
+  AttentionGroupShared &gs = sh.group[g];
+  const uint32_t head = blockIdx.y, kv_group = head / qd::kQueriesPerKvHead;
   const uint32_t t0 = (gridDim.x - 1u - blockIdx.x) * kAttentionRows;
   if (t0 >= p.count) {
     return;
   }
   const uint32_t rows = min(kAttentionRows, p.count - t0);
-  for (uint32_t i = tid; i < kAttentionRows * qd::kHeadSize / 4u; i += kAttentionThreads) {
+  for (uint32_t i = threadIdx.x; i < kAttentionRows * qd::kHeadSize / 4u; i += pf::kAttentionThreads) {
     const uint32_t row = i % kAttentionRows, d = (i / kAttentionRows) * 4u;
     float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
     if (row < rows) {
       q = *reinterpret_cast<const float4 *>(p.qkv + size_t{t0 + row} * qd::kPackedQkvSize +
                                             head * qd::kHeadSize + d);
     }
-    qt[d][row] = q.x;
-    qt[d + 1][row] = q.y;
-    qt[d + 2][row] = q.z;
-    qt[d + 3][row] = q.w;
+    sh.qt[d][row] = q.x;
+    sh.qt[d + 1][row] = q.y;
+    sh.qt[d + 2][row] = q.z;
+    sh.qt[d + 3][row] = q.w;
   }
+  __syncthreads();
   const uint32_t last = p.first_position + t0 + rows - 1u;
   uint32_t position[4];
   float maximum[4], denominator[4], acc[4][4];
@@ -427,10 +523,10 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
       acc[i][j] = 0.0f;
     }
   }
-  const size_t kv_offset = size_t{group} * qd::kHeadSize;
-  for (uint32_t base = 0; base <= last; base += kAttentionKeys) {
-    __syncthreads(); // the previous tile's reads are done (and qt is written)
-    for (uint32_t i = tid; i < kAttentionKeys * qd::kHeadSize / 4u; i += kAttentionThreads) {
+  const size_t kv_offset = size_t{kv_group} * qd::kHeadSize;
+  for (uint32_t base = g * kAttentionKeys; base <= last; base += kAttentionGroups * kAttentionKeys) {
+    group_barrier(g); // the group's previous tile reads are done
+    for (uint32_t i = tid; i < kAttentionKeys * qd::kHeadSize / 4u; i += kAttentionGroupThreads) {
       const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
       float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
       if (base + key <= last) {
@@ -438,13 +534,13 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
         k = *reinterpret_cast<const float4 *>(p.key_cache + at);
         v = *reinterpret_cast<const float4 *>(p.value_cache + at);
       }
-      kt[d][key] = k.x;
-      kt[d + 1][key] = k.y;
-      kt[d + 2][key] = k.z;
-      kt[d + 3][key] = k.w;
-      *reinterpret_cast<float4 *>(&vs[key][d]) = v;
+      gs.kt[d][key] = k.x;
+      gs.kt[d + 1][key] = k.y;
+      gs.kt[d + 2][key] = k.z;
+      gs.kt[d + 3][key] = k.w;
+      *reinterpret_cast<float4 *>(&gs.vs[key][d]) = v;
     }
-    __syncthreads();
+    group_barrier(g);
     float score[4][4];
 #pragma unroll
     for (uint32_t i = 0; i < 4; ++i) {
@@ -455,8 +551,8 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
     }
 #pragma unroll 8
     for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
-      const float4 q = *reinterpret_cast<const float4 *>(&qt[d][4u * ty]);
-      const float4 k = *reinterpret_cast<const float4 *>(&kt[d][4u * tx]);
+      const float4 q = *reinterpret_cast<const float4 *>(&sh.qt[d][4u * ty]);
+      const float4 k = *reinterpret_cast<const float4 *>(&gs.kt[d][4u * tx]);
       const float qv[4] = {q.x, q.y, q.z, q.w}, kv[4] = {k.x, k.y, k.z, k.w};
 #pragma unroll
       for (uint32_t i = 0; i < 4; ++i) {
@@ -479,8 +575,8 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
       for (uint32_t offset = 1; offset < 16; offset <<= 1u) {
         tile_maximum = fmaxf(tile_maximum, __shfl_xor_sync(kFullMask, tile_maximum, offset));
       }
-      // A row whose positions all lie after this tile keeps a -inf maximum
-      // only before its first key; then its scale is 1 and its weights 0.
+      // Rows whose positions all precede this tile's keys keep their state:
+      // scale 1, weights 0 (also while their maximum is still -inf).
       const float next = fmaxf(maximum[i], tile_maximum);
       const bool live = next != -INFINITY;
       scale[i] = live ? expf(maximum[i] - next) : 1.0f;
@@ -496,7 +592,7 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
       }
       denominator[i] = denominator[i] * scale[i] + sum;
       maximum[i] = next;
-      *reinterpret_cast<float4 *>(&ps[4u * ty + i][4u * tx]) =
+      *reinterpret_cast<float4 *>(&gs.ps[4u * ty + i][4u * tx]) =
           make_float4(weights[0], weights[1], weights[2], weights[3]);
     }
 #pragma unroll
@@ -512,7 +608,7 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
       float pv[4][4];
 #pragma unroll
       for (uint32_t i = 0; i < 4; ++i) {
-        const float4 w = *reinterpret_cast<const float4 *>(&ps[4u * ty + i][key]);
+        const float4 w = *reinterpret_cast<const float4 *>(&gs.ps[4u * ty + i][key]);
         pv[i][0] = w.x;
         pv[i][1] = w.y;
         pv[i][2] = w.z;
@@ -520,7 +616,7 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
       }
 #pragma unroll
       for (uint32_t e = 0; e < 4; ++e) {
-        const float4 v = *reinterpret_cast<const float4 *>(&vs[key + e][4u * tx]);
+        const float4 v = *reinterpret_cast<const float4 *>(&gs.vs[key + e][4u * tx]);
         const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (uint32_t i = 0; i < 4; ++i) {
@@ -532,14 +628,53 @@ extern "C" __global__ void __launch_bounds__(kAttentionThreads) prefill_attentio
       }
     }
   }
+  // Merge: groups 1..3 publish (maximum, denominator, acc) in their own
+  // buffers (acc in kt, now free), group 0 rescales all four to the common
+  // maximum. A group that saw no key keeps maximum -inf and contributes 0.
+  __syncthreads();
+  if (tx == 0) {
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+      sh.maximum[g][4u * ty + i] = maximum[i];
+      sh.denominator[g][4u * ty + i] = denominator[i];
+    }
+  }
+  if (g != 0) {
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+      *reinterpret_cast<float4 *>(&gs.kt[4u * ty + i][4u * tx]) =
+          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    }
+  }
+  __syncthreads();
+  if (g != 0) {
+    return;
+  }
 #pragma unroll
   for (uint32_t i = 0; i < 4; ++i) {
     const uint32_t row = 4u * ty + i;
+    float common = sh.maximum[0][row];
+    for (uint32_t h = 1; h < kAttentionGroups; ++h) {
+      common = fmaxf(common, sh.maximum[h][row]);
+    }
+    const float own = expf(sh.maximum[0][row] - common);
+    float total = sh.denominator[0][row] * own;
+    float out[4] = {acc[i][0] * own, acc[i][1] * own, acc[i][2] * own, acc[i][3] * own};
+    for (uint32_t h = 1; h < kAttentionGroups; ++h) {
+      const float m = sh.maximum[h][row];
+      const float weight = m != -INFINITY ? expf(m - common) : 0.0f;
+      total += sh.denominator[h][row] * weight;
+      const float4 a = *reinterpret_cast<const float4 *>(&sh.group[h].kt[row][4u * tx]);
+      out[0] += a.x * weight;
+      out[1] += a.y * weight;
+      out[2] += a.z * weight;
+      out[3] += a.w * weight;
+    }
     if (row < rows) {
       const size_t at = size_t{t0 + row} * qd::kQuerySize + head * qd::kHeadSize + 4u * tx;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        store_operand(p.out, p.out_lo, at + j, acc[i][j] / denominator[i]);
+        store_operand(p.out, p.out_lo, at + j, out[j] / total);
       }
     }
   }

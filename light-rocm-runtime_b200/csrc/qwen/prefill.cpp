@@ -93,7 +93,8 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
       gemm_swiglu_(module_.kernel("prefill_gemm_swiglu")),
       tc_n192_(module_.kernel("prefill_tc_gemm_n192")),
       tc_n224_(module_.kernel("prefill_tc_gemm_n224")),
-      tc_n256_(module_.kernel("prefill_tc_gemm_n256")), chunk_(max_chunk_tokens) {
+      tc_n256_(module_.kernel("prefill_tc_gemm_n256")),
+      finish_rows_(module_.kernel("prefill_finish_rows")), chunk_(max_chunk_tokens) {
   if (chunk_ == 0 || chunk_ > 8192) {
     throw std::invalid_argument("prefill chunk must be 1..8192 tokens");
   }
@@ -175,13 +176,16 @@ void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_gene
 }
 
 // One 3xTF32 GEMM C = A . B^T over m chunk rows with tile_columns-wide
-// tensor-core tiles. Whole waves of kSms tiles run data-parallel with the
-// epilogue in the GEMM; the tiles of a last partial wave (or all tiles, when
-// there are fewer than kSms) are split along K so that the launch fills the
-// SMs, and prefill_reduce sums their partials in split order.
-void Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b, uint32_t m,
-                      uint32_t n, uint32_t k, GemmEpilogue mode, float *c, float *c_lo,
-                      uint32_t ldc, const float *bias) {
+// tensor-core tiles. With `defer` and fewer tiles than SMs, every tile runs
+// split along K into partial accumulators and the caller's next row kernel
+// finishes them (the returned PartialTiles). Otherwise whole waves of kSms
+// tiles run data-parallel with the epilogue in the GEMM, and the tiles of a
+// last partial wave (or all tiles, when there are fewer than kSms) are split
+// along K so that the launch fills the SMs, and prefill_reduce sums their
+// partials in split order.
+PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b,
+                              uint32_t m, uint32_t n, uint32_t k, GemmEpilogue mode, float *c,
+                              float *c_lo, uint32_t ldc, const float *bias, bool defer) {
   const bool swiglu = mode == GemmEpilogue::swiglu;
   const uint32_t out_columns = swiglu ? tile_columns / 2u : tile_columns;
   const uint32_t n_tiles = ceil_div(n, out_columns);
@@ -201,45 +205,43 @@ void Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap
   args.n_gate_offset = swiglu ? n : 0u;
   args.wait_limit_ms = kWaitLimitMs;
   args.error = static_cast<uint32_t *>(error_->data());
-  auto run = [&](uint32_t offset, uint32_t count, uint32_t splits) {
+  auto *partials = static_cast<float *>(partials_->data());
+  auto run = [&](uint32_t offset, uint32_t count, uint32_t splits, bool finish) {
+    const bool partial = splits > 1 || !finish;
     args.tile_offset = offset;
     args.tile_count = count;
     args.splits = splits;
-    args.mode = static_cast<uint32_t>(splits > 1 ? GemmEpilogue::partial : mode);
-    args.c = splits > 1 ? static_cast<float *>(partials_->data()) : c;
-    args.c_lo = splits > 1 ? nullptr : c_lo;
+    args.mode = static_cast<uint32_t>(partial ? GemmEpilogue::partial : mode);
+    args.c = partial ? partials : c;
+    args.c_lo = partial ? nullptr : c_lo;
     args.bias = bias;
     const lr_launch_config_t config{
         {count * kTcThreads, 1, splits}, {kTcThreads, 1, 1}, tc_shared_bytes(tile_columns)};
     launch(kernel.get(), config, args);
-    if (splits > 1) {
-      const ReduceArgs reduce{static_cast<const float *>(partials_->data()),
-                              bias,
-                              c,
-                              c_lo,
-                              m,
-                              n,
-                              ldc,
-                              static_cast<uint32_t>(mode),
-                              offset,
-                              count,
-                              n_tiles,
-                              splits,
-                              tile_columns};
+    if (partial && finish) {
+      const ReduceArgs reduce{partials, bias,    c,        c_lo,   m,
+                              n,        ldc,     static_cast<uint32_t>(mode),
+                              offset,   count,   n_tiles,  splits, tile_columns};
       launch(reduce_.get(),
              rows_config(ceil_div(uint64_t{count} * kTcTileM * out_columns, 256), 256), reduce);
     }
   };
+  const uint32_t small_splits = std::max(1u, std::min({kSms / std::max(tiles, 1u), k_tiles / 4u, 16u}));
+  if (defer && !swiglu && tiles <= kSms) {
+    run(0, tiles, small_splits, false);
+    return PartialTiles{partials, small_splits, n_tiles, tiles, tile_columns};
+  }
   if (tiles >= kSms) {
     const uint32_t full = tiles / kSms * kSms;
-    run(0, full, 1);
+    run(0, full, 1, true);
     if (tiles > full) {
       const uint32_t rest = tiles - full;
-      run(full, rest, std::max(1u, std::min(kSms / rest, k_tiles / 2u)));
+      run(full, rest, std::max(1u, std::min(kSms / rest, k_tiles / 2u)), true);
     }
   } else {
-    run(0, tiles, std::max(1u, std::min({kSms / tiles, k_tiles / 4u, 16u})));
+    run(0, tiles, small_splits, true);
   }
+  return PartialTiles{nullptr, 0, 0, 0, 0};
 }
 
 void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_position,
@@ -254,19 +256,30 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
   auto *activated = static_cast<float *>(activated_->data());
   auto *activated_lo = tc ? static_cast<float *>(activated_lo_->data()) : nullptr;
   const uint32_t m_tiles = ceil_div(count, 128);
+  const PartialTiles direct{nullptr, 0, 0, 0, 0};
   auto simt = [&](const Kernel &kernel, const GemmArgs &args, uint32_t n_tiles) {
     const lr_launch_config_t config{{n_tiles * 256u, m_tiles, 1}, {256, 1, 1}, 0};
     launch(kernel.get(), config, args);
   };
+  // Residual finish of o_proj / down (from partial sums, when deferred) and
+  // the next RMSNorm of the same rows.
+  auto finish = [&](const PartialTiles &partials, const float *norm_weight) {
+    launch(finish_rows_.get(), rows_config(count, 256),
+           FinishArgs{partials, hidden, count, model.epsilon, norm_weight, normalized,
+                      normalized_lo});
+  };
 
+  launch(rmsnorm_.get(), rows_config(count, 256),
+         NormArgs{hidden, model.layers[0].attention_norm, normalized, normalized_lo, count,
+                  model.epsilon});
   for (size_t layer = 0; layer < model.layers.size(); ++layer) {
     const LayerView &w = model.layers[layer];
-    launch(rmsnorm_.get(), rows_config(count, 256),
-           NormArgs{hidden, w.attention_norm, normalized, normalized_lo, count, model.epsilon});
+    const float *next_norm =
+        layer + 1 < model.layers.size() ? model.layers[layer + 1].attention_norm : nullptr;
+    PartialTiles qkv_partials = direct;
     if (tc) {
-      const LayerMaps &maps = layer_maps_[layer];
-      tc_gemm(kQkvTile, normalized_maps_, maps.qkv, count, kQkv, kHidden, GemmEpilogue::bias, qkv,
-              nullptr, kQkv, w.qkv_bias);
+      qkv_partials = tc_gemm(kQkvTile, normalized_maps_, layer_maps_[layer].qkv, count, kQkv,
+                             kHidden, GemmEpilogue::bias, qkv, nullptr, kQkv, w.qkv_bias, true);
     } else {
       simt(gemm_bias_,
            GemmArgs{normalized, w.qkv, nullptr, w.qkv_bias, qkv, nullptr, count, kQkv, kHidden,
@@ -275,32 +288,32 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
     }
     launch(rope_kv_.get(), rows_config(count, 256),
            RopeArgs{qkv, model.rope_cos, model.rope_sin, w.key_cache, w.value_cache, count,
-                    first_position});
-    // Attention blocks: 32 query rows x one head each, 128 threads.
+                    first_position, qkv_partials, w.qkv_bias});
+    // Attention blocks: 32 query rows x one head each.
     const lr_launch_config_t attention_config{
-        {ceil_div(count, 32) * 128u, qd::kAttentionHeads, 1}, {128, 1, 1}, 0};
+        {ceil_div(count, 32) * kAttentionThreads, qd::kAttentionHeads, 1},
+        {kAttentionThreads, 1, 1},
+        kAttentionSharedBytes};
     launch(attend_.get(), attention_config,
            AttentionArgs{qkv, w.key_cache, w.value_cache, attention, attention_lo, count,
                          first_position});
     if (tc) {
-      const LayerMaps &maps = layer_maps_[layer];
-      tc_gemm(kHiddenTile, attention_maps_, maps.o, count, kHidden, kHidden,
-              GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr);
+      finish(tc_gemm(kHiddenTile, attention_maps_, layer_maps_[layer].o, count, kHidden, kHidden,
+                     GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr, true),
+             w.mlp_norm);
+      tc_gemm(kGateUpTile, normalized_maps_, layer_maps_[layer].gate_up, count, kIntermediate,
+              kHidden, GemmEpilogue::swiglu, activated, activated_lo, kIntermediate, nullptr,
+              false);
+      finish(tc_gemm(kHiddenTile, activated_maps_, layer_maps_[layer].down, count, kHidden,
+                     kIntermediate, GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr,
+                     true),
+             next_norm);
     } else {
       simt(gemm_residual_,
            GemmArgs{attention, w.o, nullptr, nullptr, hidden, nullptr, count, kHidden, kHidden,
                     kHidden, kHidden, kHidden},
            ceil_div(kHidden, 128));
-    }
-    launch(rmsnorm_.get(), rows_config(count, 256),
-           NormArgs{hidden, w.mlp_norm, normalized, normalized_lo, count, model.epsilon});
-    if (tc) {
-      const LayerMaps &maps = layer_maps_[layer];
-      tc_gemm(kGateUpTile, normalized_maps_, maps.gate_up, count, kIntermediate, kHidden,
-              GemmEpilogue::swiglu, activated, activated_lo, kIntermediate, nullptr);
-      tc_gemm(kHiddenTile, activated_maps_, maps.down, count, kHidden, kIntermediate,
-              GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr);
-    } else {
+      finish(direct, w.mlp_norm);
       const float *up = w.gate_up + size_t{kIntermediate} * kHidden;
       simt(gemm_swiglu_,
            GemmArgs{normalized, w.gate_up, up, nullptr, activated, nullptr, count, kIntermediate,
@@ -310,6 +323,9 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
            GemmArgs{activated, w.down, nullptr, nullptr, hidden, nullptr, count, kHidden,
                     kIntermediate, kIntermediate, kIntermediate, kHidden},
            ceil_div(kHidden, 128));
+      if (next_norm != nullptr) {
+        finish(direct, next_norm);
+      }
     }
   }
 }
@@ -364,7 +380,7 @@ void Prefill::gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, u
     const TensorMap a_maps[2] = {map_2d(ah, m, k, kTcTileM), map_2d(ah + a_floats, m, k, kTcTileM)};
     const TensorMap b_maps[2] = {map_2d(bh, rows_b, k, tile_columns / 2u),
                                  map_2d(bh + b_floats, rows_b, k, tile_columns / 2u)};
-    tc_gemm(tile_columns, a_maps, b_maps, m, n, k, mode, cd, nullptr, n, bias_ptr);
+    tc_gemm(tile_columns, a_maps, b_maps, m, n, k, mode, cd, nullptr, n, bias_ptr, false);
   }
   device_.synchronize();
   copy_to_host(c, c_dev, c_dev.size());

@@ -71,14 +71,14 @@ private:
   DeviceBuffer allocate(size_t bytes);
   void prepare_tensor_cores(const ModelView &model, uint64_t weights_generation);
   void run_chunk(const ModelView &model, uint32_t count, uint32_t first_position, Path path);
-  void tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b, uint32_t m,
-               uint32_t n, uint32_t k, GemmEpilogue mode, float *c, float *c_lo, uint32_t ldc,
-               const float *bias);
+  PartialTiles tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b, uint32_t m,
+                       uint32_t n, uint32_t k, GemmEpilogue mode, float *c, float *c_lo,
+                       uint32_t ldc, const float *bias, bool defer);
 
   Device device_;
   Module module_;
   Kernel embed_, rmsnorm_, rope_kv_, attend_, reduce_, split_, gemm_bias_, gemm_residual_,
-      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_;
+      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, finish_rows_;
   uint32_t chunk_;
   uint64_t device_bytes_ = 0;
 
