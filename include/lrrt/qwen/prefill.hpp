@@ -50,7 +50,8 @@ enum class GemmEpilogue : uint32_t {
   bias = 0,     // c = acc + bias[n]                            (QKV)
   residual = 1, // c += acc                                      (o_proj, down)
   swiglu = 2,   // c = silu(acc(gate)) * acc(up)                 (gate/up)
-  partial = 3,  // c[split] = acc  (split-K partial sums, [splits][m][ldc])
+  partial = 3,  // compact split-K partial accumulators, finished by prefill_reduce
+  store = 4,    // c = acc                                        (LM-head logits)
 };
 
 // SIMT FP32 GEMM (mode bias, residual or swiglu): A [m][k] (lda),
@@ -103,6 +104,11 @@ struct RopeArgs {
   uint32_t first_position;
   PartialTiles qkv_partials;
   const float *qkv_bias;
+  // Batched decode: row t is stream t at position positions[t], whose cache
+  // rows start stream_stride floats after stream t - 1's (null: prompt rows
+  // at first_position + t of one cache).
+  const uint32_t *positions;
+  uint64_t stream_stride;
 };
 
 // Row finish of a residual GEMM: hidden[t] += (partial sums of row t), then,
@@ -130,6 +136,40 @@ struct AttentionArgs {
   float *out_lo;
   uint32_t count;
   uint32_t first_position;
+};
+
+// Batched decode attention: one query row per stream. Block (s, g, b)
+// covers key positions [s * chunk, (s + 1) * chunk) of stream b's cache for
+// the seven query heads of KV group g and writes a partial softmax state
+// (maximum, sum, acc[64]) per head to `partials`
+// [b][g][split][7][kDecodePartialStride]; batch_attention_merge combines
+// the splits into out[b][head * 64 + d] (TF32 pair when out_lo is set).
+constexpr uint32_t kDecodePartialStride = 66;
+struct DecodeAttentionArgs {
+  const float *qkv;         // [streams][1152], q rotated
+  const float *key_cache;   // stream b's cache at key_cache + b * stream_stride
+  const float *value_cache;
+  uint64_t stream_stride;
+  const uint32_t *positions; // attend to 0..positions[b]
+  float *partials;
+  float *out;
+  float *out_lo;
+  uint32_t streams, splits, chunk;
+};
+
+// Greedy step end: per stream row, the first index of the largest logit
+// (lower index on ties, as the decode step's reduce), appended to
+// tokens[b * token_stride + generated[b]] and stored as the stream's next
+// input token; positions[b] and generated[b] advance.
+struct ArgmaxArgs {
+  const float *logits;       // [streams][vocab]
+  uint32_t vocab, streams;
+  uint32_t *next_tokens;     // [streams]
+  uint32_t *positions;
+  uint32_t *generated;
+  uint32_t *tokens;
+  uint32_t token_stride;
+  float *logit_values;       // [streams]: the chosen logit
 };
 
 constexpr uint32_t kAttentionThreads = 512;

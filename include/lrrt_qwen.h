@@ -253,6 +253,46 @@ LRRT_API lr_status_t lrq_prefill_gemm_check(lrq_model_t *model, uint32_t tile_co
                                             float *c);
 
 /*
+ * Batched multi-stream greedy decode on one GPU (BASELINE config 4's
+ * per-GPU batch; no counterpart in the reference, whose ABI decodes one
+ * stream per DecodeState). `streams` independent streams (at most the
+ * prefill chunk size) each own a KV cache of `capacity` positions (at most
+ * the model's cache_capacity), a position and a next input token; they
+ * share the model's weights, so one decode step streams the weights once
+ * for every stream. A step runs the prefill module's kernels over one row
+ * per stream (3xTF32 GEMMs, RoPE + KV append, split decode attention over
+ * each stream's own cache, the LM head and a greedy argmax with the
+ * lower-index tie rule) as one CUDA graph replayed per token. Needs
+ * lrq_model_enable_prefill; destroy batches before re-enabling the prefill
+ * (lrq_model_destroy destroys any that remain).
+ *
+ * lrq_batch_prefill: stream's prompt, lrq_model_prefill's contract
+ *   (positions 0..count-2 into the stream's cache; prompt[count-1] is the
+ *   stream's next input token, at position count-1).
+ * lrq_batch_decode: `steps` (<= max_tokens) greedy tokens of every stream,
+ *   tokens[stream * steps + i]; last_logits (optional, [streams]) receives
+ *   each stream's last chosen logit. Positions advance by `steps`; a stream
+ *   never prefilled starts from token 0 at position 0. Waits for the device.
+ * Logits match single-stream decoding to FP32 rounding (GEMM summation
+ * order), not bit for bit.
+ */
+typedef struct lrq_batch_t lrq_batch_t;
+
+LRRT_API lr_status_t lrq_batch_create(lrq_model_t *model, uint32_t streams, uint32_t capacity,
+                                      uint32_t max_tokens, lrq_batch_t **batch);
+LRRT_API lr_status_t lrq_batch_destroy(lrq_batch_t *batch);
+LRRT_API lr_status_t lrq_batch_prefill(lrq_batch_t *batch, uint32_t stream,
+                                       const uint32_t *prompt, uint32_t count, uint32_t path);
+LRRT_API lr_status_t lrq_batch_decode(lrq_batch_t *batch, uint32_t steps, uint32_t *tokens,
+                                      float *last_logits);
+/* Cache rows [0, positions) of one stream and layer, [positions][128] each
+ * (keys or values may be NULL). */
+LRRT_API lr_status_t lrq_batch_read_cache(lrq_batch_t *batch, uint32_t stream, uint32_t layer,
+                                          uint32_t positions, float *keys, float *values);
+LRRT_API lr_status_t lrq_batch_position(lrq_batch_t *batch, uint32_t stream,
+                                        uint32_t *position);
+
+/*
  * End-to-end generate from host memory: copies the host hidden vector (or,
  * when hidden is NULL, stages the embedding of start_token) to the device,
  * runs the compiled path and copies the generated tokens back into `tokens`.

@@ -277,7 +277,9 @@ template <uint32_t kStages> struct TcShared {
 __device__ __forceinline__ void finish_element(const float *bias, float *c, float *c_lo,
                                                size_t at, uint32_t column, uint32_t mode,
                                                float value, float up) {
-  if (mode == static_cast<uint32_t>(pf::GemmEpilogue::bias)) {
+  if (mode == static_cast<uint32_t>(pf::GemmEpilogue::store)) {
+    c[at] = value;
+  } else if (mode == static_cast<uint32_t>(pf::GemmEpilogue::bias)) {
     c[at] = value + bias[column];
   } else if (mode == static_cast<uint32_t>(pf::GemmEpilogue::residual)) {
     c[at] = c[at] + value;
@@ -393,7 +395,8 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p
   if (t >= p.count) {
     return;
   }
-  const uint32_t position = p.first_position + t;
+  const uint32_t position = p.positions != nullptr ? p.positions[t] : p.first_position + t;
+  const size_t stream_offset = p.positions != nullptr ? t * p.stream_stride : 0;
   float *qkv = p.qkv + size_t{t} * qd::kPackedQkvSize;
   for (uint32_t i = threadIdx.x; i < qd::kPackedQkvSize; i += 256u) {
     row[i] = p.qkv_partials.partials != nullptr ? partial_sum(p.qkv_partials, t, i) + p.qkv_bias[i]
@@ -402,8 +405,8 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p
   __syncthreads();
   const float *cos_row = p.rope_cos + size_t{position} * qd::kRotarySize;
   const float *sin_row = p.rope_sin + size_t{position} * qd::kRotarySize;
-  float *key_row = p.key_cache + size_t{position} * qd::kKvSize;
-  float *value_row = p.value_cache + size_t{position} * qd::kKvSize;
+  float *key_row = p.key_cache + stream_offset + size_t{position} * qd::kKvSize;
+  float *value_row = p.value_cache + stream_offset + size_t{position} * qd::kKvSize;
   for (uint32_t i = threadIdx.x; i < qd::kRotaryHeads * qd::kRotarySize; i += 256u) {
     const uint32_t head = i / qd::kRotarySize, f = i % qd::kRotarySize;
     const uint32_t first = head * qd::kHeadSize + f;
@@ -926,4 +929,186 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
     prefill_tc_gemm_n256(const __grid_constant__ pf::TcGemmArgs p) {
   tc_gemm<256>(p);
+}
+
+// ------------------------------------------------------- batched decode --
+
+// Decode attention of one query row per stream, split over key positions.
+// Block (s, g, b): warp h < 7 serves query head 7g + h; keys in 64-position
+// tiles of [s * chunk, min((s + 1) * chunk, positions[b] + 1)), K staged
+// transposed so lane l scores keys l and l + 32 against the warp's query
+// (held in registers); the decode step's online softmax (scale 1/8, expf)
+// per tile; lane l accumulates dims l and l + 32 of P.V.
+extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAttentionArgs p) {
+  __shared__ float kt[qd::kHeadSize][kAttentionKeys + 1]; // [d][key]
+  __shared__ float vs[kAttentionKeys][qd::kHeadSize];     // [key][d]
+  const uint32_t split = blockIdx.x, group = blockIdx.y, b = blockIdx.z;
+  const uint32_t warp = threadIdx.x >> 5u, lane = threadIdx.x & 31u;
+  const uint32_t head = group * qd::kQueriesPerKvHead + warp;
+  const uint32_t last = p.positions[b];
+  const uint32_t begin = split * p.chunk;
+  const uint32_t end = min(begin + p.chunk, last + 1u);
+  float q[qd::kHeadSize];
+  if (warp < qd::kQueriesPerKvHead) {
+    const float *row = p.qkv + size_t{b} * qd::kPackedQkvSize + head * qd::kHeadSize;
+#pragma unroll
+    for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
+      q[d] = row[d];
+    }
+  }
+  const float *keys = p.key_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
+  const float *values = p.value_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
+  float maximum = -INFINITY, denominator = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+  for (uint32_t base = begin; base < end; base += kAttentionKeys) {
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < kAttentionKeys * qd::kHeadSize / 4u; i += 256u) {
+      const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
+      float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+      if (base + key < end) {
+        const size_t at = size_t{base + key} * qd::kKvSize + d;
+        k = *reinterpret_cast<const float4 *>(keys + at);
+        v = *reinterpret_cast<const float4 *>(values + at);
+      }
+      kt[d][key] = k.x;
+      kt[d + 1][key] = k.y;
+      kt[d + 2][key] = k.z;
+      kt[d + 3][key] = k.w;
+      *reinterpret_cast<float4 *>(&vs[key][d]) = v;
+    }
+    __syncthreads();
+    if (warp < qd::kQueriesPerKvHead) {
+      float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+      for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
+        s0 = fmaf(q[d], kt[d][lane], s0);
+        s1 = fmaf(q[d], kt[d][lane + 32u], s1);
+      }
+      s0 = base + lane < end ? s0 * 0.125f : -INFINITY;
+      s1 = base + lane + 32u < end ? s1 * 0.125f : -INFINITY;
+      float tile_maximum = fmaxf(s0, s1);
+#pragma unroll
+      for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
+        tile_maximum = fmaxf(tile_maximum, __shfl_xor_sync(kFullMask, tile_maximum, offset));
+      }
+      const float next = fmaxf(maximum, tile_maximum); // finite: key `base` is in range
+      const float scale = expf(maximum - next);
+      const float w0 = expf(s0 - next), w1 = expf(s1 - next);
+      float sum = w0 + w1;
+#pragma unroll
+      for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
+        sum += __shfl_xor_sync(kFullMask, sum, offset);
+      }
+      denominator = denominator * scale + sum;
+      maximum = next;
+      acc0 *= scale;
+      acc1 *= scale;
+#pragma unroll 8
+      for (uint32_t key = 0; key < 32u; ++key) {
+        const float wa = __shfl_sync(kFullMask, w0, key);
+        const float wb = __shfl_sync(kFullMask, w1, key);
+        acc0 = fmaf(wa, vs[key][lane], acc0);
+        acc1 = fmaf(wa, vs[key][lane + 32u], acc1);
+        acc0 = fmaf(wb, vs[key + 32u][lane], acc0);
+        acc1 = fmaf(wb, vs[key + 32u][lane + 32u], acc1);
+      }
+    }
+  }
+  if (warp < qd::kQueriesPerKvHead) {
+    float *out = p.partials +
+                 ((size_t{b} * qd::kKvHeads + group) * p.splits + split) * qd::kQueriesPerKvHead *
+                     pf::kDecodePartialStride +
+                 size_t{warp} * pf::kDecodePartialStride;
+    out[lane] = acc0;
+    out[lane + 32u] = acc1;
+    if (lane == 0) {
+      out[64] = maximum;     // -inf when the split holds no key of this stream
+      out[65] = denominator; // 0 then
+    }
+  }
+}
+
+// Combines a stream's split partial states per head: rescale to the common
+// maximum, sum, divide. Block (head, b), 64 threads (one per dim).
+extern "C" __global__ void __launch_bounds__(64) batch_attention_merge(pf::DecodeAttentionArgs p) {
+  const uint32_t head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const uint32_t group = head / qd::kQueriesPerKvHead, local = head % qd::kQueriesPerKvHead;
+  const float *first = p.partials + (size_t{b} * qd::kKvHeads + group) * p.splits *
+                                        qd::kQueriesPerKvHead * pf::kDecodePartialStride +
+                       size_t{local} * pf::kDecodePartialStride;
+  const size_t stride = size_t{qd::kQueriesPerKvHead} * pf::kDecodePartialStride;
+  float common = -INFINITY;
+  for (uint32_t s = 0; s < p.splits; ++s) {
+    common = fmaxf(common, first[s * stride + 64]);
+  }
+  float total = 0.0f, value = 0.0f;
+  for (uint32_t s = 0; s < p.splits; ++s) {
+    const float m = first[s * stride + 64];
+    const float weight = m != -INFINITY ? expf(m - common) : 0.0f;
+    total += first[s * stride + 65] * weight;
+    value += first[s * stride + d] * weight;
+  }
+  store_operand(p.out, p.out_lo, size_t{b} * qd::kQuerySize + head * qd::kHeadSize + d,
+                value / total);
+}
+
+// Greedy token of each stream row (block b, 1024 threads): per-thread best
+// over a strided column range, then warp and block reductions that keep the
+// larger logit and, on equal logits, the lower index (the decode step's
+// better_top1 rule).
+extern "C" __global__ void __launch_bounds__(1024) batch_argmax(pf::ArgmaxArgs p) {
+  __shared__ float best_value[32];
+  __shared__ uint32_t best_index[32];
+  const uint32_t b = blockIdx.x;
+  if (b >= p.streams) {
+    return;
+  }
+  const float *row = p.logits + size_t{b} * p.vocab;
+  float value = -INFINITY;
+  uint32_t index = UINT32_MAX;
+  for (uint32_t i = threadIdx.x; i < p.vocab; i += blockDim.x) {
+    const float x = row[i];
+    if (x > value || index == UINT32_MAX) {
+      value = x;
+      index = i;
+    }
+  }
+  auto better = [](float va, uint32_t ia, float vb, uint32_t ib) {
+    return vb > va || (vb == va && ib < ia);
+  };
+#pragma unroll
+  for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
+    const float v = __shfl_xor_sync(kFullMask, value, offset);
+    const uint32_t i = __shfl_xor_sync(kFullMask, index, offset);
+    if (better(value, index, v, i)) {
+      value = v;
+      index = i;
+    }
+  }
+  const uint32_t warp = threadIdx.x >> 5u, lane = threadIdx.x & 31u;
+  if (lane == 0) {
+    best_value[warp] = value;
+    best_index[warp] = index;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    value = lane < blockDim.x / 32u ? best_value[lane] : -INFINITY;
+    index = lane < blockDim.x / 32u ? best_index[lane] : UINT32_MAX;
+#pragma unroll
+    for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
+      const float v = __shfl_xor_sync(kFullMask, value, offset);
+      const uint32_t i = __shfl_xor_sync(kFullMask, index, offset);
+      if (better(value, index, v, i)) {
+        value = v;
+        index = i;
+      }
+    }
+    if (lane == 0) {
+      const uint32_t slot = p.generated[b];
+      p.tokens[size_t{b} * p.token_stride + slot] = index;
+      p.generated[b] = slot + 1u;
+      p.positions[b] += 1u;
+      p.next_tokens[b] = index;
+      p.logit_values[b] = value;
+    }
+  }
 }

@@ -6,6 +6,7 @@
 #include "lrrt_qwen.h"
 
 #include "lm_head_top1_static.hpp"
+#include "batch.hpp"
 #include "prefill.hpp"
 
 #include <cuda_runtime_api.h>
@@ -306,6 +307,7 @@ struct lrq_model_t {
   // uploads so the prefill's TF32 weight copies know when to refresh.
   std::unique_ptr<lrrt::qwen::prefill::Prefill> prefill;
   uint64_t weights_generation = 0;
+  std::vector<lrq_batch_t *> batches; // live batched decoders (they use `prefill`)
 
   float *layer_weight(uint32_t layer, size_t offset) const {
     return static_cast<float *>(weights->data()) + size_t{layer} * layout.floats + offset;
@@ -862,11 +864,20 @@ LRRT_API lr_status_t lrq_model_create(lr_device_t device, const void *module_ima
   });
 }
 
+struct lrq_batch_t {
+  lrq_model_t *model;
+  std::unique_ptr<lrrt::qwen::prefill::BatchDecoder> decoder;
+};
+
 LRRT_API lr_status_t lrq_model_destroy(lrq_model_t *model) {
   return guarded("lrq_model_destroy", [&] {
     if (model == nullptr) {
       throw std::invalid_argument("null model");
     }
+    for (lrq_batch_t *batch : model->batches) {
+      delete batch;
+    }
+    model->batches.clear();
     if (model->token_graph != nullptr) {
       model->device.synchronize();
       cudaGraphExecDestroy(model->token_graph);
@@ -936,6 +947,7 @@ LRRT_API lr_status_t lrq_model_set_tail(lrq_model_t *model, const float *final_n
       throw std::invalid_argument("missing tail weight");
     }
     const size_t table = size_t{model->config.vocab_size} * qd::kHiddenSize * sizeof(float);
+    ++model->weights_generation;
     lrrt::copy_to_device(*model->final_norm, final_norm, qd::kHiddenSize * sizeof(float));
     if (model->config.tied_embeddings != 0) {
       lrrt::copy_to_device(*model->embeddings, lm_head, table);
@@ -1124,6 +1136,9 @@ lrrt::qwen::prefill::ModelView prefill_view(lrq_model_t &m) {
   view.capacity = m.config.cache_capacity;
   view.epsilon = m.config.rms_epsilon;
   view.embeddings = static_cast<const float *>(m.embeddings->data());
+  view.lm_head = static_cast<const float *>(m.config.tied_embeddings != 0 ? m.embeddings->data()
+                                                                           : m.lm_head->data());
+  view.final_norm = static_cast<const float *>(m.final_norm->data());
   view.rope_cos = static_cast<const float *>(m.rope_cos->data());
   view.rope_sin = static_cast<const float *>(m.rope_sin->data());
   const LayerLayout &l = m.layout;
@@ -1166,6 +1181,9 @@ LRRT_API lr_status_t lrq_model_enable_prefill(lrq_model_t *model, const void *mo
     if (l.k != l.q + h * h || l.v != l.k + kv * h || l.k_bias != l.q_bias + h ||
         l.v_bias != l.k_bias + kv || l.up != l.gate + i * h) {
       throw std::logic_error("layer layout does not keep QKV and gate/up contiguous");
+    }
+    if (!model->batches.empty()) {
+      throw std::logic_error("destroy the model's batches before reloading the prefill module");
     }
     model->prefill.reset();
     model->prefill = std::make_unique<lrrt::qwen::prefill::Prefill>(
@@ -1215,6 +1233,81 @@ LRRT_API lr_status_t lrq_model_prefill(lrq_model_t *model, const uint32_t *promp
     lrrt::check(static_cast<lr_status_t>(
                     lrq_model_set_hidden_from_token(model, prompt[count - 1u])),
                 "stage last prompt token");
+  });
+}
+
+LRRT_API lr_status_t lrq_batch_create(lrq_model_t *model, uint32_t streams, uint32_t capacity,
+                                      uint32_t max_tokens, lrq_batch_t **batch) {
+  return guarded("lrq_batch_create", [&] {
+    if (model == nullptr || batch == nullptr) {
+      throw std::invalid_argument("null argument");
+    }
+    if (!model->prefill) {
+      throw std::logic_error("prefill is not enabled on this model");
+    }
+    auto created = std::make_unique<lrq_batch_t>();
+    created->model = model;
+    created->decoder = std::make_unique<lrrt::qwen::prefill::BatchDecoder>(
+        *model->prefill, prefill_view(*model), streams, capacity, max_tokens);
+    model->batches.push_back(created.get());
+    *batch = created.release();
+  });
+}
+
+LRRT_API lr_status_t lrq_batch_destroy(lrq_batch_t *batch) {
+  return guarded("lrq_batch_destroy", [&] {
+    if (batch == nullptr) {
+      throw std::invalid_argument("null batch");
+    }
+    auto &list = batch->model->batches;
+    list.erase(std::remove(list.begin(), list.end(), batch), list.end());
+    delete batch;
+  });
+}
+
+LRRT_API lr_status_t lrq_batch_prefill(lrq_batch_t *batch, uint32_t stream,
+                                       const uint32_t *prompt, uint32_t count, uint32_t path) {
+  return guarded("lrq_batch_prefill", [&] {
+    if (batch == nullptr || prompt == nullptr) {
+      throw std::invalid_argument("null argument");
+    }
+    if (path != LRQ_PREFILL_SIMT && path != LRQ_PREFILL_TF32X3) {
+      throw std::invalid_argument("unknown prefill path");
+    }
+    lrq_model_t &m = *batch->model;
+    batch->decoder->prefill_stream(prefill_view(m), stream, prompt, count,
+                                   static_cast<lrrt::qwen::prefill::Path>(path),
+                                   m.weights_generation);
+  });
+}
+
+LRRT_API lr_status_t lrq_batch_decode(lrq_batch_t *batch, uint32_t steps, uint32_t *tokens,
+                                      float *last_logits) {
+  return guarded("lrq_batch_decode", [&] {
+    if (batch == nullptr) {
+      throw std::invalid_argument("null batch");
+    }
+    lrq_model_t &m = *batch->model;
+    batch->decoder->decode(prefill_view(m), steps, m.weights_generation, tokens, last_logits);
+  });
+}
+
+LRRT_API lr_status_t lrq_batch_read_cache(lrq_batch_t *batch, uint32_t stream, uint32_t layer,
+                                          uint32_t positions, float *keys, float *values) {
+  return guarded("lrq_batch_read_cache", [&] {
+    if (batch == nullptr) {
+      throw std::invalid_argument("null batch");
+    }
+    batch->decoder->read_cache(stream, layer, positions, keys, values);
+  });
+}
+
+LRRT_API lr_status_t lrq_batch_position(lrq_batch_t *batch, uint32_t stream, uint32_t *position) {
+  return guarded("lrq_batch_position", [&] {
+    if (batch == nullptr || position == nullptr || stream >= batch->decoder->streams()) {
+      throw std::invalid_argument("invalid batch position query");
+    }
+    *position = batch->decoder->position(stream);
   });
 }
 

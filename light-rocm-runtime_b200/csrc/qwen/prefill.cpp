@@ -2,87 +2,13 @@
 // and tensor maps, and the launch sequence of one chunk through all layers.
 #include "prefill.hpp"
 
-#include "lrrt/qwen/stateful_graph_context.hpp"
-
-#include <cuda.h>
-#include <cuda_runtime_api.h>
+#include "prefill_common.hpp"
 
 #include <algorithm>
-#include <cstring>
-#include <stdexcept>
-#include <string>
 
 namespace lrrt::qwen::prefill {
-namespace {
 
-namespace qd = lrrt::qwen::stateful_graph;
-
-constexpr uint32_t kHidden = qd::kHiddenSize;
-constexpr uint32_t kQkv = qd::kPackedQkvSize;
-constexpr uint32_t kIntermediate = qd::kIntermediateSize;
-constexpr uint32_t kSms = 148;           // B200 SM count: one TC GEMM CTA per SM
-constexpr uint32_t kWaitLimitMs = 2000;  // per mbarrier wait of the TC GEMM
-// Accumulator columns per tensor-core tile of each GEMM: output widths 1152
-// (QKV) = 6 x 192, 896 (o_proj, down) = 4 x 224, gate/up = 38 x (128 gate +
-// 128 up).
-constexpr uint32_t kQkvTile = 192, kHiddenTile = 224, kGateUpTile = 256;
-
-// Floats of one layer's GEMM weights: QKV, o_proj, gate/up, down.
-constexpr size_t kQkvFloats = size_t{kQkv} * kHidden;
-constexpr size_t kOFloats = size_t{kHidden} * kHidden;
-constexpr size_t kGateUpFloats = size_t{2} * kIntermediate * kHidden;
-constexpr size_t kDownFloats = size_t{kHidden} * kIntermediate;
-constexpr size_t kLayerFloats = kQkvFloats + kOFloats + kGateUpFloats + kDownFloats;
-
-static_assert(sizeof(CUtensorMap) == sizeof(TensorMap), "TensorMap must hold a CUtensorMap");
-
-using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                 const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                 const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_tiled() {
-  static const EncodeTiled function = [] {
-    void *entry = nullptr;
-    cudaDriverEntryPointQueryResult found{};
-    const cudaError_t status = cudaGetDriverEntryPointByVersion(
-        "cuTensorMapEncodeTiled", &entry, 12000, cudaEnableDefault, &found);
-    if (status != cudaSuccess || found != cudaDriverEntryPointSuccess || entry == nullptr) {
-      throw std::runtime_error("cuTensorMapEncodeTiled is not available");
-    }
-    return reinterpret_cast<EncodeTiled>(entry);
-  }();
-  return function;
-}
-
-// 2-D fp32 map over a row-major [rows][columns] array: box of 16 columns
-// (one 64-byte swizzle row) x box_rows rows, 64-byte swizzle, zero fill
-// outside the array.
-TensorMap map_2d(const float *base, uint64_t rows, uint64_t columns, uint32_t box_rows) {
-  CUtensorMap map{};
-  const cuuint64_t dims[2] = {columns, rows};
-  const cuuint64_t strides[1] = {columns * sizeof(float)};
-  const cuuint32_t box[2] = {kTcTileK, box_rows};
-  const cuuint32_t element_strides[2] = {1, 1};
-  const CUresult status = encode_tiled()(
-      &map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
-      element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (status != CUDA_SUCCESS) {
-    throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(status) + ")");
-  }
-  TensorMap out{};
-  std::memcpy(&out, &map, sizeof(out));
-  return out;
-}
-
-lr_launch_config_t rows_config(uint32_t blocks, uint32_t threads) {
-  return lr_launch_config_t{{blocks * threads, 1, 1}, {threads, 1, 1}, 0};
-}
-
-uint32_t ceil_div(uint64_t a, uint64_t b) { return static_cast<uint32_t>((a + b - 1) / b); }
-
-} // namespace
+using namespace detail;
 
 Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t max_chunk_tokens)
     : device_(device), module_(device, image, image_size), embed_(module_.kernel("prefill_embed")),
@@ -94,7 +20,10 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
       tc_n192_(module_.kernel("prefill_tc_gemm_n192")),
       tc_n224_(module_.kernel("prefill_tc_gemm_n224")),
       tc_n256_(module_.kernel("prefill_tc_gemm_n256")),
-      finish_rows_(module_.kernel("prefill_finish_rows")), chunk_(max_chunk_tokens) {
+      finish_rows_(module_.kernel("prefill_finish_rows")),
+      batch_attention_(module_.kernel("batch_attention")),
+      batch_merge_(module_.kernel("batch_attention_merge")),
+      batch_argmax_(module_.kernel("batch_argmax")), chunk_(max_chunk_tokens) {
   if (chunk_ == 0 || chunk_ > 8192) {
     throw std::invalid_argument("prefill chunk must be 1..8192 tokens");
   }
@@ -173,6 +102,28 @@ void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_gene
   }
   split_generation_ = weights_generation;
   split_source_ = model.layers[0].qkv;
+}
+
+void Prefill::prepare_tail(const ModelView &model, uint64_t weights_generation) {
+  const uint64_t floats = uint64_t{model.vocab} * kHidden;
+  if (!tail_split_ || tail_split_->size() < sizeof(float) * 2 * floats) {
+    tail_split_.reset();
+    tail_split_.emplace(allocate(sizeof(float) * 2 * floats));
+    tail_generation_ = UINT64_MAX;
+  }
+  if (tail_generation_ == weights_generation && tail_source_ == model.lm_head) {
+    return;
+  }
+  if (cudaSetDevice(static_cast<int>(device_.index())) != cudaSuccess) {
+    throw std::runtime_error("cudaSetDevice failed");
+  }
+  auto *hi = static_cast<float *>(tail_split_->data());
+  launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(floats, 256), kSms * 8), 256),
+         SplitArgs{model.lm_head, hi, hi + floats, floats});
+  tail_maps_[0] = map_2d(hi, model.vocab, kHidden, kGateUpTile / 2u);
+  tail_maps_[1] = map_2d(hi + floats, model.vocab, kHidden, kGateUpTile / 2u);
+  tail_generation_ = weights_generation;
+  tail_source_ = model.lm_head;
 }
 
 // One 3xTF32 GEMM C = A . B^T over m chunk rows with tile_columns-wide
@@ -288,7 +239,7 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
     }
     launch(rope_kv_.get(), rows_config(count, 256),
            RopeArgs{qkv, model.rope_cos, model.rope_sin, w.key_cache, w.value_cache, count,
-                    first_position, qkv_partials, w.qkv_bias});
+                    first_position, qkv_partials, w.qkv_bias, nullptr, 0});
     // Attention blocks: 32 query rows x one head each.
     const lr_launch_config_t attention_config{
         {ceil_div(count, 32) * kAttentionThreads, qd::kAttentionHeads, 1},

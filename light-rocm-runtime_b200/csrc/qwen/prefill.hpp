@@ -34,12 +34,16 @@ struct ModelView {
   uint32_t capacity;
   float epsilon;
   const float *embeddings; // [vocab][896]
+  const float *lm_head;    // [vocab][896] (the embeddings when tied)
+  const float *final_norm; // [896]
   const float *rope_cos;   // [capacity][32]
   const float *rope_sin;
   std::vector<LayerView> layers;
 };
 
 enum class Path : uint32_t { simt = 0, tf32x3 = 1 };
+
+class BatchDecoder;
 
 class Prefill {
 public:
@@ -63,6 +67,8 @@ public:
   uint32_t max_chunk_tokens() const { return chunk_; }
 
 private:
+  friend class BatchDecoder;
+
   // (hi, lo) tensor maps of one layer's weights.
   struct LayerMaps {
     TensorMap qkv[2], o[2], gate_up[2], down[2];
@@ -70,6 +76,8 @@ private:
 
   DeviceBuffer allocate(size_t bytes);
   void prepare_tensor_cores(const ModelView &model, uint64_t weights_generation);
+  // TF32 (hi, lo) copy of the LM head and its tensor maps (batched decode).
+  void prepare_tail(const ModelView &model, uint64_t weights_generation);
   void run_chunk(const ModelView &model, uint32_t count, uint32_t first_position, Path path);
   PartialTiles tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b, uint32_t m,
                        uint32_t n, uint32_t k, GemmEpilogue mode, float *c, float *c_lo,
@@ -78,7 +86,8 @@ private:
   Device device_;
   Module module_;
   Kernel embed_, rmsnorm_, rope_kv_, attend_, reduce_, split_, gemm_bias_, gemm_residual_,
-      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, finish_rows_;
+      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, finish_rows_, batch_attention_, batch_merge_,
+      batch_argmax_;
   uint32_t chunk_;
   uint64_t device_bytes_ = 0;
 
@@ -90,6 +99,10 @@ private:
   TensorMap normalized_maps_[2]{}, attention_maps_[2]{}, activated_maps_[2]{};
   uint64_t split_generation_ = UINT64_MAX;
   const void *split_source_ = nullptr;
+  std::optional<DeviceBuffer> tail_split_;
+  TensorMap tail_maps_[2]{};
+  uint64_t tail_generation_ = UINT64_MAX;
+  const void *tail_source_ = nullptr;
 };
 
 } // namespace lrrt::qwen::prefill

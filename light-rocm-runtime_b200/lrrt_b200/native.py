@@ -185,6 +185,12 @@ DRIVER_FUNCTIONS = {
     "lrq_model_prefill": (u32, [vp, P(u32), u32, u32]),
     "lrq_model_prefill_at": (u32, [vp, P(u32), u32, u32, u32]),
     "lrq_prefill_gemm_check": (u32, [vp, u32, u32, u32, u32, u32, vp, vp, vp, vp]),
+    "lrq_batch_create": (u32, [vp, u32, u32, u32, P(vp)]),
+    "lrq_batch_destroy": (u32, [vp]),
+    "lrq_batch_prefill": (u32, [vp, u32, P(u32), u32, u32]),
+    "lrq_batch_decode": (u32, [vp, u32, vp, vp]),
+    "lrq_batch_read_cache": (u32, [vp, u32, u32, u32, vp, vp]),
+    "lrq_batch_position": (u32, [vp, u32, P(u32)]),
     "lrq_generate": (u32, [vp, vp, u32, u32, u32, u32, P(u32), P(RunState)]),
     "lrq_model_read": (u32, [vp, u32, u32, vp, sz]),
     "lrq_model_info": (u32, [vp, P(ModelInfo)]),

@@ -355,3 +355,56 @@ class EventTimer:
             if event:
                 N.runtime().lr_event_destroy(event)
         self.start = self.end = None
+
+
+class Batch:
+    """Batched multi-stream greedy decode on one GPU (lrq_batch_* C ABI):
+    `streams` independent streams with their own KV caches share the model's
+    weights; every decode step produces one token per stream."""
+
+    def __init__(self, model: Model, streams: int, capacity: int, max_tokens: int):
+        self.model = model
+        self.streams = streams
+        self.max_tokens = max_tokens
+        handle = C.c_void_p()
+        N.check(N.driver().lrq_batch_create(model.handle, streams, capacity, max_tokens,
+                                            C.byref(handle)), "lrq_batch_create")
+        self.handle = handle
+
+    def close(self) -> None:
+        if self.handle:
+            N.check(N.driver().lrq_batch_destroy(self.handle), "lrq_batch_destroy")
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def prefill(self, stream: int, prompt, path: int = PREFILL_TF32X3) -> None:
+        tokens = (C.c_uint32 * len(prompt))(*[int(t) for t in prompt])
+        N.check(N.driver().lrq_batch_prefill(self.handle, stream, tokens, len(prompt), path),
+                "lrq_batch_prefill")
+
+    def decode(self, steps: int):
+        """(tokens [streams, steps], last chosen logit per stream)."""
+        tokens = np.zeros((self.streams, steps), np.uint32)
+        logits = np.zeros(self.streams, np.float32)
+        N.check(N.driver().lrq_batch_decode(self.handle, steps, _ptr(tokens), _ptr(logits)),
+                "lrq_batch_decode")
+        return tokens, logits
+
+    def read_cache(self, stream: int, layer: int, positions: int):
+        keys = np.zeros((positions, 128), np.float32)
+        values = np.zeros((positions, 128), np.float32)
+        N.check(N.driver().lrq_batch_read_cache(self.handle, stream, layer, positions,
+                                                _ptr(keys), _ptr(values)),
+                "lrq_batch_read_cache")
+        return keys, values
+
+    def position(self, stream: int) -> int:
+        value = C.c_uint32()
+        N.check(N.driver().lrq_batch_position(self.handle, stream, C.byref(value)),
+                "lrq_batch_position")
+        return value.value
