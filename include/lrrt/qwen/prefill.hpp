@@ -113,7 +113,9 @@ struct RopeArgs {
 
 // Row finish of a residual GEMM: hidden[t] += (partial sums of row t), then,
 // when norm_weight is set, out[t] = RMSNorm(hidden[t]) * norm_weight (TF32
-// hi/lo pair when out_lo is set). One block per row.
+// hi/lo pair when out_lo is set). One block per row (also for
+// prefill_rope_kv) of 256 threads or kRowThreads: both kernels work for any
+// block size of at least 256.
 struct FinishArgs {
   PartialTiles partials;
   float *hidden; // [count][896]
@@ -142,9 +144,15 @@ struct AttentionArgs {
 // covers key positions [s * chunk, (s + 1) * chunk) of stream b's cache for
 // the seven query heads of KV group g and writes a partial softmax state
 // (maximum, sum, acc[64]) per head to `partials`
-// [b][g][split][7][kDecodePartialStride]; batch_attention_merge combines
-// the splits into out[b][head * 64 + d] (TF32 pair when out_lo is set).
+// [b][g][split][7][kDecodePartialStride]; the last block of (b, g) to finish
+// (arrivals[b * 2 + g], reset by that block) combines the splits into
+// out[b][head * 64 + d] (TF32 pair when out_lo is set).
 constexpr uint32_t kDecodePartialStride = 66;
+constexpr uint32_t kDecodeMaximumSplits = 32;
+// Dynamic shared memory of batch_attention: q[7][64], K^T[64][129],
+// V[128][64], merge weights [7][32] and totals [7].
+constexpr uint32_t kDecodeSharedBytes =
+    4u * (7u * 64u + 64u * 129u + 128u * 64u + 7u * 32u + 7u);
 struct DecodeAttentionArgs {
   const float *qkv;         // [streams][1152], q rotated
   const float *key_cache;   // stream b's cache at key_cache + b * stream_stride
@@ -155,6 +163,7 @@ struct DecodeAttentionArgs {
   float *out;
   float *out_lo;
   uint32_t streams, splits, chunk;
+  uint32_t *arrivals; // [streams][2], zero between steps
 };
 
 // Greedy step end: per stream row, the first index of the largest logit
@@ -170,7 +179,14 @@ struct ArgmaxArgs {
   uint32_t *tokens;
   uint32_t token_stride;
   float *logit_values;       // [streams]: the chosen logit
+  float *candidate_values;   // [streams][partitions] per-block winners
+  uint32_t *candidate_indices;
+  uint32_t *arrivals;        // [streams], zero between steps
 };
+
+constexpr uint32_t kArgmaxPartitions = 8; // blocks per stream row
+constexpr uint32_t kRowThreads = 1024;     // prefill_rope_kv, prefill_finish_rows
+constexpr uint32_t kMaximumDeferredSplits = 16;
 
 constexpr uint32_t kAttentionThreads = 512;
 constexpr uint32_t kAttentionSharedBytes =

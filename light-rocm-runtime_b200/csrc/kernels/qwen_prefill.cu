@@ -347,7 +347,10 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rmsnorm(pf::NormArgs p
 }
 
 // Sum over splits of one element of a deferred GEMM's partial tiles: row t,
-// column c of the output.
+// column c of the output. All (at most kMaximumDeferredSplits) loads are
+// issued before the additions, which stay in split order.
+using pf::kMaximumDeferredSplits;
+
 __device__ __forceinline__ float partial_sum(const pf::PartialTiles &tiles, uint32_t t,
                                              uint32_t column) {
   const uint32_t tile = (t / pf::kTcTileM) * tiles.n_tiles + column / tiles.tile_columns;
@@ -355,23 +358,38 @@ __device__ __forceinline__ float partial_sum(const pf::PartialTiles &tiles, uint
   const float *at = tiles.partials + size_t{tile} * tile_floats +
                     size_t{t % pf::kTcTileM} * tiles.tile_columns + column % tiles.tile_columns;
   const size_t split_stride = size_t{tiles.tile_count} * tile_floats;
-  float sum = at[0];
-  for (uint32_t s = 1; s < tiles.splits; ++s) {
-    sum += at[s * split_stride];
+  float values[kMaximumDeferredSplits];
+#pragma unroll
+  for (uint32_t s = 0; s < kMaximumDeferredSplits; ++s) {
+    values[s] = s < tiles.splits ? __ldcg(at + s * split_stride) : 0.0f;
+  }
+  float sum = values[0];
+#pragma unroll
+  for (uint32_t s = 1; s < kMaximumDeferredSplits; ++s) {
+    if (s < tiles.splits) {
+      sum += values[s];
+    }
   }
   return sum;
 }
 
-// The decode step's RMSNorm of one 896-float row held in shared memory
-// (per-thread strided sum of squares, shared tree, 1/sqrt(mean + eps)).
+// The decode step's RMSNorm of one 896-float row held in shared memory:
+// per-thread strided sums of squares as the decode step's 256 threads form
+// them (thread j adds x[j], x[j + 256], ...), the same shared tree, then
+// 1/sqrt(mean + eps). Blocks of kRowThreads threads; threads >= 256 only
+// help with the stores.
+using pf::kRowThreads;
+
 __device__ __forceinline__ void row_rmsnorm(const float *x, const float *weight, float epsilon,
                                             float *out, float *out_lo, size_t at,
                                             float *partial) {
-  float sum = 0.0f;
-  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
-    sum = fmaf(x[i], x[i], sum);
+  if (threadIdx.x < 256u) {
+    float sum = 0.0f;
+    for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+      sum = fmaf(x[i], x[i], sum);
+    }
+    partial[threadIdx.x] = sum;
   }
-  partial[threadIdx.x] = sum;
   __syncthreads();
   for (uint32_t stride = 128; stride != 0; stride >>= 1u) {
     if (threadIdx.x < stride) {
@@ -380,7 +398,7 @@ __device__ __forceinline__ void row_rmsnorm(const float *x, const float *weight,
     __syncthreads();
   }
   const float inverse = 1.0f / sqrtf(partial[0] / static_cast<float>(qd::kHiddenSize) + epsilon);
-  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += blockDim.x) {
     store_operand(out, out_lo, at + i, x[i] * inverse * weight[i]);
   }
 }
@@ -389,7 +407,7 @@ __device__ __forceinline__ void row_rmsnorm(const float *x, const float *weight,
 // position first_position + t, then the cache append of k and v; one block
 // per token. The row is first finished from the QKV GEMM's partial sums when
 // those are given.
-extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p) {
+extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_rope_kv(pf::RopeArgs p) {
   __shared__ float row[qd::kPackedQkvSize];
   const uint32_t t = blockIdx.x;
   if (t >= p.count) {
@@ -398,7 +416,7 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p
   const uint32_t position = p.positions != nullptr ? p.positions[t] : p.first_position + t;
   const size_t stream_offset = p.positions != nullptr ? t * p.stream_stride : 0;
   float *qkv = p.qkv + size_t{t} * qd::kPackedQkvSize;
-  for (uint32_t i = threadIdx.x; i < qd::kPackedQkvSize; i += 256u) {
+  for (uint32_t i = threadIdx.x; i < qd::kPackedQkvSize; i += blockDim.x) {
     row[i] = p.qkv_partials.partials != nullptr ? partial_sum(p.qkv_partials, t, i) + p.qkv_bias[i]
                                                 : qkv[i];
   }
@@ -407,7 +425,7 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p
   const float *sin_row = p.rope_sin + size_t{position} * qd::kRotarySize;
   float *key_row = p.key_cache + stream_offset + size_t{position} * qd::kKvSize;
   float *value_row = p.value_cache + stream_offset + size_t{position} * qd::kKvSize;
-  for (uint32_t i = threadIdx.x; i < qd::kRotaryHeads * qd::kRotarySize; i += 256u) {
+  for (uint32_t i = threadIdx.x; i < qd::kRotaryHeads * qd::kRotarySize; i += blockDim.x) {
     const uint32_t head = i / qd::kRotarySize, f = i % qd::kRotarySize;
     const uint32_t first = head * qd::kHeadSize + f;
     const float x0 = row[first], x1 = row[first + qd::kRotarySize];
@@ -422,14 +440,14 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rope_kv(pf::RopeArgs p
       key_row[local + qd::kRotarySize] = r1;
     }
   }
-  for (uint32_t i = threadIdx.x; i < qd::kKvSize; i += 256u) {
+  for (uint32_t i = threadIdx.x; i < qd::kKvSize; i += blockDim.x) {
     value_row[i] = row[qd::kQuerySize + qd::kKvSize + i];
   }
 }
 
 // Residual finish of o_proj / down from their partial sums, then the next
 // RMSNorm of the same row (mlp norm, or the next layer's attention norm).
-extern "C" __global__ void __launch_bounds__(256) prefill_finish_rows(pf::FinishArgs p) {
+extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_finish_rows(pf::FinishArgs p) {
   __shared__ float row[qd::kHiddenSize];
   __shared__ float partial[256];
   const uint32_t t = blockIdx.x;
@@ -437,7 +455,7 @@ extern "C" __global__ void __launch_bounds__(256) prefill_finish_rows(pf::Finish
     return;
   }
   float *hidden = p.hidden + size_t{t} * qd::kHiddenSize;
-  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += 256u) {
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += blockDim.x) {
     const float value = p.partials.partials != nullptr
                             ? hidden[i] + partial_sum(p.partials, t, i)
                             : hidden[i];
@@ -529,19 +547,36 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
   const size_t kv_offset = size_t{kv_group} * qd::kHeadSize;
   for (uint32_t base = g * kAttentionKeys; base <= last; base += kAttentionGroups * kAttentionKeys) {
     group_barrier(g); // the group's previous tile reads are done
-    for (uint32_t i = tid; i < kAttentionKeys * qd::kHeadSize / 4u; i += kAttentionGroupThreads) {
+    // All of the thread's K/V loads are issued before any shared store.
+    constexpr uint32_t kLoads = kAttentionKeys * qd::kHeadSize / 4u / kAttentionGroupThreads;
+    float4 k[kLoads], v[kLoads];
+#pragma unroll
+    for (uint32_t j = 0; j < kLoads; ++j) {
+      const uint32_t i = tid + kAttentionGroupThreads * j;
       const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
-      float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+      // K key-fastest (transposed store), V dim-fastest (row store): no
+      // shared-store conflicts.
+      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
+      k[j] = v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (base + key <= last) {
-        const size_t at = size_t{base + key} * qd::kKvSize + kv_offset + d;
-        k = *reinterpret_cast<const float4 *>(p.key_cache + at);
-        v = *reinterpret_cast<const float4 *>(p.value_cache + at);
+        k[j] = *reinterpret_cast<const float4 *>(p.key_cache + size_t{base + key} * qd::kKvSize +
+                                                 kv_offset + d);
       }
-      gs.kt[d][key] = k.x;
-      gs.kt[d + 1][key] = k.y;
-      gs.kt[d + 2][key] = k.z;
-      gs.kt[d + 3][key] = k.w;
-      *reinterpret_cast<float4 *>(&gs.vs[key][d]) = v;
+      if (base + vkey <= last) {
+        v[j] = *reinterpret_cast<const float4 *>(p.value_cache + size_t{base + vkey} * qd::kKvSize +
+                                                 kv_offset + vd);
+      }
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < kLoads; ++j) {
+      const uint32_t i = tid + kAttentionGroupThreads * j;
+      const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
+      gs.kt[d][key] = k[j].x;
+      gs.kt[d + 1][key] = k[j].y;
+      gs.kt[d + 2][key] = k[j].z;
+      gs.kt[d + 3][key] = k[j].w;
+      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
+      *reinterpret_cast<float4 *>(&gs.vs[vkey][vd]) = v[j];
     }
     group_barrier(g);
     float score[4][4];
@@ -868,7 +903,7 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
     for (uint32_t chunk = 0; chunk < kN / 32u; ++chunk) {
       float v[32];
       tc_load32(lane_address + chunk * 32u, v);
-      if (store) {
+      if (store && row < p.m) {
         float4 *o = reinterpret_cast<float4 *>(out + chunk * 32u);
 #pragma unroll
         for (uint32_t j = 0; j < 8; ++j) {
@@ -933,67 +968,102 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 
 // ------------------------------------------------------- batched decode --
 
-// Decode attention of one query row per stream, split over key positions.
-// Block (s, g, b): warp h < 7 serves query head 7g + h; keys in 64-position
-// tiles of [s * chunk, min((s + 1) * chunk, positions[b] + 1)), K staged
-// transposed so lane l scores keys l and l + 32 against the warp's query
-// (held in registers); the decode step's online softmax (scale 1/8, expf)
-// per tile; lane l accumulates dims l and l + 32 of P.V.
+// Decode attention of one query row per stream, split over key positions;
+// the last split block of a (stream, KV group) merges the splits.
+// Block (s, g, b): warp h < 7 serves query head 7g + h over key positions
+// [s * chunk, min((s + 1) * chunk, positions[b] + 1)), in tiles of
+// kDecodeKeys keys staged in shared memory in one load phase (K transposed,
+// so lane l scores keys l, l + 32, l + 64, l + 96 against the head's query,
+// read from shared memory); the decode step's online softmax (scale 1/8,
+// expf) per tile; lane l accumulates dims l and l + 32 of P.V.
+constexpr uint32_t kDecodeKeys = 128;
+
+struct DecodeShared {
+  float q[qd::kQueriesPerKvHead][qd::kHeadSize];
+  float kt[qd::kHeadSize][kDecodeKeys + 1]; // [d][key]
+  float vs[kDecodeKeys][qd::kHeadSize];     // [key][d]
+  float weight[qd::kQueriesPerKvHead][32];  // merge: per (head, split) scale
+  float total[qd::kQueriesPerKvHead];
+};
+
+static_assert(sizeof(DecodeShared) == pf::kDecodeSharedBytes, "decode shared layout");
+
 extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAttentionArgs p) {
-  __shared__ float kt[qd::kHeadSize][kAttentionKeys + 1]; // [d][key]
-  __shared__ float vs[kAttentionKeys][qd::kHeadSize];     // [key][d]
+  extern __shared__ __align__(16) unsigned char decode_raw[];
+  DecodeShared &sh = *reinterpret_cast<DecodeShared *>(decode_raw);
   const uint32_t split = blockIdx.x, group = blockIdx.y, b = blockIdx.z;
   const uint32_t warp = threadIdx.x >> 5u, lane = threadIdx.x & 31u;
-  const uint32_t head = group * qd::kQueriesPerKvHead + warp;
   const uint32_t last = p.positions[b];
   const uint32_t begin = split * p.chunk;
   const uint32_t end = min(begin + p.chunk, last + 1u);
-  float q[qd::kHeadSize];
-  if (warp < qd::kQueriesPerKvHead) {
-    const float *row = p.qkv + size_t{b} * qd::kPackedQkvSize + head * qd::kHeadSize;
-#pragma unroll
-    for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
-      q[d] = row[d];
-    }
+  for (uint32_t i = threadIdx.x; i < qd::kQueriesPerKvHead * qd::kHeadSize; i += 256u) {
+    sh.q[i / qd::kHeadSize][i % qd::kHeadSize] =
+        p.qkv[size_t{b} * qd::kPackedQkvSize + group * qd::kQueriesPerKvHead * qd::kHeadSize + i];
   }
   const float *keys = p.key_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
   const float *values = p.value_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
   float maximum = -INFINITY, denominator = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
-  for (uint32_t base = begin; base < end; base += kAttentionKeys) {
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < kAttentionKeys * qd::kHeadSize / 4u; i += 256u) {
-      const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
-      float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+  for (uint32_t base = begin; base < end; base += kDecodeKeys) {
+    __syncthreads(); // previous tile's reads are done (and q is written)
+    // All of the thread's K/V loads are issued before any shared store.
+    constexpr uint32_t kLoads = kDecodeKeys * qd::kHeadSize / 4u / 256u;
+    float4 k[kLoads], v[kLoads];
+#pragma unroll
+    for (uint32_t j = 0; j < kLoads; ++j) {
+      const uint32_t i = threadIdx.x + 256u * j;
+      const uint32_t key = i % kDecodeKeys, d = (i / kDecodeKeys) * 4u;
+      // K: key-fastest threads (transposed shared store, consecutive keys);
+      // V: dim-fastest threads (row store, consecutive float4s), so that
+      // neither shared store conflicts.
+      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
+      k[j] = v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (base + key < end) {
-        const size_t at = size_t{base + key} * qd::kKvSize + d;
-        k = *reinterpret_cast<const float4 *>(keys + at);
-        v = *reinterpret_cast<const float4 *>(values + at);
+        k[j] = *reinterpret_cast<const float4 *>(keys + size_t{base + key} * qd::kKvSize + d);
       }
-      kt[d][key] = k.x;
-      kt[d + 1][key] = k.y;
-      kt[d + 2][key] = k.z;
-      kt[d + 3][key] = k.w;
-      *reinterpret_cast<float4 *>(&vs[key][d]) = v;
+      if (base + vkey < end) {
+        v[j] = *reinterpret_cast<const float4 *>(values + size_t{base + vkey} * qd::kKvSize + vd);
+      }
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < kLoads; ++j) {
+      const uint32_t i = threadIdx.x + 256u * j;
+      const uint32_t key = i % kDecodeKeys, d = (i / kDecodeKeys) * 4u;
+      sh.kt[d][key] = k[j].x;
+      sh.kt[d + 1][key] = k[j].y;
+      sh.kt[d + 2][key] = k[j].z;
+      sh.kt[d + 3][key] = k[j].w;
+      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
+      *reinterpret_cast<float4 *>(&sh.vs[vkey][vd]) = v[j];
     }
     __syncthreads();
     if (warp < qd::kQueriesPerKvHead) {
-      float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
+      float score[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 16
       for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
-        s0 = fmaf(q[d], kt[d][lane], s0);
-        s1 = fmaf(q[d], kt[d][lane + 32u], s1);
+        const float q = sh.q[warp][d];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          score[j] = fmaf(q, sh.kt[d][lane + 32u * j], score[j]);
+        }
       }
-      s0 = base + lane < end ? s0 * 0.125f : -INFINITY;
-      s1 = base + lane + 32u < end ? s1 * 0.125f : -INFINITY;
-      float tile_maximum = fmaxf(s0, s1);
+      float tile_maximum = -INFINITY;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        score[j] = base + lane + 32u * j < end ? score[j] * 0.125f : -INFINITY;
+        tile_maximum = fmaxf(tile_maximum, score[j]);
+      }
 #pragma unroll
       for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
         tile_maximum = fmaxf(tile_maximum, __shfl_xor_sync(kFullMask, tile_maximum, offset));
       }
       const float next = fmaxf(maximum, tile_maximum); // finite: key `base` is in range
       const float scale = expf(maximum - next);
-      const float w0 = expf(s0 - next), w1 = expf(s1 - next);
-      float sum = w0 + w1;
+      float w[4], sum = 0.0f;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        w[j] = expf(score[j] - next);
+        sum += w[j];
+      }
 #pragma unroll
       for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
         sum += __shfl_xor_sync(kFullMask, sum, offset);
@@ -1002,21 +1072,22 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       maximum = next;
       acc0 *= scale;
       acc1 *= scale;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
 #pragma unroll 8
-      for (uint32_t key = 0; key < 32u; ++key) {
-        const float wa = __shfl_sync(kFullMask, w0, key);
-        const float wb = __shfl_sync(kFullMask, w1, key);
-        acc0 = fmaf(wa, vs[key][lane], acc0);
-        acc1 = fmaf(wa, vs[key][lane + 32u], acc1);
-        acc0 = fmaf(wb, vs[key + 32u][lane], acc0);
-        acc1 = fmaf(wb, vs[key + 32u][lane + 32u], acc1);
+        for (uint32_t key = 0; key < 32u; ++key) {
+          const float weight = __shfl_sync(kFullMask, w[j], key);
+          acc0 = fmaf(weight, sh.vs[32u * j + key][lane], acc0);
+          acc1 = fmaf(weight, sh.vs[32u * j + key][lane + 32u], acc1);
+        }
       }
     }
   }
+  const float *group_partials = p.partials + (size_t{b} * qd::kKvHeads + group) * p.splits *
+                                                 qd::kQueriesPerKvHead * pf::kDecodePartialStride;
+  const size_t split_stride = size_t{qd::kQueriesPerKvHead} * pf::kDecodePartialStride;
   if (warp < qd::kQueriesPerKvHead) {
-    float *out = p.partials +
-                 ((size_t{b} * qd::kKvHeads + group) * p.splits + split) * qd::kQueriesPerKvHead *
-                     pf::kDecodePartialStride +
+    float *out = const_cast<float *>(group_partials) + split * split_stride +
                  size_t{warp} * pf::kDecodePartialStride;
     out[lane] = acc0;
     out[lane + 32u] = acc1;
@@ -1025,90 +1096,182 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       out[65] = denominator; // 0 then
     }
   }
-}
-
-// Combines a stream's split partial states per head: rescale to the common
-// maximum, sum, divide. Block (head, b), 64 threads (one per dim).
-extern "C" __global__ void __launch_bounds__(64) batch_attention_merge(pf::DecodeAttentionArgs p) {
-  const uint32_t head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const uint32_t group = head / qd::kQueriesPerKvHead, local = head % qd::kQueriesPerKvHead;
-  const float *first = p.partials + (size_t{b} * qd::kKvHeads + group) * p.splits *
-                                        qd::kQueriesPerKvHead * pf::kDecodePartialStride +
-                       size_t{local} * pf::kDecodePartialStride;
-  const size_t stride = size_t{qd::kQueriesPerKvHead} * pf::kDecodePartialStride;
-  float common = -INFINITY;
-  for (uint32_t s = 0; s < p.splits; ++s) {
-    common = fmaxf(common, first[s * stride + 64]);
+  // The last split block of (b, group) to arrive combines the splits: per
+  // head, rescale to the common maximum, sum, divide.
+  __shared__ bool finisher;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t arrived = atomicAdd(&p.arrivals[b * qd::kKvHeads + group], 1u);
+    finisher = arrived == p.splits - 1u;
   }
-  float total = 0.0f, value = 0.0f;
-  for (uint32_t s = 0; s < p.splits; ++s) {
-    const float m = first[s * stride + 64];
-    const float weight = m != -INFINITY ? expf(m - common) : 0.0f;
-    total += first[s * stride + 65] * weight;
-    value += first[s * stride + d] * weight;
-  }
-  store_operand(p.out, p.out_lo, size_t{b} * qd::kQuerySize + head * qd::kHeadSize + d,
-                value / total);
-}
-
-// Greedy token of each stream row (block b, 1024 threads): per-thread best
-// over a strided column range, then warp and block reductions that keep the
-// larger logit and, on equal logits, the lower index (the decode step's
-// better_top1 rule).
-extern "C" __global__ void __launch_bounds__(1024) batch_argmax(pf::ArgmaxArgs p) {
-  __shared__ float best_value[32];
-  __shared__ uint32_t best_index[32];
-  const uint32_t b = blockIdx.x;
-  if (b >= p.streams) {
+  __syncthreads();
+  if (!finisher) {
     return;
   }
-  const float *row = p.logits + size_t{b} * p.vocab;
-  float value = -INFINITY;
-  uint32_t index = UINT32_MAX;
-  for (uint32_t i = threadIdx.x; i < p.vocab; i += blockDim.x) {
-    const float x = row[i];
-    if (x > value || index == UINT32_MAX) {
-      value = x;
-      index = i;
+  __threadfence();
+  if (warp < qd::kQueriesPerKvHead) {
+    // Warp h: the head's per-split maxima and sums (lane = split).
+    const float *first = group_partials + size_t{warp} * pf::kDecodePartialStride;
+    const float m = lane < p.splits ? __ldcg(first + lane * split_stride + 64) : -INFINITY;
+    const float l = lane < p.splits ? __ldcg(first + lane * split_stride + 65) : 0.0f;
+    float common = m;
+#pragma unroll
+    for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
+      common = fmaxf(common, __shfl_xor_sync(kFullMask, common, offset));
+    }
+    const float weight = m != -INFINITY ? expf(m - common) : 0.0f;
+    sh.weight[warp][lane] = weight;
+    // Sum in split order (lane 0 walks the lanes' terms).
+    float total = 0.0f;
+    for (uint32_t s2 = 0; s2 < p.splits; ++s2) {
+      total += __shfl_sync(kFullMask, l * weight, s2);
+    }
+    if (lane == 0) {
+      sh.total[warp] = total;
     }
   }
-  auto better = [](float va, uint32_t ia, float vb, uint32_t ib) {
-    return vb > va || (vb == va && ib < ia);
-  };
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < qd::kQueriesPerKvHead * qd::kHeadSize; i += blockDim.x) {
+    const uint32_t local = i / qd::kHeadSize, d = i % qd::kHeadSize;
+    const float *first = group_partials + size_t{local} * pf::kDecodePartialStride + d;
+    float value = 0.0f;
+    uint32_t s2 = 0;
+    for (; s2 + 4u <= p.splits; s2 += 4u) {
+      const float a0 = __ldcg(first + s2 * split_stride);
+      const float a1 = __ldcg(first + (s2 + 1u) * split_stride);
+      const float a2 = __ldcg(first + (s2 + 2u) * split_stride);
+      const float a3 = __ldcg(first + (s2 + 3u) * split_stride);
+      value += a0 * sh.weight[local][s2];
+      value += a1 * sh.weight[local][s2 + 1u];
+      value += a2 * sh.weight[local][s2 + 2u];
+      value += a3 * sh.weight[local][s2 + 3u];
+    }
+    for (; s2 < p.splits; ++s2) {
+      value += __ldcg(first + s2 * split_stride) * sh.weight[local][s2];
+    }
+    const uint32_t head = group * qd::kQueriesPerKvHead + local;
+    store_operand(p.out, p.out_lo, size_t{b} * qd::kQuerySize + head * qd::kHeadSize + d,
+                  value / sh.total[local]);
+  }
+  if (threadIdx.x == 0) {
+    p.arrivals[b * qd::kKvHeads + group] = 0; // ready for the next step
+  }
+}
+
+// Greedy token of each stream row. Block (part, b) scans columns
+// [part * width, (part + 1) * width) of row b (per-thread best over a strided
+// range, loads issued four at a time), then warp and block reductions keep
+// the larger logit and, on equal logits, the lower index (the decode step's
+// better_top1 rule); the block's winner goes to the row's candidate slot. The
+// last block of the row to finish (per-row arrival counter, reset by that
+// block) reduces the candidates in partition order and publishes the token.
+__device__ __forceinline__ bool better_top1(float va, uint32_t ia, float vb, uint32_t ib) {
+  return vb > va || (vb == va && ib < ia);
+}
+
+__device__ __forceinline__ void block_top1(float &value, uint32_t &index, float *values,
+                                           uint32_t *indices) {
+  const uint32_t warp = threadIdx.x >> 5u, lane = threadIdx.x & 31u;
 #pragma unroll
   for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
     const float v = __shfl_xor_sync(kFullMask, value, offset);
     const uint32_t i = __shfl_xor_sync(kFullMask, index, offset);
-    if (better(value, index, v, i)) {
+    if (better_top1(value, index, v, i)) {
       value = v;
       index = i;
     }
   }
-  const uint32_t warp = threadIdx.x >> 5u, lane = threadIdx.x & 31u;
   if (lane == 0) {
-    best_value[warp] = value;
-    best_index[warp] = index;
+    values[warp] = value;
+    indices[warp] = index;
   }
   __syncthreads();
   if (warp == 0) {
-    value = lane < blockDim.x / 32u ? best_value[lane] : -INFINITY;
-    index = lane < blockDim.x / 32u ? best_index[lane] : UINT32_MAX;
+    value = lane < blockDim.x / 32u ? values[lane] : -INFINITY;
+    index = lane < blockDim.x / 32u ? indices[lane] : UINT32_MAX;
 #pragma unroll
     for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
       const float v = __shfl_xor_sync(kFullMask, value, offset);
       const uint32_t i = __shfl_xor_sync(kFullMask, index, offset);
-      if (better(value, index, v, i)) {
+      if (better_top1(value, index, v, i)) {
         value = v;
         index = i;
       }
     }
-    if (lane == 0) {
+  }
+}
+
+extern "C" __global__ void __launch_bounds__(1024) batch_argmax(pf::ArgmaxArgs p) {
+  __shared__ float values[32];
+  __shared__ uint32_t indices[32];
+  __shared__ bool finisher;
+  const uint32_t part = blockIdx.x, b = blockIdx.y;
+  const uint32_t width = (p.vocab + gridDim.x - 1u) / gridDim.x;
+  const uint32_t begin = part * width, end = min(begin + width, p.vocab);
+  const float *row = p.logits + size_t{b} * p.vocab;
+  float value = -INFINITY;
+  uint32_t index = UINT32_MAX;
+  uint32_t i = begin + threadIdx.x;
+  for (; i + 3u * blockDim.x < end; i += 4u * blockDim.x) {
+    const float x0 = row[i], x1 = row[i + blockDim.x];
+    const float x2 = row[i + 2u * blockDim.x], x3 = row[i + 3u * blockDim.x];
+    const float xs[4] = {x0, x1, x2, x3};
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      if (xs[j] > value || index == UINT32_MAX) {
+        value = xs[j];
+        index = i + j * blockDim.x;
+      }
+    }
+  }
+  for (; i < end; i += blockDim.x) {
+    if (row[i] > value || index == UINT32_MAX) {
+      value = row[i];
+      index = i;
+    }
+  }
+  block_top1(value, index, values, indices);
+  if (threadIdx.x == 0) {
+    p.candidate_values[b * gridDim.x + part] = value;
+    p.candidate_indices[b * gridDim.x + part] = index;
+    __threadfence();
+    const uint32_t arrived = atomicAdd(&p.arrivals[b], 1u);
+    finisher = arrived == gridDim.x - 1u;
+  }
+  __syncthreads();
+  if (!finisher) {
+    return;
+  }
+  __threadfence();
+  if (threadIdx.x < 32u) {
+    value = -INFINITY;
+    index = UINT32_MAX;
+    for (uint32_t c = threadIdx.x; c < gridDim.x; c += 32u) {
+      const float v = __ldcg(&p.candidate_values[b * gridDim.x + c]);
+      const uint32_t x = __ldcg(&p.candidate_indices[b * gridDim.x + c]);
+      if (better_top1(value, index, v, x)) {
+        value = v;
+        index = x;
+      }
+    }
+#pragma unroll
+    for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
+      const float v = __shfl_xor_sync(kFullMask, value, offset);
+      const uint32_t x = __shfl_xor_sync(kFullMask, index, offset);
+      if (better_top1(value, index, v, x)) {
+        value = v;
+        index = x;
+      }
+    }
+    if (threadIdx.x == 0) {
       const uint32_t slot = p.generated[b];
       p.tokens[size_t{b} * p.token_stride + slot] = index;
       p.generated[b] = slot + 1u;
       p.positions[b] += 1u;
       p.next_tokens[b] = index;
       p.logit_values[b] = value;
+      p.arrivals[b] = 0; // ready for the next step
     }
   }
 }

@@ -30,9 +30,10 @@ BatchDecoder::BatchDecoder(Prefill &prefill, const ModelView &model, uint32_t st
         "batch needs 1..prefill-chunk streams, capacity <= the model's RoPE rows and "
         "1..capacity tokens per decode");
   }
-  // Enough position splits that B streams x 2 KV groups x splits fill the SMs.
+  // Position splits of about two 64-key tiles each (at most 32), so that
+  // every block's K/V loads are few and many blocks are in flight.
   const uint32_t tiles = ceil_div(capacity_, 64);
-  splits_ = std::max(1u, std::min({kSms / (2u * streams_), tiles, 16u}));
+  splits_ = std::max(1u, std::min(ceil_div(tiles, 2), kDecodeMaximumSplits));
   chunk_ = ceil_div(tiles, splits_) * 64u;
   const size_t cache = size_t{streams_} * layers_ * capacity_ * qd::kKvSize;
   key_cache_.emplace(allocate(sizeof(float) * cache));
@@ -45,6 +46,10 @@ BatchDecoder::BatchDecoder(Prefill &prefill, const ModelView &model, uint32_t st
   logit_values_.emplace(allocate(sizeof(float) * streams_));
   attention_partials_.emplace(allocate(sizeof(float) * streams_ * qd::kKvHeads * splits_ *
                                        qd::kQueriesPerKvHead * kDecodePartialStride));
+  candidate_values_.emplace(allocate(sizeof(float) * streams_ * kArgmaxPartitions));
+  candidate_indices_.emplace(allocate(sizeof(uint32_t) * streams_ * kArgmaxPartitions));
+  arrivals_.emplace(allocate(sizeof(uint32_t) * streams_));
+  attention_arrivals_.emplace(allocate(sizeof(uint32_t) * streams_ * qd::kKvHeads));
   // Zeroed caches: rows a stream has not written are never read (each
   // stream attends to its own positions 0..position only).
   const std::vector<unsigned char> zeros(1u << 20, 0);
@@ -58,6 +63,9 @@ BatchDecoder::BatchDecoder(Prefill &prefill, const ModelView &model, uint32_t st
   }
   positions_host_.assign(streams_, 0);
   next_host_.assign(streams_, 0);
+  copy_to_device(*arrivals_, positions_host_.data(), sizeof(uint32_t) * streams_);
+  const std::vector<uint32_t> no_arrivals(size_t{streams_} * qd::kKvHeads, 0);
+  copy_to_device(*attention_arrivals_, no_arrivals.data(), sizeof(uint32_t) * no_arrivals.size());
   copy_to_device(*positions_, positions_host_.data(), sizeof(uint32_t) * streams_);
   copy_to_device(*next_tokens_, next_host_.data(), sizeof(uint32_t) * streams_);
 }
@@ -118,7 +126,7 @@ void BatchDecoder::enqueue_step(const ModelView &model) {
   auto *positions = static_cast<uint32_t *>(positions_->data());
   const uint64_t stream_stride = uint64_t{layers_} * capacity_ * qd::kKvSize;
   auto finish = [&](const PartialTiles &partials, const float *norm_weight) {
-    launch(p.finish_rows_.get(), rows_config(b, 256),
+    launch(p.finish_rows_.get(), rows_config(b, row_threads(b)),
            FinishArgs{partials, hidden, b, model.epsilon, norm_weight, normalized, normalized_lo});
   };
 
@@ -137,7 +145,7 @@ void BatchDecoder::enqueue_step(const ModelView &model) {
     const PartialTiles qkv_partials =
         p.tc_gemm(kQkvTile, p.normalized_maps_, maps.qkv, b, kQkv, kHidden, GemmEpilogue::bias,
                   qkv, nullptr, kQkv, w.qkv_bias, true);
-    launch(p.rope_kv_.get(), rows_config(b, 256),
+    launch(p.rope_kv_.get(), rows_config(b, row_threads(b)),
            RopeArgs{qkv, model.rope_cos, model.rope_sin, keys, values, b, 0, qkv_partials,
                     w.qkv_bias, positions, stream_stride});
     const DecodeAttentionArgs attend{qkv,
@@ -150,11 +158,11 @@ void BatchDecoder::enqueue_step(const ModelView &model) {
                                      attention_lo,
                                      b,
                                      splits_,
-                                     chunk_};
+                                     chunk_,
+                                     static_cast<uint32_t *>(attention_arrivals_->data())};
     launch(p.batch_attention_.get(),
-           lr_launch_config_t{{splits_ * 256u, qd::kKvHeads, b}, {256, 1, 1}, 0}, attend);
-    launch(p.batch_merge_.get(),
-           lr_launch_config_t{{qd::kAttentionHeads * 64u, b, 1}, {64, 1, 1}, 0}, attend);
+           lr_launch_config_t{{splits_ * 256u, qd::kKvHeads, b}, {256, 1, 1}, kDecodeSharedBytes},
+           attend);
     finish(p.tc_gemm(kHiddenTile, p.attention_maps_, maps.o, b, kHidden, kHidden,
                      GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr, true),
            w.mlp_norm);
@@ -168,11 +176,15 @@ void BatchDecoder::enqueue_step(const ModelView &model) {
   auto *logits = static_cast<float *>(logits_->data());
   p.tc_gemm(kGateUpTile, p.normalized_maps_, p.tail_maps_, b, model.vocab, kHidden,
             GemmEpilogue::store, logits, nullptr, model.vocab, nullptr, false);
-  launch(p.batch_argmax_.get(), rows_config(b, 1024),
+  launch(p.batch_argmax_.get(),
+         lr_launch_config_t{{kArgmaxPartitions * 1024u, b, 1}, {1024, 1, 1}, 0},
          ArgmaxArgs{logits, model.vocab, b, static_cast<uint32_t *>(next_tokens_->data()),
                     positions, static_cast<uint32_t *>(generated_->data()),
                     static_cast<uint32_t *>(tokens_->data()), max_tokens_,
-                    static_cast<float *>(logit_values_->data())});
+                    static_cast<float *>(logit_values_->data()),
+                    static_cast<float *>(candidate_values_->data()),
+                    static_cast<uint32_t *>(candidate_indices_->data()),
+                    static_cast<uint32_t *>(arrivals_->data())});
 }
 
 void BatchDecoder::capture_step(const ModelView &model) {

@@ -62,10 +62,10 @@ private:
   uint32_t splits_, chunk_;
   uint64_t device_bytes_ = 0;
   std::optional<DeviceBuffer> key_cache_, value_cache_, positions_, next_tokens_, generated_,
-      tokens_, logits_, logit_values_, attention_partials_;
+      tokens_, logits_, logit_values_, attention_partials_, candidate_values_,
+      candidate_indices_, arrivals_, attention_arrivals_;
   std::vector<uint32_t> positions_host_, next_host_;
-  cudaGraphExec_t graph_ = nullptr;
-  uint64_t graph_generation_ = UINT64_MAX;
+  cudaGraphExec_t graph_ = nullptr; // one step; kernels read positions from the device
 };
 
 } // namespace lrrt::qwen::prefill

@@ -22,7 +22,6 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
       tc_n256_(module_.kernel("prefill_tc_gemm_n256")),
       finish_rows_(module_.kernel("prefill_finish_rows")),
       batch_attention_(module_.kernel("batch_attention")),
-      batch_merge_(module_.kernel("batch_attention_merge")),
       batch_argmax_(module_.kernel("batch_argmax")), chunk_(max_chunk_tokens) {
   if (chunk_ == 0 || chunk_ > 8192) {
     throw std::invalid_argument("prefill chunk must be 1..8192 tokens");
@@ -177,7 +176,8 @@ PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const T
              rows_config(ceil_div(uint64_t{count} * kTcTileM * out_columns, 256), 256), reduce);
     }
   };
-  const uint32_t small_splits = std::max(1u, std::min({kSms / std::max(tiles, 1u), k_tiles / 4u, 16u}));
+  const uint32_t small_splits = std::max(
+      1u, std::min({kSms / std::max(tiles, 1u), k_tiles / 4u, kMaximumDeferredSplits}));
   if (defer && !swiglu && tiles <= kSms) {
     run(0, tiles, small_splits, false);
     return PartialTiles{partials, small_splits, n_tiles, tiles, tile_columns};
@@ -215,7 +215,7 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
   // Residual finish of o_proj / down (from partial sums, when deferred) and
   // the next RMSNorm of the same rows.
   auto finish = [&](const PartialTiles &partials, const float *norm_weight) {
-    launch(finish_rows_.get(), rows_config(count, 256),
+    launch(finish_rows_.get(), rows_config(count, row_threads(count)),
            FinishArgs{partials, hidden, count, model.epsilon, norm_weight, normalized,
                       normalized_lo});
   };
@@ -237,7 +237,7 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
                     kHidden, kHidden, kQkv},
            ceil_div(kQkv, 128));
     }
-    launch(rope_kv_.get(), rows_config(count, 256),
+    launch(rope_kv_.get(), rows_config(count, row_threads(count)),
            RopeArgs{qkv, model.rope_cos, model.rope_sin, w.key_cache, w.value_cache, count,
                     first_position, qkv_partials, w.qkv_bias, nullptr, 0});
     // Attention blocks: 32 query rows x one head each.

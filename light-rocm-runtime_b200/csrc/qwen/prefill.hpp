@@ -86,8 +86,7 @@ private:
   Device device_;
   Module module_;
   Kernel embed_, rmsnorm_, rope_kv_, attend_, reduce_, split_, gemm_bias_, gemm_residual_,
-      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, finish_rows_, batch_attention_, batch_merge_,
-      batch_argmax_;
+      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, finish_rows_, batch_attention_, batch_argmax_;
   uint32_t chunk_;
   uint64_t device_bytes_ = 0;
 

@@ -84,6 +84,11 @@ inline lr_launch_config_t rows_config(uint32_t blocks, uint32_t threads) {
 
 inline uint32_t ceil_div(uint64_t a, uint64_t b) { return static_cast<uint32_t>((a + b - 1) / b); }
 
+// Threads per block of the one-block-per-row kernels (RoPE, residual finish):
+// wide blocks when a few rows must use the whole GPU (batched decode), 256
+// when there are enough rows to fill the SMs several times (prefill).
+inline uint32_t row_threads(uint32_t rows) { return rows >= kSms ? 256u : kRowThreads; }
+
 } // namespace lrrt::qwen::prefill::detail
 
 #endif // LRRT_B200_QWEN_PREFILL_COMMON_HPP_
