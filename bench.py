@@ -14,6 +14,13 @@ Reported (one JSON line, rank 0):
               measured HBM copy bandwidth in MEASURED_PEAKS.json
   cpu_baseline  the CPU oracle (reference algorithm restated) on the host
               cores, bounded sample
+  prefill     BASELINE config 5 on the same model: a 512-token prompt
+              (seed 3) through the 3xTF32 tensor-core prefill (511 rows),
+              device-timed, against the 3xTF32 tensor roof; then 256 greedy
+              decode tokens after it
+  batched     BASELINE config 4: 32 streams at context 1024 (seed 2),
+              32/N per GPU decoded as one batch per GPU, 128 tokens each;
+              aggregate tokens/s over all ranks (max-over-ranks time)
 Weights (2 GB) exceed L2 (126 MB), so no flush is needed between steps.
 
 --impl reference times the reference's CPU implementation of the path (the
@@ -38,6 +45,9 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "light-rocm-runtime_b200"))
 
 LAYERS, VOCAB, PROMPT, NEW_TOKENS = 24, 151936, 32, 128
+PREFILL_PROMPT, PREFILL_DECODE = 512, 256              # config 5
+STREAMS, STREAM_CONTEXT, STREAM_TOKENS = 32, 1024, 128  # config 4
+CAPACITY = STREAM_CONTEXT + STREAM_TOKENS + 8          # RoPE rows / KV positions
 SEED = 1
 KV_BYTES_PER_LAYER_POSITION = 128 * 4 * 2  # K and V rows of one position
 METRIC = "decode tokens/s, Qwen2.5-0.5B-arch FP32, batch 1 (config 2: 24 layers, 128 new tokens)"
@@ -54,6 +64,8 @@ def parse_args():
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
                         help="tokens per step (smaller only for profiler captures)")
+    parser.add_argument("--no-extra", action="store_true",
+                        help="skip the config-5 prefill and config-4 batched lines")
     return parser.parse_args()
 
 
@@ -72,6 +84,16 @@ def measured_peaks():
         data = json.loads(path.read_text())
         return float(data["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16 TFLOP/s from MEASURED_PEAKS.json (burst figure: the prefill
+    is timed alone), else the pool's fallback measurement."""
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def profiled_traffic_per_token():
@@ -219,13 +241,88 @@ def reference_arm(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def prefill_flops(rows: int) -> int:
+    """Algorithmic FLOPs of one prefill pass over `rows` prompt rows: the
+    four projections (2 * rows * weight elements) plus causal attention
+    (S = Q.K^T and P.V: 2 * 2 * 64 FLOPs per (row, head, key), keys 1..row+1)."""
+    h, kv, i = 896, 128, 4864
+    per_layer_weights = h * (h + 2 * kv) + h * h + 2 * i * h + i * h
+    attention = 4 * 64 * 14 * rows * (rows + 1) // 2
+    return LAYERS * (2 * rows * per_layer_weights + attention)
+
+
+def extra_configs(model, Q, S, rank: int, world: int, dist, warmup: int):
+    """Config 5 (prefill) and config 4 (batched streams) on the bench's model."""
+    timer = Q.EventTimer(model.device)
+    model.enable_prefill(1024)
+    # Config 5: seed-3 prompt of 512 tokens, 3xTF32 prefill of rows 0..510.
+    prompt5 = [int(t) for t in S.prompt(3, PREFILL_PROMPT, VOCAB)]
+    for _ in range(max(1, warmup)):
+        model.prefill(prompt5, Q.PREFILL_TF32X3)
+    times = []
+    for _ in range(3):
+        model.synchronize()
+        timer.record_start()
+        model.prefill(prompt5, Q.PREFILL_TF32X3)
+        timer.record_end()
+        model.synchronize()
+        times.append(timer.elapsed_ns() / 1e9)
+    prefill_s = min(times)
+    timer.record_start()
+    state, _ = model.decode(PREFILL_PROMPT - 1, PREFILL_DECODE)
+    timer.record_end()
+    decode_s = timer.elapsed_ns() / 1e9
+    if state.status != 2 or state.generated_tokens != PREFILL_DECODE:
+        raise RuntimeError(f"decode after prefill failed: status {state.status}")
+    peak_bf16, _ = measured_tensor_peak()
+    roof = peak_bf16 / 2.0 / 3.0  # TF32 runs at half the bf16 rate; 3 products per FP32 product
+    flops = prefill_flops(PREFILL_PROMPT - 1)
+    achieved = flops / prefill_s / 1e12
+    # Config 4: streams [rank * per_rank, ...) of 32, each a 1025-token prompt
+    # (context 1024), one batch per GPU, 128 greedy tokens per stream.
+    per_rank = STREAMS // world
+    all_prompts = S.prompt(2, STREAMS * (STREAM_CONTEXT + 1), VOCAB).reshape(STREAMS, -1)
+    with Q.Batch(model, per_rank, CAPACITY, STREAM_TOKENS) as batch:
+        for local in range(per_rank):
+            batch.prefill(local, [int(t) for t in all_prompts[rank * per_rank + local]])
+        batch.decode(4)  # graph capture and warm-up
+        model.synchronize()
+        timer.record_start()
+        tokens, _ = batch.decode(STREAM_TOKENS - 4)
+        timer.record_end()
+        model.synchronize()
+        batch_s = timer.elapsed_ns() / 1e9
+    steps = STREAM_TOKENS - 4
+    if world > 1:
+        prefill_s, decode_s, batch_s = max_over_ranks([prefill_s, decode_s, batch_s], dist)
+    return {
+        "prefill": {
+            "workload": "config5: 512-token prompt (seed 3), prefill of rows 0..510 through "
+                        "24 layers, 3xTF32 tcgen05 GEMMs + causal attention",
+            "ms": 1000.0 * prefill_s, "rows": PREFILL_PROMPT - 1,
+            "algorithmic_flops": flops, "achieved_tflops": achieved,
+            "roof_tflops": roof, "frac": achieved / roof,
+            "roof": "3xTF32 roof = measured bf16 dense peak / 2 (TF32) / 3",
+            "decode_after": {"tokens": PREFILL_DECODE, "positions": "511..766",
+                             "tokens_per_s": PREFILL_DECODE / decode_s},
+        },
+        "batched": {
+            "workload": f"config4: {STREAMS} streams at context {STREAM_CONTEXT} (seed 2), "
+                        f"{per_rank} per GPU decoded as one batch (3xTF32 GEMMs, one CUDA "
+                        f"graph per step), {steps} timed greedy steps",
+            "value": world * per_rank * steps / batch_s, "unit": "tokens/s",
+            "streams_per_gpu": per_rank, "ms_per_step": 1000.0 * batch_s / steps,
+            "n_gpus": world,
+        },
+    }
+
+
 def our_arm(args, rank: int, world: int, local_rank: int):
     from lrrt_b200 import qwen as Q
 
     weights, tail, prompt = make_weights(rank)
-    capacity = PROMPT + NEW_TOKENS
-    config = Q.ModelConfig(layer_count=LAYERS, vocab_size=VOCAB, cache_capacity=capacity,
-                           max_tokens_per_run=NEW_TOKENS)
+    config = Q.ModelConfig(layer_count=LAYERS, vocab_size=VOCAB, cache_capacity=CAPACITY,
+                           max_tokens_per_run=max(NEW_TOKENS, PREFILL_DECODE))
     model = Q.Model(config, device_index=local_rank)
     for i, w in enumerate(weights):
         model.set_layer(i, w)
@@ -321,6 +418,9 @@ def our_arm(args, rank: int, world: int, local_rank: int):
         "roofline": roofline,
         "clocks": clock_summary,
     }
+    if not args.no_extra:
+        from lrrt_b200 import synthetic as S
+        line.update(extra_configs(model, Q, S, rank, world, dist, args.warmup))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, str(REPO / "oracle"))
         import oracle as O
