@@ -14,6 +14,9 @@ Reported (one JSON line, rank 0):
               measured HBM copy bandwidth in MEASURED_PEAKS.json
   cpu_baseline  the CPU oracle (reference algorithm restated) on the host
               cores, bounded sample
+  long_context  BASELINE config 3 on the same model: KV cache rows 0..4095
+              N(0, 1), 256 decode tokens at positions 4096..4351, one
+              resident launch, device-timed, with its HBM roofline
   prefill     BASELINE config 5 on the same model: a 512-token prompt
               (seed 3) through the 3xTF32 tensor-core prefill (511 rows),
               device-timed, against the 3xTF32 tensor roof; then 256 greedy
@@ -47,7 +50,9 @@ sys.path.insert(0, str(REPO / "light-rocm-runtime_b200"))
 LAYERS, VOCAB, PROMPT, NEW_TOKENS = 24, 151936, 32, 128
 PREFILL_PROMPT, PREFILL_DECODE = 512, 256              # config 5
 STREAMS, STREAM_CONTEXT, STREAM_TOKENS = 32, 1024, 128  # config 4
-CAPACITY = STREAM_CONTEXT + STREAM_TOKENS + 8          # RoPE rows / KV positions
+LONG_CONTEXT, LONG_TOKENS = 4096, 256                  # config 3
+BATCH_CAPACITY = STREAM_CONTEXT + STREAM_TOKENS + 8    # KV positions per batched stream
+CAPACITY = LONG_CONTEXT + LONG_TOKENS + 8              # model RoPE rows / KV positions
 SEED = 1
 KV_BYTES_PER_LAYER_POSITION = 128 * 4 * 2  # K and V rows of one position
 METRIC = "decode tokens/s, Qwen2.5-0.5B-arch FP32, batch 1 (config 2: 24 layers, 128 new tokens)"
@@ -252,8 +257,28 @@ def prefill_flops(rows: int) -> int:
 
 
 def extra_configs(model, Q, S, rank: int, world: int, dist, warmup: int):
-    """Config 5 (prefill) and config 4 (batched streams) on the bench's model."""
+    """Config 3 (long context), config 5 (prefill) and config 4 (batched
+    streams) on the bench's model."""
     timer = Q.EventTimer(model.device)
+    # Config 3: KV rows 0..4095 ~ N(0, 1), then 256 tokens in one launch.
+    for layer, (keys, values) in enumerate(S.kv_prefill(SEED, LAYERS, LONG_CONTEXT)):
+        model.set_kv(layer, 0, keys, values)
+    model.set_hidden(S.hidden(SEED))
+    long_request = model.request(LONG_CONTEXT, LONG_TOKENS)
+    for _ in range(max(1, min(warmup, 2))):
+        model.launch(long_request)
+    model.synchronize()
+    timer.record_start()
+    model.launch(long_request)
+    timer.record_end()
+    model.synchronize()
+    long_s = timer.elapsed_ns() / 1e9
+    state = model.read_state()
+    if state.status != 2 or state.generated_tokens != LONG_TOKENS:
+        raise RuntimeError(f"long-context decode failed: status {state.status}")
+    long_bytes = algorithmic_bytes_per_launch(int(model.info.weight_bytes_per_token),
+                                              LONG_CONTEXT, LONG_TOKENS)
+    hbm_peak, _ = measured_peaks()
     model.enable_prefill(1024)
     # Config 5: seed-3 prompt of 512 tokens, 3xTF32 prefill of rows 0..510.
     prompt5 = [int(t) for t in S.prompt(3, PREFILL_PROMPT, VOCAB)]
@@ -282,7 +307,7 @@ def extra_configs(model, Q, S, rank: int, world: int, dist, warmup: int):
     # (context 1024), one batch per GPU, 128 greedy tokens per stream.
     per_rank = STREAMS // world
     all_prompts = S.prompt(2, STREAMS * (STREAM_CONTEXT + 1), VOCAB).reshape(STREAMS, -1)
-    with Q.Batch(model, per_rank, CAPACITY, STREAM_TOKENS) as batch:
+    with Q.Batch(model, per_rank, BATCH_CAPACITY, STREAM_TOKENS) as batch:
         for local in range(per_rank):
             batch.prefill(local, [int(t) for t in all_prompts[rank * per_rank + local]])
         batch.decode(4)  # graph capture and warm-up
@@ -294,8 +319,19 @@ def extra_configs(model, Q, S, rank: int, world: int, dist, warmup: int):
         batch_s = timer.elapsed_ns() / 1e9
     steps = STREAM_TOKENS - 4
     if world > 1:
-        prefill_s, decode_s, batch_s = max_over_ranks([prefill_s, decode_s, batch_s], dist)
+        long_s, prefill_s, decode_s, batch_s = max_over_ranks(
+            [long_s, prefill_s, decode_s, batch_s], dist)
     return {
+        "long_context": {
+            "workload": "config3: KV cache rows 0..4095 N(0,1), 256 greedy tokens at positions "
+                        "4096..4351 in one resident launch, batch 1",
+            "value": world * LONG_TOKENS / long_s, "unit": "tokens/s",
+            "ms_per_token": 1000.0 * long_s / LONG_TOKENS,
+            "roofline": {"bound": "hbm", "achieved": long_bytes / long_s / 1e9,
+                         "peak": hbm_peak, "unit": "GB/s",
+                         "frac": long_bytes / long_s / 1e9 / hbm_peak,
+                         "algorithmic_bytes_per_launch": long_bytes},
+        },
         "prefill": {
             "workload": "config5: 512-token prompt (seed 3), prefill of rows 0..510 through "
                         "24 layers, 3xTF32 tcgen05 GEMMs + causal attention",

@@ -1277,21 +1277,29 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
   __syncthreads();
   for (uint32_t tile = begin; tile < end; tile += kKvTile) {
     const uint32_t count = min(kKvTile, end - tile);
-    // Stage K (padded rows) and V: 32 positions x 16 float4 each.
-    for (uint32_t v = threadIdx.x; v < kKvTile * 16u; v += kThreads) {
-      const uint32_t p = v / 16u, q4 = v % 16u;
-      float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = k4;
+    // Stage K (padded rows) and V: 32 positions x 16 float4 each; every
+    // load of the thread is issued before its shared stores.
+    constexpr uint32_t kStageLoads = kKvTile * 16u / kThreads;
+    float4 k4[kStageLoads], v4[kStageLoads];
+#pragma unroll
+    for (uint32_t i = 0; i < kStageLoads; ++i) {
+      const uint32_t v = threadIdx.x + i * kThreads, p = v / 16u, q4 = v % 16u;
+      k4[i] = v4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (p < count) {
         const size_t row = size_t{tile + p} * qd::kKvSize + kv_offset + 4u * q4;
-        k4 = dev::load_cg4(c->key_cache + row);
-        v4 = dev::load_cg4(c->value_cache + row);
+        k4[i] = dev::load_cg4(c->key_cache + row);
+        v4[i] = dev::load_cg4(c->value_cache + row);
       }
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < kStageLoads; ++i) {
+      const uint32_t v = threadIdx.x + i * kThreads, p = v / 16u, q4 = v % 16u;
       float *k = keys + p * kKeyStride + 4u * q4;
-      k[0] = k4.x;
-      k[1] = k4.y;
-      k[2] = k4.z;
-      k[3] = k4.w;
-      reinterpret_cast<float4 *>(values + p * qd::kHeadSize)[q4] = v4;
+      k[0] = k4[i].x;
+      k[1] = k4[i].y;
+      k[2] = k4[i].z;
+      k[3] = k4[i].w;
+      reinterpret_cast<float4 *>(values + p * qd::kHeadSize)[q4] = v4[i];
     }
     __syncthreads();
     if (threadIdx.x < kHeads * kKvTile) {
@@ -1372,10 +1380,26 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
   float *maxima = s->input;                                  // [chunks][7]
   float *sums = maxima + kMaxAttentionChunks * kHeads;       // [chunks][7]
   float *weights = sums + kMaxAttentionChunks * kHeads;      // [7][chunks]
-  for (uint32_t t = threadIdx.x; t < chunks * kHeads; t += kThreads) {
-    const float *entry = group_partials + size_t{t} * qd::kAttentionPartialStride;
-    maxima[t] = dev::load_cg(entry + qd::kHeadSize);
-    sums[t] = dev::load_cg(entry + qd::kHeadSize + 1u);
+  {
+    // chunks * kHeads <= 128 * 7 = 896 entries: at most four per thread,
+    // all loaded before any store.
+    constexpr uint32_t kPerThread = (kMaxAttentionChunks * kHeads + kThreads - 1u) / kThreads;
+    float m[kPerThread], l[kPerThread];
+#pragma unroll
+    for (uint32_t i = 0; i < kPerThread; ++i) {
+      const uint32_t t = threadIdx.x + i * kThreads;
+      const float *entry = group_partials + size_t{t} * qd::kAttentionPartialStride;
+      m[i] = t < chunks * kHeads ? dev::load_cg(entry + qd::kHeadSize) : 0.0f;
+      l[i] = t < chunks * kHeads ? dev::load_cg(entry + qd::kHeadSize + 1u) : 0.0f;
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < kPerThread; ++i) {
+      const uint32_t t = threadIdx.x + i * kThreads;
+      if (t < chunks * kHeads) {
+        maxima[t] = m[i];
+        sums[t] = l[i];
+      }
+    }
   }
   __syncthreads();
   if (warp < kHeads) {
@@ -1398,20 +1422,49 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
     }
   }
   __syncthreads();
+  // Both outputs of the thread, six chunks at a time: all 12 loads of a
+  // round are issued before the multiply-adds (which stay in chunk order).
+  {
+    const size_t stride = size_t{kHeads} * qd::kAttentionPartialStride;
+    const float *entry[2];
+    const float *w[2];
+    bool valid[2];
+    float value[2] = {0.0f, 0.0f};
 #pragma unroll
-  for (uint32_t k = 0; k < 2; ++k) {
-    const uint32_t o = threadIdx.x + k * kThreads;
-    if (o < kOutputs) {
-      const uint32_t h = o / qd::kHeadSize, d = o % qd::kHeadSize;
-      const float *w = weights + h * kMaxAttentionChunks;
-      const float *entry = group_partials + h * qd::kAttentionPartialStride + d;
-      const size_t stride = size_t{kHeads} * qd::kAttentionPartialStride;
-      float value = 0.0f;
-#pragma unroll 8
-      for (uint32_t j = 0; j < chunks; ++j) {
-        value = fmaf(w[j], dev::load_cg(entry + j * stride), value);
+    for (uint32_t k = 0; k < 2; ++k) {
+      const uint32_t o = threadIdx.x + k * kThreads;
+      valid[k] = o < kOutputs;
+      const uint32_t h = valid[k] ? o / qd::kHeadSize : 0u, d = o % qd::kHeadSize;
+      w[k] = weights + h * kMaxAttentionChunks;
+      entry[k] = group_partials + h * qd::kAttentionPartialStride + d;
+    }
+    constexpr uint32_t kRound = 6;
+    for (uint32_t j0 = 0; j0 < chunks; j0 += kRound) {
+      float x[2][kRound];
+#pragma unroll
+      for (uint32_t k = 0; k < 2; ++k) {
+#pragma unroll
+        for (uint32_t j = 0; j < kRound; ++j) {
+          x[k][j] = valid[k] && j0 + j < chunks ? dev::load_cg(entry[k] + (j0 + j) * stride)
+                                                : 0.0f;
+        }
       }
-      c->query[(head0 + h) * qd::kHeadSize + d] = value;
+#pragma unroll
+      for (uint32_t k = 0; k < 2; ++k) {
+#pragma unroll
+        for (uint32_t j = 0; j < kRound; ++j) {
+          if (j0 + j < chunks) {
+            value[k] = fmaf(w[k][j0 + j], x[k][j], value[k]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < 2; ++k) {
+      const uint32_t o = threadIdx.x + k * kThreads;
+      if (valid[k]) {
+        c->query[(head0 + o / qd::kHeadSize) * qd::kHeadSize + o % qd::kHeadSize] = value[k];
+      }
     }
   }
   if (threadIdx.x == 0) {
