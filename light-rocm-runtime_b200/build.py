@@ -5,6 +5,7 @@ Outputs (git-ignored, shipped with the working tree):
   lib/liblrrt_qwen.so             Qwen decode driver (include/lrrt_qwen.h)
   lib/qwen_stateful_graph.cubin   sm_100a decode megakernels
   lib/qwen_prefill.cubin          sm_100a prompt prefill kernels
+  lib/decoder_ops.cubin + .json   per-operation decode kernels as an lrrt::bundle
   lib/stateful_graph_fixture.cubin  sm_100a scheduler fixture kernels
   _build/tests/*                  C++ host tests (tests/cpp)
 
@@ -84,12 +85,16 @@ def build(verbose: bool = False) -> dict[str, Path]:
               "-lrt", "-ldl", "-lpthread", "-Wl,-rpath,$ORIGIN"], verbose)
     outputs["driver"] = driver
 
-    for name in ("qwen_stateful_graph", "qwen_prefill", "stateful_graph_fixture"):
+    for name in ("qwen_stateful_graph", "qwen_prefill", "stateful_graph_fixture", "decoder_ops"):
         source = csrc / "kernels" / f"{name}.cu"
         cubin = LIB / f"{name}.cubin"
         if _stale(cubin, [source] + headers):
             _run([NVCC, *NVCCFLAGS, "-cubin", str(source), "-o", str(cubin)], verbose)
         outputs[name] = cubin
+    # Per-operation decode kernels as a bundle: manifest next to its cubin.
+    ops_manifest = LIB / "decoder_ops.json"
+    shutil.copyfile(csrc / "kernels" / "decoder_ops.json", ops_manifest)
+    outputs["decoder_ops_manifest"] = ops_manifest
 
     tests_dir = REPO / "tests" / "cpp"
     test_build = BUILD / "tests"
