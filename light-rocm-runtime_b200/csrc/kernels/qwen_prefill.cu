@@ -741,9 +741,24 @@ extern "C" __global__ void __launch_bounds__(256) prefill_reduce(pf::ReduceArgs 
   const float *partial = p.partials + local * tile_floats + size_t{r} * p.tile_columns +
                          column_in_tile;
   const size_t split_stride = size_t{p.tile_count} * tile_floats;
+  // Loads four splits at a time, sums in split order.
   float value = partial[0];
   float up = swiglu ? partial[out_columns] : 0.0f;
-  for (uint32_t s = 1; s < p.splits; ++s) {
+  uint32_t s = 1;
+  for (; s + 4u <= p.splits; s += 4u) {
+    float v[4], u[4];
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      v[j] = partial[(s + j) * split_stride];
+      u[j] = swiglu ? partial[(s + j) * split_stride + out_columns] : 0.0f;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      value += v[j];
+      up += u[j];
+    }
+  }
+  for (; s < p.splits; ++s) {
     value += partial[s * split_stride];
     if (swiglu) {
       up += partial[s * split_stride + out_columns];
@@ -885,30 +900,62 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
   }
   __syncwarp();
 
-  // Epilogue: thread (warp, lane) holds tile row 32 * warp + lane.
+  // Epilogue: thread (warp, lane) reads accumulator row 32 * warp + lane
+  // from TMEM, 32 columns at a time; the warp stages the 32 x 32 chunk in
+  // shared memory (the consumed stage ring) and stores it row by row, eight
+  // lanes per 128-byte row segment.
   const dev::Deadline finish(p.wait_limit_ms);
   const bool ready = dev::mbarrier_wait(&s.done, 0, finish);
   if (!ready) {
     fail();
   }
   tc_fence_after();
-  const uint32_t r = warp * 32u + lane;
-  const uint32_t row = m0 + r;
   const uint32_t lane_address = tmem + ((warp * 32u) << 16);
-  const bool store = ready && s.abort == 0 && count != 0;
-  if (p.mode == static_cast<uint32_t>(pf::GemmEpilogue::partial)) {
+  const uint32_t row_base = m0 + warp * 32u;
+  // Warps whose 32 rows all lie past m (short batches) store nothing.
+  const bool store = ready && s.abort == 0 && count != 0 && row_base < p.m;
+  float *stage = reinterpret_cast<float *>(tiles) + warp * 32u * 33u; // [32][33] per warp
+  const bool partial = p.mode == static_cast<uint32_t>(pf::GemmEpilogue::partial);
+  // Writes this thread's 32 values into the staging rows, then each lane
+  // emits float4 (row, column) pieces through `emit`. A tile with at most 32
+  // valid rows (short batches: warp 0 alone stores) skips the staging: each
+  // thread emits its own row, whose eight float4s already fill whole lines.
+  const bool direct_rows = p.m <= m0 + 32u;
+  auto staged = [&](const float (&v)[32], auto emit) {
+    if (direct_rows) {
+#pragma unroll
+      for (uint32_t c = 0; c < 32u; c += 4u) {
+        emit(lane, c, make_float4(v[c], v[c + 1u], v[c + 2u], v[c + 3u]));
+      }
+      return;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 32; ++j) {
+      stage[lane * 33u + j] = v[j];
+    }
+    __syncwarp();
+#pragma unroll
+    for (uint32_t it = 0; it < 8; ++it) {
+      const uint32_t r = it * 4u + lane / 8u, c = (lane % 8u) * 4u;
+      const float4 x = make_float4(stage[r * 33u + c], stage[r * 33u + c + 1u],
+                                   stage[r * 33u + c + 2u], stage[r * 33u + c + 3u]);
+      emit(r, c, x);
+    }
+    __syncwarp();
+  };
+  if (partial) {
     float *out = p.c + (size_t{blockIdx.z} * p.tile_count + blockIdx.x) * pf::kTcTileM * kN +
-                 size_t{r} * kN;
+                 size_t{warp * 32u} * kN;
 #pragma unroll 1
     for (uint32_t chunk = 0; chunk < kN / 32u; ++chunk) {
       float v[32];
       tc_load32(lane_address + chunk * 32u, v);
-      if (store && row < p.m) {
-        float4 *o = reinterpret_cast<float4 *>(out + chunk * 32u);
-#pragma unroll
-        for (uint32_t j = 0; j < 8; ++j) {
-          o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        }
+      if (store) {
+        staged(v, [&](uint32_t r, uint32_t c, float4 x) {
+          if (row_base + r < p.m) {
+            *reinterpret_cast<float4 *>(out + size_t{r} * kN + chunk * 32u + c) = x;
+          }
+        });
       }
     }
   } else if (swiglu) {
@@ -918,12 +965,25 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
       tc_load32(lane_address + chunk * 32u, gate);
       tc_load32(lane_address + kN / 2u + chunk * 32u, up);
       const uint32_t column = n_tile * (kN / 2u) + chunk * 32u;
-      if (store && row < p.m && column < p.n) {
-        const size_t at = size_t{row} * p.ldc + column;
+      if (store && column < p.n) {
 #pragma unroll
         for (uint32_t j = 0; j < 32; ++j) {
-          store_operand(p.c, p.c_lo, at + j, silu_times(gate[j], up[j]));
+          gate[j] = silu_times(gate[j], up[j]);
         }
+        staged(gate, [&](uint32_t r, uint32_t c, float4 x) {
+          if (row_base + r < p.m) {
+            const size_t at = size_t{row_base + r} * p.ldc + column + c;
+            if (p.c_lo == nullptr) {
+              *reinterpret_cast<float4 *>(p.c + at) = x;
+            } else {
+              const float4 hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+              *reinterpret_cast<float4 *>(p.c + at) = hi;
+              *reinterpret_cast<float4 *>(p.c_lo + at) =
+                  make_float4(to_tf32(x.x - hi.x), to_tf32(x.y - hi.y), to_tf32(x.z - hi.z),
+                              to_tf32(x.w - hi.w));
+            }
+          }
+        });
       }
     }
   } else {
@@ -932,12 +992,18 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
       float v[32];
       tc_load32(lane_address + chunk * 32u, v);
       const uint32_t column = n_tile * kN + chunk * 32u;
-      if (store && row < p.m && column < p.n) {
-        const size_t at = size_t{row} * p.ldc + column;
+      if (store && column < p.n) {
+        staged(v, [&](uint32_t r, uint32_t c, float4 x) {
+          if (row_base + r < p.m) {
+            const size_t at = size_t{row_base + r} * p.ldc + column + c;
+            const float values[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-        for (uint32_t j = 0; j < 32; ++j) {
-          finish_element(p.bias, p.c, p.c_lo, at + j, column + j, p.mode, v[j], 0.0f);
-        }
+            for (uint32_t e = 0; e < 4; ++e) {
+              finish_element(p.bias, p.c, p.c_lo, at + e, column + c + e, p.mode, values[e],
+                             0.0f);
+            }
+          }
+        });
       }
     }
   }

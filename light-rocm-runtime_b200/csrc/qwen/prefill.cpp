@@ -186,8 +186,11 @@ PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const T
     const uint32_t full = tiles / kSms * kSms;
     run(0, full, 1, true);
     if (tiles > full) {
+      // A few leftover tiles: split K to spread them over the SMs, keeping
+      // each slice at least four K steps long (shorter slices spend their
+      // time filling the pipeline and writing partials).
       const uint32_t rest = tiles - full;
-      run(full, rest, std::max(1u, std::min(kSms / rest, k_tiles / 2u)), true);
+      run(full, rest, std::max(1u, std::min(kSms / rest, k_tiles / 4u)), true);
     }
   } else {
     run(0, tiles, small_splits, true);
