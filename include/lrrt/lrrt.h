@@ -229,6 +229,16 @@ LRRT_API lr_status_t lr_kernel_set_resident(lr_kernel_t *kernel,
                                             uint32_t resident);
 
 /*
+ * Marks a kernel for overlapped (programmatic dependent) launches: each launch
+ * carries CUDA's programmatic stream serialization, so the kernel may begin
+ * while the previous kernel on the same queue is finishing. The kernel must
+ * execute `griddepcontrol.wait` before it reads anything an earlier launch
+ * wrote (and may execute `griddepcontrol.launch_dependents` to let the next
+ * overlapped launch begin). Unmarked kernels launch in plain stream order.
+ */
+LRRT_API lr_status_t lr_kernel_set_overlapped(lr_kernel_t *kernel, uint32_t overlapped);
+
+/*
  * Maximum number of blocks of `kernel` with `block_threads` threads and
  * `dynamic_shared_memory_bytes` of dynamic shared memory that can be resident
  * on the device at once (SMs x blocks per SM).

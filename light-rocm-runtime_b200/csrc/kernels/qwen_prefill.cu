@@ -53,6 +53,15 @@ __device__ __forceinline__ void store_operand(float *out, float *lo, size_t inde
   }
 }
 
+// Overlapped launches (lr_kernel_set_overlapped): every kernel of this
+// module may start while its predecessor on the queue finishes. It waits for
+// that grid (and so for every earlier one) before reading device data, then
+// lets its own successor start.
+__device__ __forceinline__ void dependent_launch_entry() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float silu_times(float gate, float up) {
   return (gate / (1.0f + expf(-gate))) * up;
 }
@@ -69,6 +78,7 @@ constexpr uint32_t kTileM = 128, kTileN = 128, kTileK = 16, kGemmThreads = 256;
 
 template <pf::GemmEpilogue kMode>
 __device__ __forceinline__ void simt_gemm(const pf::GemmArgs &p) {
+  dependent_launch_entry();
   constexpr bool kTwo = kMode == pf::GemmEpilogue::swiglu;
   __shared__ __align__(16) float as[kTileK][kTileM + 4];
   __shared__ __align__(16) float bs[kTileK][kTileN + 4];
@@ -308,6 +318,7 @@ extern "C" __global__ void __launch_bounds__(kGemmThreads) prefill_gemm_swiglu(p
 // One block per token; out-of-range token ids write a zero row (the host
 // rejects them before launching).
 extern "C" __global__ void __launch_bounds__(256) prefill_embed(pf::EmbedArgs p) {
+  dependent_launch_entry();
   const uint32_t t = blockIdx.x;
   if (t >= p.count) {
     return;
@@ -322,6 +333,7 @@ extern "C" __global__ void __launch_bounds__(256) prefill_embed(pf::EmbedArgs p)
 // One block per token: the decode step's RMSNorm (per-thread strided sum of
 // squares, shared-memory tree, 1/sqrt(mean + eps), x * inverse * weight).
 extern "C" __global__ void __launch_bounds__(256) prefill_rmsnorm(pf::NormArgs p) {
+  dependent_launch_entry();
   __shared__ float partial[256];
   const uint32_t t = blockIdx.x;
   if (t >= p.count) {
@@ -408,6 +420,7 @@ __device__ __forceinline__ void row_rmsnorm(const float *x, const float *weight,
 // per token. The row is first finished from the QKV GEMM's partial sums when
 // those are given.
 extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_rope_kv(pf::RopeArgs p) {
+  dependent_launch_entry();
   __shared__ float row[qd::kPackedQkvSize];
   const uint32_t t = blockIdx.x;
   if (t >= p.count) {
@@ -448,6 +461,7 @@ extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_rope_kv(pf::Ro
 // Residual finish of o_proj / down from their partial sums, then the next
 // RMSNorm of the same row (mlp norm, or the next layer's attention norm).
 extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_finish_rows(pf::FinishArgs p) {
+  dependent_launch_entry();
   __shared__ float row[qd::kHiddenSize];
   __shared__ float partial[256];
   const uint32_t t = blockIdx.x;
@@ -506,6 +520,7 @@ static_assert(sizeof(AttentionShared) == pf::kAttentionSharedBytes, "shared layo
 
 extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
     prefill_attention(pf::AttentionArgs p) {
+  dependent_launch_entry();
   extern __shared__ __align__(16) unsigned char attention_raw[];
   AttentionShared &sh = *reinterpret_cast<AttentionShared *>(attention_raw);
   const uint32_t g = threadIdx.x / kAttentionGroupThreads;
@@ -722,6 +737,7 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
 // [tile_offset, tile_offset + tile_count); partial sums are added in split
 // order, so the result does not depend on which CTA finished first.
 extern "C" __global__ void __launch_bounds__(256) prefill_reduce(pf::ReduceArgs p) {
+  dependent_launch_entry();
   const bool swiglu = p.mode == static_cast<uint32_t>(pf::GemmEpilogue::swiglu);
   const uint32_t out_columns = swiglu ? p.tile_columns / 2u : p.tile_columns;
   const uint64_t i = uint64_t{blockIdx.x} * blockDim.x + threadIdx.x;
@@ -769,6 +785,7 @@ extern "C" __global__ void __launch_bounds__(256) prefill_reduce(pf::ReduceArgs 
 
 // TF32 (hi, lo) split of an FP32 array (weights, once per weight change).
 extern "C" __global__ void __launch_bounds__(256) prefill_split(pf::SplitArgs p) {
+  dependent_launch_entry();
   const uint64_t stride = uint64_t{gridDim.x} * blockDim.x;
   for (uint64_t i = uint64_t{blockIdx.x} * blockDim.x + threadIdx.x; i < p.count; i += stride) {
     const float x = p.x[i];
@@ -837,6 +854,7 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem;
+  dependent_launch_entry(); // barriers and TMEM are ready; operands come next
 
   auto fail = [&]() {
     s.abort = 1;
@@ -1055,6 +1073,7 @@ struct DecodeShared {
 static_assert(sizeof(DecodeShared) == pf::kDecodeSharedBytes, "decode shared layout");
 
 extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAttentionArgs p) {
+  dependent_launch_entry();
   extern __shared__ __align__(16) unsigned char decode_raw[];
   DecodeShared &sh = *reinterpret_cast<DecodeShared *>(decode_raw);
   const uint32_t split = blockIdx.x, group = blockIdx.y, b = blockIdx.z;
@@ -1269,6 +1288,7 @@ __device__ __forceinline__ void block_top1(float &value, uint32_t &index, float 
 }
 
 extern "C" __global__ void __launch_bounds__(1024) batch_argmax(pf::ArgmaxArgs p) {
+  dependent_launch_entry();
   __shared__ float values[32];
   __shared__ uint32_t indices[32];
   __shared__ bool finisher;

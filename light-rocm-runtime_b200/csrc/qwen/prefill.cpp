@@ -26,6 +26,16 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   if (chunk_ == 0 || chunk_ > 8192) {
     throw std::invalid_argument("prefill chunk must be 1..8192 tokens");
   }
+  // Every kernel of the module waits for its predecessor before reading
+  // device data (griddepcontrol.wait), so all of them may launch overlapped:
+  // a kernel's prologue (barrier setup, TMEM allocation) runs while the
+  // previous kernel drains.
+  for (const Kernel *kernel :
+       {&embed_, &rmsnorm_, &rope_kv_, &attend_, &reduce_, &split_, &gemm_bias_, &gemm_residual_,
+        &gemm_swiglu_, &tc_n192_, &tc_n224_, &tc_n256_, &finish_rows_, &batch_attention_,
+        &batch_argmax_}) {
+    check(lr_kernel_set_overlapped(kernel->get(), 1), "lr_kernel_set_overlapped");
+  }
   const size_t c = chunk_;
   hidden_.emplace(allocate(sizeof(float) * c * kHidden));
   normalized_.emplace(allocate(sizeof(float) * c * kHidden));

@@ -52,6 +52,7 @@ struct lr_kernel_t {
   uint32_t local_bytes;
   uint32_t dynamic_shared_limit; // last MAX_DYNAMIC_SHARED_SIZE_BYTES set
   bool resident;
+  bool overlapped; // launches carry programmatic stream serialization
 };
 
 struct lr_module_t {
@@ -366,12 +367,19 @@ lr_status_t launch_impl(lr_kernel_t *kernel, const lr_launch_config_t *config,
   launch.blockDimZ = block.z;
   launch.sharedMemBytes = config->shared_memory_bytes;
   launch.hStream = stream;
-  CUlaunchAttribute attribute{};
+  CUlaunchAttribute attributes[2]{};
+  uint32_t attribute_count = 0;
   if (kernel->resident) {
-    attribute.id = CU_LAUNCH_ATTRIBUTE_COOPERATIVE;
-    attribute.value.cooperative = 1;
-    launch.attrs = &attribute;
-    launch.numAttrs = 1;
+    attributes[attribute_count].id = CU_LAUNCH_ATTRIBUTE_COOPERATIVE;
+    attributes[attribute_count++].value.cooperative = 1;
+  }
+  if (kernel->overlapped) {
+    attributes[attribute_count].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attributes[attribute_count++].value.programmaticStreamSerializationAllowed = 1;
+  }
+  if (attribute_count != 0) {
+    launch.attrs = attributes;
+    launch.numAttrs = attribute_count;
   }
   return cu(g_driver.cuLaunchKernelEx_(&launch, kernel->function,
                                        parameters.empty() ? nullptr
@@ -1093,6 +1101,7 @@ LRRT_API lr_status_t lr_kernel_get(lr_module_t *module, const char *name,
   created->local_bytes = static_cast<uint32_t>(local);
   created->dynamic_shared_limit = 48u * 1024u;
   created->resident = false;
+  created->overlapped = false;
   lr_kernel_t *handle = created.get();
   module->kernels.push_back(std::move(created));
   g_kernels.insert(handle);
@@ -1188,6 +1197,18 @@ LRRT_API lr_status_t lr_kernel_set_resident(lr_kernel_t *kernel,
     return LR_ERROR_INVALID_ARGUMENT;
   }
   kernel->resident = resident != 0;
+  return LR_SUCCESS;
+}
+
+LRRT_API lr_status_t lr_kernel_set_overlapped(lr_kernel_t *kernel, uint32_t overlapped) {
+  Lock lock(g_mutex);
+  if (!g_initialized) {
+    return LR_ERROR_NOT_INITIALIZED;
+  }
+  if (kernel == nullptr || g_kernels.count(kernel) == 0) {
+    return LR_ERROR_INVALID_ARGUMENT;
+  }
+  kernel->overlapped = overlapped != 0;
   return LR_SUCCESS;
 }
 

@@ -157,6 +157,7 @@ RUNTIME_FUNCTIONS = {
                                                    sz]),
     "lr_synchronize": (u32, [Device]),
     "lr_kernel_set_resident": (u32, [vp, u32]),
+    "lr_kernel_set_overlapped": (u32, [vp, u32]),
     "lr_kernel_max_resident_blocks": (u32, [vp, u32, u32, P(u32)]),
     "lr_queue_native_handle": (u32, [Device, vp, P(vp)]),
     "lr_last_error_detail": (u32, [C.c_char_p, sz]),

@@ -23,7 +23,7 @@ def declared(header: Path):
 def test_runtime_library_exports_every_declared_symbol(built):
     library = N.runtime()
     names = declared(REPO / "include" / "lrrt" / "lrrt.h")
-    assert len(names) == 39  # 35 reference entry points + 4 B200 additions
+    assert len(names) == 40  # 35 reference entry points + 5 B200 additions
     for name in names:
         assert hasattr(library, name), name
 
