@@ -1057,14 +1057,15 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 // Block (s, g, b): warp h < 7 serves query head 7g + h over key positions
 // [s * chunk, min((s + 1) * chunk, positions[b] + 1)), in tiles of
 // kDecodeKeys keys staged in shared memory in one load phase (K transposed,
-// so lane l scores keys l, l + 32, l + 64, l + 96 against the head's query,
-// read from shared memory); the decode step's online softmax (scale 1/8,
-// expf) per tile; lane l accumulates dims l and l + 32 of P.V.
+// so lane l scores keys 4l..4l+3 with one float4 read per dimension against
+// the head's query held in registers); the decode step's online softmax
+// (scale 1/8, expf) per tile; lane l accumulates dims 2l, 2l + 1 of P.V.
 constexpr uint32_t kDecodeKeys = 128;
 
 struct DecodeShared {
-  float q[qd::kQueriesPerKvHead][qd::kHeadSize];
-  float kt[qd::kHeadSize][kDecodeKeys + 1]; // [d][key]
+  // [d][key], rows padded to 132 floats: 16-byte aligned for the float4
+  // score reads, and the key-fastest transposed stores stay conflict-free.
+  float kt[qd::kHeadSize][kDecodeKeys + 4];
   float vs[kDecodeKeys][qd::kHeadSize];     // [key][d]
   float weight[qd::kQueriesPerKvHead][32];  // merge: per (head, split) scale
   float total[qd::kQueriesPerKvHead];
@@ -1081,15 +1082,24 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
   const uint32_t last = p.positions[b];
   const uint32_t begin = split * p.chunk;
   const uint32_t end = min(begin + p.chunk, last + 1u);
-  for (uint32_t i = threadIdx.x; i < qd::kQueriesPerKvHead * qd::kHeadSize; i += 256u) {
-    sh.q[i / qd::kHeadSize][i % qd::kHeadSize] =
-        p.qkv[size_t{b} * qd::kPackedQkvSize + group * qd::kQueriesPerKvHead * qd::kHeadSize + i];
+  float q[qd::kHeadSize]; // the warp's query head (lanes hold the same values)
+  if (warp < qd::kQueriesPerKvHead) {
+    const float4 *row = reinterpret_cast<const float4 *>(
+        p.qkv + size_t{b} * qd::kPackedQkvSize + (group * qd::kQueriesPerKvHead + warp) * qd::kHeadSize);
+#pragma unroll
+    for (uint32_t d = 0; d < qd::kHeadSize / 4u; ++d) {
+      const float4 x = row[d];
+      q[4 * d] = x.x;
+      q[4 * d + 1] = x.y;
+      q[4 * d + 2] = x.z;
+      q[4 * d + 3] = x.w;
+    }
   }
   const float *keys = p.key_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
   const float *values = p.value_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
   float maximum = -INFINITY, denominator = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
   for (uint32_t base = begin; base < end; base += kDecodeKeys) {
-    __syncthreads(); // previous tile's reads are done (and q is written)
+    __syncthreads(); // the previous tile's reads are done
     // All of the thread's K/V loads are issued before any shared store.
     constexpr uint32_t kLoads = kDecodeKeys * qd::kHeadSize / 4u / 256u;
     float4 k[kLoads], v[kLoads];
@@ -1123,18 +1133,18 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
     __syncthreads();
     if (warp < qd::kQueriesPerKvHead) {
       float score[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 16
-      for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
-        const float q = sh.q[warp][d];
 #pragma unroll
-        for (uint32_t j = 0; j < 4; ++j) {
-          score[j] = fmaf(q, sh.kt[d][lane + 32u * j], score[j]);
-        }
+      for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
+        const float4 k = *reinterpret_cast<const float4 *>(&sh.kt[d][4u * lane]);
+        score[0] = fmaf(q[d], k.x, score[0]);
+        score[1] = fmaf(q[d], k.y, score[1]);
+        score[2] = fmaf(q[d], k.z, score[2]);
+        score[3] = fmaf(q[d], k.w, score[3]);
       }
       float tile_maximum = -INFINITY;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        score[j] = base + lane + 32u * j < end ? score[j] * 0.125f : -INFINITY;
+        score[j] = base + 4u * lane + j < end ? score[j] * 0.125f : -INFINITY;
         tile_maximum = fmaxf(tile_maximum, score[j]);
       }
 #pragma unroll
@@ -1157,13 +1167,15 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       maximum = next;
       acc0 *= scale;
       acc1 *= scale;
+      // Key 4k + j's weight lives in lane k, slot j.
+#pragma unroll 4
+      for (uint32_t k = 0; k < 32u; ++k) {
 #pragma unroll
-      for (uint32_t j = 0; j < 4; ++j) {
-#pragma unroll 8
-        for (uint32_t key = 0; key < 32u; ++key) {
-          const float weight = __shfl_sync(kFullMask, w[j], key);
-          acc0 = fmaf(weight, sh.vs[32u * j + key][lane], acc0);
-          acc1 = fmaf(weight, sh.vs[32u * j + key][lane + 32u], acc1);
+        for (uint32_t j = 0; j < 4; ++j) {
+          const float weight = __shfl_sync(kFullMask, w[j], k);
+          const float2 v = *reinterpret_cast<const float2 *>(&sh.vs[4u * k + j][2u * lane]);
+          acc0 = fmaf(weight, v.x, acc0);
+          acc1 = fmaf(weight, v.y, acc1);
         }
       }
     }
@@ -1174,8 +1186,8 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
   if (warp < qd::kQueriesPerKvHead) {
     float *out = const_cast<float *>(group_partials) + split * split_stride +
                  size_t{warp} * pf::kDecodePartialStride;
-    out[lane] = acc0;
-    out[lane + 32u] = acc1;
+    out[2u * lane] = acc0;
+    out[2u * lane + 1u] = acc1;
     if (lane == 0) {
       out[64] = maximum;     // -inf when the split holds no key of this stream
       out[65] = denominator; // 0 then
