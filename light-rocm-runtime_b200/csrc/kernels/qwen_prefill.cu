@@ -1054,20 +1054,36 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 
 // Decode attention of one query row per stream, split over key positions;
 // the last split block of a (stream, KV group) merges the splits.
-// Block (s, g, b): warp h < 7 serves query head 7g + h over key positions
-// [s * chunk, min((s + 1) * chunk, positions[b] + 1)), in tiles of
-// kDecodeKeys keys staged in shared memory in one load phase (K transposed,
-// so lane l scores keys 4l..4l+3 with one float4 read per dimension against
-// the head's query held in registers); the decode step's online softmax
-// (scale 1/8, expf) per tile; lane l accumulates dims 2l, 2l + 1 of P.V.
+// Block (s, g, b) serves the 7 query heads 7g..7g+6 of KV head g of stream b
+// over key positions [s * chunk, min((s + 1) * chunk, positions[b] + 1)), in
+// tiles of kDecodeKeys keys staged in shared memory in one load phase (K
+// transposed, V row-major), each staged element read once per block for all
+// 7 heads:
+//   scores: warp w sums dims 8w..8w+7 of keys 4l..4l+3 (lane l, one float4
+//           K read per dim) for all 7 heads; the 8 dim-slice partials are
+//           summed in slice order by warp h (head h), which runs the decode
+//           step's online softmax (scale 1/8, expf) for the tile;
+//   P.V:    warp w accumulates keys 16w..16w+15 into dims 2l, 2l + 1 of all
+//           7 heads; the 8 key-slice sums are added in slice order after the
+//           last tile.
 constexpr uint32_t kDecodeKeys = 128;
+constexpr uint32_t kDecodeSlices = 8; // warps
 
 struct DecodeShared {
-  // [d][key], rows padded to 132 floats: 16-byte aligned for the float4
-  // score reads, and the key-fastest transposed stores stay conflict-free.
-  float kt[qd::kHeadSize][kDecodeKeys + 4];
-  float vs[kDecodeKeys][qd::kHeadSize];     // [key][d]
-  float weight[qd::kQueriesPerKvHead][32];  // merge: per (head, split) scale
+  // The load phase's K^T [d][key] (rows padded to 132 floats: 16-byte aligned
+  // float4 reads, conflict-free key-fastest stores); after the score sums,
+  // the same bytes hold the dim-slice partial scores, and after the last
+  // tile the key-slice partial P.V sums.
+  union {
+    float kt[qd::kHeadSize][kDecodeKeys + 4];
+    float scores[kDecodeSlices][qd::kQueriesPerKvHead][kDecodeKeys];
+    float sums[kDecodeSlices][qd::kQueriesPerKvHead][qd::kHeadSize];
+  };
+  float vs[kDecodeKeys][qd::kHeadSize]; // [key][d]
+  float q[qd::kQueriesPerKvHead][qd::kHeadSize];
+  float probability[qd::kQueriesPerKvHead][kDecodeKeys]; // the tile's softmax weights
+  float rescale[kDecodeSlices];                          // per head, [7] unused
+  float weight[qd::kQueriesPerKvHead][32];               // merge: per (head, split) scale
   float total[qd::kQueriesPerKvHead];
 };
 
@@ -1082,24 +1098,18 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
   const uint32_t last = p.positions[b];
   const uint32_t begin = split * p.chunk;
   const uint32_t end = min(begin + p.chunk, last + 1u);
-  float q[qd::kHeadSize]; // the warp's query head (lanes hold the same values)
-  if (warp < qd::kQueriesPerKvHead) {
-    const float4 *row = reinterpret_cast<const float4 *>(
-        p.qkv + size_t{b} * qd::kPackedQkvSize + (group * qd::kQueriesPerKvHead + warp) * qd::kHeadSize);
-#pragma unroll
-    for (uint32_t d = 0; d < qd::kHeadSize / 4u; ++d) {
-      const float4 x = row[d];
-      q[4 * d] = x.x;
-      q[4 * d + 1] = x.y;
-      q[4 * d + 2] = x.z;
-      q[4 * d + 3] = x.w;
-    }
+  if (threadIdx.x < qd::kQueriesPerKvHead * qd::kHeadSize / 4u) {
+    reinterpret_cast<float4 *>(&sh.q[0][0])[threadIdx.x] = reinterpret_cast<const float4 *>(
+        p.qkv + size_t{b} * qd::kPackedQkvSize +
+        group * qd::kQueriesPerKvHead * qd::kHeadSize)[threadIdx.x];
   }
   const float *keys = p.key_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
   const float *values = p.value_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
-  float maximum = -INFINITY, denominator = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+  // Warp h < 7: head h's running maximum and denominator (all lanes alike).
+  float maximum = -INFINITY, denominator = 0.0f;
+  float acc[qd::kQueriesPerKvHead][2] = {};
   for (uint32_t base = begin; base < end; base += kDecodeKeys) {
-    __syncthreads(); // the previous tile's reads are done
+    __syncthreads(); // the previous tile's reads are done (and q is written)
     // All of the thread's K/V loads are issued before any shared store.
     constexpr uint32_t kLoads = kDecodeKeys * qd::kHeadSize / 4u / 256u;
     float4 k[kLoads], v[kLoads];
@@ -1131,21 +1141,52 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       *reinterpret_cast<float4 *>(&sh.vs[vkey][vd]) = v[j];
     }
     __syncthreads();
-    if (warp < qd::kQueriesPerKvHead) {
-      float score[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    // Dim slice `warp` of the 7 x 4 scores of keys 4l..4l+3.
+    float score[qd::kQueriesPerKvHead][4] = {};
 #pragma unroll
-      for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
-        const float4 k = *reinterpret_cast<const float4 *>(&sh.kt[d][4u * lane]);
-        score[0] = fmaf(q[d], k.x, score[0]);
-        score[1] = fmaf(q[d], k.y, score[1]);
-        score[2] = fmaf(q[d], k.z, score[2]);
-        score[3] = fmaf(q[d], k.w, score[3]);
+    for (uint32_t half = 0; half < 2u; ++half) {
+      const uint32_t d0 = kDecodeSlices * warp + 4u * half;
+      float4 q[qd::kQueriesPerKvHead];
+#pragma unroll
+      for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+        q[h] = *reinterpret_cast<const float4 *>(&sh.q[h][d0]);
       }
+#pragma unroll
+      for (uint32_t i = 0; i < 4u; ++i) {
+        const float4 key4 = *reinterpret_cast<const float4 *>(&sh.kt[d0 + i][4u * lane]);
+#pragma unroll
+        for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+          const float qd_i = i == 0 ? q[h].x : i == 1 ? q[h].y : i == 2 ? q[h].z : q[h].w;
+          score[h][0] = fmaf(qd_i, key4.x, score[h][0]);
+          score[h][1] = fmaf(qd_i, key4.y, score[h][1]);
+          score[h][2] = fmaf(qd_i, key4.z, score[h][2]);
+          score[h][3] = fmaf(qd_i, key4.w, score[h][3]);
+        }
+      }
+    }
+    __syncthreads(); // K^T reads are done: its bytes take the partial scores
+#pragma unroll
+    for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+      *reinterpret_cast<float4 *>(&sh.scores[warp][h][4u * lane]) =
+          make_float4(score[h][0], score[h][1], score[h][2], score[h][3]);
+    }
+    __syncthreads();
+    if (warp < qd::kQueriesPerKvHead) {
+      float4 sum4 = *reinterpret_cast<const float4 *>(&sh.scores[0][warp][4u * lane]);
+#pragma unroll
+      for (uint32_t slice = 1; slice < kDecodeSlices; ++slice) {
+        const float4 x = *reinterpret_cast<const float4 *>(&sh.scores[slice][warp][4u * lane]);
+        sum4.x += x.x;
+        sum4.y += x.y;
+        sum4.z += x.z;
+        sum4.w += x.w;
+      }
+      float s4[4] = {sum4.x, sum4.y, sum4.z, sum4.w};
       float tile_maximum = -INFINITY;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        score[j] = base + 4u * lane + j < end ? score[j] * 0.125f : -INFINITY;
-        tile_maximum = fmaxf(tile_maximum, score[j]);
+        s4[j] = base + 4u * lane + j < end ? s4[j] * 0.125f : -INFINITY;
+        tile_maximum = fmaxf(tile_maximum, s4[j]);
       }
 #pragma unroll
       for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
@@ -1156,7 +1197,7 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       float w[4], sum = 0.0f;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        w[j] = expf(score[j] - next);
+        w[j] = expf(s4[j] - next);
         sum += w[j];
       }
 #pragma unroll
@@ -1165,33 +1206,64 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       }
       denominator = denominator * scale + sum;
       maximum = next;
-      acc0 *= scale;
-      acc1 *= scale;
-      // Key 4k + j's weight lives in lane k, slot j.
-#pragma unroll 4
-      for (uint32_t k = 0; k < 32u; ++k) {
+      *reinterpret_cast<float4 *>(&sh.probability[warp][4u * lane]) =
+          make_float4(w[0], w[1], w[2], w[3]);
+      if (lane == 0) {
+        sh.rescale[warp] = scale;
+      }
+    }
+    __syncthreads();
+    // Key slice `warp` (keys 16w..16w+15) into dims 2l, 2l + 1 of the 7 heads.
 #pragma unroll
-        for (uint32_t j = 0; j < 4; ++j) {
-          const float weight = __shfl_sync(kFullMask, w[j], k);
-          const float2 v = *reinterpret_cast<const float2 *>(&sh.vs[4u * k + j][2u * lane]);
-          acc0 = fmaf(weight, v.x, acc0);
-          acc1 = fmaf(weight, v.y, acc1);
+    for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+      const float scale = sh.rescale[h];
+      acc[h][0] *= scale;
+      acc[h][1] *= scale;
+    }
+#pragma unroll
+    for (uint32_t c = 0; c < 4u; ++c) {
+      const uint32_t key0 = 16u * warp + 4u * c;
+      float4 weight[qd::kQueriesPerKvHead];
+#pragma unroll
+      for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+        weight[h] = *reinterpret_cast<const float4 *>(&sh.probability[h][key0]);
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < 4u; ++j) {
+        const float2 v2 = *reinterpret_cast<const float2 *>(&sh.vs[key0 + j][2u * lane]);
+#pragma unroll
+        for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+          const float pj =
+              j == 0 ? weight[h].x : j == 1 ? weight[h].y : j == 2 ? weight[h].z : weight[h].w;
+          acc[h][0] = fmaf(pj, v2.x, acc[h][0]);
+          acc[h][1] = fmaf(pj, v2.y, acc[h][1]);
         }
       }
     }
   }
+  // No thread reads the K^T / score bytes after the last softmax: the key
+  // slices' sums go there.
+#pragma unroll
+  for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+    *reinterpret_cast<float2 *>(&sh.sums[warp][h][2u * lane]) = make_float2(acc[h][0], acc[h][1]);
+  }
+  __syncthreads();
   const float *group_partials = p.partials + (size_t{b} * qd::kKvHeads + group) * p.splits *
                                                  qd::kQueriesPerKvHead * pf::kDecodePartialStride;
   const size_t split_stride = size_t{qd::kQueriesPerKvHead} * pf::kDecodePartialStride;
-  if (warp < qd::kQueriesPerKvHead) {
-    float *out = const_cast<float *>(group_partials) + split * split_stride +
-                 size_t{warp} * pf::kDecodePartialStride;
-    out[2u * lane] = acc0;
-    out[2u * lane + 1u] = acc1;
-    if (lane == 0) {
-      out[64] = maximum;     // -inf when the split holds no key of this stream
-      out[65] = denominator; // 0 then
+  float *own = const_cast<float *>(group_partials) + split * split_stride;
+  for (uint32_t i = threadIdx.x; i < qd::kQueriesPerKvHead * qd::kHeadSize; i += 256u) {
+    const uint32_t h = i / qd::kHeadSize, d = i % qd::kHeadSize;
+    float value = sh.sums[0][h][d];
+#pragma unroll
+    for (uint32_t slice = 1; slice < kDecodeSlices; ++slice) {
+      value += sh.sums[slice][h][d];
     }
+    own[size_t{h} * pf::kDecodePartialStride + d] = value;
+  }
+  if (warp < qd::kQueriesPerKvHead && lane == 0) {
+    own[size_t{warp} * pf::kDecodePartialStride + 64] = maximum;     // -inf: the split holds
+    own[size_t{warp} * pf::kDecodePartialStride + 65] = denominator; // no key of this stream
   }
   // The last split block of (b, group) to arrive combines the splits: per
   // head, rescale to the common maximum, sum, divide.
