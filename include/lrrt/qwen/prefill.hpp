@@ -149,11 +149,11 @@ struct AttentionArgs {
 // out[b][head * 64 + d] (TF32 pair when out_lo is set).
 constexpr uint32_t kDecodePartialStride = 66;
 constexpr uint32_t kDecodeMaximumSplits = 32;
-// Dynamic shared memory of batch_attention: K^T[64][132] (reused for the
+// Dynamic shared memory of batch_attention: K[128][68] (reused for the
 // partial scores and sums), V[128][64], queries [7][64], softmax weights
 // [7][128], rescales [8], merge weights [7][32] and totals [7].
 constexpr uint32_t kDecodeSharedBytes =
-    4u * (64u * 132u + 128u * 64u + 7u * 64u + 7u * 128u + 8u + 7u * 32u + 7u);
+    4u * (128u * 68u + 128u * 64u + 7u * 64u + 7u * 128u + 8u + 7u * 32u + 7u);
 struct DecodeAttentionArgs {
   const float *qkv;         // [streams][1152], q rotated
   const float *key_cache;   // stream b's cache at key_cache + b * stream_stride

@@ -1056,26 +1056,27 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 // the last split block of a (stream, KV group) merges the splits.
 // Block (s, g, b) serves the 7 query heads 7g..7g+6 of KV head g of stream b
 // over key positions [s * chunk, min((s + 1) * chunk, positions[b] + 1)), in
-// tiles of kDecodeKeys keys staged in shared memory in one load phase (K
-// transposed, V row-major), each staged element read once per block for all
-// 7 heads:
-//   scores: warp w sums dims 8w..8w+7 of keys 4l..4l+3 (lane l, one float4
-//           K read per dim) for all 7 heads; the 8 dim-slice partials are
-//           summed in slice order by warp h (head h), which runs the decode
-//           step's online softmax (scale 1/8, expf) for the tile;
+// tiles of kDecodeKeys keys copied into shared memory with cp.async (K, then
+// V as a second group that lands while the scores are computed; positions
+// past the range are zero-filled), each staged element read once per block
+// for all 7 heads:
+//   scores: warp w sums dims 8w..8w+7 of keys l, l + 32, l + 64, l + 96
+//           (lane l, float4 reads along the key rows) for all 7 heads; the 8
+//           dim-slice partials are summed in slice order by warp h (head h),
+//           which runs the decode step's online softmax (scale 1/8, expf);
 //   P.V:    warp w accumulates keys 16w..16w+15 into dims 2l, 2l + 1 of all
 //           7 heads; the 8 key-slice sums are added in slice order after the
 //           last tile.
 constexpr uint32_t kDecodeKeys = 128;
 constexpr uint32_t kDecodeSlices = 8; // warps
+constexpr uint32_t kDecodeKeyPitch = qd::kHeadSize + 4u; // conflict-free float4 column reads
 
 struct DecodeShared {
-  // The load phase's K^T [d][key] (rows padded to 132 floats: 16-byte aligned
-  // float4 reads, conflict-free key-fastest stores); after the score sums,
-  // the same bytes hold the dim-slice partial scores, and after the last
-  // tile the key-slice partial P.V sums.
+  // The tile's K rows; after the score sums, the same bytes hold the
+  // dim-slice partial scores, and after the last tile the key-slice partial
+  // P.V sums.
   union {
-    float kt[qd::kHeadSize][kDecodeKeys + 4];
+    float ks[kDecodeKeys][kDecodeKeyPitch];
     float scores[kDecodeSlices][qd::kQueriesPerKvHead][kDecodeKeys];
     float sums[kDecodeSlices][qd::kQueriesPerKvHead][qd::kHeadSize];
   };
@@ -1088,6 +1089,15 @@ struct DecodeShared {
 };
 
 static_assert(sizeof(DecodeShared) == pf::kDecodeSharedBytes, "decode shared layout");
+
+// 16 bytes global -> shared without registers; `bytes` 0 zero-fills.
+__device__ __forceinline__ void copy16_async(void *destination, const void *source,
+                                             uint32_t bytes) {
+  const uint32_t address = static_cast<uint32_t>(__cvta_generic_to_shared(destination));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(address), "l"(source),
+               "r"(bytes)
+               : "memory");
+}
 
 extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAttentionArgs p) {
   dependent_launch_entry();
@@ -1110,82 +1120,75 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
   float acc[qd::kQueriesPerKvHead][2] = {};
   for (uint32_t base = begin; base < end; base += kDecodeKeys) {
     __syncthreads(); // the previous tile's reads are done (and q is written)
-    // All of the thread's K/V loads are issued before any shared store.
-    constexpr uint32_t kLoads = kDecodeKeys * qd::kHeadSize / 4u / 256u;
-    float4 k[kLoads], v[kLoads];
+    // Thread t copies 16-byte chunks t + 256j (row = chunk / 16): coalesced
+    // 256-byte row reads; rows at or past `end` read nothing and become 0.
+    constexpr uint32_t kChunks = kDecodeKeys * qd::kHeadSize / 4u / 256u;
 #pragma unroll
-    for (uint32_t j = 0; j < kLoads; ++j) {
-      const uint32_t i = threadIdx.x + 256u * j;
-      const uint32_t key = i % kDecodeKeys, d = (i / kDecodeKeys) * 4u;
-      // K: key-fastest threads (transposed shared store, consecutive keys);
-      // V: dim-fastest threads (row store, consecutive float4s), so that
-      // neither shared store conflicts.
-      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
-      k[j] = v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (base + key < end) {
-        k[j] = *reinterpret_cast<const float4 *>(keys + size_t{base + key} * qd::kKvSize + d);
-      }
-      if (base + vkey < end) {
-        v[j] = *reinterpret_cast<const float4 *>(values + size_t{base + vkey} * qd::kKvSize + vd);
-      }
+    for (uint32_t j = 0; j < kChunks; ++j) {
+      const uint32_t i = threadIdx.x + 256u * j, key = i / 16u, c = (i % 16u) * 4u;
+      const bool valid = base + key < end;
+      copy16_async(&sh.ks[key][c], keys + size_t{valid ? base + key : base} * qd::kKvSize + c,
+                   valid ? 16u : 0u);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
 #pragma unroll
-    for (uint32_t j = 0; j < kLoads; ++j) {
-      const uint32_t i = threadIdx.x + 256u * j;
-      const uint32_t key = i % kDecodeKeys, d = (i / kDecodeKeys) * 4u;
-      sh.kt[d][key] = k[j].x;
-      sh.kt[d + 1][key] = k[j].y;
-      sh.kt[d + 2][key] = k[j].z;
-      sh.kt[d + 3][key] = k[j].w;
-      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
-      *reinterpret_cast<float4 *>(&sh.vs[vkey][vd]) = v[j];
+    for (uint32_t j = 0; j < kChunks; ++j) {
+      const uint32_t i = threadIdx.x + 256u * j, key = i / 16u, c = (i % 16u) * 4u;
+      const bool valid = base + key < end;
+      copy16_async(&sh.vs[key][c], values + size_t{valid ? base + key : base} * qd::kKvSize + c,
+                   valid ? 16u : 0u);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory"); // this thread's K chunks
     __syncthreads();
-    // Dim slice `warp` of the 7 x 4 scores of keys 4l..4l+3.
+    // Dim slice `warp` of the 7 x 4 scores of keys l + 32j.
     float score[qd::kQueriesPerKvHead][4] = {};
 #pragma unroll
     for (uint32_t half = 0; half < 2u; ++half) {
       const uint32_t d0 = kDecodeSlices * warp + 4u * half;
-      float4 q[qd::kQueriesPerKvHead];
+      float4 key4[4];
 #pragma unroll
-      for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
-        q[h] = *reinterpret_cast<const float4 *>(&sh.q[h][d0]);
+      for (uint32_t j = 0; j < 4u; ++j) {
+        key4[j] = *reinterpret_cast<const float4 *>(&sh.ks[lane + 32u * j][d0]);
       }
 #pragma unroll
-      for (uint32_t i = 0; i < 4u; ++i) {
-        const float4 key4 = *reinterpret_cast<const float4 *>(&sh.kt[d0 + i][4u * lane]);
+      for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
+        const float4 q = *reinterpret_cast<const float4 *>(&sh.q[h][d0]);
 #pragma unroll
-        for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
-          const float qd_i = i == 0 ? q[h].x : i == 1 ? q[h].y : i == 2 ? q[h].z : q[h].w;
-          score[h][0] = fmaf(qd_i, key4.x, score[h][0]);
-          score[h][1] = fmaf(qd_i, key4.y, score[h][1]);
-          score[h][2] = fmaf(qd_i, key4.z, score[h][2]);
-          score[h][3] = fmaf(qd_i, key4.w, score[h][3]);
+        for (uint32_t j = 0; j < 4u; ++j) {
+          score[h][j] = fmaf(q.x, key4[j].x, score[h][j]);
+          score[h][j] = fmaf(q.y, key4[j].y, score[h][j]);
+          score[h][j] = fmaf(q.z, key4[j].z, score[h][j]);
+          score[h][j] = fmaf(q.w, key4[j].w, score[h][j]);
         }
       }
     }
-    __syncthreads(); // K^T reads are done: its bytes take the partial scores
+    __syncthreads(); // K reads are done: its bytes take the partial scores
 #pragma unroll
     for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
-      *reinterpret_cast<float4 *>(&sh.scores[warp][h][4u * lane]) =
-          make_float4(score[h][0], score[h][1], score[h][2], score[h][3]);
+#pragma unroll
+      for (uint32_t j = 0; j < 4u; ++j) {
+        sh.scores[warp][h][lane + 32u * j] = score[h][j];
+      }
     }
     __syncthreads();
     if (warp < qd::kQueriesPerKvHead) {
-      float4 sum4 = *reinterpret_cast<const float4 *>(&sh.scores[0][warp][4u * lane]);
+      float s4[4];
+#pragma unroll
+      for (uint32_t j = 0; j < 4u; ++j) {
+        s4[j] = sh.scores[0][warp][lane + 32u * j];
+      }
 #pragma unroll
       for (uint32_t slice = 1; slice < kDecodeSlices; ++slice) {
-        const float4 x = *reinterpret_cast<const float4 *>(&sh.scores[slice][warp][4u * lane]);
-        sum4.x += x.x;
-        sum4.y += x.y;
-        sum4.z += x.z;
-        sum4.w += x.w;
+#pragma unroll
+        for (uint32_t j = 0; j < 4u; ++j) {
+          s4[j] += sh.scores[slice][warp][lane + 32u * j];
+        }
       }
-      float s4[4] = {sum4.x, sum4.y, sum4.z, sum4.w};
       float tile_maximum = -INFINITY;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        s4[j] = base + 4u * lane + j < end ? s4[j] * 0.125f : -INFINITY;
+        s4[j] = base + lane + 32u * j < end ? s4[j] * 0.125f : -INFINITY;
         tile_maximum = fmaxf(tile_maximum, s4[j]);
       }
 #pragma unroll
@@ -1194,11 +1197,12 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       }
       const float next = fmaxf(maximum, tile_maximum); // finite: key `base` is in range
       const float scale = expf(maximum - next);
-      float w[4], sum = 0.0f;
+      float sum = 0.0f;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        w[j] = expf(s4[j] - next);
-        sum += w[j];
+        const float w = expf(s4[j] - next);
+        sh.probability[warp][lane + 32u * j] = w;
+        sum += w;
       }
 #pragma unroll
       for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
@@ -1206,12 +1210,11 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       }
       denominator = denominator * scale + sum;
       maximum = next;
-      *reinterpret_cast<float4 *>(&sh.probability[warp][4u * lane]) =
-          make_float4(w[0], w[1], w[2], w[3]);
       if (lane == 0) {
         sh.rescale[warp] = scale;
       }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory"); // this thread's V chunks
     __syncthreads();
     // Key slice `warp` (keys 16w..16w+15) into dims 2l, 2l + 1 of the 7 heads.
 #pragma unroll
@@ -1241,7 +1244,7 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       }
     }
   }
-  // No thread reads the K^T / score bytes after the last softmax: the key
+  // No thread reads the K / score bytes after the last softmax: the key
   // slices' sums go there.
 #pragma unroll
   for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
