@@ -80,14 +80,15 @@ struct ReduceArgs {
   uint32_t mode;          // GemmEpilogue (not partial)
   uint32_t tile_offset, tile_count, n_tiles, splits;
   uint32_t tile_columns;  // accumulator columns per tile (swiglu: gate + up)
+  uint32_t tile_rows;     // rows per tile: kTcTileM, or kNarrowRows
 };
 
 // Split-K partial accumulators of a tensor-core GEMM whose finish is left
 // to the next row kernel: tiles [0, tile_count) of the output's tile grid
-// (n_tiles per 128-row band), [split][tile][128][tile_columns].
+// (n_tiles per band of tile_rows rows), [split][tile][tile_rows][tile_columns].
 struct PartialTiles {
   const float *partials; // null: the GEMM wrote its output directly
-  uint32_t splits, n_tiles, tile_count, tile_columns;
+  uint32_t splits, n_tiles, tile_count, tile_columns, tile_rows;
 };
 
 // RoPE on the q and k parts of qkv rows [count][1152] at positions
@@ -237,6 +238,25 @@ LRRT_PREFILL_HD constexpr uint32_t tc_stages(uint32_t n) {
 }
 LRRT_PREFILL_HD constexpr uint32_t tc_shared_bytes(uint32_t n) {
   return tc_stages(n) * tc_stage_bytes(n) + 1024u /* alignment */ + 256u /* barriers */;
+}
+
+// Narrow GEMMs (at most kNarrowRows rows: batched decode, short chunks) swap
+// the operands: a tile is kNarrowTileN weight rows (the MMA's M) times the
+// kNarrowRows activation rows (its N). Paired tiles (swiglu) hold the gate
+// rows and the matching up rows in two accumulators.
+constexpr uint32_t kNarrowRows = 32;
+constexpr uint32_t kNarrowTileN = 128;
+constexpr uint32_t kNarrowTmemColumns = 64;
+LRRT_PREFILL_HD constexpr uint32_t tc_narrow_stage_bytes(bool paired) {
+  return 2u * ((paired ? 2u : 1u) * kNarrowTileN + kNarrowRows) * kTcTileK * 4u;
+}
+LRRT_PREFILL_HD constexpr uint32_t tc_narrow_stages(bool paired) {
+  return (200u * 1024u) / tc_narrow_stage_bytes(paired) > 8u
+             ? 8u
+             : (200u * 1024u) / tc_narrow_stage_bytes(paired);
+}
+LRRT_PREFILL_HD constexpr uint32_t tc_narrow_shared_bytes(bool paired) {
+  return tc_narrow_stages(paired) * tc_narrow_stage_bytes(paired) + 1024u + 256u;
 }
 
 constexpr uint32_t kTcErrorWaitTimeout = 1;

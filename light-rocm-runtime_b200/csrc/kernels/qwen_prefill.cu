@@ -365,10 +365,10 @@ using pf::kMaximumDeferredSplits;
 
 __device__ __forceinline__ float partial_sum(const pf::PartialTiles &tiles, uint32_t t,
                                              uint32_t column) {
-  const uint32_t tile = (t / pf::kTcTileM) * tiles.n_tiles + column / tiles.tile_columns;
-  const size_t tile_floats = size_t{pf::kTcTileM} * tiles.tile_columns;
+  const uint32_t tile = (t / tiles.tile_rows) * tiles.n_tiles + column / tiles.tile_columns;
+  const size_t tile_floats = size_t{tiles.tile_rows} * tiles.tile_columns;
   const float *at = tiles.partials + size_t{tile} * tile_floats +
-                    size_t{t % pf::kTcTileM} * tiles.tile_columns + column % tiles.tile_columns;
+                    size_t{t % tiles.tile_rows} * tiles.tile_columns + column % tiles.tile_columns;
   const size_t split_stride = size_t{tiles.tile_count} * tile_floats;
   float values[kMaximumDeferredSplits];
 #pragma unroll
@@ -741,19 +741,19 @@ extern "C" __global__ void __launch_bounds__(256) prefill_reduce(pf::ReduceArgs 
   const bool swiglu = p.mode == static_cast<uint32_t>(pf::GemmEpilogue::swiglu);
   const uint32_t out_columns = swiglu ? p.tile_columns / 2u : p.tile_columns;
   const uint64_t i = uint64_t{blockIdx.x} * blockDim.x + threadIdx.x;
-  if (i >= uint64_t{p.tile_count} * pf::kTcTileM * out_columns) {
+  if (i >= uint64_t{p.tile_count} * p.tile_rows * out_columns) {
     return;
   }
-  const uint32_t local = static_cast<uint32_t>(i / (uint64_t{pf::kTcTileM} * out_columns));
-  const uint32_t r = static_cast<uint32_t>((i / out_columns) % pf::kTcTileM);
+  const uint32_t local = static_cast<uint32_t>(i / (uint64_t{p.tile_rows} * out_columns));
+  const uint32_t r = static_cast<uint32_t>((i / out_columns) % p.tile_rows);
   const uint32_t column_in_tile = static_cast<uint32_t>(i % out_columns);
   const uint32_t tile = p.tile_offset + local;
-  const uint32_t row = (tile / p.n_tiles) * pf::kTcTileM + r;
+  const uint32_t row = (tile / p.n_tiles) * p.tile_rows + r;
   const uint32_t column = (tile % p.n_tiles) * out_columns + column_in_tile;
   if (row >= p.m || column >= p.n) {
     return;
   }
-  const size_t tile_floats = size_t{pf::kTcTileM} * p.tile_columns;
+  const size_t tile_floats = size_t{p.tile_rows} * p.tile_columns;
   const float *partial = p.partials + local * tile_floats + size_t{r} * p.tile_columns +
                          column_in_tile;
   const size_t split_stride = size_t{p.tile_count} * tile_floats;
@@ -1048,6 +1048,191 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
     prefill_tc_gemm_n256(const __grid_constant__ pf::TcGemmArgs p) {
   tc_gemm<256>(p);
+}
+
+// Narrow 3xTF32 GEMM (m <= kNarrowRows rows) with the operands swapped:
+// CTA (x, 0, z) computes output columns [n0, n0 + 128), n0 = 128 *
+// (tile_offset + x), over K slice z as D^T = W . X^T: the 128 weight rows
+// (TMA maps a_hi / a_lo, box 16 x 128) are the MMA's A operand (M = 128) and
+// the 32 activation rows (b_hi / b_lo, box 16 x 32; rows past m are never
+// stored) its B operand (N = 32), so the tensor cores spend nothing on
+// padding rows and each weight byte is read once per step. kPaired
+// (swiglu): a second accumulator takes the up rows n_gate_offset + n0...;
+// the gate/up pair lands on the same thread. Same ring, roles and bounded
+// waits as tc_gemm; thread (warp, lane) owns output column n0 + 32 * warp +
+// lane and walks the rows, so each row's 32 columns per warp are one
+// 128-byte store. Partial tiles: [split][tile][kNarrowRows][128 or 256].
+template <bool kPaired>
+__device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
+  constexpr uint32_t kStages = pf::tc_narrow_stages(kPaired);
+  constexpr uint32_t kStageBytes = pf::tc_narrow_stage_bytes(kPaired);
+  constexpr uint32_t kWeightBytes = pf::kNarrowTileN * pf::kTcTileK * 4u;
+  constexpr uint32_t kRowBytes = pf::kNarrowRows * pf::kTcTileK * 4u;
+  constexpr uint32_t kWeights = kPaired ? 2u : 1u;
+  constexpr uint32_t kTileColumns = kWeights * pf::kNarrowTileN;
+  constexpr uint32_t kInstruction = tc_instruction<pf::kNarrowRows>();
+  static_assert(kWeightBytes % 512 == 0 && kRowBytes % 512 == 0, "swizzle atom alignment");
+  extern __shared__ __align__(1024) unsigned char raw_shared[];
+  unsigned char *tiles = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(raw_shared) + 1023u) & ~uintptr_t{1023});
+  auto &s = *reinterpret_cast<TcShared<kStages> *>(tiles + kStages * kStageBytes);
+  // Stage: W_hi, W_lo (then the up rows' W_hi, W_lo), X_hi, X_lo.
+  auto w_hi = [&](uint32_t st, uint32_t w) { return tiles + st * kStageBytes + 2u * w * kWeightBytes; };
+  auto w_lo = [&](uint32_t st, uint32_t w) { return w_hi(st, w) + kWeightBytes; };
+  auto x_hi = [&](uint32_t st) { return tiles + st * kStageBytes + 2u * kWeights * kWeightBytes; };
+  auto x_lo = [&](uint32_t st) { return x_hi(st) + kRowBytes; };
+
+  const uint32_t warp = threadIdx.x >> 5u, lane = threadIdx.x & 31u;
+  const uint32_t tile = p.tile_offset + blockIdx.x;
+  const uint32_t n0 = tile * pf::kNarrowTileN;
+  const uint32_t k_tiles = p.k / pf::kTcTileK;
+  const uint32_t first_tile = blockIdx.z * k_tiles / p.splits;
+  const uint32_t count = (blockIdx.z + 1u) * k_tiles / p.splits - first_tile;
+  const dev::Deadline deadline(p.wait_limit_ms);
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < kStages; ++i) {
+      dev::mbarrier_init(&s.full[i], 1);
+      dev::mbarrier_init(&s.empty[i], 1);
+    }
+    dev::mbarrier_init(&s.done, 1);
+    s.abort = 0;
+    dev::mbarrier_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     dev::shared_address(&s.tmem)),
+                 "r"(pf::kNarrowTmemColumns)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem;
+  dependent_launch_entry(); // barriers and TMEM are ready; operands come next
+
+  auto fail = [&]() {
+    s.abort = 1;
+    atomicExch(p.error, pf::kTcErrorWaitTimeout);
+  };
+
+  if (warp == 0 && lane == 0) {
+    uint32_t issued = 0;
+    for (uint32_t i = 0; i < count && s.abort == 0; ++i) {
+      const uint32_t st = i % kStages;
+      if (i >= kStages && !dev::mbarrier_wait(&s.empty[st], ((i / kStages) + 1u) & 1u, deadline)) {
+        fail();
+        break;
+      }
+      const uint32_t k0 = (first_tile + i) * pf::kTcTileK;
+      dev::mbarrier_arrive_expect_tx(&s.full[st], kStageBytes);
+#pragma unroll
+      for (uint32_t w = 0; w < kWeights; ++w) {
+        const uint32_t row = w == 0 ? n0 : p.n_gate_offset + n0;
+        tma_load_2d(w_hi(st, w), &p.a_hi, k0, row, &s.full[st]);
+        tma_load_2d(w_lo(st, w), &p.a_lo, k0, row, &s.full[st]);
+      }
+      tma_load_2d(x_hi(st), &p.b_hi, k0, 0, &s.full[st]);
+      tma_load_2d(x_lo(st), &p.b_lo, k0, 0, &s.full[st]);
+      ++issued;
+    }
+    const dev::Deadline drain(p.wait_limit_ms);
+    for (uint32_t i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+      if (!dev::mbarrier_wait(&s.full[i % kStages], (i / kStages) & 1u, drain)) {
+        fail();
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // Per stage two K = 8 steps, three products per accumulator each.
+    for (uint32_t i = 0; i < count; ++i) {
+      const uint32_t st = i % kStages;
+      if (!dev::mbarrier_wait(&s.full[st], (i / kStages) & 1u, deadline)) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const uint64_t xh = sw64_descriptor(x_hi(st)), xl = sw64_descriptor(x_lo(st));
+#pragma unroll
+      for (uint32_t w = 0; w < kWeights; ++w) {
+        const uint64_t wh = sw64_descriptor(w_hi(st, w)), wl = sw64_descriptor(w_lo(st, w));
+        const uint32_t d = tmem + w * pf::kNarrowRows;
+#pragma unroll
+        for (uint32_t kk = 0; kk < pf::kTcTileK / 8u; ++kk) {
+          const uint64_t step = kk * 2u; // 32 bytes, in 16-byte descriptor units
+          tc_mma(d, wh + step, xh + step, kInstruction, (i | kk) != 0 ? 1u : 0u);
+          tc_mma(d, wh + step, xl + step, kInstruction, 1u);
+          tc_mma(d, wl + step, xh + step, kInstruction, 1u);
+        }
+      }
+      tc_commit(&s.empty[st]);
+    }
+    tc_commit(&s.done);
+  }
+  __syncwarp();
+
+  const dev::Deadline finish(p.wait_limit_ms);
+  const bool ready = dev::mbarrier_wait(&s.done, 0, finish);
+  if (!ready) {
+    fail();
+  }
+  tc_fence_after();
+  const uint32_t lane_address = tmem + ((warp * 32u) << 16);
+  const uint32_t local = warp * 32u + lane; // column within the tile
+  const uint32_t column = n0 + local;
+  const bool store = ready && s.abort == 0 && count != 0;
+  float v[32];
+  tc_load32(lane_address, v);
+  float up[32];
+  if (kPaired) {
+    tc_load32(lane_address + pf::kNarrowRows, up);
+  }
+  if (store) {
+    if (p.mode == static_cast<uint32_t>(pf::GemmEpilogue::partial)) {
+      float *out = p.c + (size_t{blockIdx.z} * p.tile_count + blockIdx.x) * pf::kNarrowRows *
+                             kTileColumns +
+                   local;
+#pragma unroll
+      for (uint32_t r = 0; r < pf::kNarrowRows; ++r) {
+        if (r < p.m) {
+          out[r * kTileColumns] = v[r];
+          if (kPaired) {
+            out[r * kTileColumns + pf::kNarrowTileN] = up[r];
+          }
+        }
+      }
+    } else if (column < p.n) {
+#pragma unroll
+      for (uint32_t r = 0; r < pf::kNarrowRows; ++r) {
+        if (r < p.m) {
+          const size_t at = size_t{r} * p.ldc + column;
+          if (kPaired) {
+            store_operand(p.c, p.c_lo, at, silu_times(v[r], up[r]));
+          } else {
+            finish_element(p.bias, p.c, p.c_lo, at, column, p.mode, v[r], 0.0f);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(pf::kNarrowTmemColumns)
+                 : "memory");
+  }
+}
+
+extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
+    prefill_tc_narrow(const __grid_constant__ pf::TcGemmArgs p) {
+  tc_narrow<false>(p);
+}
+
+extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
+    prefill_tc_narrow_pair(const __grid_constant__ pf::TcGemmArgs p) {
+  tc_narrow<true>(p);
 }
 
 // ------------------------------------------------------- batched decode --

@@ -20,6 +20,8 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
       tc_n192_(module_.kernel("prefill_tc_gemm_n192")),
       tc_n224_(module_.kernel("prefill_tc_gemm_n224")),
       tc_n256_(module_.kernel("prefill_tc_gemm_n256")),
+      tc_narrow_(module_.kernel("prefill_tc_narrow")),
+      tc_narrow_pair_(module_.kernel("prefill_tc_narrow_pair")),
       finish_rows_(module_.kernel("prefill_finish_rows")),
       batch_attention_(module_.kernel("batch_attention")),
       batch_argmax_(module_.kernel("batch_argmax")), chunk_(max_chunk_tokens) {
@@ -32,8 +34,8 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   // previous kernel drains.
   for (const Kernel *kernel :
        {&embed_, &rmsnorm_, &rope_kv_, &attend_, &reduce_, &split_, &gemm_bias_, &gemm_residual_,
-        &gemm_swiglu_, &tc_n192_, &tc_n224_, &tc_n256_, &finish_rows_, &batch_attention_,
-        &batch_argmax_}) {
+        &gemm_swiglu_, &tc_n192_, &tc_n224_, &tc_n256_, &tc_narrow_, &tc_narrow_pair_,
+        &finish_rows_, &batch_attention_, &batch_argmax_}) {
     check(lr_kernel_set_overlapped(kernel->get(), 1), "lr_kernel_set_overlapped");
   }
   const size_t c = chunk_;
@@ -55,6 +57,35 @@ DeviceBuffer Prefill::allocate(size_t bytes) {
   return DeviceBuffer(device_, std::max<size_t>(bytes, 16));
 }
 
+namespace {
+
+// Maps of a (hi, lo) activation pair [rows][columns]: 128-row boxes (the
+// wide kernels' A operand) and kNarrowRows-row boxes (the narrow kernels' B).
+OperandMaps activation_maps(const float *hi, const float *lo, uint64_t rows,
+                                     uint64_t columns) {
+  OperandMaps maps;
+  maps.wide[0] = map_2d(hi, rows, columns, kTcTileM);
+  maps.wide[1] = map_2d(lo, rows, columns, kTcTileM);
+  maps.narrow[0] = map_2d(hi, rows, columns, kNarrowRows);
+  maps.narrow[1] = map_2d(lo, rows, columns, kNarrowRows);
+  return maps;
+}
+
+// Maps of a (hi, lo) weight pair [rows][columns]: boxes of half a
+// tile_columns-wide tile (the wide kernels' B operand) and kNarrowTileN-row
+// boxes (the narrow kernels' A).
+OperandMaps weight_maps(const float *hi, const float *lo, uint64_t rows, uint64_t columns,
+                                 uint32_t tile_columns) {
+  OperandMaps maps;
+  maps.wide[0] = map_2d(hi, rows, columns, tile_columns / 2u);
+  maps.wide[1] = map_2d(lo, rows, columns, tile_columns / 2u);
+  maps.narrow[0] = map_2d(hi, rows, columns, kNarrowTileN);
+  maps.narrow[1] = map_2d(lo, rows, columns, kNarrowTileN);
+  return maps;
+}
+
+} // namespace
+
 // (Re)builds the TF32 (hi, lo) weight copies when the weights changed since
 // the last split, and the tensor maps over them and the chunk operands.
 void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_generation) {
@@ -73,13 +104,12 @@ void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_gene
   }
   const size_t c = chunk_;
   auto *hi_lo = static_cast<float *>(split_weights_->data());
-  normalized_maps_[0] = map_2d(static_cast<float *>(normalized_->data()), c, kHidden, kTcTileM);
-  normalized_maps_[1] = map_2d(static_cast<float *>(normalized_lo_->data()), c, kHidden, kTcTileM);
-  attention_maps_[0] = map_2d(static_cast<float *>(attention_->data()), c, kHidden, kTcTileM);
-  attention_maps_[1] = map_2d(static_cast<float *>(attention_lo_->data()), c, kHidden, kTcTileM);
-  activated_maps_[0] = map_2d(static_cast<float *>(activated_->data()), c, kIntermediate, kTcTileM);
-  activated_maps_[1] =
-      map_2d(static_cast<float *>(activated_lo_->data()), c, kIntermediate, kTcTileM);
+  normalized_maps_ = activation_maps(static_cast<float *>(normalized_->data()),
+                                     static_cast<float *>(normalized_lo_->data()), c, kHidden);
+  attention_maps_ = activation_maps(static_cast<float *>(attention_->data()),
+                                    static_cast<float *>(attention_lo_->data()), c, kHidden);
+  activated_maps_ = activation_maps(static_cast<float *>(activated_->data()),
+                                    static_cast<float *>(activated_lo_->data()), c, kIntermediate);
   layer_maps_.assign(layers, LayerMaps{});
   for (size_t layer = 0; layer < layers; ++layer) {
     const LayerView &w = model.layers[layer];
@@ -98,16 +128,11 @@ void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_gene
              args);
     }
     LayerMaps &maps = layer_maps_[layer];
-    const float *gate_up = hi + kQkvFloats + kOFloats;
-    const float *down = gate_up + kGateUpFloats;
-    for (uint32_t part = 0; part < 2; ++part) {
-      const float *base = part == 0 ? hi : lo;
-      const size_t shift = base - hi;
-      maps.qkv[part] = map_2d(base, kQkv, kHidden, kQkvTile / 2u);
-      maps.o[part] = map_2d(base + kQkvFloats, kHidden, kHidden, kHiddenTile / 2u);
-      maps.gate_up[part] = map_2d(gate_up + shift, 2 * kIntermediate, kHidden, kGateUpTile / 2u);
-      maps.down[part] = map_2d(down + shift, kHidden, kIntermediate, kHiddenTile / 2u);
-    }
+    const size_t gate_up = kQkvFloats + kOFloats, down = gate_up + kGateUpFloats;
+    maps.qkv = weight_maps(hi, lo, kQkv, kHidden, kQkvTile);
+    maps.o = weight_maps(hi + kQkvFloats, lo + kQkvFloats, kHidden, kHidden, kHiddenTile);
+    maps.gate_up = weight_maps(hi + gate_up, lo + gate_up, 2 * kIntermediate, kHidden, kGateUpTile);
+    maps.down = weight_maps(hi + down, lo + down, kHidden, kIntermediate, kHiddenTile);
   }
   split_generation_ = weights_generation;
   split_source_ = model.layers[0].qkv;
@@ -129,8 +154,7 @@ void Prefill::prepare_tail(const ModelView &model, uint64_t weights_generation) 
   auto *hi = static_cast<float *>(tail_split_->data());
   launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(floats, 256), kSms * 8), 256),
          SplitArgs{model.lm_head, hi, hi + floats, floats});
-  tail_maps_[0] = map_2d(hi, model.vocab, kHidden, kGateUpTile / 2u);
-  tail_maps_[1] = map_2d(hi + floats, model.vocab, kHidden, kGateUpTile / 2u);
+  tail_maps_ = weight_maps(hi, hi + floats, model.vocab, kHidden, kGateUpTile);
   tail_generation_ = weights_generation;
   tail_source_ = model.lm_head;
 }
@@ -142,21 +166,35 @@ void Prefill::prepare_tail(const ModelView &model, uint64_t weights_generation) 
 // tiles run data-parallel with the epilogue in the GEMM, and the tiles of a
 // last partial wave (or all tiles, when there are fewer than kSms) are split
 // along K so that the launch fills the SMs, and prefill_reduce sums their
-// partials in split order.
-PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b,
+// partials in split order. At most kNarrowRows rows run the narrow
+// (swapped-operand) kernels under the same schedule; tile_columns then
+// follows from them.
+PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const OperandMaps &a, const OperandMaps &b,
                               uint32_t m, uint32_t n, uint32_t k, GemmEpilogue mode, float *c,
                               float *c_lo, uint32_t ldc, const float *bias, bool defer) {
   const bool swiglu = mode == GemmEpilogue::swiglu;
+  // At most kNarrowRows rows: the swapped-operand kernels, whose tiles are
+  // kNarrowTileN output columns (paired with the up columns for swiglu).
+  const bool narrow = m <= kNarrowRows;
+  if (narrow) {
+    tile_columns = swiglu ? 2u * kNarrowTileN : kNarrowTileN;
+  }
+  const uint32_t tile_rows = narrow ? kNarrowRows : kTcTileM;
   const uint32_t out_columns = swiglu ? tile_columns / 2u : tile_columns;
   const uint32_t n_tiles = ceil_div(n, out_columns);
-  const uint32_t tiles = n_tiles * ceil_div(m, kTcTileM);
+  const uint32_t tiles = n_tiles * ceil_div(m, tile_rows);
   const uint32_t k_tiles = k / kTcTileK;
-  const Kernel &kernel = tile_columns == 192 ? tc_n192_ : tile_columns == 224 ? tc_n224_ : tc_n256_;
+  const Kernel &kernel = narrow ? (swiglu ? tc_narrow_pair_ : tc_narrow_)
+                         : tile_columns == 192 ? tc_n192_
+                         : tile_columns == 224 ? tc_n224_
+                                               : tc_n256_;
+  const uint32_t shared = narrow ? tc_narrow_shared_bytes(swiglu) : tc_shared_bytes(tile_columns);
   TcGemmArgs args{};
-  args.a_hi = a[0];
-  args.a_lo = a[1];
-  args.b_hi = b[0];
-  args.b_lo = b[1];
+  // The narrow kernels take the weights as the MMA's A operand.
+  args.a_hi = narrow ? b.narrow[0] : a.wide[0];
+  args.a_lo = narrow ? b.narrow[1] : a.wide[1];
+  args.b_hi = narrow ? a.narrow[0] : b.wide[0];
+  args.b_lo = narrow ? a.narrow[1] : b.wide[1];
   args.m = m;
   args.n = n;
   args.k = k;
@@ -175,22 +213,22 @@ PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const T
     args.c = partial ? partials : c;
     args.c_lo = partial ? nullptr : c_lo;
     args.bias = bias;
-    const lr_launch_config_t config{
-        {count * kTcThreads, 1, splits}, {kTcThreads, 1, 1}, tc_shared_bytes(tile_columns)};
+    const lr_launch_config_t config{{count * kTcThreads, 1, splits}, {kTcThreads, 1, 1}, shared};
     launch(kernel.get(), config, args);
     if (partial && finish) {
-      const ReduceArgs reduce{partials, bias,    c,        c_lo,   m,
-                              n,        ldc,     static_cast<uint32_t>(mode),
-                              offset,   count,   n_tiles,  splits, tile_columns};
+      const ReduceArgs reduce{partials, bias,   c,      c_lo,   m,
+                              n,        ldc,    static_cast<uint32_t>(mode),
+                              offset,   count,  n_tiles, splits, tile_columns,
+                              tile_rows};
       launch(reduce_.get(),
-             rows_config(ceil_div(uint64_t{count} * kTcTileM * out_columns, 256), 256), reduce);
+             rows_config(ceil_div(uint64_t{count} * tile_rows * out_columns, 256), 256), reduce);
     }
   };
   const uint32_t small_splits = std::max(
       1u, std::min({kSms / std::max(tiles, 1u), k_tiles / 4u, kMaximumDeferredSplits}));
   if (defer && !swiglu && tiles <= kSms) {
     run(0, tiles, small_splits, false);
-    return PartialTiles{partials, small_splits, n_tiles, tiles, tile_columns};
+    return PartialTiles{partials, small_splits, n_tiles, tiles, tile_columns, tile_rows};
   }
   if (tiles >= kSms) {
     const uint32_t full = tiles / kSms * kSms;
@@ -205,7 +243,7 @@ PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const TensorMap *a, const T
   } else {
     run(0, tiles, small_splits, true);
   }
-  return PartialTiles{nullptr, 0, 0, 0, 0};
+  return PartialTiles{nullptr, 0, 0, 0, 0, 0};
 }
 
 void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_position,
@@ -300,7 +338,7 @@ void Prefill::gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, u
   const bool swiglu = mode == GemmEpilogue::swiglu;
   if (m == 0 || n == 0 || k == 0 || k % kTcTileK != 0 || n % 32 != 0 || mode == GemmEpilogue::partial ||
       (tile_columns != 0 && tile_columns != 192 && tile_columns != 224 && tile_columns != 256) ||
-      (swiglu && tile_columns != 0 &&
+      (swiglu && tile_columns != 0 && m > kNarrowRows &&
        (n % (tile_columns / 2u) != 0 || (tile_columns / 2u) % 32u != 0))) {
     throw std::invalid_argument("unsupported GEMM check shape");
   }
@@ -341,10 +379,9 @@ void Prefill::gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, u
            SplitArgs{static_cast<const float *>(a_dev.data()), ah, ah + a_floats, a_floats});
     launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(b_floats, 256), kSms * 8), 256),
            SplitArgs{static_cast<const float *>(b_dev.data()), bh, bh + b_floats, b_floats});
-    const TensorMap a_maps[2] = {map_2d(ah, m, k, kTcTileM), map_2d(ah + a_floats, m, k, kTcTileM)};
-    const TensorMap b_maps[2] = {map_2d(bh, rows_b, k, tile_columns / 2u),
-                                 map_2d(bh + b_floats, rows_b, k, tile_columns / 2u)};
-    tc_gemm(tile_columns, a_maps, b_maps, m, n, k, mode, cd, nullptr, n, bias_ptr, false);
+    tc_gemm(tile_columns, activation_maps(ah, ah + a_floats, m, k),
+            weight_maps(bh, bh + b_floats, rows_b, k, tile_columns), m, n, k, mode, cd, nullptr,
+            n, bias_ptr, false);
   }
   device_.synchronize();
   copy_to_host(c, c_dev, c_dev.size());

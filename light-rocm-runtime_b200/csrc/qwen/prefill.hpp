@@ -45,6 +45,14 @@ enum class Path : uint32_t { simt = 0, tf32x3 = 1 };
 
 class BatchDecoder;
 
+// (hi, lo) tensor maps of one GEMM operand: `wide` boxes for the
+// 128-row-band kernels (activations: 128 rows; weights: half a tile), and
+// `narrow` boxes for the swapped-operand kernels of at most kNarrowRows rows
+// (activations: kNarrowRows rows; weights: kNarrowTileN rows).
+struct OperandMaps {
+  TensorMap wide[2]{}, narrow[2]{};
+};
+
 class Prefill {
 public:
   Prefill(Device device, const void *image, size_t image_size, uint32_t max_chunk_tokens);
@@ -69,9 +77,9 @@ public:
 private:
   friend class BatchDecoder;
 
-  // (hi, lo) tensor maps of one layer's weights.
+  // One layer's weights.
   struct LayerMaps {
-    TensorMap qkv[2], o[2], gate_up[2], down[2];
+    OperandMaps qkv, o, gate_up, down;
   };
 
   DeviceBuffer allocate(size_t bytes);
@@ -79,14 +87,15 @@ private:
   // TF32 (hi, lo) copy of the LM head and its tensor maps (batched decode).
   void prepare_tail(const ModelView &model, uint64_t weights_generation);
   void run_chunk(const ModelView &model, uint32_t count, uint32_t first_position, Path path);
-  PartialTiles tc_gemm(uint32_t tile_columns, const TensorMap *a, const TensorMap *b, uint32_t m,
-                       uint32_t n, uint32_t k, GemmEpilogue mode, float *c, float *c_lo,
-                       uint32_t ldc, const float *bias, bool defer);
+  PartialTiles tc_gemm(uint32_t tile_columns, const OperandMaps &a, const OperandMaps &b,
+                       uint32_t m, uint32_t n, uint32_t k, GemmEpilogue mode, float *c,
+                       float *c_lo, uint32_t ldc, const float *bias, bool defer);
 
   Device device_;
   Module module_;
   Kernel embed_, rmsnorm_, rope_kv_, attend_, reduce_, split_, gemm_bias_, gemm_residual_,
-      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, finish_rows_, batch_attention_, batch_argmax_;
+      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, tc_narrow_, tc_narrow_pair_, finish_rows_,
+      batch_attention_, batch_argmax_;
   uint32_t chunk_;
   uint64_t device_bytes_ = 0;
 
@@ -95,11 +104,11 @@ private:
   // 3xTF32 path: per-layer (hi, lo) weight copies and tensor maps.
   std::optional<DeviceBuffer> split_weights_;
   std::vector<LayerMaps> layer_maps_;
-  TensorMap normalized_maps_[2]{}, attention_maps_[2]{}, activated_maps_[2]{};
+  OperandMaps normalized_maps_, attention_maps_, activated_maps_;
   uint64_t split_generation_ = UINT64_MAX;
   const void *split_source_ = nullptr;
   std::optional<DeviceBuffer> tail_split_;
-  TensorMap tail_maps_[2]{};
+  OperandMaps tail_maps_;
   uint64_t tail_generation_ = UINT64_MAX;
   const void *tail_source_ = nullptr;
 };

@@ -185,6 +185,23 @@ def test_prefill_gemm_matches_float64(gemm_model, tile, mode, m, n, k):
     remainder (512 rows x 4864: 152 tiles of 128 x 256)."""
     if mode == 2 and tile != 0 and (n % (tile // 2) != 0 or tile == 224):
         pytest.skip("swiglu tiles: 192 or 256 columns whose halves divide n")
+    _check_gemm(gemm_model, tile, mode, m, n, k)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", [0, 1, 2], ids=["bias", "residual", "swiglu"])
+@pytest.mark.parametrize("m,n,k", [(1, 1152, 896), (17, 480, 4864), (32, 4864, 896),
+                                   (32, 896, 4864)])
+def test_narrow_gemm_matches_float64(gemm_model, mode, m, n, k):
+    """At most 32 rows run the swapped-operand kernels (weights as the MMA's
+    A operand, 128 output columns per tile, gate/up pairs in two
+    accumulators) under the same split-K schedule: one row, a ragged last
+    column tile (480 = 3.75 x 128) with a long K, a 32-row swiglu of
+    Qwen2-0.5B's MLP width, and the down projection's shape."""
+    _check_gemm(gemm_model, 256, mode, m, n, k)
+
+
+def _check_gemm(gemm_model, tile, mode, m, n, k):
     rng = np.random.default_rng(m * 7 + n + k + mode)
     a = rng.standard_normal((m, k), dtype=np.float32)
     b = (rng.standard_normal((2 * n if mode == 2 else n, k), dtype=np.float32) * 0.02)
