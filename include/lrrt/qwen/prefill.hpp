@@ -150,11 +150,17 @@ struct AttentionArgs {
 // out[b][head * 64 + d] (TF32 pair when out_lo is set).
 constexpr uint32_t kDecodePartialStride = 66;
 constexpr uint32_t kDecodeMaximumSplits = 32;
-// Dynamic shared memory of batch_attention: K[128][68] (reused for the
-// partial scores and sums), V[128][64], queries [7][64], softmax weights
-// [7][128], rescales [8], merge weights [7][32] and totals [7].
+// Keys per batch_attention tile; each block streams its key range through
+// two tile buffers, and the batch sizes its splits so that all blocks fit
+// one wave of kDecodeBlocksPerSm blocks per SM.
+constexpr uint32_t kDecodeTileKeys = 64;
+constexpr uint32_t kDecodeBlocksPerSm = 3;
+// Dynamic shared memory of batch_attention: two tile buffers of K[64][68]
+// (reused for the partial scores) and V[64][64] (both reused for the final
+// sums), queries [7][64], softmax weights [7][64], rescales [8], merge
+// weights [7][32] and totals [7].
 constexpr uint32_t kDecodeSharedBytes =
-    4u * (128u * 68u + 128u * 64u + 7u * 64u + 7u * 128u + 8u + 7u * 32u + 7u);
+    4u * (2u * (64u * 68u + 64u * 64u) + 7u * 64u + 7u * 64u + 8u + 7u * 32u + 7u);
 struct DecodeAttentionArgs {
   const float *qkv;         // [streams][1152], q rotated
   const float *key_cache;   // stream b's cache at key_cache + b * stream_stride

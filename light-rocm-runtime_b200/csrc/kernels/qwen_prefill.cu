@@ -1241,35 +1241,41 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 // the last split block of a (stream, KV group) merges the splits.
 // Block (s, g, b) serves the 7 query heads 7g..7g+6 of KV head g of stream b
 // over key positions [s * chunk, min((s + 1) * chunk, positions[b] + 1)), in
-// tiles of kDecodeKeys keys copied into shared memory with cp.async (K, then
-// V as a second group that lands while the scores are computed; positions
-// past the range are zero-filled), each staged element read once per block
-// for all 7 heads:
-//   scores: warp w sums dims 8w..8w+7 of keys l, l + 32, l + 64, l + 96
-//           (lane l, float4 reads along the key rows) for all 7 heads; the 8
-//           dim-slice partials are summed in slice order by warp h (head h),
-//           which runs the decode step's online softmax (scale 1/8, expf);
-//   P.V:    warp w accumulates keys 16w..16w+15 into dims 2l, 2l + 1 of all
-//           7 heads; the 8 key-slice sums are added in slice order after the
+// tiles of kDecodeTileKeys keys copied into shared memory with cp.async into
+// two buffers: tile t + 1 (K, then V, as two groups; positions past the
+// range zero-filled) is in flight while tile t is computed. Each staged
+// element is read once per block for all 7 heads:
+//   scores: warp w sums dims 8w..8w+7 of keys l and l + 32 (lane l, float4
+//           reads along the key rows) for all 7 heads; the 8 dim-slice
+//           partials are summed in slice order by warp h (head h), which
+//           runs the decode step's online softmax (scale 1/8, expf);
+//   P.V:    warp w accumulates keys 8w..8w+7 into dims 2l, 2l + 1 of all 7
+//           heads; the 8 key-slice sums are added in slice order after the
 //           last tile.
-constexpr uint32_t kDecodeKeys = 128;
+using pf::kDecodeTileKeys;
 constexpr uint32_t kDecodeSlices = 8; // warps
 constexpr uint32_t kDecodeKeyPitch = qd::kHeadSize + 4u; // conflict-free float4 column reads
 
-struct DecodeShared {
+struct DecodeBuffer {
   // The tile's K rows; after the score sums, the same bytes hold the
-  // dim-slice partial scores, and after the last tile the key-slice partial
-  // P.V sums.
+  // dim-slice partial scores.
   union {
-    float ks[kDecodeKeys][kDecodeKeyPitch];
-    float scores[kDecodeSlices][qd::kQueriesPerKvHead][kDecodeKeys];
+    float ks[kDecodeTileKeys][kDecodeKeyPitch];
+    float scores[kDecodeSlices][qd::kQueriesPerKvHead][kDecodeTileKeys];
+  };
+  float vs[kDecodeTileKeys][qd::kHeadSize]; // [key][d]
+};
+
+struct DecodeShared {
+  union {
+    DecodeBuffer buffer[2];
+    // After the last tile: the key slices' partial P.V sums.
     float sums[kDecodeSlices][qd::kQueriesPerKvHead][qd::kHeadSize];
   };
-  float vs[kDecodeKeys][qd::kHeadSize]; // [key][d]
   float q[qd::kQueriesPerKvHead][qd::kHeadSize];
-  float probability[qd::kQueriesPerKvHead][kDecodeKeys]; // the tile's softmax weights
-  float rescale[kDecodeSlices];                          // per head, [7] unused
-  float weight[qd::kQueriesPerKvHead][32];               // merge: per (head, split) scale
+  float probability[qd::kQueriesPerKvHead][kDecodeTileKeys]; // the tile's softmax weights
+  float rescale[kDecodeSlices];                              // per head, [7] unused
+  float weight[qd::kQueriesPerKvHead][32];                   // merge: per (head, split) scale
   float total[qd::kQueriesPerKvHead];
 };
 
@@ -1282,6 +1288,10 @@ __device__ __forceinline__ void copy16_async(void *destination, const void *sour
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(address), "l"(source),
                "r"(bytes)
                : "memory");
+}
+
+template <uint32_t kPending> __device__ __forceinline__ void copy_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
 }
 
 extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAttentionArgs p) {
@@ -1300,47 +1310,61 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
   }
   const float *keys = p.key_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
   const float *values = p.value_cache + b * p.stream_stride + size_t{group} * qd::kHeadSize;
+  // Thread t copies 16-byte chunks t + 256j of the tile (row = chunk / 16):
+  // coalesced 256-byte row reads; rows at or past `end` read nothing and
+  // become 0. K and V are committed as two groups.
+  auto issue = [&](DecodeBuffer &buffer, uint32_t base) {
+    constexpr uint32_t kChunks = kDecodeTileKeys * qd::kHeadSize / 4u / 256u;
+#pragma unroll
+    for (uint32_t j = 0; j < kChunks; ++j) {
+      const uint32_t i = threadIdx.x + 256u * j, key = i / 16u, c = (i % 16u) * 4u;
+      const bool valid = base + key < end;
+      copy16_async(&buffer.ks[key][c], keys + size_t{valid ? base + key : base} * qd::kKvSize + c,
+                   valid ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+#pragma unroll
+    for (uint32_t j = 0; j < kChunks; ++j) {
+      const uint32_t i = threadIdx.x + 256u * j, key = i / 16u, c = (i % 16u) * 4u;
+      const bool valid = base + key < end;
+      copy16_async(&buffer.vs[key][c], values + size_t{valid ? base + key : base} * qd::kKvSize + c,
+                   valid ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
   // Warp h < 7: head h's running maximum and denominator (all lanes alike).
   float maximum = -INFINITY, denominator = 0.0f;
   float acc[qd::kQueriesPerKvHead][2] = {};
-  for (uint32_t base = begin; base < end; base += kDecodeKeys) {
+  if (begin < end) {
+    issue(sh.buffer[0], begin);
+  }
+  uint32_t t = 0;
+  for (uint32_t base = begin; base < end; base += kDecodeTileKeys, ++t) {
+    DecodeBuffer &buffer = sh.buffer[t & 1u];
     __syncthreads(); // the previous tile's reads are done (and q is written)
-    // Thread t copies 16-byte chunks t + 256j (row = chunk / 16): coalesced
-    // 256-byte row reads; rows at or past `end` read nothing and become 0.
-    constexpr uint32_t kChunks = kDecodeKeys * qd::kHeadSize / 4u / 256u;
-#pragma unroll
-    for (uint32_t j = 0; j < kChunks; ++j) {
-      const uint32_t i = threadIdx.x + 256u * j, key = i / 16u, c = (i % 16u) * 4u;
-      const bool valid = base + key < end;
-      copy16_async(&sh.ks[key][c], keys + size_t{valid ? base + key : base} * qd::kKvSize + c,
-                   valid ? 16u : 0u);
+    const bool next = base + kDecodeTileKeys < end;
+    if (next) {
+      issue(sh.buffer[(t + 1u) & 1u], base + kDecodeTileKeys);
+      copy_wait<3>(); // this thread's K chunks of tile t
+    } else {
+      copy_wait<1>();
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-#pragma unroll
-    for (uint32_t j = 0; j < kChunks; ++j) {
-      const uint32_t i = threadIdx.x + 256u * j, key = i / 16u, c = (i % 16u) * 4u;
-      const bool valid = base + key < end;
-      copy16_async(&sh.vs[key][c], values + size_t{valid ? base + key : base} * qd::kKvSize + c,
-                   valid ? 16u : 0u);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 1;" ::: "memory"); // this thread's K chunks
     __syncthreads();
-    // Dim slice `warp` of the 7 x 4 scores of keys l + 32j.
-    float score[qd::kQueriesPerKvHead][4] = {};
+    // Dim slice `warp` of the 7 x 2 scores of keys l + 32j.
+    float score[qd::kQueriesPerKvHead][2] = {};
 #pragma unroll
     for (uint32_t half = 0; half < 2u; ++half) {
       const uint32_t d0 = kDecodeSlices * warp + 4u * half;
-      float4 key4[4];
+      float4 key4[2];
 #pragma unroll
-      for (uint32_t j = 0; j < 4u; ++j) {
-        key4[j] = *reinterpret_cast<const float4 *>(&sh.ks[lane + 32u * j][d0]);
+      for (uint32_t j = 0; j < 2u; ++j) {
+        key4[j] = *reinterpret_cast<const float4 *>(&buffer.ks[lane + 32u * j][d0]);
       }
 #pragma unroll
       for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
         const float4 q = *reinterpret_cast<const float4 *>(&sh.q[h][d0]);
 #pragma unroll
-        for (uint32_t j = 0; j < 4u; ++j) {
+        for (uint32_t j = 0; j < 2u; ++j) {
           score[h][j] = fmaf(q.x, key4[j].x, score[h][j]);
           score[h][j] = fmaf(q.y, key4[j].y, score[h][j]);
           score[h][j] = fmaf(q.z, key4[j].z, score[h][j]);
@@ -1352,40 +1376,40 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
 #pragma unroll
     for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
 #pragma unroll
-      for (uint32_t j = 0; j < 4u; ++j) {
-        sh.scores[warp][h][lane + 32u * j] = score[h][j];
+      for (uint32_t j = 0; j < 2u; ++j) {
+        buffer.scores[warp][h][lane + 32u * j] = score[h][j];
       }
     }
     __syncthreads();
     if (warp < qd::kQueriesPerKvHead) {
-      float s4[4];
+      float s2[2];
 #pragma unroll
-      for (uint32_t j = 0; j < 4u; ++j) {
-        s4[j] = sh.scores[0][warp][lane + 32u * j];
+      for (uint32_t j = 0; j < 2u; ++j) {
+        s2[j] = buffer.scores[0][warp][lane + 32u * j];
       }
 #pragma unroll
       for (uint32_t slice = 1; slice < kDecodeSlices; ++slice) {
 #pragma unroll
-        for (uint32_t j = 0; j < 4u; ++j) {
-          s4[j] += sh.scores[slice][warp][lane + 32u * j];
+        for (uint32_t j = 0; j < 2u; ++j) {
+          s2[j] += buffer.scores[slice][warp][lane + 32u * j];
         }
       }
       float tile_maximum = -INFINITY;
 #pragma unroll
-      for (uint32_t j = 0; j < 4; ++j) {
-        s4[j] = base + lane + 32u * j < end ? s4[j] * 0.125f : -INFINITY;
-        tile_maximum = fmaxf(tile_maximum, s4[j]);
+      for (uint32_t j = 0; j < 2u; ++j) {
+        s2[j] = base + lane + 32u * j < end ? s2[j] * 0.125f : -INFINITY;
+        tile_maximum = fmaxf(tile_maximum, s2[j]);
       }
 #pragma unroll
       for (uint32_t offset = 16; offset != 0; offset >>= 1u) {
         tile_maximum = fmaxf(tile_maximum, __shfl_xor_sync(kFullMask, tile_maximum, offset));
       }
-      const float next = fmaxf(maximum, tile_maximum); // finite: key `base` is in range
-      const float scale = expf(maximum - next);
+      const float next_maximum = fmaxf(maximum, tile_maximum); // finite: key `base` is in range
+      const float scale = expf(maximum - next_maximum);
       float sum = 0.0f;
 #pragma unroll
-      for (uint32_t j = 0; j < 4; ++j) {
-        const float w = expf(s4[j] - next);
+      for (uint32_t j = 0; j < 2u; ++j) {
+        const float w = expf(s2[j] - next_maximum);
         sh.probability[warp][lane + 32u * j] = w;
         sum += w;
       }
@@ -1394,14 +1418,18 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
         sum += __shfl_xor_sync(kFullMask, sum, offset);
       }
       denominator = denominator * scale + sum;
-      maximum = next;
+      maximum = next_maximum;
       if (lane == 0) {
         sh.rescale[warp] = scale;
       }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory"); // this thread's V chunks
+    if (next) {
+      copy_wait<2>(); // this thread's V chunks of tile t
+    } else {
+      copy_wait<0>();
+    }
     __syncthreads();
-    // Key slice `warp` (keys 16w..16w+15) into dims 2l, 2l + 1 of the 7 heads.
+    // Key slice `warp` (keys 8w..8w+7) into dims 2l, 2l + 1 of the 7 heads.
 #pragma unroll
     for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
       const float scale = sh.rescale[h];
@@ -1409,8 +1437,8 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       acc[h][1] *= scale;
     }
 #pragma unroll
-    for (uint32_t c = 0; c < 4u; ++c) {
-      const uint32_t key0 = 16u * warp + 4u * c;
+    for (uint32_t c = 0; c < 2u; ++c) {
+      const uint32_t key0 = 8u * warp + 4u * c;
       float4 weight[qd::kQueriesPerKvHead];
 #pragma unroll
       for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
@@ -1418,7 +1446,7 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       }
 #pragma unroll
       for (uint32_t j = 0; j < 4u; ++j) {
-        const float2 v2 = *reinterpret_cast<const float2 *>(&sh.vs[key0 + j][2u * lane]);
+        const float2 v2 = *reinterpret_cast<const float2 *>(&buffer.vs[key0 + j][2u * lane]);
 #pragma unroll
         for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
           const float pj =
@@ -1429,8 +1457,7 @@ extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAtte
       }
     }
   }
-  // No thread reads the K / score bytes after the last softmax: the key
-  // slices' sums go there.
+  __syncthreads(); // the last tile's reads are done: its bytes take the sums
 #pragma unroll
   for (uint32_t h = 0; h < qd::kQueriesPerKvHead; ++h) {
     *reinterpret_cast<float2 *>(&sh.sums[warp][h][2u * lane]) = make_float2(acc[h][0], acc[h][1]);

@@ -30,11 +30,14 @@ BatchDecoder::BatchDecoder(Prefill &prefill, const ModelView &model, uint32_t st
         "batch needs 1..prefill-chunk streams, capacity <= the model's RoPE rows and "
         "1..capacity tokens per decode");
   }
-  // Position splits of about two 64-key tiles each (at most 32), so that
-  // every block's K/V loads are few and many blocks are in flight.
-  const uint32_t tiles = ceil_div(capacity_, 64);
-  splits_ = std::max(1u, std::min(ceil_div(tiles, 2), kDecodeMaximumSplits));
-  chunk_ = ceil_div(tiles, splits_) * 64u;
+  // Position splits: as many as one wave of kDecodeBlocksPerSm blocks per SM
+  // holds (streams x KV heads x splits blocks), at most one per key tile and
+  // at most kDecodeMaximumSplits; each block streams its tiles double
+  // buffered.
+  const uint32_t tiles = ceil_div(capacity_, kDecodeTileKeys);
+  const uint32_t per_head = std::max(1u, kSms * kDecodeBlocksPerSm / (streams_ * qd::kKvHeads));
+  splits_ = std::max(1u, std::min({per_head, tiles, kDecodeMaximumSplits}));
+  chunk_ = ceil_div(tiles, splits_) * kDecodeTileKeys;
   const size_t cache = size_t{streams_} * layers_ * capacity_ * qd::kKvSize;
   key_cache_.emplace(allocate(sizeof(float) * cache));
   value_cache_.emplace(allocate(sizeof(float) * cache));
