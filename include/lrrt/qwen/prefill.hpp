@@ -129,8 +129,10 @@ struct FinishArgs {
 
 // Causal GQA attention: query row t attends to cache positions
 // 0..first_position + t. out [count][896] (hi part when out_lo is set).
-// Launch: blocks of kAttentionThreads threads over (ceil(count / 32), 14)
-// with kAttentionSharedBytes of dynamic shared memory.
+// Launch: blocks of kAttentionThreads threads over (key chunks,
+// ceil(count / kAttentionTileRows), 14) with kAttentionSharedBytes of dynamic
+// shared memory;
+// chunk_keys * max_chunks covers first_position + count positions.
 struct AttentionArgs {
   const float *qkv;
   const float *key_cache;
@@ -139,6 +141,10 @@ struct AttentionArgs {
   float *out_lo;
   uint32_t count;
   uint32_t first_position;
+  uint32_t chunk_keys;   // key positions per block (a multiple of 64)
+  uint32_t max_chunks;   // partial-state slots per (row tile, head)
+  float *partials;       // [row tile][14][max_chunks][rows][kAttentionPartialStride]
+  uint32_t *arrivals;    // [row tile][14], zero between launches
 };
 
 // Batched decode attention: one query row per stream. Block (s, g, b)
@@ -196,9 +202,13 @@ constexpr uint32_t kArgmaxPartitions = 8; // blocks per stream row
 constexpr uint32_t kRowThreads = 1024;     // prefill_rope_kv, prefill_finish_rows
 constexpr uint32_t kMaximumDeferredSplits = 16;
 
-constexpr uint32_t kAttentionThreads = 512;
-constexpr uint32_t kAttentionSharedBytes =
-    4u * (64u * 32u + 4u * (64u * 64u * 2u + 32u * 64u) + 2u * 4u * 32u);
+constexpr uint32_t kAttentionTileRows = 64; // query rows per block
+constexpr uint32_t kAttentionThreads = 256;
+// Shared memory of prefill_attention: Q [64][68], K [2][64][68], V [2][64][64]
+// and the tile's softmax weights [64][68].
+constexpr uint32_t kAttentionSharedBytes = 4u * (64u * 68u + 2u * 64u * 68u + 2u * 64u * 64u + 64u * 68u);
+constexpr uint32_t kAttentionPartialStride = 68; // acc[64], maximum, sum, 2 pad: 16-byte rows
+constexpr uint32_t kAttentionMaximumChunks = 16;
 
 // hi[i] = tf32(x[i]), lo[i] = tf32(x[i] - hi[i]) for i < count.
 struct SplitArgs {

@@ -483,70 +483,94 @@ extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_finish_rows(pf
   }
 }
 
-// Causal GQA attention, register-blocked. Block (x, y) serves 32 query rows
-// of head y (the heaviest row tiles get the lowest block indices) over cache
-// positions 0..first_position + row, in 64-position key tiles. Four groups
-// of four warps take every fourth key tile, each with its own shared K/V/P
-// buffers and a named barrier, and their softmax states are merged at the
-// end. In a group, thread (ty, tx) = (tid / 16, tid % 16) owns query rows
-// 4ty..4ty+3 and, per tile, keys 4tx..4tx+3 of S = Q.K^T / 8 and output
-// dims 4tx..4tx+3 of O; a row's sixteen threads reduce with shuffles. Q and
-// K are stored transposed ([dim][row], [dim][key]) so that both inner loops
-// read broadcast or contiguous float4 values. Each group runs the decode
-// step's online softmax (expf) per tile; the merge rescales the groups'
-// partial sums to the common maximum. out[t][head * 64 + d].
-constexpr uint32_t kAttentionRows = 32, kAttentionKeys = 64, kAttentionGroups = 4;
-constexpr uint32_t kAttentionGroupThreads = 128;
-static_assert(kAttentionGroups * kAttentionGroupThreads == pf::kAttentionThreads, "block size");
+// 16 bytes global -> shared without registers; `bytes` 0 zero-fills.
+__device__ __forceinline__ void copy16_async(void *destination, const void *source,
+                                             uint32_t bytes) {
+  const uint32_t address = static_cast<uint32_t>(__cvta_generic_to_shared(destination));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(address), "l"(source),
+               "r"(bytes)
+               : "memory");
+}
 
-struct AttentionGroupShared {
-  float kt[qd::kHeadSize][kAttentionKeys];  // [d][key]
-  float vs[kAttentionKeys][qd::kHeadSize];  // [key][d]
-  float ps[kAttentionRows][kAttentionKeys]; // [row][key]
-};
+template <uint32_t kPending> __device__ __forceinline__ void copy_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
+// Causal GQA attention, register-blocked and split over key chunks. Block
+// (c, r, h) serves query rows t0 = 64r .. t0 + 63 of head h against cache
+// positions [c * chunk_keys, (c + 1) * chunk_keys) up to each row's own
+// position first_position + t; key chunks that start past the tile's last
+// position exit at once. The chunk's 64-key tiles are copied with cp.async
+// into two buffers (K and V row-major; tile t + 1 lands while tile t is
+// computed). Thread (ty, tx) = (tid / 16, tid % 16) owns query rows
+// 4ty..4ty+3 and, per tile, keys tx + 16j of S = Q.K^T / 8 (float4 reads
+// along the rows of Q and K; 68-float row pitch keeps them conflict-free)
+// and output dims 4tx..4tx+3 of O; a row's sixteen threads reduce with
+// shuffles. The decode step's online softmax (expf) runs per tile. A tile
+// row with a single chunk is written directly; otherwise each chunk writes
+// (acc, maximum, sum) per row to `partials` and the last chunk block of
+// (r, h) to finish merges them in chunk order. out[t][head * 64 + d].
+constexpr uint32_t kAttentionRows = pf::kAttentionTileRows, kAttentionKeys = 64;
+constexpr uint32_t kAttentionPitch = qd::kHeadSize + 4u;
+static_assert(pf::kAttentionThreads == 4u * kAttentionRows, "16 x (rows / 4) thread tile");
+static_assert(pf::kAttentionPartialStride % 4u == 0, "float4 partial-state rows");
 
 struct AttentionShared {
-  float qt[qd::kHeadSize][kAttentionRows];  // [d][row]
-  AttentionGroupShared group[kAttentionGroups];
-  float maximum[kAttentionGroups][kAttentionRows];
-  float denominator[kAttentionGroups][kAttentionRows];
+  float q[kAttentionRows][kAttentionPitch];
+  float k[2][kAttentionKeys][kAttentionPitch];
+  float v[2][kAttentionKeys][qd::kHeadSize];
+  float ps[kAttentionRows][kAttentionPitch]; // [row][key]
 };
-
-__device__ __forceinline__ void group_barrier(uint32_t group) {
-  asm volatile("bar.sync %0, %1;" ::"r"(group + 1u), "r"(kAttentionGroupThreads) : "memory");
-}
 
 static_assert(sizeof(AttentionShared) == pf::kAttentionSharedBytes, "shared layout");
 
-extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
+extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads)
     prefill_attention(pf::AttentionArgs p) {
   dependent_launch_entry();
   extern __shared__ __align__(16) unsigned char attention_raw[];
   AttentionShared &sh = *reinterpret_cast<AttentionShared *>(attention_raw);
-  const uint32_t g = threadIdx.x / kAttentionGroupThreads;
-  const uint32_t tid = threadIdx.x % kAttentionGroupThreads;
-  const uint32_t ty = tid / 16u, tx = tid % 16u;
-  AttentionGroupShared &gs = sh.group[g];
-  const uint32_t head = blockIdx.y, kv_group = head / qd::kQueriesPerKvHead;
-  const uint32_t t0 = (gridDim.x - 1u - blockIdx.x) * kAttentionRows;
+  const uint32_t tid = threadIdx.x, ty = tid / 16u, tx = tid % 16u;
+  const uint32_t chunk = blockIdx.x, r = blockIdx.y, head = blockIdx.z;
+  const uint32_t kv_group = head / qd::kQueriesPerKvHead;
+  const uint32_t t0 = r * kAttentionRows;
   if (t0 >= p.count) {
     return;
   }
   const uint32_t rows = min(kAttentionRows, p.count - t0);
-  for (uint32_t i = threadIdx.x; i < kAttentionRows * qd::kHeadSize / 4u; i += pf::kAttentionThreads) {
-    const uint32_t row = i % kAttentionRows, d = (i / kAttentionRows) * 4u;
-    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (row < rows) {
-      q = *reinterpret_cast<const float4 *>(p.qkv + size_t{t0 + row} * qd::kPackedQkvSize +
-                                            head * qd::kHeadSize + d);
-    }
-    sh.qt[d][row] = q.x;
-    sh.qt[d + 1][row] = q.y;
-    sh.qt[d + 2][row] = q.z;
-    sh.qt[d + 3][row] = q.w;
+  const uint32_t last = p.first_position + t0 + rows - 1u; // the tile's last position
+  const uint32_t chunks = last / p.chunk_keys + 1u;
+  const uint32_t begin = chunk * p.chunk_keys;
+  if (chunk >= chunks) {
+    return;
   }
-  __syncthreads();
-  const uint32_t last = p.first_position + t0 + rows - 1u;
+  const uint32_t end = min(begin + p.chunk_keys, last + 1u);
+  const uint32_t tiles = (end - begin + kAttentionKeys - 1u) / kAttentionKeys;
+  const size_t kv_offset = size_t{kv_group} * qd::kHeadSize;
+  // 16-byte copies; rows past `end` (or past count, for Q) become 0.
+  auto issue = [&](uint32_t buffer, uint32_t base) {
+#pragma unroll
+    for (uint32_t j = 0; j < kAttentionKeys * 16u / pf::kAttentionThreads; ++j) {
+      const uint32_t i = tid + pf::kAttentionThreads * j, key = i / 16u, c = (i % 16u) * 4u;
+      const bool valid = base + key < end;
+      const size_t row = size_t{valid ? base + key : begin} * qd::kKvSize + kv_offset + c;
+      copy16_async(&sh.k[buffer][key][c], p.key_cache + row, valid ? 16u : 0u);
+      copy16_async(&sh.v[buffer][key][c], p.value_cache + row, valid ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (uint32_t j = 0; j < kAttentionRows * 16u / pf::kAttentionThreads; ++j) {
+    const uint32_t i = tid + pf::kAttentionThreads * j, row = i / 16u, c = (i % 16u) * 4u;
+    const bool valid = row < rows;
+    copy16_async(&sh.q[row][c],
+                 p.qkv + size_t{t0 + (valid ? row : 0u)} * qd::kPackedQkvSize +
+                     head * qd::kHeadSize + c,
+                 valid ? 16u : 0u);
+  }
+  issue(0, begin); // with Q in the same group
+  if (tiles > 1u) {
+    issue(1, begin + kAttentionKeys);
+  }
   uint32_t position[4];
   float maximum[4], denominator[4], acc[4][4];
 #pragma unroll
@@ -559,41 +583,14 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
       acc[i][j] = 0.0f;
     }
   }
-  const size_t kv_offset = size_t{kv_group} * qd::kHeadSize;
-  for (uint32_t base = g * kAttentionKeys; base <= last; base += kAttentionGroups * kAttentionKeys) {
-    group_barrier(g); // the group's previous tile reads are done
-    // All of the thread's K/V loads are issued before any shared store.
-    constexpr uint32_t kLoads = kAttentionKeys * qd::kHeadSize / 4u / kAttentionGroupThreads;
-    float4 k[kLoads], v[kLoads];
-#pragma unroll
-    for (uint32_t j = 0; j < kLoads; ++j) {
-      const uint32_t i = tid + kAttentionGroupThreads * j;
-      const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
-      // K key-fastest (transposed store), V dim-fastest (row store): no
-      // shared-store conflicts.
-      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
-      k[j] = v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (base + key <= last) {
-        k[j] = *reinterpret_cast<const float4 *>(p.key_cache + size_t{base + key} * qd::kKvSize +
-                                                 kv_offset + d);
-      }
-      if (base + vkey <= last) {
-        v[j] = *reinterpret_cast<const float4 *>(p.value_cache + size_t{base + vkey} * qd::kKvSize +
-                                                 kv_offset + vd);
-      }
+  for (uint32_t t = 0; t < tiles; ++t) {
+    const uint32_t buffer = t & 1u, base = begin + t * kAttentionKeys;
+    if (t + 1u < tiles) {
+      copy_wait<1>();
+    } else {
+      copy_wait<0>();
     }
-#pragma unroll
-    for (uint32_t j = 0; j < kLoads; ++j) {
-      const uint32_t i = tid + kAttentionGroupThreads * j;
-      const uint32_t key = i % kAttentionKeys, d = (i / kAttentionKeys) * 4u;
-      gs.kt[d][key] = k[j].x;
-      gs.kt[d + 1][key] = k[j].y;
-      gs.kt[d + 2][key] = k[j].z;
-      gs.kt[d + 3][key] = k[j].w;
-      const uint32_t vkey = i / (qd::kHeadSize / 4u), vd = (i % (qd::kHeadSize / 4u)) * 4u;
-      *reinterpret_cast<float4 *>(&gs.vs[vkey][vd]) = v[j];
-    }
-    group_barrier(g);
+    __syncthreads();
     float score[4][4];
 #pragma unroll
     for (uint32_t i = 0; i < 4; ++i) {
@@ -602,16 +599,22 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
         score[i][j] = 0.0f;
       }
     }
-#pragma unroll 8
-    for (uint32_t d = 0; d < qd::kHeadSize; ++d) {
-      const float4 q = *reinterpret_cast<const float4 *>(&sh.qt[d][4u * ty]);
-      const float4 k = *reinterpret_cast<const float4 *>(&gs.kt[d][4u * tx]);
-      const float qv[4] = {q.x, q.y, q.z, q.w}, kv[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll 4
+    for (uint32_t d = 0; d < qd::kHeadSize; d += 4u) {
+      float4 q[4], k[4];
+#pragma unroll
+      for (uint32_t i = 0; i < 4; ++i) {
+        q[i] = *reinterpret_cast<const float4 *>(&sh.q[4u * ty + i][d]);
+        k[i] = *reinterpret_cast<const float4 *>(&sh.k[buffer][tx + 16u * i][d]);
+      }
 #pragma unroll
       for (uint32_t i = 0; i < 4; ++i) {
 #pragma unroll
         for (uint32_t j = 0; j < 4; ++j) {
-          score[i][j] = fmaf(qv[i], kv[j], score[i][j]);
+          score[i][j] = fmaf(q[i].x, k[j].x, score[i][j]);
+          score[i][j] = fmaf(q[i].y, k[j].y, score[i][j]);
+          score[i][j] = fmaf(q[i].z, k[j].z, score[i][j]);
+          score[i][j] = fmaf(q[i].w, k[j].w, score[i][j]);
         }
       }
     }
@@ -621,7 +624,8 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
       float tile_maximum = -INFINITY;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        score[i][j] = base + 4u * tx + j <= position[i] ? score[i][j] * 0.125f : -INFINITY;
+        const uint32_t key = base + tx + 16u * j;
+        score[i][j] = key <= position[i] && key < end ? score[i][j] * 0.125f : -INFINITY;
         tile_maximum = fmaxf(tile_maximum, score[i][j]);
       }
 #pragma unroll
@@ -633,11 +637,12 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
       const float next = fmaxf(maximum[i], tile_maximum);
       const bool live = next != -INFINITY;
       scale[i] = live ? expf(maximum[i] - next) : 1.0f;
-      float weights[4], sum = 0.0f;
+      float sum = 0.0f;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        weights[j] = live ? expf(score[i][j] - next) : 0.0f;
-        sum += weights[j];
+        const float w = live ? expf(score[i][j] - next) : 0.0f;
+        sh.ps[4u * ty + i][tx + 16u * j] = w;
+        sum += w;
       }
 #pragma unroll
       for (uint32_t offset = 1; offset < 16; offset <<= 1u) {
@@ -645,8 +650,6 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
       }
       denominator[i] = denominator[i] * scale[i] + sum;
       maximum[i] = next;
-      *reinterpret_cast<float4 *>(&gs.ps[4u * ty + i][4u * tx]) =
-          make_float4(weights[0], weights[1], weights[2], weights[3]);
     }
 #pragma unroll
     for (uint32_t i = 0; i < 4; ++i) {
@@ -661,7 +664,7 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
       float pv[4][4];
 #pragma unroll
       for (uint32_t i = 0; i < 4; ++i) {
-        const float4 w = *reinterpret_cast<const float4 *>(&gs.ps[4u * ty + i][key]);
+        const float4 w = *reinterpret_cast<const float4 *>(&sh.ps[4u * ty + i][key]);
         pv[i][0] = w.x;
         pv[i][1] = w.y;
         pv[i][2] = w.z;
@@ -669,7 +672,7 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
       }
 #pragma unroll
       for (uint32_t e = 0; e < 4; ++e) {
-        const float4 v = *reinterpret_cast<const float4 *>(&gs.vs[key + e][4u * tx]);
+        const float4 v = *reinterpret_cast<const float4 *>(&sh.v[buffer][key + e][4u * tx]);
         const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (uint32_t i = 0; i < 4; ++i) {
@@ -680,56 +683,89 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads, 1)
         }
       }
     }
-  }
-  // Merge: groups 1..3 publish (maximum, denominator, acc) in their own
-  // buffers (acc in kt, now free), group 0 rescales all four to the common
-  // maximum. A group that saw no key keeps maximum -inf and contributes 0.
-  __syncthreads();
-  if (tx == 0) {
-#pragma unroll
-    for (uint32_t i = 0; i < 4; ++i) {
-      sh.maximum[g][4u * ty + i] = maximum[i];
-      sh.denominator[g][4u * ty + i] = denominator[i];
+    __syncthreads(); // buffer `buffer` and the weights are free again
+    if (t + 2u < tiles) {
+      issue(buffer, base + 2u * kAttentionKeys);
     }
   }
-  if (g != 0) {
-#pragma unroll
-    for (uint32_t i = 0; i < 4; ++i) {
-      *reinterpret_cast<float4 *>(&gs.kt[4u * ty + i][4u * tx]) =
-          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-    }
-  }
-  __syncthreads();
-  if (g != 0) {
-    return;
-  }
-#pragma unroll
-  for (uint32_t i = 0; i < 4; ++i) {
-    const uint32_t row = 4u * ty + i;
-    float common = sh.maximum[0][row];
-    for (uint32_t h = 1; h < kAttentionGroups; ++h) {
-      common = fmaxf(common, sh.maximum[h][row]);
-    }
-    const float own = expf(sh.maximum[0][row] - common);
-    float total = sh.denominator[0][row] * own;
-    float out[4] = {acc[i][0] * own, acc[i][1] * own, acc[i][2] * own, acc[i][3] * own};
-    for (uint32_t h = 1; h < kAttentionGroups; ++h) {
-      const float m = sh.maximum[h][row];
-      const float weight = m != -INFINITY ? expf(m - common) : 0.0f;
-      total += sh.denominator[h][row] * weight;
-      const float4 a = *reinterpret_cast<const float4 *>(&sh.group[h].kt[row][4u * tx]);
-      out[0] += a.x * weight;
-      out[1] += a.y * weight;
-      out[2] += a.z * weight;
-      out[3] += a.w * weight;
-    }
+  auto store_row = [&](uint32_t row, const float (&o)[4]) {
     if (row < rows) {
       const size_t at = size_t{t0 + row} * qd::kQuerySize + head * qd::kHeadSize + 4u * tx;
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j) {
-        store_operand(p.out, p.out_lo, at + j, out[j] / total);
+        store_operand(p.out, p.out_lo, at + j, o[j]);
       }
     }
+  };
+  if (chunks == 1u) {
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+      const float inverse = 1.0f / denominator[i];
+      const float o[4] = {acc[i][0] * inverse, acc[i][1] * inverse, acc[i][2] * inverse,
+                          acc[i][3] * inverse};
+      store_row(4u * ty + i, o);
+    }
+    return;
+  }
+  // Partial state of this chunk: [r][head][chunk][row][kAttentionPartialStride].
+  const size_t tile_state = size_t{r} * qd::kAttentionHeads + head;
+  float *states = p.partials + tile_state * p.max_chunks * kAttentionRows *
+                                   pf::kAttentionPartialStride;
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) {
+    float *row = states + (size_t{chunk} * kAttentionRows + 4u * ty + i) *
+                              pf::kAttentionPartialStride;
+    *reinterpret_cast<float4 *>(row + 4u * tx) =
+        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    if (tx == 0) {
+      row[64] = maximum[i];     // -inf: no key of this chunk precedes the row
+      row[65] = denominator[i]; // 0 then
+    }
+  }
+  __shared__ bool finisher;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    finisher = atomicAdd(&p.arrivals[tile_state], 1u) == chunks - 1u;
+  }
+  __syncthreads();
+  if (!finisher) {
+    return;
+  }
+  __threadfence();
+  // Merge in chunk order: per row, the common maximum, then the rescaled
+  // sums and accumulators.
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) {
+    const uint32_t row = 4u * ty + i;
+    const float *first = states + size_t{row} * pf::kAttentionPartialStride;
+    const size_t chunk_stride = size_t{kAttentionRows} * pf::kAttentionPartialStride;
+    float common = -INFINITY;
+    for (uint32_t c = 0; c < chunks; ++c) {
+      common = fmaxf(common, __ldcg(first + c * chunk_stride + 64));
+    }
+    float total = 0.0f, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (uint32_t c = 0; c < chunks; ++c) {
+      const float m = __ldcg(first + c * chunk_stride + 64);
+      if (m == -INFINITY) {
+        continue;
+      }
+      const float weight = expf(m - common);
+      total += __ldcg(first + c * chunk_stride + 65) * weight;
+      const float4 a = __ldcg(reinterpret_cast<const float4 *>(first + c * chunk_stride + 4u * tx));
+      o[0] += a.x * weight;
+      o[1] += a.y * weight;
+      o[2] += a.z * weight;
+      o[3] += a.w * weight;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      o[j] /= total;
+    }
+    store_row(row, o);
+  }
+  if (tid == 0) {
+    p.arrivals[tile_state] = 0; // ready for the next layer
   }
 }
 
@@ -1280,19 +1316,6 @@ struct DecodeShared {
 };
 
 static_assert(sizeof(DecodeShared) == pf::kDecodeSharedBytes, "decode shared layout");
-
-// 16 bytes global -> shared without registers; `bytes` 0 zero-fills.
-__device__ __forceinline__ void copy16_async(void *destination, const void *source,
-                                             uint32_t bytes) {
-  const uint32_t address = static_cast<uint32_t>(__cvta_generic_to_shared(destination));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(address), "l"(source),
-               "r"(bytes)
-               : "memory");
-}
-
-template <uint32_t kPending> __device__ __forceinline__ void copy_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
-}
 
 extern "C" __global__ void __launch_bounds__(256) batch_attention(pf::DecodeAttentionArgs p) {
   dependent_launch_entry();

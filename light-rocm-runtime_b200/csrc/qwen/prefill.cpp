@@ -50,6 +50,17 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   // Split-K partials: at most one 128 x 256 tile per SM in flight.
   partials_.emplace(allocate(sizeof(float) * kSms * kTcTileM * kTcMaximumN));
   error_.emplace(allocate(sizeof(uint32_t)));
+  // Attention: per (row tile, head) the key chunks' softmax states, and the
+  // arrival counters (zero; the last chunk block resets its counter).
+  const size_t row_tiles = ceil_div(chunk_, kAttentionTileRows);
+  attention_partials_.emplace(allocate(sizeof(float) * row_tiles * qd::kAttentionHeads *
+                                       kAttentionMaximumChunks * kAttentionTileRows *
+                                       kAttentionPartialStride));
+  attention_arrivals_.emplace(allocate(sizeof(uint32_t) * row_tiles * qd::kAttentionHeads));
+  const std::vector<uint32_t> no_arrivals(row_tiles * qd::kAttentionHeads, 0u);
+  check(lr_memcpy(device_.get(), attention_arrivals_->data(), no_arrivals.data(),
+                  sizeof(uint32_t) * no_arrivals.size(), LR_MEMCPY_HOST_TO_DEVICE),
+        "lr_memcpy attention arrivals");
 }
 
 DeviceBuffer Prefill::allocate(size_t bytes) {
@@ -291,14 +302,21 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
     launch(rope_kv_.get(), rows_config(count, row_threads(count)),
            RopeArgs{qkv, model.rope_cos, model.rope_sin, w.key_cache, w.value_cache, count,
                     first_position, qkv_partials, w.qkv_bias, nullptr, 0});
-    // Attention blocks: 32 query rows x one head each.
+    // Attention blocks: a key chunk x 64 query rows x one head; chunks of
+    // 128 positions (more when the context needs over kAttentionMaximumChunks).
+    const uint32_t keys = first_position + count;
+    const uint32_t chunk_keys =
+        128u * std::max(1u, ceil_div(keys, 128u * kAttentionMaximumChunks));
     const lr_launch_config_t attention_config{
-        {ceil_div(count, 32) * kAttentionThreads, qd::kAttentionHeads, 1},
+        {ceil_div(keys, chunk_keys) * kAttentionThreads, ceil_div(count, kAttentionTileRows),
+         qd::kAttentionHeads},
         {kAttentionThreads, 1, 1},
         kAttentionSharedBytes};
     launch(attend_.get(), attention_config,
            AttentionArgs{qkv, w.key_cache, w.value_cache, attention, attention_lo, count,
-                         first_position});
+                         first_position, chunk_keys, kAttentionMaximumChunks,
+                         static_cast<float *>(attention_partials_->data()),
+                         static_cast<uint32_t *>(attention_arrivals_->data())});
     if (tc) {
       finish(tc_gemm(kHiddenTile, attention_maps_, layer_maps_[layer].o, count, kHidden, kHidden,
                      GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr, true),

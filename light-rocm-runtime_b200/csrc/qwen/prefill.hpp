@@ -100,7 +100,8 @@ private:
   uint64_t device_bytes_ = 0;
 
   std::optional<DeviceBuffer> tokens_, hidden_, normalized_, normalized_lo_, qkv_, attention_,
-      attention_lo_, activated_, activated_lo_, partials_, error_;
+      attention_lo_, activated_, activated_lo_, partials_, error_, attention_partials_,
+      attention_arrivals_;
   // 3xTF32 path: per-layer (hi, lo) weight copies and tensor maps.
   std::optional<DeviceBuffer> split_weights_;
   std::vector<LayerMaps> layer_maps_;
