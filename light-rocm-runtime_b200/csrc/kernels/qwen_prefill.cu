@@ -358,29 +358,49 @@ extern "C" __global__ void __launch_bounds__(256) prefill_rmsnorm(pf::NormArgs p
   }
 }
 
-// Sum over splits of one element of a deferred GEMM's partial tiles: row t,
-// column c of the output. All (at most kMaximumDeferredSplits) loads are
-// issued before the additions, which stay in split order.
-using pf::kMaximumDeferredSplits;
-
-__device__ __forceinline__ float partial_sum(const pf::PartialTiles &tiles, uint32_t t,
-                                             uint32_t column) {
-  const uint32_t tile = (t / tiles.tile_rows) * tiles.n_tiles + column / tiles.tile_columns;
+// Copies the deferred GEMM's partial sums of row t, columns [0, columns),
+// into shared memory stage[split][column]: 16-byte loads in batches of
+// eight per thread, so that a row's loads of every split are in flight
+// together (tile_columns and columns are multiples of 4).
+__device__ __forceinline__ void stage_partials(const pf::PartialTiles &tiles, uint32_t t,
+                                               uint32_t columns, float *stage) {
+  const uint32_t vectors = columns / 4u;
+  const uint32_t total = tiles.splits * vectors;
+  const uint32_t band = t / tiles.tile_rows;
   const size_t tile_floats = size_t{tiles.tile_rows} * tiles.tile_columns;
-  const float *at = tiles.partials + size_t{tile} * tile_floats +
-                    size_t{t % tiles.tile_rows} * tiles.tile_columns + column % tiles.tile_columns;
   const size_t split_stride = size_t{tiles.tile_count} * tile_floats;
-  float values[kMaximumDeferredSplits];
+  const float *row = tiles.partials + size_t{t % tiles.tile_rows} * tiles.tile_columns;
+  constexpr uint32_t kBatch = 8;
+  for (uint32_t first = threadIdx.x; first < total; first += kBatch * blockDim.x) {
+    float4 v[kBatch];
 #pragma unroll
-  for (uint32_t s = 0; s < kMaximumDeferredSplits; ++s) {
-    values[s] = s < tiles.splits ? __ldcg(at + s * split_stride) : 0.0f;
-  }
-  float sum = values[0];
-#pragma unroll
-  for (uint32_t s = 1; s < kMaximumDeferredSplits; ++s) {
-    if (s < tiles.splits) {
-      sum += values[s];
+    for (uint32_t j = 0; j < kBatch; ++j) {
+      const uint32_t i = first + j * blockDim.x;
+      if (i < total) {
+        const uint32_t split = i / vectors, column = (i % vectors) * 4u;
+        const uint32_t tile = band * tiles.n_tiles + column / tiles.tile_columns;
+        v[j] = __ldcg(reinterpret_cast<const float4 *>(row + split * split_stride +
+                                                       tile * tile_floats +
+                                                       column % tiles.tile_columns));
+      }
     }
+#pragma unroll
+    for (uint32_t j = 0; j < kBatch; ++j) {
+      const uint32_t i = first + j * blockDim.x;
+      if (i < total) {
+        const uint32_t split = i / vectors, column = (i % vectors) * 4u;
+        *reinterpret_cast<float4 *>(stage + split * columns + column) = v[j];
+      }
+    }
+  }
+}
+
+// Sum over splits, in split order, of a staged column.
+__device__ __forceinline__ float staged_sum(const float *stage, uint32_t splits, uint32_t columns,
+                                            uint32_t column) {
+  float sum = stage[column];
+  for (uint32_t s = 1; s < splits; ++s) {
+    sum += stage[s * columns + column];
   }
   return sum;
 }
@@ -422,6 +442,7 @@ __device__ __forceinline__ void row_rmsnorm(const float *x, const float *weight,
 extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_rope_kv(pf::RopeArgs p) {
   dependent_launch_entry();
   __shared__ float row[qd::kPackedQkvSize];
+  extern __shared__ __align__(16) float stage[]; // [splits][1152] when deferred
   const uint32_t t = blockIdx.x;
   if (t >= p.count) {
     return;
@@ -429,9 +450,15 @@ extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_rope_kv(pf::Ro
   const uint32_t position = p.positions != nullptr ? p.positions[t] : p.first_position + t;
   const size_t stream_offset = p.positions != nullptr ? t * p.stream_stride : 0;
   float *qkv = p.qkv + size_t{t} * qd::kPackedQkvSize;
+  const bool deferred = p.qkv_partials.partials != nullptr;
+  if (deferred) {
+    stage_partials(p.qkv_partials, t, qd::kPackedQkvSize, stage);
+    __syncthreads();
+  }
   for (uint32_t i = threadIdx.x; i < qd::kPackedQkvSize; i += blockDim.x) {
-    row[i] = p.qkv_partials.partials != nullptr ? partial_sum(p.qkv_partials, t, i) + p.qkv_bias[i]
-                                                : qkv[i];
+    row[i] = deferred ? staged_sum(stage, p.qkv_partials.splits, qd::kPackedQkvSize, i) +
+                            p.qkv_bias[i]
+                      : qkv[i];
   }
   __syncthreads();
   const float *cos_row = p.rope_cos + size_t{position} * qd::kRotarySize;
@@ -464,15 +491,23 @@ extern "C" __global__ void __launch_bounds__(kRowThreads) prefill_finish_rows(pf
   dependent_launch_entry();
   __shared__ float row[qd::kHiddenSize];
   __shared__ float partial[256];
+  extern __shared__ __align__(16) float stage[]; // [splits][896] when deferred
   const uint32_t t = blockIdx.x;
   if (t >= p.count) {
     return;
   }
   float *hidden = p.hidden + size_t{t} * qd::kHiddenSize;
+  const bool deferred = p.partials.partials != nullptr;
   for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += blockDim.x) {
-    const float value = p.partials.partials != nullptr
-                            ? hidden[i] + partial_sum(p.partials, t, i)
-                            : hidden[i];
+    row[i] = hidden[i];
+  }
+  if (deferred) {
+    stage_partials(p.partials, t, qd::kHiddenSize, stage);
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < qd::kHiddenSize; i += blockDim.x) {
+    const float value =
+        deferred ? row[i] + staged_sum(stage, p.partials.splits, qd::kHiddenSize, i) : row[i];
     hidden[i] = value;
     row[i] = value;
   }

@@ -129,7 +129,7 @@ void BatchDecoder::enqueue_step(const ModelView &model) {
   auto *positions = static_cast<uint32_t *>(positions_->data());
   const uint64_t stream_stride = uint64_t{layers_} * capacity_ * qd::kKvSize;
   auto finish = [&](const PartialTiles &partials, const float *norm_weight) {
-    launch(p.finish_rows_.get(), rows_config(b, row_threads(b)),
+    launch(p.finish_rows_.get(), rows_config(b, row_threads(b), staged_bytes(partials, kHidden)),
            FinishArgs{partials, hidden, b, model.epsilon, norm_weight, normalized, normalized_lo});
   };
 
@@ -148,7 +148,7 @@ void BatchDecoder::enqueue_step(const ModelView &model) {
     const PartialTiles qkv_partials =
         p.tc_gemm(kQkvTile, p.normalized_maps_, maps.qkv, b, kQkv, kHidden, GemmEpilogue::bias,
                   qkv, nullptr, kQkv, w.qkv_bias, true);
-    launch(p.rope_kv_.get(), rows_config(b, row_threads(b)),
+    launch(p.rope_kv_.get(), rows_config(b, row_threads(b), staged_bytes(qkv_partials, kQkv)),
            RopeArgs{qkv, model.rope_cos, model.rope_sin, keys, values, b, 0, qkv_partials,
                     w.qkv_bias, positions, stream_stride});
     const DecodeAttentionArgs attend{qkv,

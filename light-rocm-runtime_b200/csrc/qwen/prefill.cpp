@@ -277,7 +277,8 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
   // Residual finish of o_proj / down (from partial sums, when deferred) and
   // the next RMSNorm of the same rows.
   auto finish = [&](const PartialTiles &partials, const float *norm_weight) {
-    launch(finish_rows_.get(), rows_config(count, row_threads(count)),
+    launch(finish_rows_.get(),
+           rows_config(count, row_threads(count), staged_bytes(partials, kHidden)),
            FinishArgs{partials, hidden, count, model.epsilon, norm_weight, normalized,
                       normalized_lo});
   };
@@ -299,7 +300,8 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
                     kHidden, kHidden, kQkv},
            ceil_div(kQkv, 128));
     }
-    launch(rope_kv_.get(), rows_config(count, row_threads(count)),
+    launch(rope_kv_.get(),
+           rows_config(count, row_threads(count), staged_bytes(qkv_partials, kQkv)),
            RopeArgs{qkv, model.rope_cos, model.rope_sin, w.key_cache, w.value_cache, count,
                     first_position, qkv_partials, w.qkv_bias, nullptr, 0});
     // Attention blocks: a key chunk x 64 query rows x one head; chunks of

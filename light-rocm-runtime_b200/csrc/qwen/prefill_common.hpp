@@ -78,8 +78,14 @@ inline TensorMap map_2d(const float *base, uint64_t rows, uint64_t columns, uint
   return out;
 }
 
-inline lr_launch_config_t rows_config(uint32_t blocks, uint32_t threads) {
-  return lr_launch_config_t{{blocks * threads, 1, 1}, {threads, 1, 1}, 0};
+inline lr_launch_config_t rows_config(uint32_t blocks, uint32_t threads, uint32_t shared = 0) {
+  return lr_launch_config_t{{blocks * threads, 1, 1}, {threads, 1, 1}, shared};
+}
+
+// Dynamic shared memory of a row kernel that stages `columns` partial sums
+// per split of a deferred GEMM (none when the GEMM wrote its output).
+inline uint32_t staged_bytes(const PartialTiles &partials, uint32_t columns) {
+  return partials.partials != nullptr ? partials.splits * columns * 4u : 0u;
 }
 
 inline uint32_t ceil_div(uint64_t a, uint64_t b) { return static_cast<uint32_t>((a + b - 1) / b); }
