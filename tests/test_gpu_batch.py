@@ -75,6 +75,34 @@ def test_batch_argument_errors(gpu):
 
 
 @pytest.mark.gpu
+def test_batch_of_40_streams_runs_the_wide_gemms(gpu):
+    """More than 32 streams run the 128-row-band GEMM kernels instead of the
+    narrow ones: 40 streams with prompts of 1..40 tokens, 6 greedy steps;
+    three streams against the oracle's single-stream runs."""
+    layers, vocab, steps = 2, 4096, 6
+    model, oracle, _, _ = build_pair(seed=37, layers=layers, vocab=vocab, capacity=64,
+                                     max_tokens=steps)
+    model.enable_prefill(64)
+    prompts = [S.prompt(300 + i, 1 + i, vocab) for i in range(40)]
+    with Q.Batch(model, len(prompts), 64, steps) as batch:
+        for stream, prompt in enumerate(prompts):
+            batch.prefill(stream, prompt)
+        tokens, logits = batch.decode(steps)
+    for stream in (0, 17, 39):
+        prompt = prompts[stream]
+        start = len(prompt) - 1
+        for cache in oracle.key_cache + oracle.value_cache:
+            cache[:] = 0
+        for i, token in enumerate(prompt[:-1]):
+            oracle.decode(oracle.embedding(int(token)), i, 1)
+        oracle.decode(oracle.embedding(int(prompt[-1])), start, steps)
+        assert tokens[stream].tolist() == oracle.output_tokens[:steps].tolist(), stream
+        d = oracle.decode_state
+        assert abs(logits[stream] - d.sampled_logit) <= LOGIT_RTOL * max(1.0, abs(d.sampled_logit))
+    model.close()
+
+
+@pytest.mark.gpu
 def test_config4_batch_32_streams_context_1024(gpu):
     """BASELINE config 4 on one GPU: 32 streams, each with a 1025-token random
     prompt (seed 2; context 1024), 128 greedy tokens per stream. Streams 0, 13
