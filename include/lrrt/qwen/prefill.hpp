@@ -200,7 +200,9 @@ struct ArgmaxArgs {
 
 constexpr uint32_t kArgmaxPartitions = 8; // blocks per stream row
 constexpr uint32_t kRowThreads = 1024;     // prefill_rope_kv, prefill_finish_rows
-constexpr uint32_t kMaximumDeferredSplits = 16;
+// At most this many K splits for a GEMM whose partials the next row kernel
+// finishes (it stages splits x columns floats of shared memory per row).
+constexpr uint32_t kMaximumDeferredSplits = 24;
 
 constexpr uint32_t kAttentionTileRows = 64; // query rows per block
 constexpr uint32_t kAttentionThreads = 256;
