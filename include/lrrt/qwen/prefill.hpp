@@ -129,9 +129,10 @@ struct FinishArgs {
 
 // Causal GQA attention: query row t attends to cache positions
 // 0..first_position + t. out [count][896] (hi part when out_lo is set).
-// Launch: blocks of kAttentionThreads threads over (key chunks,
-// ceil(count / kAttentionTileRows), 14) with kAttentionSharedBytes of dynamic
-// shared memory;
+// Launch: blocks of kAttentionThreads threads over (the (row tile, key
+// chunk) pairs with work, 14) with kAttentionSharedBytes of dynamic shared
+// memory; a row tile of kAttentionTileRows rows holds the chunks up to its
+// last position;
 // chunk_keys * max_chunks covers first_position + count positions.
 struct AttentionArgs {
   const float *qkv;

@@ -532,10 +532,10 @@ template <uint32_t kPending> __device__ __forceinline__ void copy_wait() {
 }
 
 // Causal GQA attention, register-blocked and split over key chunks. Block
-// (c, r, h) serves query rows t0 = 64r .. t0 + 63 of head h against cache
-// positions [c * chunk_keys, (c + 1) * chunk_keys) up to each row's own
-// position first_position + t; key chunks that start past the tile's last
-// position exit at once. The chunk's 64-key tiles are copied with cp.async
+// (x, h) serves, for the x-th (row tile r, key chunk c) pair that holds
+// work, query rows t0 = 64r .. t0 + 63 of head h against cache positions
+// [c * chunk_keys, (c + 1) * chunk_keys) up to each row's own position
+// first_position + t. The chunk's 64-key tiles are copied with cp.async
 // into two buffers (K and V row-major; tile t + 1 lands while tile t is
 // computed). Thread (ty, tx) = (tid / 16, tid % 16) owns query rows
 // 4ty..4ty+3 and, per tile, keys tx + 16j of S = Q.K^T / 8 (float4 reads
@@ -565,19 +565,32 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads)
   extern __shared__ __align__(16) unsigned char attention_raw[];
   AttentionShared &sh = *reinterpret_cast<AttentionShared *>(attention_raw);
   const uint32_t tid = threadIdx.x, ty = tid / 16u, tx = tid % 16u;
-  const uint32_t chunk = blockIdx.x, r = blockIdx.y, head = blockIdx.z;
+  // blockIdx.x enumerates the (row tile, key chunk) pairs that hold work,
+  // the last (heaviest) row tile first, chunks in order.
+  const uint32_t head = blockIdx.y;
+  const uint32_t row_tiles = (p.count + kAttentionRows - 1u) / kAttentionRows;
+  auto chunks_of = [&](uint32_t tile) {
+    const uint32_t tile_last = p.first_position + min(p.count, (tile + 1u) * kAttentionRows) - 1u;
+    return tile_last / p.chunk_keys + 1u;
+  };
+  uint32_t r = row_tiles, chunk = blockIdx.x;
+  while (r > 0u) {
+    --r;
+    const uint32_t n = chunks_of(r);
+    if (chunk < n) {
+      break;
+    }
+    chunk -= n;
+  }
   const uint32_t kv_group = head / qd::kQueriesPerKvHead;
   const uint32_t t0 = r * kAttentionRows;
-  if (t0 >= p.count) {
-    return;
+  const uint32_t chunks = chunks_of(r);
+  if (t0 >= p.count || chunk >= chunks) {
+    return; // past the enumeration (not launched by the host)
   }
   const uint32_t rows = min(kAttentionRows, p.count - t0);
   const uint32_t last = p.first_position + t0 + rows - 1u; // the tile's last position
-  const uint32_t chunks = last / p.chunk_keys + 1u;
   const uint32_t begin = chunk * p.chunk_keys;
-  if (chunk >= chunks) {
-    return;
-  }
   const uint32_t end = min(begin + p.chunk_keys, last + 1u);
   const uint32_t tiles = (end - begin + kAttentionKeys - 1u) / kAttentionKeys;
   const size_t kv_offset = size_t{kv_group} * qd::kHeadSize;

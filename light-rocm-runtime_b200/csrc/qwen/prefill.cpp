@@ -309,9 +309,13 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
     const uint32_t keys = first_position + count;
     const uint32_t chunk_keys =
         128u * std::max(1u, ceil_div(keys, 128u * kAttentionMaximumChunks));
+    uint32_t attention_blocks = 0; // (row tile, key chunk) pairs with work
+    for (uint32_t t0 = 0; t0 < count; t0 += kAttentionTileRows) {
+      const uint32_t tile_last = first_position + std::min(count, t0 + kAttentionTileRows) - 1u;
+      attention_blocks += tile_last / chunk_keys + 1u;
+    }
     const lr_launch_config_t attention_config{
-        {ceil_div(keys, chunk_keys) * kAttentionThreads, ceil_div(count, kAttentionTileRows),
-         qd::kAttentionHeads},
+        {attention_blocks * kAttentionThreads, qd::kAttentionHeads, 1},
         {kAttentionThreads, 1, 1},
         kAttentionSharedBytes};
     launch(attend_.get(), attention_config,
