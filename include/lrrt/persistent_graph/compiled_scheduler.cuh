@@ -14,8 +14,10 @@
 //  * Workloads may declare that a stage boundary needs no grid barrier
 //    (barrier_after), because they carry the dependency inside each block
 //    (e.g. a norm recomputed per block, or a RoPE epilogue fused into the
-//    projection). Barriers are then counted per executed barrier, not per
-//    stage; the Program's final stage always ends with a barrier.
+//    projection) or exchange the data through self-validating words.
+//    Barriers are then counted per executed barrier, not per stage. The
+//    Program's final stage ends with a barrier unless the workload runs in
+//    local-transition mode and barrier_at_end says otherwise.
 //  * Workloads get a per-block state object (Workload::Block) created before
 //    the loop (begin) and retired after it (end), so a block can keep a TMA
 //    weight-streaming ring running across stages and barriers.
@@ -27,6 +29,8 @@
 //   execute_stage(Block&, const Stage&, const Task*, State*, void* context,
 //                 uint32_t worker, uint32_t active_workers)
 //   barrier_after(Block&, const Stage&, const Stage& next, const Task*)
+//   barrier_at_end(const Block&)        // local mode: barrier after the last stage
+//   barrier_poll(Block&)                // thread 0, between grid-barrier polls
 //   end(Block&)                         // before the block returns
 //   initialize_profile(void*)
 //   complete_profile_stage(Block&, const Stage&, const Task*, void*)
@@ -94,15 +98,16 @@ __device__ bool validate_plan(const State *state, const Task *tasks,
 // Program's final barrier the last arrival first runs `on_last` (the Program
 // transition, on thread 0 of that block only) and then publishes
 // completed_mask = index + 1, which the other blocks wait for. Returns false
-// when the run failed or the wait limit passed.
+// when the run failed or the wait limit passed. Thread 0 calls `on_poll`
+// between polls (the workload's barrier_poll hook).
 //
 // The block-wide __syncthreads before the arrival orders every thread's writes
 // before thread 0's release; thread 0's acquire and the __syncthreads after the
 // wait order every thread's later reads after the other blocks' writes.
-template <typename OnLast>
+template <typename OnLast, typename OnPoll>
 __device__ bool grid_barrier(State *state, MaskState *barrier, uint32_t index,
                              uint32_t workers, bool final, const Deadline &deadline,
-                             OnLast on_last) {
+                             OnLast on_last, OnPoll on_poll) {
   __shared__ uint32_t barrier_ok;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -123,6 +128,7 @@ __device__ bool grid_barrier(State *state, MaskState *barrier, uint32_t index,
     uint32_t ok = 1;
     uint32_t spins = 0;
     while (load_acquire(watched) < goal) {
+      on_poll();
       if ((++spins & 127u) == 0u) {
         if (load_status(state) != static_cast<uint32_t>(Status::running)) {
           ok = 0;
@@ -151,6 +157,13 @@ struct CompiledWorkloadDefaults {
                                        uint64_t, uint64_t) {}
   __device__ static void begin(Block &, const ResidentArgs &) {}
   __device__ static bool local_transitions(const Block &) { return false; }
+  // Thread 0, between polls of a grid barrier.
+  __device__ static void barrier_poll(Block &) {}
+  // Local-transition mode: whether the current Program ends with a grid
+  // barrier. A workload that carries every dependency across the Program
+  // boundary itself (and whose transition needs no other block's writes) may
+  // skip it.
+  __device__ static bool barrier_at_end(const Block &) { return true; }
   __device__ static void program_begin(Block &, uint32_t /*program*/, uint32_t /*step*/) {}
   __device__ static void stage_begin(Block &, uint32_t /*stage index in program*/) {}
   // Local-transition mode: the branch_value the finished Program's tasks
@@ -317,6 +330,7 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
     Workload::program_begin(block, phase_program(phase), control.step);
     uint32_t barrier_index = 0;
     bool ok = true;
+    bool ended_with_barrier = false;
     for (uint32_t s = 0; s < compiled.stage_count && ok; ++s) {
       const Stage stage = stages[compiled.stage_offset + s];
       Workload::stage_begin(block, s);
@@ -325,11 +339,14 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
                                 worker, workers);
       }
       const bool last = s + 1u == compiled.stage_count;
-      if (!last && !Workload::barrier_after(block, stage,
-                                            stages[compiled.stage_offset + s + 1u],
-                                            args.tasks)) {
+      const bool skip =
+          last ? local && !Workload::barrier_at_end(block)
+               : !Workload::barrier_after(block, stage,
+                                          stages[compiled.stage_offset + s + 1u], args.tasks);
+      if (skip) {
         continue;
       }
+      ended_with_barrier = last;
       const uint64_t arrive_ns = Workload::kTraceBarriers ? global_timer_ns() : 0;
       ok = detail::grid_barrier(state, barrier, barrier_index++, workers, last && !local,
                                 deadline, [&] {
@@ -340,7 +357,8 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
                                   }
                                   Workload::complete_profile_stage(
                                       block, stage, args.tasks, args.context);
-                                });
+                                },
+                                [&] { Workload::barrier_poll(block); });
       if (Workload::kTraceBarriers && threadIdx.x == 0) {
         Workload::trace_barrier(block, args.context, stage, args.tasks, arrive_ns,
                                 global_timer_ns());
@@ -360,7 +378,12 @@ __device__ void run_compiled_resident(const ResidentArgs &args) {
                                     : 0u;
         detail::local_transition(shared_control, state, program, generation,
                                  args.phase_state_count, max_steps, stop_value, branch);
-        if (worker == 0) {
+        // State is mirrored only where every block is known to have read the
+        // launch's initial State: after a Program-ending grid barrier, or when
+        // the run stops (which needs every block's contribution).
+        if (worker == 0 &&
+            (ended_with_barrier ||
+             shared_control.status != static_cast<uint32_t>(Status::running))) {
           detail::publish_control(state, shared_control);
         }
       }

@@ -138,11 +138,55 @@ __device__ __forceinline__ void bulk_copy_to_shared(void *destination,
       : "memory");
 }
 
+// 2-D TMA tile load of the box at (x, y) of the tensor map `map` (a
+// CUtensorMap in global memory) into shared memory, completing on `barrier`.
+// No multicast. x times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tensor_load_2d(void *destination, const void *map, uint32_t x,
+                                               uint32_t y, uint64_t *barrier) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(shared_address(destination)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(shared_address(barrier))
+      : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
                : "=l"(policy));
   return policy;
+}
+
+// ---- exchange words ---------------------------------------------------------
+// A value published to other blocks together with its readiness: one 64-bit
+// word tag << 32 | float bits, written and read as single 64-bit accesses
+// (single-copy atomic), so a reader that sees the tag it waits for also sees
+// the value stored with it, without fences or a separate flag.
+
+__device__ __forceinline__ uint64_t exchange_word(float value, uint32_t tag) {
+  return (uint64_t{tag} << 32) | __float_as_uint(value);
+}
+
+__device__ __forceinline__ void exchange_store(uint64_t *word, float value, uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(word),
+               "l"(exchange_word(value, tag))
+               : "memory");
+}
+
+// Two consecutive words (16-byte aligned).
+__device__ __forceinline__ void exchange_load2(const uint64_t *word, uint64_t &first,
+                                               uint64_t &second) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
+               : "=l"(first), "=l"(second)
+               : "l"(word));
+}
+
+__device__ __forceinline__ uint32_t exchange_tag(uint64_t word) {
+  return static_cast<uint32_t>(word >> 32);
+}
+
+__device__ __forceinline__ float exchange_value(uint64_t word) {
+  return __uint_as_float(static_cast<uint32_t>(word));
 }
 
 // L2-coherent loads for data other blocks wrote during this kernel.

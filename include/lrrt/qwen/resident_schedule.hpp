@@ -5,15 +5,23 @@
 // weight matrix; a unit is what one shared-memory ring slot holds:
 //   QKV   144 units: 8 rows = rows f..f+3 of one head and their rotary
 //                    partners f+32..f+35 (Q heads 0-13, K heads, then V)
-//   OUT   112 units: 8 consecutive o_proj rows
+//   KV      3 units per block (not partitioned: every block reads its own
+//                    KV group): cached K and V rows of positions 56j..56j+55,
+//                    loaded only for the positions the step attends to
+//   OUT   224 units: 8 consecutive o_proj rows restricted to the 448 input
+//                    columns of one KV group (units 0-111 group 0, 112-223
+//                    group 1); o_proj is split along its input over the groups
 //   GU   1216 units: gate rows 4u..4u+3 followed by up rows 4u..4u+3
 //   DOWN  896 units: one 4864-float down_proj row
 //   LM   ceil(V/8) units: 8 LM-head rows (the last may be shorter)
-// QKV, OUT, DOWN and LM units are split evenly; gate/up units are assigned so
-// that each block's bytes per layer (all four matrices) are balanced.
+// QKV, DOWN and LM units are split evenly. OUT units follow the attention
+// split: the first ceil(W/2) blocks compute the attention of KV group 0 and
+// own group 0's OUT units (split evenly among them), the others group 1's
+// (one block owns both when W == 1). Gate/up units are assigned so that each
+// block's bytes per layer (all four matrices) are balanced.
 //
 // A block's weight stream is the cyclic sequence
-//   [QKV(l), OUT(l), GU(l), DOWN(l)] for l = 0..L-1, then LM(0), repeat,
+//   [QKV(l), KV(l), OUT(l), GU(l), DOWN(l)] for l = 0..L-1, then LM(0), repeat,
 // restricted to its own units. The producer issues it in this order; the
 // consumer walks the compiled stages, which visit the same units in the same
 // order, and checks each slot's tag.
@@ -28,14 +36,21 @@
 
 namespace lrrt::qwen::stateful_graph::resident {
 
-enum StreamKind : uint32_t { kNoKind = 0, kQkv = 1, kOut = 2, kGateUp = 3, kDown = 4,
-                             kLmHead = 5 };
-constexpr uint32_t kKinds = 6;
+// Kinds in stream order within a layer (the cursor walks them in sequence).
+enum StreamKind : uint32_t { kNoKind = 0, kQkv = 1, kKv = 2, kOut = 3, kGateUp = 4,
+                             kDown = 5, kLmHead = 6 };
+constexpr uint32_t kKinds = 7;
+constexpr uint32_t kKvUnits = 3;                               // per block and layer
+constexpr uint32_t kKvUnitPositions = kSlotBytes / (2u * kKvSize / kKvHeads * 4u); // 56
+static_assert(kKvUnits * kKvUnitPositions + 1u >= kLocalAttentionLimit,
+              "KV units cover every cached position of a local-attention step");
 
 constexpr uint32_t kQkvUnits = kPackedQkvSize / kSlotRows;     // 144
 constexpr uint32_t kQUnits = kQuerySize / kSlotRows;           // 112
 constexpr uint32_t kKUnits = kKvSize / kSlotRows;              // 16
-constexpr uint32_t kOUnits = kHiddenSize / kSlotRows;          // 112
+constexpr uint32_t kOGroupUnits = kHiddenSize / kSlotRows;     // 112 per KV group
+constexpr uint32_t kOUnits = kKvHeads * kOGroupUnits;          // 224
+constexpr uint32_t kOUnitBytes = kSlotRows * kHalfRowBytes;    // 14336
 constexpr uint32_t kGuRowsPerUnit = kSlotRows / 2u;            // 4
 constexpr uint32_t kGuUnits = kIntermediateSize / kGuRowsPerUnit; // 1216
 constexpr uint32_t kDownUnits = kHiddenSize;                   // 896
@@ -63,11 +78,32 @@ LRRT_HOST_DEVICE inline uint32_t even_owner(uint32_t unit, uint32_t units,
   return static_cast<uint32_t>((uint64_t{unit + 1u} * workers - 1u) / units);
 }
 
+// Blocks [0, attention_split(W)) attend KV group 0, the rest group 1.
+LRRT_HOST_DEVICE constexpr uint32_t attention_split(uint32_t workers) {
+  return (workers + 1u) / 2u;
+}
+
+LRRT_HOST_DEVICE constexpr uint32_t attention_group(uint32_t worker, uint32_t workers) {
+  return worker < attention_split(workers) ? 0u : 1u;
+}
+
+LRRT_HOST_DEVICE inline UnitRange out_range(uint32_t worker, uint32_t workers) {
+  if (workers == 1u) {
+    return {0, kOUnits};
+  }
+  const uint32_t split = attention_split(workers);
+  if (worker < split) {
+    return even_range(kOGroupUnits, worker, split);
+  }
+  const UnitRange r = even_range(kOGroupUnits, worker - split, workers - split);
+  return {kOGroupUnits + r.begin, kOGroupUnits + r.end};
+}
+
 LRRT_HOST_DEVICE inline uint64_t fixed_layer_bytes(uint32_t worker, uint32_t workers) {
   const UnitRange q = even_range(kQkvUnits, worker, workers);
-  const UnitRange o = even_range(kOUnits, worker, workers);
+  const UnitRange o = out_range(worker, workers);
   const UnitRange d = even_range(kDownUnits, worker, workers);
-  return uint64_t{q.end - q.begin + o.end - o.begin} * kSlotBytes +
+  return uint64_t{q.end - q.begin} * kSlotBytes + uint64_t{o.end - o.begin} * kOUnitBytes +
          uint64_t{d.end - d.begin} * kDownRowBytes;
 }
 
@@ -79,7 +115,8 @@ LRRT_HOST_DEVICE inline uint32_t gate_up_boundary(uint32_t worker, uint32_t work
   if (worker + 1u >= workers) {
     return kGuUnits;
   }
-  const uint64_t total = uint64_t{kQkvUnits + kOUnits + kGuUnits} * kSlotBytes +
+  const uint64_t total = uint64_t{kQkvUnits + kGuUnits} * kSlotBytes +
+                         uint64_t{kOUnits} * kOUnitBytes +
                          uint64_t{kDownUnits} * kDownRowBytes;
   const int64_t want = static_cast<int64_t>(total * (worker + 1u) / workers) -
                        static_cast<int64_t>(fixed_prefix);
@@ -109,7 +146,8 @@ LRRT_HOST_DEVICE inline UnitRanges unit_ranges(uint32_t worker, uint32_t workers
   UnitRanges r{};
   r.of[kNoKind] = {0, 0};
   r.of[kQkv] = even_range(kQkvUnits, worker, workers);
-  r.of[kOut] = even_range(kOUnits, worker, workers);
+  r.of[kKv] = {0, kKvUnits};
+  r.of[kOut] = out_range(worker, workers);
   r.of[kGateUp] = balanced_gate_up(worker, workers);
   r.of[kDown] = even_range(kDownUnits, worker, workers);
   r.of[kLmHead] = even_range(lm_units_for(vocab), worker, workers);
@@ -199,13 +237,14 @@ LRRT_HOST_DEVICE inline StreamMap make_stream_map(const UnitRanges &r, uint32_t 
     m.first[k] = r.of[k].begin;
     m.count[k] = r.of[k].end - r.of[k].begin;
   }
-  m.per_layer = m.count[kQkv] + m.count[kOut] + m.count[kGateUp] + m.count[kDown];
+  m.per_layer =
+      m.count[kQkv] + m.count[kKv] + m.count[kOut] + m.count[kGateUp] + m.count[kDown];
   m.cycle = layers * m.per_layer + m.count[kLmHead];
   // program 0 starts at the QKV units of `layer`, program 1 at its gate/up
   // units, program 2 at the LM head.
   const uint32_t layer_offset = layer * m.per_layer;
   m.start = program == 0   ? layer_offset
-            : program == 1 ? layer_offset + m.count[kQkv] + m.count[kOut]
+            : program == 1 ? layer_offset + m.count[kQkv] + m.count[kKv] + m.count[kOut]
                            : layers * m.per_layer;
   return m;
 }
@@ -227,12 +266,14 @@ LRRT_HOST_DEVICE inline StreamCursor stream_unit(const StreamMap &m, uint32_t n)
 }
 
 // Incremental form of stream_unit for the lane that refills a ring slot:
-// (layer, index) with layer == layers meaning the LM-head region; advancing
-// by a ring's depth costs a compare and a subtraction per region crossed
-// instead of a division.
+// (layer, index) with layer == layers meaning the LM-head region, and the
+// number of whole cycles (decode tokens) since the launch's stream start;
+// advancing by a ring's depth costs a compare and a subtraction per region
+// crossed instead of a division.
 struct StreamPosition {
   uint32_t layer;
   uint32_t index;
+  uint32_t cycle;
 };
 
 LRRT_HOST_DEVICE inline uint32_t region_units(const StreamMap &m, uint32_t layer) {
@@ -240,12 +281,14 @@ LRRT_HOST_DEVICE inline uint32_t region_units(const StreamMap &m, uint32_t layer
 }
 
 LRRT_HOST_DEVICE inline StreamPosition stream_position(const StreamMap &m, uint32_t n) {
-  const uint32_t at = static_cast<uint32_t>((uint64_t{m.start} + n) % m.cycle);
+  const uint64_t absolute = uint64_t{m.start} + n;
+  const uint32_t at = static_cast<uint32_t>(absolute % m.cycle);
+  const uint32_t cycle = static_cast<uint32_t>(absolute / m.cycle);
   const uint32_t decoder = m.layers * m.per_layer;
   if (at >= decoder) {
-    return {m.layers, at - decoder};
+    return {m.layers, at - decoder, cycle};
   }
-  return {at / m.per_layer, at % m.per_layer};
+  return {at / m.per_layer, at % m.per_layer, cycle};
 }
 
 // Moves `p` forward by `by` units (the stream must not be empty).
@@ -260,7 +303,12 @@ LRRT_HOST_DEVICE inline void advance_position(const StreamMap &m, StreamPosition
       return;
     }
     p.index -= size;
-    p.layer = p.layer >= m.layers ? 0u : p.layer + 1u;
+    if (p.layer >= m.layers) {
+      p.layer = 0;
+      ++p.cycle;
+    } else {
+      ++p.layer;
+    }
   }
 }
 

@@ -112,13 +112,37 @@ struct alignas(16) DecodeState {
   float sampled_logit;
 };
 
-constexpr uint32_t kWorkspaceMagic = 0x51573230u; // "QW20"
+constexpr uint32_t kWorkspaceMagic = 0x51573231u; // "QW21"
 constexpr uint32_t kAttentionPartialStride = kHeadSize + 2u; // acc[64], max, sum
 
-// B200 scratch for the fused resident path (no reference counterpart).
+// Exchange words of the fused path: every value one block produces for the
+// others within a decoder layer travels as one 64-bit word, tag << 32 | float
+// bits, with tag = graph step + 1. A consumer polls the words it needs until
+// each carries the step's tag, so the wait and the data read are the same
+// loads. Arrays alternate by step parity; offsets in words:
+//   qkv  [2][kPackedQkvSize]          rotated q, rotated k, v of the step
+//   out  [2][kKvHeads][kHiddenSize]   o_proj split over the two KV groups
+//   act  [2][kIntermediateSize]       silu(gate) * up
+//   down [2][kHiddenSize]             down projection
+// All words are zero when no launch is running (a launch clears the words it
+// wrote before it returns; zero never matches a tag).
+constexpr uint32_t kExchangeQkv = 0;
+constexpr uint32_t kExchangeOut = kExchangeQkv + 2u * kPackedQkvSize;
+constexpr uint32_t kExchangeAct = kExchangeOut + 2u * kKvHeads * kHiddenSize;
+constexpr uint32_t kExchangeDown = kExchangeAct + 2u * kIntermediateSize;
+constexpr uint32_t kExchangeWords = kExchangeDown + 2u * kHiddenSize;
+
+// B200 scratch for the fused resident path (no reference counterpart). One
+// zero-filled allocation: this header, then
 //  attention_partials: [worker_capacity][kQueriesPerKvHead][kAttentionPartialStride]
 //  attention_arrivals: [kKvHeads], zero whenever no attention stage is running
 //  top1_values/top1_indices: [worker_capacity + kMaximumLmHeadPartitions]
+//  exchange: [kExchangeWords] 64-bit words (see above)
+//  kv_maps: [kWorkspaceMapLayers][2] CUtensorMap (128 B each: key cache,
+//    value cache of each layer; dims {kKvSize, cache_capacity}, box 32
+//    columns x 56 rows, 128-byte swizzle) for the fused path's KV ring units
+constexpr uint32_t kWorkspaceMapLayers = 48;
+constexpr uint32_t kTensorMapBytes = 128;
 struct alignas(16) Workspace {
   uint32_t magic;
   uint32_t worker_capacity;
@@ -127,6 +151,8 @@ struct alignas(16) Workspace {
   uint32_t *attention_arrivals;
   float *top1_values;
   uint32_t *top1_indices;
+  uint64_t *exchange;
+  const void *kv_maps;
 };
 
 // Bytes of one allocation holding a Workspace header followed by its arrays.
@@ -136,7 +162,8 @@ constexpr size_t workspace_bytes(uint32_t worker_capacity) {
              sizeof(float) +
          256u + 2u * (size_t{worker_capacity} + kMaximumLmHeadPartitions) *
                     sizeof(uint32_t) +
-         256u;
+         256u + size_t{kExchangeWords} * sizeof(uint64_t) + 256u +
+         size_t{kWorkspaceMapLayers} * 2u * kTensorMapBytes + 256u;
 }
 
 // Model tail shared by every layer Context.
@@ -206,7 +233,7 @@ static_assert(offsetof(TailContext, workspace) == 88);
 static_assert(sizeof(StageProfile) == 240);
 static_assert(sizeof(StageProfileEntry) == 16);
 static_assert(sizeof(DecodeState) == 32);
-static_assert(sizeof(Workspace) == 48);
+static_assert(sizeof(Workspace) == 64);
 static_assert(kAttentionTaskCount <= lrrt::persistent_graph::kMaximumTasks);
 static_assert(kFfnTaskCount <= lrrt::persistent_graph::kMaximumTasks);
 static_assert(kMaximumTailTaskCount <= lrrt::persistent_graph::kMaximumTasks);

@@ -13,20 +13,25 @@
 //   global memory.
 //
 // * Fused path (compiled kernel, canonical Qwen table, workspace bound): the
-//   decode step is a weight stream. Each block owns a balanced share of every
-//   weight matrix (QKV, o_proj, gate/up, down, LM head) and keeps a ring of
-//   7 x 28 KB shared-memory slots filled by 1-D TMA bulk copies
-//   (cp.async.bulk, no multicast). The ring is refilled as slots are consumed,
-//   so weight loads for the next stage are already in flight while the block
-//   waits at a grid barrier. Stage boundaries that only carry a per-block
-//   dependency skip the barrier: RMSNorm is recomputed by every block from the
-//   3.5 KB hidden vector, RoPE + KV-cache append run in the QKV epilogue (each
-//   block owns whole rotary pairs), the residual add runs in the o_proj and
-//   down epilogues, and the top-1 reduce and embedding feedback run in one
-//   block. That leaves 5 grid barriers per layer and 2 per token tail instead
-//   of 9 and 4. Decode attention is split over positions (flash-decoding):
-//   each (kv-head, chunk) item produces partial (max, sum, acc) for its 7
-//   query heads and the last arrival per kv head combines them.
+//   decode step is a weight stream plus a chain of small exchanges.
+//   - Each block owns a balanced share of every weight matrix (QKV, o_proj,
+//     gate/up, down, LM head) and keeps a ring of 7 x 28 KB shared-memory
+//     slots filled by TMA (1-D bulk copies for weights, 2-D tensor copies for
+//     its KV group's cached rows; no multicast). A consumer refills the slot
+//     it releases, so the stream runs ahead across stages and layers.
+//   - Values one block produces for the others inside a layer (q/k/v, the
+//     o_proj rows, silu(gate) * up, the down rows) travel as 64-bit exchange
+//     words carrying the step as a tag; consumers poll the words they need,
+//     so the wait and the data read are one round trip, and Programs 0 and 1
+//     run without grid barriers. Every block keeps the residual stream in
+//     shared memory and adds the exchanged o_proj and down rows itself.
+//   - RMSNorm is recomputed by every block; RoPE and the KV-cache append run
+//     in the QKV epilogue. Each block computes the attention of one KV group
+//     (seven query heads) over the cached rows in its ring, and o_proj is
+//     split along its input over the two groups. Contexts longer than the
+//     ring holds use split-position attention between two grid barriers.
+//   - The tail (LM-head top-1 partitions, reduce, embedding feedback) keeps
+//     its grid barriers.
 #include "lrrt/persistent_graph/compiled_scheduler.cuh"
 #include "lrrt/persistent_graph/device_scheduler.cuh"
 #include "lrrt/qwen/resident_layout.hpp"
@@ -533,12 +538,10 @@ using namespace qd::resident;
 constexpr uint32_t kMaxAttentionChunks = 128;
 constexpr uint32_t kKvTile = 32;                       // positions per attention tile
 constexpr uint32_t kKeyStride = qd::kHeadSize + 1u;    // padded K rows (bank-conflict free)
-constexpr uint32_t kLmScratch = 1024;                  // LM-head candidates (input floats)
-// Up to this many KV positions every block computes the attention output of
-// all 14 query heads itself, inside the o_proj stage, so the attention stage
-// needs no grid barrier; longer contexts use the split path.
-constexpr uint32_t kLocalAttentionLimit = 192;
-constexpr uint32_t kLocalAttentionBatch = 4;           // positions per warp per load batch
+// Up to kLocalAttentionLimit KV positions every block computes the attention
+// output of its KV group's seven query heads itself from shared memory, inside
+// the o_proj stage, so the attention stage needs no grid barrier; longer
+// contexts use the split path.
 enum Matrix : uint32_t { kMq, kMk, kMv, kMo, kMgate, kMup, kMdown };
 
 // Block-uniform launch facts, written once by thread 0 in `begin` and kept in
@@ -550,14 +553,20 @@ struct QwenConfig {
   FusedShared *shared;
   const qd::Context *contexts;
   qd::Workspace *workspace;
+  uint64_t *exchange;       // workspace exchange words
+  const unsigned char *kv_maps; // [layer][K, V] tensor maps of the KV caches
   const float *lm_head;
   uint32_t worker, workers, layers, vocab, lm_units;
   uint32_t limit_ms;
+  uint32_t group;           // KV group whose attention this block computes
+  bool group_writer;        // first block of its group: publishes the attention output
   UnitRanges ranges;
   StreamMap map;
   uint64_t policy;
   sg::Stage lm_stage;
   qd::StageProfile *unit_trace; // stage-profile runs: block 0 unit timeline
+  qd::StageProfileEntry *event_trace; // stage-profile runs: every block's exchange waits
+  uint32_t event_capacity;            // entries of event_trace this trace may use
   // Token position / KV length at the launch's first decode step and the
   // token index (step / layers, adjusted) they belong to: the fused path
   // derives each step's values instead of reading DecodeState, which only
@@ -585,19 +594,23 @@ __device__ __forceinline__ void fetch_layer_context(uint32_t step) {
   }
 }
 
-// The same copy without stalling the issuing threads (cp.async); it must be
-// completed with cp.async.wait_all by those threads before a block sync that
-// precedes the first read.
+// The same copy without stalling the issuing threads (cp.async), issued by
+// the last warp, which is otherwise idle while the MLP norm waits for the
+// o_proj exchange; those threads complete it (cp.async.wait_all) before that
+// norm's block sync, which precedes the first read.
+constexpr uint32_t kContextCopyThread = kThreads - 32u;
 __device__ __forceinline__ void prefetch_layer_context(uint32_t step) {
   constexpr uint32_t kWords = sizeof(qd::Context) / sizeof(uint4);
-  if (threadIdx.x < kWords) {
+  static_assert(kWords <= 32u);
+  const uint32_t word = threadIdx.x - kContextCopyThread;
+  if (threadIdx.x >= kContextCopyThread && word < kWords) {
     const uint4 *source =
         reinterpret_cast<const uint4 *>(block_config.contexts + step % block_config.layers);
     const uint32_t destination =
-        dev::shared_address(reinterpret_cast<uint4 *>(&layer_cache[step & 1u]) + threadIdx.x);
+        dev::shared_address(reinterpret_cast<uint4 *>(&layer_cache[step & 1u]) + word);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n"
                  "cp.async.commit_group;" ::"r"(destination),
-                 "l"(source + threadIdx.x)
+                 "l"(source + word)
                  : "memory");
   }
 }
@@ -610,7 +623,9 @@ __device__ __forceinline__ void wait_prefetched_context() {
 // of a block).
 struct QwenBlock {
   bool fused;
-  bool attention_pending;   // block 0 owes the global query copy of attention
+  bool split_attention;     // this step's attention runs split over blocks
+  bool hidden_exchanged;    // the residual's last update is the down exchange
+  bool failed;              // a wait of this block gave up (block-uniform)
   uint32_t consumed;        // stream sequence number of the next unit to consume
   uint32_t traced_barriers; // stage-profile barrier trace position (thread 0)
   uint32_t program;         // current Program and stage within it
@@ -665,12 +680,15 @@ __device__ __forceinline__ void trace_unit(const QwenBlock &b, uint32_t n, uint6
 }
 
 // Global source ranges of one stream unit (second part empty for
-// single-range units).
+// single-range units). An o_proj unit is `rows` half-row copies of
+// first_bytes each, `stride` floats apart.
 struct UnitSource {
   const float *first;
   const float *second;
   uint32_t first_bytes;
   uint32_t second_bytes;
+  uint32_t rows;
+  uint32_t stride;
 };
 
 __device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
@@ -691,20 +709,27 @@ __device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
     const float *first =
         weight + size_t{(local / 8u) * qd::kHeadSize + (local % 8u) * 4u} * qd::kHiddenSize;
     return {first, first + size_t{qd::kRotarySize} * qd::kHiddenSize, 4u * kRowBytes,
-            4u * kRowBytes};
+            4u * kRowBytes, 1, 0};
   }
-  case kOut:
-    return {w[kMo] + size_t{u} * kSlotRows * qd::kHiddenSize, nullptr, kSlotBytes, 0};
+  case kOut: {
+    // Rows 8v..8v+7 of o_proj, input columns of KV group u / 112 only.
+    const uint32_t group = u / kOGroupUnits;
+    const uint32_t row = (u % kOGroupUnits) * kSlotRows;
+    return {w[kMo] + size_t{row} * qd::kHiddenSize + group * kGroupColumns, nullptr,
+            kHalfRowBytes, 0, kSlotRows, qd::kHiddenSize};
+  }
+  case kKv: // filled by tensor copies in issue_unit
+    return {nullptr, nullptr, 0, 0, 1, 0};
   case kGateUp:
     return {w[kMgate] + size_t{u} * kGuRowsPerUnit * qd::kHiddenSize,
             w[kMup] + size_t{u} * kGuRowsPerUnit * qd::kHiddenSize,
-            kGuRowsPerUnit * kRowBytes, kGuRowsPerUnit * kRowBytes};
+            kGuRowsPerUnit * kRowBytes, kGuRowsPerUnit * kRowBytes, 1, 0};
   case kDown:
-    return {w[kMdown] + size_t{u} * qd::kIntermediateSize, nullptr, kDownRowBytes, 0};
+    return {w[kMdown] + size_t{u} * qd::kIntermediateSize, nullptr, kDownRowBytes, 0, 1, 0};
   default: { // kLmHead
     const uint32_t row = u * kSlotRows;
     return {block_config.lm_head + size_t{row} * qd::kHiddenSize, nullptr,
-            min(kSlotRows, block_config.vocab - row) * kRowBytes, 0};
+            min(kSlotRows, block_config.vocab - row) * kRowBytes, 0, 1, 0};
   }
   }
 }
@@ -716,18 +741,16 @@ __device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
 __shared__ StreamPosition slot_position[kSlots];
 
 // Gate/up refills the down stage postpones: deferred_unit[s] is the sequence
-// number slot s is still to receive (UINT32_MAX: none). Every block releases
-// its down rows at the end of the stage, and issuing all those refills at
-// once puts the whole grid's next-layer gate/up bytes in front of the grid
-// barrier that follows (its release then takes three times as long). Gate/up
-// units are first needed in the next gate/up stage, so they are issued after
-// the next QKV barrier instead (issue_deferred_refills, attention stage).
+// number slot s is still to receive (UINT32_MAX: none). Gate/up units are
+// first needed in the next gate/up stage; issued at the end of the down
+// stage, their bytes would sit in front of the next layer's first exchanges
+// in the memory queues, so they are issued in the attention stage instead
+// (issue_deferred_refills).
 __shared__ uint32_t deferred_unit[kSlots];
 
-// Issues the bulk copies of stream unit `n` into its ring slot (one lane).
-// The slot's previous unit (n - kSlots) has been released by its consumers.
-// (An L2 bulk prefetch of units further ahead was measured slower on B200.)
-__device__ void issue_unit(const QwenBlock &b, uint32_t n) {
+// Issues the copies of stream unit `n` into its ring slot (one lane). The
+// slot's previous unit (n - kSlots) has been released by its consumers.
+__device__ __noinline__ void issue_unit(const QwenBlock &b, uint32_t n) {
   FusedShared *s = block_config.shared;
   const uint32_t slot = n % kSlots;
   const StreamPosition position = slot_position[slot];
@@ -745,9 +768,35 @@ __device__ void issue_unit(const QwenBlock &b, uint32_t n) {
   slot_position[slot] = next;
   s->unit_tag[slot] = make_tag(c.kind, c.layer, c.unit);
   *reinterpret_cast<volatile uint32_t *>(&s->sequence[slot]) = n;
-  dev::mbarrier_arrive_expect_tx(&s->full[slot], src.first_bytes + src.second_bytes);
+  if (c.kind == kKv) {
+    // Cached rows 56j..56j+55 of this block's KV group, for the token this
+    // layer's unit belongs to (one per stream cycle): K then V, each as two
+    // 32-column boxes. Units past the token's cached positions, and every
+    // unit of a step whose attention runs split, carry no bytes.
+    const uint32_t cached = block_config.base_position + position.cycle;
+    const bool load = cached + 1u <= kLocalAttentionLimit && c.unit * kKvUnitPositions < cached;
+    dev::mbarrier_arrive_expect_tx(&s->full[slot], load ? kSlotBytes : 0u);
+    if (load) {
+      const unsigned char *maps = block_config.kv_maps + size_t{c.layer} * 2u * qd::kTensorMapBytes;
+      const uint32_t x = block_config.group * qd::kHeadSize;
+      const uint32_t y = c.unit * kKvUnitPositions;
+      constexpr uint32_t kBox = kSlotBytes / 4u; // 32 columns x 56 rows
+#pragma unroll
+      for (uint32_t box = 0; box < 4; ++box) {
+        dev::tensor_load_2d(destination + box * kBox, maps + (box >> 1) * qd::kTensorMapBytes,
+                            x + 32u * (box & 1u), y, &s->full[slot]);
+      }
+    }
+    return;
+  }
+  dev::mbarrier_arrive_expect_tx(&s->full[slot],
+                                 src.rows * src.first_bytes + src.second_bytes);
   dev::bulk_copy_to_shared(destination, src.first, src.first_bytes, &s->full[slot],
                            block_config.policy);
+  for (uint32_t r = 1; r < src.rows; ++r) {
+    dev::bulk_copy_to_shared(destination + r * src.first_bytes, src.first + r * src.stride,
+                             src.first_bytes, &s->full[slot], block_config.policy);
+  }
   if (src.second_bytes != 0) {
     dev::bulk_copy_to_shared(destination + src.first_bytes, src.second, src.second_bytes,
                              &s->full[slot], block_config.policy);
@@ -819,68 +868,181 @@ __device__ const float *wait_unit(const QwenBlock &b, sg::State *state, uint32_t
   return reinterpret_cast<const float *>(s->ring + size_t{slot} * kSlotBytes);
 }
 
-// Lane 0 of the warp that consumed unit `n` (each unit has exactly one
-// consumer warp) refills its slot with unit n + kSlots. The warp's shuffles of
-// the unit's sums have completed every lane's reads of the slot, so the copy
-// may overwrite it: no fence is needed (a CTA fence here waits for the lane's
-// earlier global stores, about a microsecond while the weight stream runs).
+// A lane of the warp that consumed unit `n` last (each unit's consumers are
+// done reading the slot: the warp's shuffles of the unit's sums, or a block
+// sync, completed every read) refills the slot with unit n + kSlots. No
+// fence is needed before the copy overwrites the slot (a CTA fence here
+// waits for the lane's earlier global stores, about a microsecond while the
+// weight stream runs).
 __device__ __forceinline__ void release_unit(const QwenBlock &b, uint32_t n) {
   if (!block_config.stream_empty) {
     issue_unit(b, n + kSlots);
   }
 }
 
-// Block-wide RMSNorm of the hidden vector into shared input (every block
-// computes the same values in the same order).
-__device__ void fused_rmsnorm(QwenBlock &b, qd::Context *c, const float *weight,
-                              float epsilon, float *global_copy) {
+// ------------------------------------------------------------ exchanges --
+
+__device__ __forceinline__ uint64_t *exchange_words(uint32_t offset, uint32_t words,
+                                                    uint32_t step) {
+  return block_config.exchange + offset + (step & 1u) * words;
+}
+
+// One thread: waits until every word of the pairs selected by `mask` (pair i
+// is the two words at address(i), 16-byte aligned) carries `tag`, and returns
+// pair i's values in out[2i], out[2i + 1]. All pending pairs are loaded before
+// any is checked, so one round trip serves them all. False when the run
+// failed elsewhere or the wait limit passed (the run is then failed).
+template <uint32_t kPairs, typename Address>
+__device__ bool exchange_wait(sg::State *state, uint32_t tag, uint32_t mask, Address address,
+                              float (&out)[2 * kPairs]) {
+  uint32_t pending = mask;
+  uint32_t polls = 0;
+  uint64_t deadline_ns = 0;
+  while (pending != 0) {
+    uint64_t words[2 * kPairs];
+#pragma unroll
+    for (uint32_t i = 0; i < kPairs; ++i) {
+      words[2 * i] = words[2 * i + 1] = 0;
+      if ((pending >> i) & 1u) {
+        dev::exchange_load2(address(i), words[2 * i], words[2 * i + 1]);
+      }
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < kPairs; ++i) {
+      if (((pending >> i) & 1u) && dev::exchange_tag(words[2 * i]) == tag &&
+          dev::exchange_tag(words[2 * i + 1]) == tag) {
+        out[2 * i] = dev::exchange_value(words[2 * i]);
+        out[2 * i + 1] = dev::exchange_value(words[2 * i + 1]);
+        pending &= ~(1u << i);
+      }
+    }
+    if (pending != 0 && (++polls & 15u) == 0u) {
+      const uint64_t now = dev::global_timer_ns();
+      if (deadline_ns == 0) {
+        deadline_ns = now + uint64_t{block_config.limit_ms} * 1000000ull;
+      } else if (now > deadline_ns) {
+        dev::detail::fail(state, sg::kErrorWaitTimeout);
+        return false;
+      }
+      if (dev::detail::load_status(state) != static_cast<uint32_t>(sg::Status::running)) {
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Stage-profile runs: thread 0 records (start, now) of an exchange wait of
+// this block at entries[event * workers + worker].
+__device__ __forceinline__ void trace_event(QwenBlock &b, uint64_t start_ns) {
+  qd::StageProfileEntry *entries = block_config.event_trace;
+  if (entries == nullptr) {
+    return;
+  }
+  if (threadIdx.x == 0) {
+    const uint64_t now = dev::global_timer_ns();
+    const uint64_t index = uint64_t{b.traced_barriers} * block_config.workers + block_config.worker;
+    if (index < block_config.event_capacity) {
+      entries[index] = {start_ns, now};
+    }
+  }
+  ++b.traced_barriers;
+}
+
+// Stage-profile runs: a point in this block's timeline, (marker id, now).
+// Ids: 20 + opcode at a stage's entry; at a stage's end 1 attention norm,
+// 2 QKV, 3 local attention, 4 o_proj, 5 MLP norm, 6 gate/up, 7 down,
+// 8 final norm, 9 LM head, 10 embedding feedback. Exchange waits record
+// (start, end) in the same sequence.
+__device__ __forceinline__ void trace_mark(QwenBlock &b, uint32_t id) {
+  if (block_config.event_trace == nullptr) {
+    return;
+  }
+  __syncthreads();
+  trace_event(b, id);
+}
+
+__device__ __forceinline__ uint64_t trace_start() {
+  return block_config.event_trace != nullptr ? dev::global_timer_ns() : 0;
+}
+
+// Where a Program's first stage takes the residual from.
+enum class HiddenSource : uint32_t {
+  global,   // launch start, or after the tail (the next token's embedding row)
+  down,     // after Program 1: hidden += down projection of step - 1
+  attention // Program 1: hidden += o_proj of this step, both KV groups
+};
+
+// Brings this block's copy of the residual stream up to date and RMS-
+// normalises it into shared input (every block computes the same values in
+// the same order). Thread t < 224 owns hidden[4t, 4t + 4).
+__device__ void fused_norm(QwenBlock &b, sg::State *state, const qd::Context *c,
+                           HiddenSource source, const float *weight, float epsilon,
+                           float *global_copy) {
   FusedShared *s = block_config.shared;
   constexpr uint32_t kVectors = qd::kHiddenSize / 4u; // 224
-  if (b.attention_pending) {
-    // Block 0 publishes the attention output it computed in the o_proj stage
-    // now that every block has finished reading the query vectors.
-    if (threadIdx.x < kVectors) {
-      reinterpret_cast<float4 *>(c->query)[threadIdx.x] =
-          reinterpret_cast<const float4 *>(s->input)[threadIdx.x];
-    }
-    b.attention_pending = false;
-    __syncthreads();
-  }
+  const uint32_t t = threadIdx.x;
   float4 h = make_float4(0.f, 0.f, 0.f, 0.f);
   float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (threadIdx.x < kVectors) {
-    h = dev::load_cg4(c->hidden + 4u * threadIdx.x);
-    w = __ldg(reinterpret_cast<const float4 *>(weight) + threadIdx.x); // in flight with h
+  bool ok = true;
+  const uint64_t started = trace_start();
+  if (t < kVectors) {
+    w = __ldg(reinterpret_cast<const float4 *>(weight) + t); // in flight with the wait
+    if (source == HiddenSource::global) {
+      h = dev::load_cg4(c->hidden + 4u * t);
+    } else if (source == HiddenSource::down) {
+      h = reinterpret_cast<const float4 *>(s->hidden)[t];
+      const uint32_t step = b.step - 1u;
+      const uint64_t *words =
+          exchange_words(qd::kExchangeDown, qd::kHiddenSize, step) + 4u * t;
+      float v[4];
+      ok = exchange_wait<2>(state, step + 1u, 3u, [&](uint32_t i) { return words + 2u * i; },
+                            v);
+      h = make_float4(h.x + v[0], h.y + v[1], h.z + v[2], h.w + v[3]);
+    } else {
+      h = reinterpret_cast<const float4 *>(s->hidden)[t];
+      const uint64_t *words =
+          exchange_words(qd::kExchangeOut, qd::kKvHeads * qd::kHiddenSize, b.step) + 4u * t;
+      float v[8];
+      ok = exchange_wait<4>(state, b.step + 1u, 15u,
+                            [&](uint32_t i) {
+                              return words + (i >> 1) * qd::kHiddenSize + 2u * (i & 1u);
+                            },
+                            v);
+      h = make_float4((h.x + v[0]) + v[4], (h.y + v[1]) + v[5], (h.z + v[2]) + v[6],
+                      (h.w + v[3]) + v[7]);
+    }
+    reinterpret_cast<float4 *>(s->hidden)[t] = h;
+  }
+  if (source == HiddenSource::attention && threadIdx.x >= kContextCopyThread) {
+    wait_prefetched_context(); // the next step's Context (Program 1's begin)
   }
   float sum = fmaf(h.x, h.x, fmaf(h.y, h.y, fmaf(h.z, h.z, h.w * h.w)));
   sum = warp_sum(sum);
   if ((threadIdx.x & 31u) == 0) {
     s->reduce[threadIdx.x >> 5u] = sum;
   }
-  __syncthreads();
+  if (__syncthreads_or(ok ? 0 : 1) != 0) {
+    b.failed = true;
+    return;
+  }
+  if (source != HiddenSource::global) {
+    trace_event(b, started);
+  }
   float total = 0.0f;
 #pragma unroll
-  for (uint32_t w = 0; w < kWarps; ++w) {
-    total += s->reduce[w];
+  for (uint32_t w8 = 0; w8 < kWarps; ++w8) {
+    total += s->reduce[w8];
   }
   const float inverse_rms =
       1.0f / sqrtf(total / static_cast<float>(qd::kHiddenSize) + epsilon);
-  if (threadIdx.x < kVectors) {
+  if (t < kVectors) {
     const float4 x = make_float4(h.x * inverse_rms * w.x, h.y * inverse_rms * w.y,
                                  h.z * inverse_rms * w.z, h.w * inverse_rms * w.w);
-    reinterpret_cast<float4 *>(s->input)[threadIdx.x] = x;
+    reinterpret_cast<float4 *>(s->input)[t] = x;
     if (global_copy != nullptr && block_config.worker == 0) {
-      reinterpret_cast<float4 *>(global_copy)[threadIdx.x] = x;
+      reinterpret_cast<float4 *>(global_copy)[t] = x;
     }
-  }
-  __syncthreads();
-}
-
-// Copies a vector written by other blocks into shared input.
-__device__ void fused_load_input(QwenBlock &b, const float *source, uint32_t count) {
-  float4 *destination = reinterpret_cast<float4 *>(block_config.shared->input);
-  for (uint32_t i = threadIdx.x; i < count / 4u; i += kThreads) {
-    destination[i] = dev::load_cg4(source + 4u * i);
   }
   __syncthreads();
 }
@@ -1064,6 +1226,9 @@ __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32
   const uint32_t position = b.position;
   const size_t rope = size_t{position} * qd::kRotarySize;
   const size_t cache_row = size_t{position} * qd::kKvSize;
+  uint64_t *words = exchange_words(qd::kExchangeQkv, qd::kPackedQkvSize, b.step);
+  const uint32_t tag = b.step + 1u;
+  const bool split = b.split_attention;
   consume_units(
       b, state, kQkv, layer,
       [&](uint32_t u, uint32_t row, float value, bool valid, float4 operand) {
@@ -1082,13 +1247,24 @@ __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32
           r0 = x0 * operand.z - x1 * operand.w;
           r1 = x1 * operand.z + x0 * operand.w;
         }
-        float *out = r.which == 0 ? c->query : (r.which == 1 ? c->key : c->value);
-        out[r.first] = r0;
-        out[r.second] = r1;
+        // The exchange words first (the other blocks wait for them), then
+        // the global copies: K/V rows, the cache rows of this position, and
+        // the query when the attention runs split (it reads it from there).
+        uint64_t *packed = words + (r.which == 0 ? 0u
+                                    : r.which == 1 ? qd::kQuerySize
+                                                   : qd::kQuerySize + qd::kKvSize);
+        dev::exchange_store(packed + r.first, r0, tag);
+        dev::exchange_store(packed + r.second, r1, tag);
         if (r.which != 0) {
+          float *out = r.which == 1 ? c->key : c->value;
+          out[r.first] = r0;
+          out[r.second] = r1;
           float *cache = (r.which == 1 ? c->key_cache : c->value_cache) + cache_row;
           cache[r.first] = r0;
           cache[r.second] = r1;
+        } else if (split) {
+          c->query[r.first] = r0;
+          c->query[r.second] = r1;
         }
       },
       [&](uint32_t u, uint32_t row) {
@@ -1102,48 +1278,106 @@ __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32
       });
 }
 
-__device__ void local_attention(QwenBlock &b, const qd::Context *c, uint32_t positions);
+__device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Context *c,
+                                uint32_t layer);
 
 __device__ __forceinline__ bool use_local_attention(uint32_t positions) {
   return positions <= kLocalAttentionLimit;
 }
 
+// o_proj split along its input over the two KV groups: this block's units
+// are rows 8v..8v+7 restricted to its group's 448 columns, each row computed
+// by one warp against the group's attention output in shared input[0, 448).
+// The two groups' partial rows go to the out exchange; every block adds both
+// to its residual at the start of Program 1.
 __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32_t layer) {
-  const uint32_t positions = b.kv_length + 1u;
-  if (use_local_attention(positions)) {
-    local_attention(b, c, positions);
-    b.attention_pending = block_config.worker == 0;
+  FusedShared *s = block_config.shared;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = threadIdx.x >> 5u;
+  const uint32_t group = block_config.group;
+  if (!b.split_attention) {
+    local_attention(b, state, c, layer);
+    if (b.failed) {
+      return;
+    }
+    trace_mark(b, 3);
   } else {
-    fused_load_input(b, c->query, qd::kQuerySize);
+    // The split attention wrote the output over the query (grid barrier since).
+    const float *source = c->query + group * kGroupColumns;
+    for (uint32_t i = threadIdx.x; i < kGroupColumns / 4u; i += kThreads) {
+      reinterpret_cast<float4 *>(s->input)[i] = dev::load_cg4(source + 4u * i);
+    }
+    __syncthreads();
   }
-  consume_units(
-      b, state, kOut, layer,
-      [&](uint32_t u, uint32_t row, float value, bool valid, float4 residual) {
-        if (valid && (threadIdx.x & 3u) == 0u) {
-          c->hidden[u * kSlotRows + row] = residual.x + value;
-        }
-      },
-      [&](uint32_t u, uint32_t row) {
-        return make_float4(dev::load_cg(c->hidden + u * kSlotRows + row), 0.f, 0.f, 0.f);
-      });
+  constexpr uint32_t kVectors = kGroupColumns / 4u; // 112 float4 per half row
+  float4 x[4];
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    const uint32_t v = lane + 32u * j;
+    x[j] = v < kVectors ? reinterpret_cast<const float4 *>(s->input)[v]
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const UnitRange range = block_config.ranges.of[kOut];
+  const uint32_t tag = b.step + 1u;
+  uint64_t *words = exchange_words(qd::kExchangeOut, qd::kKvHeads * qd::kHiddenSize, b.step);
+  bool ok = true;
+  for (uint32_t i = 0; ok && i < range.end - range.begin; ++i) {
+    const uint32_t n = b.consumed + i;
+    const uint32_t u = range.begin + i;
+    const float *slot = wait_unit(b, state, n, make_tag(kOut, layer, u));
+    if (slot == nullptr) {
+      ok = false;
+      break;
+    }
+    const float4 *row = reinterpret_cast<const float4 *>(slot + warp * kGroupColumns);
+    float a = 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      const uint32_t v = lane + 32u * j;
+      if (v < kVectors) {
+        const float4 w = row[v];
+        a = fmaf(w.x, x[j].x, a);
+        a = fmaf(w.y, x[j].y, a);
+        a = fmaf(w.z, x[j].z, a);
+        a = fmaf(w.w, x[j].w, a);
+      }
+    }
+    a = warp_all_sum(a); // completes the warp's reads of the slot
+    if (lane == 0) {
+      const uint32_t out_row = (u % kOGroupUnits) * kSlotRows + warp;
+      dev::exchange_store(words + (u / kOGroupUnits) * qd::kHiddenSize + out_row, a, tag);
+      // The unit's eighth warp refills the slot.
+      if ((atomicAdd(&s->rows_done[n % kSlots], 1u) & (kWarps - 1u)) == kWarps - 1u) {
+        release_unit(b, n);
+      }
+    }
+  }
+  b.consumed += range.end - range.begin;
+  if (__syncthreads_or(ok ? 0 : 1) != 0) {
+    b.failed = true;
+  }
 }
 
 __device__ void fused_gate_up(QwenBlock &b, sg::State *state, qd::Context *c,
                               uint32_t layer) {
   // Rows 0-3 of a unit are gate rows 4u..4u+3, rows 4-7 the matching up rows.
+  uint64_t *words = exchange_words(qd::kExchangeAct, qd::kIntermediateSize, b.step);
+  const uint32_t tag = b.step + 1u;
   consume_units(b, state, kGateUp, layer,
                 [&](uint32_t u, uint32_t row, float value, bool valid, float4) {
                   const float up = __shfl_xor_sync(kFullMask, value, 16);
                   if (row < 4u && valid && (threadIdx.x & 3u) == 0u) {
-                    c->activated[u * kGuRowsPerUnit + row] = silu_times(value, up);
+                    const float act = silu_times(value, up);
+                    dev::exchange_store(words + u * kGuRowsPerUnit + row, act, tag);
+                    c->activated[u * kGuRowsPerUnit + row] = act;
                   }
                 });
 }
 
 // Down projection: one 4864-float row per unit, every row computed by all
 // warps together. Warp w owns the float4 columns lane + 32k for k = w, w + 8,
-// ... (five or four per lane) and loads that slice of the activated vector
-// straight into registers. For a batch of up to kSlots rows, warp r waits for
+// ... (five or four per lane) and takes that slice of the activated vector
+// straight from the act exchange into registers. For a batch of up to kSlots rows, warp r waits for
 // row r (the waits overlap), a block sync publishes the landed rows, every
 // warp accumulates its columns of all rows, reduce_rows8 sums lanes, and
 // lane 0 of warp r adds the eight warps' partials of row r in warp order,
@@ -1158,20 +1392,41 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
   const uint32_t row = (lane >> 2u) & 7u;
   FusedShared *shared = block_config.shared;
   float4 x[kMine];
+  {
+    const uint64_t started = trace_start();
+    const uint64_t *act = exchange_words(qd::kExchangeAct, qd::kIntermediateSize, b.step);
+    uint32_t mask = 0;
 #pragma unroll
-  for (uint32_t m = 0; m < kMine; ++m) {
-    const uint32_t k = warp + kWarps * m;
-    x[m] = k < kChunks ? dev::load_cg4(c->activated + 4u * (lane + 32u * k))
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t m = 0; m < kMine; ++m) {
+      mask |= warp + kWarps * m < kChunks ? 3u << (2u * m) : 0u;
+    }
+    float v[4 * kMine];
+    const bool ok = exchange_wait<2 * kMine>(
+        state, b.step + 1u, mask,
+        [&](uint32_t i) { return act + 4u * (lane + 32u * (warp + kWarps * (i >> 1))) + 2u * (i & 1u); },
+        v);
+#pragma unroll
+    for (uint32_t m = 0; m < kMine; ++m) {
+      x[m] = warp + kWarps * m < kChunks
+                 ? make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3])
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (__syncthreads_or(ok ? 0 : 1) != 0) {
+      b.failed = true;
+      b.consumed += block_config.ranges.of[kDown].end - block_config.ranges.of[kDown].begin;
+      return;
+    }
+    trace_event(b, started);
   }
   float *partial = shared->reduce; // [kWarps][kSlots]
   const UnitRange range = block_config.ranges.of[kDown];
   const uint32_t units = range.end - range.begin;
+  uint64_t *words = exchange_words(qd::kExchangeDown, qd::kHiddenSize, b.step);
   for (uint32_t batch = 0; batch < units; batch += kSlots) {
     const uint32_t count = min(kSlots, units - batch);
     const bool finisher = lane == 0 && warp < count; // finishes row `warp` of the batch
     const uint32_t mine = batch + warp;
-    const float residual = finisher ? dev::load_cg(c->hidden + range.begin + mine) : 0.0f;
+    const float residual = finisher ? shared->hidden[range.begin + mine] : 0.0f;
     bool ok = true;
     if (warp < count) {
       const uint32_t n = b.consumed + batch + warp;
@@ -1227,8 +1482,9 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
         sum += partial[w * kSlots + warp];
       }
       const uint32_t u = range.begin + mine;
+      dev::exchange_store(words + u, sum, b.step + 1u);
       c->projected[u] = sum;
-      c->hidden[u] = residual + sum;
+      c->hidden[u] = residual + sum; // the residual for a launch that resumes here
       const uint32_t n = b.consumed + mine;
       if (!block_config.stream_empty &&
           position_cursor(block_config.map, slot_position[n % kSlots]).kind == kGateUp) {
@@ -1248,7 +1504,7 @@ __device__ void fused_down(QwenBlock &b, sg::State *state, qd::Context *c, uint3
 // finish combines all chunks into the attention output (written over query).
 __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
                                uint32_t chunk, uint32_t chunks, uint32_t positions,
-                               uint32_t item) {
+                               uint32_t item, float *scratch) {
   FusedShared *s = block_config.shared;
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
@@ -1257,7 +1513,7 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
   const uint32_t end = min(positions, begin + per_chunk);
   constexpr uint32_t kHeads = qd::kQueriesPerKvHead;
   constexpr uint32_t kOutputs = kHeads * qd::kHeadSize; // 448
-  float *keys = s->input;                                // [32][65]
+  float *keys = scratch;                                 // [32][65]
   float *values = keys + kKvTile * kKeyStride;           // [32][64]
   float *scores = values + kKvTile * qd::kHeadSize;      // [7][32]
   float *query = scores + kHeads * kKvTile;              // [7][64]
@@ -1377,7 +1633,7 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
   // Last arrival: weights w_j = exp(m_j - M) / sum_j l_j exp(m_j - M) per head.
   const float *group_partials = block_config.workspace->attention_partials +
                                 size_t{group * chunks} * kHeads * qd::kAttentionPartialStride;
-  float *maxima = s->input;                                  // [chunks][7]
+  float *maxima = scratch;                                   // [chunks][7]
   float *sums = maxima + kMaxAttentionChunks * kHeads;       // [chunks][7]
   float *weights = sums + kMaxAttentionChunks * kHeads;      // [7][chunks]
   {
@@ -1473,132 +1729,211 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
   __syncthreads();
 }
 
-// Attention output of all 14 query heads computed by this block alone into
-// shared input[0..895] ([head][dim]), for short contexts. Lane l of a warp
-// owns dims 4*(l%16)..+3 of kv head l/16 and that head's seven query heads;
-// warp w takes positions w, w+8, ...; each warp keeps an online softmax per
-// head, and the eight warps' states are merged pairwise at the end.
-__device__ void local_attention(QwenBlock &b, const qd::Context *c, uint32_t positions) {
+// Local attention (contexts up to kLocalAttentionLimit positions): this block
+// computes the attention output of its KV group's seven query heads from
+// shared memory. The cached K/V rows of the earlier positions arrive as the
+// layer's three KV ring units (56 positions each: K then V, each as two
+// 32-column boxes of 56 rows, 128-byte rows swizzled by XOR of the 16-byte
+// chunk index with row % 8); the current position's K/V and the group's
+// queries come from the qkv exchange. The output, [head][dim] of the group,
+// goes to input[0, 448).
+__device__ __forceinline__ const float4 *kv_chunk(const unsigned char *unit, uint32_t row,
+                                                   uint32_t chunk, uint32_t part) {
+  // part 0: K, 1: V; chunk = float4 index 0..15 of the 64-float row.
+  constexpr uint32_t kBox = kSlotBytes / 4u;
+  return reinterpret_cast<const float4 *>(unit + (2u * part + (chunk >> 3)) * kBox + row * 128u +
+                                          (((chunk & 7u) ^ (row & 7u)) << 4));
+}
+
+__device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Context *c,
+                                uint32_t layer) {
   FusedShared *s = block_config.shared;
+  float *work = s->work;
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
-  const uint32_t group = lane >> 4u;
-  const uint32_t dim = 4u * (lane & 15u);
+  const uint32_t group = block_config.group;
+  const uint32_t positions = b.kv_length + 1u;
+  const uint32_t current = b.kv_length;
   constexpr uint32_t kHeads = qd::kQueriesPerKvHead;
-  float4 q[kHeads], acc[kHeads];
-  float maximum[kHeads], total[kHeads];
-#pragma unroll
-  for (uint32_t j = 0; j < kHeads; ++j) {
-    q[j] = dev::load_cg4(c->query + (group * kHeads + j) * qd::kHeadSize + dim);
-    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    maximum[j] = -INFINITY;
-    total[j] = 0.0f;
+  // Group entries of the qkv exchange: q [448], k [64], v [64]; thread t < 144
+  // takes entries 4t..4t+3 (one region each).
+  bool ok = true;
+  const uint64_t started = trace_start();
+  if (threadIdx.x < (kGroupColumns + 2u * qd::kHeadSize) / 4u) {
+    const uint32_t e = 4u * threadIdx.x;
+    uint32_t index;
+    if (e < kGroupColumns) {
+      index = group * kGroupColumns + e;
+    } else if (e < kGroupColumns + qd::kHeadSize) {
+      index = qd::kQuerySize + group * qd::kHeadSize + (e - kGroupColumns);
+    } else {
+      index = qd::kQuerySize + qd::kKvSize + group * qd::kHeadSize +
+              (e - kGroupColumns - qd::kHeadSize);
+    }
+    // q lands at work[0, 448), current K at work[kLocalCurrent], V after it.
+    float *destination = work + (e < kGroupColumns ? kLocalQuery + e
+                                                   : kLocalCurrent + (e - kGroupColumns));
+    const uint64_t *words =
+        exchange_words(qd::kExchangeQkv, qd::kPackedQkvSize, b.step) + index;
+    float v[4];
+    ok = exchange_wait<2>(state, b.step + 1u, 3u, [&](uint32_t i) { return words + 2u * i; },
+                          v);
+    reinterpret_cast<float4 *>(destination)[0] = make_float4(v[0], v[1], v[2], v[3]);
   }
-  const float *keys = c->key_cache + 4u * lane;
-  const float *values = c->value_cache + 4u * lane;
-  for (uint32_t base = warp; base < positions; base += kWarps * kLocalAttentionBatch) {
-    float4 k4[kLocalAttentionBatch], v4[kLocalAttentionBatch];
+  // The three KV units (every warp waits; an empty unit completes at once).
+  const unsigned char *units[kKvUnits];
 #pragma unroll
-    for (uint32_t i = 0; i < kLocalAttentionBatch; ++i) {
-      const uint32_t p = base + i * kWarps;
-      if (p < positions) {
-        k4[i] = dev::load_cg4(keys + size_t{p} * qd::kKvSize);
-        v4[i] = dev::load_cg4(values + size_t{p} * qd::kKvSize);
+  for (uint32_t j = 0; j < kKvUnits; ++j) {
+    const float *slot = wait_unit(b, state, b.consumed + j, make_tag(kKv, layer, j));
+    ok = ok && slot != nullptr;
+    units[j] = reinterpret_cast<const unsigned char *>(slot);
+  }
+  if (__syncthreads_or(ok ? 0 : 1) != 0) {
+    b.failed = true;
+    return;
+  }
+  trace_event(b, started);
+  // Scores: thread p computes position p for all seven heads (each K chunk
+  // read once; the query chunks are warp-wide broadcasts).
+  if (threadIdx.x < positions) {
+    const uint32_t p = threadIdx.x;
+    const uint32_t u = p / kKvUnitPositions, row = p - u * kKvUnitPositions;
+    const unsigned char *unit = units[u < kKvUnits ? u : 0u];
+    float acc[kHeads];
+#pragma unroll
+    for (uint32_t h = 0; h < kHeads; ++h) {
+      acc[h] = 0.0f;
+    }
+#pragma unroll 4
+    for (uint32_t j = 0; j < qd::kHeadSize / 4u; ++j) {
+      const float4 k = p == current
+                           ? reinterpret_cast<const float4 *>(work + kLocalCurrent)[j]
+                           : *kv_chunk(unit, row, j, 0);
+#pragma unroll
+      for (uint32_t h = 0; h < kHeads; ++h) {
+        const float4 q =
+            reinterpret_cast<const float4 *>(work + kLocalQuery + h * qd::kHeadSize)[j];
+        acc[h] = fmaf(q.x, k.x, fmaf(q.y, k.y, fmaf(q.z, k.z, fmaf(q.w, k.w, acc[h]))));
       }
     }
 #pragma unroll
-    for (uint32_t i = 0; i < kLocalAttentionBatch; ++i) {
-      if (base + i * kWarps >= positions) {
-        break;
-      }
-#pragma unroll
-      for (uint32_t j = 0; j < kHeads; ++j) {
-        float dot = q[j].x * k4[i].x + q[j].y * k4[i].y + q[j].z * k4[i].z + q[j].w * k4[i].w;
-        dot += __shfl_xor_sync(kFullMask, dot, 8);
-        dot += __shfl_xor_sync(kFullMask, dot, 4);
-        dot += __shfl_xor_sync(kFullMask, dot, 2);
-        dot += __shfl_xor_sync(kFullMask, dot, 1);
-        const float score = dot * 0.125f; // 1/sqrt(head_dim)
-        const float next = fmaxf(maximum[j], score);
-        const float alpha = expf(maximum[j] - next);
-        const float e = expf(score - next);
-        total[j] = total[j] * alpha + e;
-        acc[j].x = acc[j].x * alpha + e * v4[i].x;
-        acc[j].y = acc[j].y * alpha + e * v4[i].y;
-        acc[j].z = acc[j].z * alpha + e * v4[i].z;
-        acc[j].w = acc[j].w * alpha + e * v4[i].w;
-        maximum[j] = next;
-      }
+    for (uint32_t h = 0; h < kHeads; ++h) {
+      work[kLocalScores + h * kLocalAttentionLimit + p] = acc[h] * 0.125f; // 1/sqrt(64)
     }
   }
-  // Pairwise merge of the warps' softmax states: half the remaining warps
-  // write theirs, the other half fold them in.
-  float *scratch = s->input + qd::kQuerySize;          // [4][896] accumulators
-  float *scratch_max = scratch + 4u * qd::kQuerySize;  // [4][14]
-  float *scratch_sum = scratch_max + 4u * qd::kAttentionHeads;
-  for (uint32_t active = kWarps / 2u; active >= 1u; active /= 2u) {
-    if (warp >= active && warp < 2u * active) {
-      const uint32_t slot = warp - active;
-#pragma unroll
-      for (uint32_t j = 0; j < kHeads; ++j) {
-        const uint32_t head = group * kHeads + j;
-        reinterpret_cast<float4 *>(scratch + slot * qd::kQuerySize + head * qd::kHeadSize +
-                                   dim)[0] = acc[j];
-        if ((lane & 15u) == 0u) {
-          scratch_max[slot * qd::kAttentionHeads + head] = maximum[j];
-          scratch_sum[slot * qd::kAttentionHeads + head] = total[j];
-        }
-      }
+  static_assert(kLocalAttentionLimit <= kThreads, "one score row per thread");
+  __syncthreads();
+  // Softmax of head h in warp h: exp(score - max), and 1 / sum.
+  if (warp < kHeads) {
+    float *scores = work + kLocalScores + warp * kLocalAttentionLimit;
+    float maximum = -INFINITY;
+    for (uint32_t p = lane; p < positions; p += 32u) {
+      maximum = fmaxf(maximum, scores[p]);
     }
-    __syncthreads();
-    if (warp < active) {
-#pragma unroll
-      for (uint32_t j = 0; j < kHeads; ++j) {
-        const uint32_t head = group * kHeads + j;
-        const float other_max = scratch_max[warp * qd::kAttentionHeads + head];
-        if (other_max == -INFINITY) {
-          continue;
-        }
-        const float other_sum = scratch_sum[warp * qd::kAttentionHeads + head];
-        const float4 other = reinterpret_cast<const float4 *>(
-            scratch + warp * qd::kQuerySize + head * qd::kHeadSize + dim)[0];
-        const float next = fmaxf(maximum[j], other_max);
-        const float mine = maximum[j] == -INFINITY ? 0.0f : expf(maximum[j] - next);
-        const float theirs = expf(other_max - next);
-        total[j] = total[j] * mine + other_sum * theirs;
-        acc[j].x = acc[j].x * mine + other.x * theirs;
-        acc[j].y = acc[j].y * mine + other.y * theirs;
-        acc[j].z = acc[j].z * mine + other.z * theirs;
-        acc[j].w = acc[j].w * mine + other.w * theirs;
-        maximum[j] = next;
-      }
+    maximum = warp_all_max(maximum);
+    float sum = 0.0f;
+    for (uint32_t p = lane; p < positions; p += 32u) {
+      const float e = expf(scores[p] - maximum);
+      scores[p] = e;
+      sum += e;
     }
-    __syncthreads();
+    sum = warp_all_sum(sum);
+    if (lane == 0) {
+      s->reduce[warp] = 1.0f / sum;
+    }
   }
-  if (warp == 0) {
-#pragma unroll
-    for (uint32_t j = 0; j < kHeads; ++j) {
-      const float inverse = 1.0f / total[j];
-      reinterpret_cast<float4 *>(s->input + (group * kHeads + j) * qd::kHeadSize + dim)[0] =
-          make_float4(acc[j].x * inverse, acc[j].y * inverse, acc[j].z * inverse,
-                      acc[j].w * inverse);
+  __syncthreads();
+  // Weighted values: (head, 4 dims) item t % 112 over the even (t < 112) or
+  // odd (112 <= t < 224) rows of each KV unit, then the current position;
+  // the odd half is added through smem.
+  constexpr uint32_t kItems = kGroupColumns / 4u; // 112
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint32_t item = threadIdx.x % kItems, half = threadIdx.x / kItems;
+  const uint32_t h = item / (qd::kHeadSize / 4u), chunk = item % (qd::kHeadSize / 4u);
+  if (half < 2u) {
+    const float *e = work + kLocalScores + h * kLocalAttentionLimit;
+    // V chunk `chunk` of row r: box 2 + chunk / 8, 16-byte column
+    // (chunk % 8) ^ (r % 8) of the 128-byte row.
+    constexpr uint32_t kBox = kSlotBytes / 4u;
+    const uint32_t box = (2u + (chunk >> 3)) * kBox;
+    for (uint32_t u = 0; u * kKvUnitPositions < current; ++u) {
+      const unsigned char *base = units[u] + box;
+      const uint32_t rows = min(kKvUnitPositions, current - u * kKvUnitPositions);
+      const float *weights = e + u * kKvUnitPositions;
+#pragma unroll 2
+      for (uint32_t row = half; row < rows; row += 2u) {
+        const float weight = weights[row];
+        const float4 x = *reinterpret_cast<const float4 *>(base + row * 128u +
+                                                           (((chunk & 7u) ^ (row & 7u)) << 4));
+        acc.x = fmaf(weight, x.x, acc.x);
+        acc.y = fmaf(weight, x.y, acc.y);
+        acc.z = fmaf(weight, x.z, acc.z);
+        acc.w = fmaf(weight, x.w, acc.w);
+      }
+    }
+    if (half == (current & 1u)) { // the current position, in its parity's half
+      const float weight = e[current];
+      const float4 x = reinterpret_cast<const float4 *>(work + kLocalCurrent + qd::kHeadSize)[chunk];
+      acc.x = fmaf(weight, x.x, acc.x);
+      acc.y = fmaf(weight, x.y, acc.y);
+      acc.z = fmaf(weight, x.z, acc.z);
+      acc.w = fmaf(weight, x.w, acc.w);
+    }
+    if (half == 1u) {
+      reinterpret_cast<float4 *>(work + kLocalPartial)[item] = acc;
+    }
+  }
+  __syncthreads(); // also: every thread is done with the KV units
+  if (lane == 0 && warp < kKvUnits) {
+    release_unit(b, b.consumed + warp);
+  }
+  b.consumed += kKvUnits;
+  if (half == 0u) {
+    const float4 other = reinterpret_cast<const float4 *>(work + kLocalPartial)[item];
+    const float inverse = s->reduce[h];
+    const float4 out = make_float4((acc.x + other.x) * inverse, (acc.y + other.y) * inverse,
+                                   (acc.z + other.z) * inverse, (acc.w + other.w) * inverse);
+    reinterpret_cast<float4 *>(s->input)[item] = out;
+    if (block_config.group_writer) {
+      // The reference leaves the attention output in the query buffer.
+      reinterpret_cast<float4 *>(c->query + group * kGroupColumns)[item] = out;
     }
   }
   __syncthreads();
 }
 
-__device__ void fused_attention(QwenBlock &b, qd::Context *c) {
+__device__ void fused_attention(QwenBlock &b, sg::State *state, qd::Context *c,
+                                uint32_t layer) {
   issue_deferred_refills(b); // gate/up units the last down stage postponed
   const uint32_t positions = b.kv_length + 1u;
-  if (use_local_attention(positions)) {
+  if (!b.split_attention) {
     return; // computed per block inside the o_proj stage
+  }
+  // The layer's KV units carry no bytes for a split step; the first one's
+  // slot serves as staging and combine scratch until they are released.
+  bool ok = true;
+  float *scratch = nullptr;
+#pragma unroll
+  for (uint32_t j = 0; j < kKvUnits; ++j) {
+    const float *slot = wait_unit(b, state, b.consumed + j, make_tag(kKv, layer, j));
+    ok = ok && slot != nullptr;
+    scratch = j == 0 ? const_cast<float *>(slot) : scratch;
+  }
+  if (__syncthreads_or(ok ? 0 : 1) != 0) {
+    b.failed = true;
+    return;
   }
   uint32_t chunks = (positions + 15u) / 16u;
   chunks = min(chunks, max(1u, min(block_config.workers / 2u, kMaxAttentionChunks)));
   const uint32_t items = qd::kKvHeads * chunks;
   for (uint32_t item = block_config.worker; item < items; item += block_config.workers) {
-    attention_item(b, c, item / chunks, item % chunks, chunks, positions, item);
+    attention_item(b, c, item / chunks, item % chunks, chunks, positions, item, scratch);
   }
+  __syncthreads();
+  if ((threadIdx.x & 31u) == 0 && (threadIdx.x >> 5u) < kKvUnits) {
+    release_unit(b, b.consumed + (threadIdx.x >> 5u));
+  }
+  b.consumed += kKvUnits;
 }
 
 // LM head: lane 0 of each warp keeps its own best (value, index) per Program
@@ -1609,7 +1944,7 @@ __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &s
   FusedShared *s = block_config.shared;
   const uint32_t warp = threadIdx.x >> 5u;
   const uint32_t task_count = stage.task_count;
-  float *best_values = s->input + kLmScratch;                     // [8][32]
+  float *best_values = s->work;                                   // [8][32]
   uint32_t *best_indices =
       reinterpret_cast<uint32_t *>(best_values + kWarps * qd::kMaximumLmHeadPartitions);
   uint32_t *task_ends = best_indices + kWarps * qd::kMaximumLmHeadPartitions; // [32]
@@ -1709,10 +2044,10 @@ __device__ void fused_reduce_top1(QwenBlock &b, const sg::Stage &stage,
   const sg::Task *lm_tasks = tasks + stage.task_offset;
   qd::TailContext *tail = c->tail;
   const uint32_t slots = block_config.workers + stage.task_count;
-  float *values = s->input;
-  uint32_t *indices = reinterpret_cast<uint32_t *>(s->input + 512);
-  float *partial_values = s->input + 1024;
-  uint32_t *partial_indices = reinterpret_cast<uint32_t *>(s->input + 1024 + 64);
+  float *values = s->work;
+  uint32_t *indices = reinterpret_cast<uint32_t *>(s->work + 512);
+  float *partial_values = s->work + 1024;
+  uint32_t *partial_indices = reinterpret_cast<uint32_t *>(s->work + 1024 + 64);
   for (uint32_t t = threadIdx.x; t < slots; t += kThreads) {
     values[t] = dev::load_cg(block_config.workspace->top1_values + t);
     indices[t] = dev::load_cg(block_config.workspace->top1_indices + t);
@@ -1842,8 +2177,16 @@ __device__ bool fused_possible(const sg::ResidentArgs &args, uint32_t workers) {
   const auto *contexts = static_cast<const qd::Context *>(args.context);
   const qd::TailContext *tail = contexts[0].tail;
   const qd::Workspace *workspace = tail->workspace;
+  // Every block owns at least one down row (so every block publishes to the
+  // exchange that gates the next layer) and each KV group has a block; a
+  // launch never starts between Programs 0 and 1 (runs only stop after
+  // Program 1 or 2), so the residual it starts from is in global memory.
   if (workspace == nullptr || workspace->magic != qd::kWorkspaceMagic ||
-      workspace->worker_capacity < max(workers, 2u) ||
+      workspace->worker_capacity < max(workers, 2u) || workspace->exchange == nullptr ||
+      workspace->kv_maps == nullptr ||
+      (reinterpret_cast<uintptr_t>(workspace->kv_maps) & 63u) != 0 ||
+      !aligned16(workspace->exchange) || workers < 2u || workers > kDownUnits ||
+      sg::phase_program(dev::load_relaxed(&args.state->phase)) == 1u ||
       dev::dynamic_shared_bytes() < kFusedSharedBytes || gridDim.x != workers ||
       contexts[0].layer_count > kMaxFusedLayers || tail->vocab_size >= (1u << 23) ||
       !aligned16(tail->lm_head_weight) || !aligned16(tail->final_norm_weight) ||
@@ -1864,6 +2207,44 @@ __device__ bool fused_possible(const sg::ResidentArgs &args, uint32_t workers) {
   return canonical_table(args, tail->vocab_size);
 }
 
+// Zeroes the exchange words this block publishes (both parities) before the
+// launch returns, so a later launch, whose steps count from zero again,
+// never mistakes them for its own.
+__device__ void clear_exchange() {
+  uint64_t *x = block_config.exchange;
+  const UnitRanges &r = block_config.ranges;
+  const uint32_t qkv = r.of[kQkv].end - r.of[kQkv].begin;   // 8 rows each
+  const uint32_t out = r.of[kOut].end - r.of[kOut].begin;   // 8 rows each
+  const uint32_t gu = r.of[kGateUp].end - r.of[kGateUp].begin; // 4 rows each
+  const uint32_t down = r.of[kDown].end - r.of[kDown].begin;
+  const uint32_t words = 8u * qkv + 8u * out + 4u * gu + down;
+  for (uint32_t i = threadIdx.x; i < 2u * words; i += kThreads) {
+    const uint32_t parity = i / words;
+    uint32_t k = i % words;
+    uint32_t index;
+    if (k < 8u * qkv) {
+      const uint32_t u = r.of[kQkv].begin + k / 8u, row = k % 8u;
+      const QkvRows rows = qkv_rows(u, row % 4u);
+      const uint32_t base = rows.which == 0 ? 0u
+                            : rows.which == 1 ? qd::kQuerySize
+                                              : qd::kQuerySize + qd::kKvSize;
+      index = qd::kExchangeQkv + parity * qd::kPackedQkvSize + base +
+              (row < 4u ? rows.first : rows.second);
+    } else if ((k -= 8u * qkv) < 8u * out) {
+      const uint32_t u = r.of[kOut].begin + k / 8u;
+      index = qd::kExchangeOut + parity * qd::kKvHeads * qd::kHiddenSize +
+              (u / kOGroupUnits) * qd::kHiddenSize + (u % kOGroupUnits) * kSlotRows + k % 8u;
+    } else if ((k -= 8u * out) < 4u * gu) {
+      index = qd::kExchangeAct + parity * qd::kIntermediateSize +
+              (r.of[kGateUp].begin + k / 4u) * kGuRowsPerUnit + k % 4u;
+    } else {
+      k -= 4u * gu;
+      index = qd::kExchangeDown + parity * qd::kHiddenSize + r.of[kDown].begin + k;
+    }
+    x[index] = 0;
+  }
+}
+
 // =============================================================== workloads ==
 
 template <bool kStageProfile> struct QwenWorkloadT {
@@ -1876,6 +2257,17 @@ template <bool kStageProfile> struct QwenWorkloadT {
   __device__ static void trace_barrier(QwenBlock &b, void *opaque, const sg::Stage &,
                                        const sg::Task *, uint64_t arrive_ns,
                                        uint64_t leave_ns) {
+    if (b.fused) { // the entries pointer is cached in shared memory
+      if (block_config.event_trace != nullptr) {
+        const uint64_t index =
+            uint64_t{b.traced_barriers} * block_config.workers + block_config.worker;
+        if (index < block_config.event_capacity) {
+          block_config.event_trace[index] = {arrive_ns, leave_ns};
+        }
+      }
+      ++b.traced_barriers;
+      return;
+    }
     auto *contexts = static_cast<qd::Context *>(opaque);
     qd::StageProfile *profile = contexts[0].tail->stage_profile;
     if (profile != nullptr && profile->entries != nullptr) {
@@ -1901,7 +2293,10 @@ template <bool kStageProfile> struct QwenWorkloadT {
     b = QwenBlock{};
     QwenConfig &k = block_config;
     extern __shared__ __align__(128) unsigned char dynamic_shared[];
-    FusedShared *s = reinterpret_cast<FusedShared *>(dynamic_shared);
+    // The ring's KV units need 1024-byte aligned slots (128-byte swizzle).
+    FusedShared *s = reinterpret_cast<FusedShared *>(
+        (reinterpret_cast<uintptr_t>(dynamic_shared) + kFusedSharedAlign - 1u) &
+        ~uintptr_t{kFusedSharedAlign - 1u});
     if (threadIdx.x == 0) {
       k = QwenConfig{};
       k.worker = blockIdx.x;
@@ -1910,12 +2305,16 @@ template <bool kStageProfile> struct QwenWorkloadT {
       const bool fused = fused_possible(args, k.workers);
       k.contexts = static_cast<const qd::Context *>(args.context);
       k.workspace = k.contexts[0].tail->workspace;
+      k.group = attention_group(k.worker, k.workers);
+      k.group_writer = k.worker == 0 || k.worker == attention_split(k.workers);
       if (blockIdx.x == 0 && k.workspace != nullptr) {
         k.workspace->reserved[0] = fused ? 1u : 2u; // which path ran
       }
       if (fused) { // k.shared stays null on the generic path
         k.shared = s;
         k.lm_head = k.contexts[0].tail->lm_head_weight;
+        k.exchange = k.workspace->exchange;
+        k.kv_maps = static_cast<const unsigned char *>(k.workspace->kv_maps);
         k.layers = k.contexts[0].layer_count;
         k.vocab = k.contexts[0].tail->vocab_size;
         k.lm_units = lm_units_for(k.vocab);
@@ -1925,6 +2324,10 @@ template <bool kStageProfile> struct QwenWorkloadT {
         // The stream starts where the initial Program starts (see make_stream_map).
         k.unit_trace = kStageProfile && k.worker == 0 ? k.contexts[0].tail->stage_profile
                                                      : nullptr;
+        if (kStageProfile && k.contexts[0].tail->stage_profile != nullptr) {
+          k.event_trace = k.contexts[0].tail->stage_profile->entries;
+          k.event_capacity = k.contexts[0].tail->stage_profile->entry_count / 2u;
+        }
         unit_trace_position = 0;
         const uint32_t program = sg::phase_program(dev::load_relaxed(&args.state->phase));
         const uint32_t step = dev::load_relaxed(&args.state->step);
@@ -1964,6 +2367,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
     if (threadIdx.x < kSlots) {
       deferred_unit[threadIdx.x] = UINT32_MAX;
       s->pair_done[threadIdx.x] = 0;
+      s->rows_done[threadIdx.x] = 0;
       s->sequence[threadIdx.x] = UINT32_MAX;
       s->unit_tag[threadIdx.x] = 0;
     }
@@ -1972,6 +2376,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
         dev::mbarrier_init(&s->full[slot], 1);
       }
       dev::mbarrier_init_fence();
+
       if (block_config.worker == 0) {
         // A launch that stopped early may have left arrivals behind. No block
         // reaches attention before passing the first barrier, which block 0
@@ -2009,10 +2414,18 @@ template <bool kStageProfile> struct QwenWorkloadT {
         }
       }
     }
+    clear_exchange();
     __syncthreads();
   }
 
   __device__ static bool local_transitions(const QwenBlock &b) { return b.fused; }
+  __device__ static void barrier_poll(QwenBlock &) {}
+  // Programs 0 and 1 hand their results on through the exchange words; only
+  // the tail (LM-head candidates, the sampled token's embedding, the stop
+  // predicate) ends with a grid barrier.
+  __device__ static bool barrier_at_end(const QwenBlock &b) {
+    return !b.fused || b.program == 2u;
+  }
   __device__ static void program_begin(QwenBlock &b, uint32_t program, uint32_t step) {
     b.program = program;
     b.step = step;
@@ -2021,6 +2434,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
                              block_config.base_token;
       b.position = block_config.base_position + static_cast<uint32_t>(tokens);
       b.kv_length = block_config.base_kv_length + static_cast<uint32_t>(tokens);
+      b.split_attention = !use_local_attention(b.kv_length + 1u);
       if (program == 1) {
         // Completed in this Program's residual_advance stage, read after the
         // block syncs of its final barrier.
@@ -2048,14 +2462,16 @@ template <bool kStageProfile> struct QwenWorkloadT {
     case qd::Opcode::mlp_rmsnorm_f32:
     case qd::Opcode::final_rmsnorm_f32:
     case qd::Opcode::qkv_projection_f32: // RoPE + KV append in its epilogue
-    case qd::Opcode::down_matvec_f32:    // residual add in its epilogue
+    case qd::Opcode::gate_up_silu_f32:   // act exchange
+    case qd::Opcode::down_matvec_f32:    // down exchange
     case qd::Opcode::top1_reduce:        // feedback runs in the same block
       return false;
     case qd::Opcode::rope_kv_cache_f32:
-      return following != qd::Opcode::rope_kv_cache_f32;
+      // Split attention reads the query and this position's K/V from global
+      // memory; local attention takes them from the qkv exchange.
+      return following != qd::Opcode::rope_kv_cache_f32 && b.split_attention;
     case qd::Opcode::grouped_query_attention_f32:
-      // Short contexts: attention runs per block inside the o_proj stage.
-      return !use_local_attention(b.kv_length + 1u);
+      return b.split_attention;
     default:
       return true;
     }
@@ -2068,35 +2484,46 @@ template <bool kStageProfile> struct QwenWorkloadT {
       generic_execute_stage(stage, tasks, state, opaque, worker, workers);
       return;
     }
+    if (b.failed) {
+      return; // a wait gave up; the run ends at the next Program boundary
+    }
+    trace_mark(b, 20u + static_cast<uint32_t>(fused_opcode(b.program, b.stage)));
     const uint32_t layer = b.step % block_config.layers;
     qd::Context *c = &layer_cache[b.step & 1u];
     switch (fused_opcode(b.program, b.stage)) {
     case qd::Opcode::attention_rmsnorm_f32:
-      fused_rmsnorm(b, c, c->attention_norm_weight, block_config.epsilon[0],
-                    c->attention_normalized);
+      fused_norm(b, state, c, b.hidden_exchanged ? HiddenSource::down : HiddenSource::global,
+                 c->attention_norm_weight, block_config.epsilon[0], c->attention_normalized);
+      trace_mark(b, 1);
       return;
     case qd::Opcode::qkv_projection_f32:
       fused_qkv(b, state, c, layer);
+      trace_mark(b, 2);
       return;
     case qd::Opcode::rope_kv_cache_f32:
       return;
     case qd::Opcode::grouped_query_attention_f32:
-      fused_attention(b, c);
+      fused_attention(b, state, c, layer);
       return;
     case qd::Opcode::attention_output_residual_f32:
       fused_out(b, state, c, layer);
+      trace_mark(b, 4);
       return;
     case qd::Opcode::mlp_rmsnorm_f32:
-      fused_rmsnorm(b, c, c->mlp_norm_weight, block_config.epsilon[1], c->mlp_normalized);
+      fused_norm(b, state, c, HiddenSource::attention, c->mlp_norm_weight,
+                 block_config.epsilon[1], c->mlp_normalized);
+      trace_mark(b, 5);
       return;
     case qd::Opcode::gate_up_silu_f32:
       fused_gate_up(b, state, c, layer);
+      trace_mark(b, 6);
       return;
     case qd::Opcode::down_matvec_f32:
       fused_down(b, state, c, layer);
+      trace_mark(b, 7);
       return;
     case qd::Opcode::residual_advance:
-      wait_prefetched_context(); // the next step's Context (program_begin)
+      b.hidden_exchanged = true; // the next Program adds this step's down exchange
       // The residual was added in the down epilogue; what remains is the
       // branch / predicate bookkeeping, which State carries for the host.
       if (worker == 0 && threadIdx.x == 0) {
@@ -2108,11 +2535,14 @@ template <bool kStageProfile> struct QwenWorkloadT {
       }
       return;
     case qd::Opcode::final_rmsnorm_f32:
-      fused_rmsnorm(b, c, c->tail->final_norm_weight, block_config.epsilon[2],
-                    c->tail->final_normalized);
+      fused_norm(b, state, c, b.hidden_exchanged ? HiddenSource::down : HiddenSource::global,
+                 c->tail->final_norm_weight, block_config.epsilon[2],
+                 c->tail->final_normalized);
+      trace_mark(b, 8);
       return;
     case qd::Opcode::lm_head_top1_partition_f32:
       fused_lm_head(b, state, stage, tasks);
+      trace_mark(b, 9);
       return;
     case qd::Opcode::top1_reduce:
       if (worker == 0) {
@@ -2120,9 +2550,13 @@ template <bool kStageProfile> struct QwenWorkloadT {
       }
       return;
     case qd::Opcode::embedding_feedback_f32:
+      // The next Program 0 reads the residual (the new token's embedding row)
+      // from global memory after the tail's final barrier.
+      b.hidden_exchanged = false;
       if (worker == 0) {
         embedding_feedback(c, state);
       }
+      trace_mark(b, 10);
       return;
     }
   }

@@ -8,6 +8,7 @@
 #include "lm_head_top1_static.hpp"
 #include "batch.hpp"
 #include "prefill.hpp"
+#include "prefill_common.hpp"
 
 #include <cuda_runtime_api.h>
 #include "lrrt/qwen/weight_bundle.hpp"
@@ -15,6 +16,7 @@
 #include "lrrt/lrrt.hpp"
 #include "lrrt/persistent_graph.hpp"
 #include "lrrt/qwen/resident_layout.hpp"
+#include "lrrt/qwen/resident_schedule.hpp"
 #include "lrrt/qwen/stateful_graph_context.hpp"
 
 #include <algorithm>
@@ -414,6 +416,41 @@ void build_model(lrq_model_t &m) {
     header.top1_values = reinterpret_cast<float *>(base + at);
     at += (size_t{capacity} + qd::kMaximumLmHeadPartitions) * sizeof(float);
     header.top1_indices = reinterpret_cast<uint32_t *>(base + at);
+    at += (size_t{capacity} + qd::kMaximumLmHeadPartitions) * sizeof(uint32_t);
+    at = (at + 255) / 256 * 256;
+    header.exchange = reinterpret_cast<uint64_t *>(base + at); // zero-filled above
+    at += size_t{qd::kExchangeWords} * sizeof(uint64_t);
+    at = (at + 255) / 256 * 256;
+    // 2-D maps over every layer's K and V cache ([capacity][128] floats): the
+    // fused path loads a KV group's cached rows as boxes of 32 columns x 56
+    // rows with 128-byte swizzle.
+    std::vector<unsigned char> maps(size_t{qd::kWorkspaceMapLayers} * 2u * qd::kTensorMapBytes, 0);
+    for (uint32_t layer = 0; layer < c.layer_count && layer < qd::kWorkspaceMapLayers; ++layer) {
+      for (uint32_t which = 0; which < 2; ++which) {
+        const float *cache = static_cast<const float *>(
+                                 (which == 0 ? m.key_cache : m.value_cache)->data()) +
+                             layer * m.cache_floats();
+        CUtensorMap map{};
+        const cuuint64_t dims[2] = {qd::kKvSize, c.cache_capacity};
+        const cuuint64_t strides[1] = {qd::kKvSize * sizeof(float)};
+        const cuuint32_t box[2] = {32, qd::resident::kKvUnitPositions};
+        const cuuint32_t element_strides[2] = {1, 1};
+        const CUresult status = lrrt::qwen::prefill::detail::encode_tiled()(
+            &map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(cache), dims, strides,
+            box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (status != CUDA_SUCCESS) {
+          throw std::runtime_error("cuTensorMapEncodeTiled failed for a KV cache map (" +
+                                   std::to_string(status) + ")");
+        }
+        std::memcpy(maps.data() + (size_t{layer} * 2u + which) * qd::kTensorMapBytes, &map,
+                    sizeof(map));
+      }
+    }
+    header.kv_maps = base + at;
+    lrrt::check(lr_memcpy(m.workspace->device(), base + at, maps.data(), maps.size(),
+                          LR_MEMCPY_HOST_TO_DEVICE),
+                "lr_memcpy KV cache maps");
     lrrt::copy_to_device(*m.workspace, &header, sizeof(header));
   }
 

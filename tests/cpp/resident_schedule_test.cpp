@@ -25,6 +25,7 @@ static void expect(bool condition, const char *what, uint32_t a = 0, uint32_t b 
 static uint32_t units_of(uint32_t kind, uint32_t vocab) {
   switch (kind) {
   case r::kQkv: return r::kQkvUnits;
+  case r::kKv: return r::kKvUnits;
   case r::kOut: return r::kOUnits;
   case r::kGateUp: return r::kGuUnits;
   case r::kDown: return r::kDownUnits;
@@ -47,6 +48,7 @@ static std::vector<uint32_t> consumer_tags(const r::UnitRanges &ranges, uint32_t
       if (!(first && program == 2)) {
         if (!(first && program == 1 && l == 0)) {
           visit(r::kQkv, l);
+          visit(r::kKv, l);
           visit(r::kOut, l);
         }
         visit(r::kGateUp, l);
@@ -66,6 +68,14 @@ int main() {
     for (uint32_t vocab : vocabs) {
       for (uint32_t kind = r::kQkv; kind <= r::kLmHead; ++kind) {
         const uint32_t units = units_of(kind, vocab);
+        if (kind == r::kKv) {
+          // Not partitioned: every block streams its own KV group's rows.
+          for (uint32_t w = 0; w < workers; ++w) {
+            const r::UnitRange range = r::unit_ranges(w, workers, vocab).of[kind];
+            expect(range.begin == 0 && range.end == r::kKvUnits, "KV units per block", w);
+          }
+          continue;
+        }
         std::vector<uint32_t> owners(units, 0);
         uint32_t next = 0;
         for (uint32_t w = 0; w < workers; ++w) {
@@ -74,7 +84,7 @@ int main() {
                  workers, kind, w);
           for (uint32_t u = range.begin; u < range.end && u < units; ++u) {
             ++owners[u];
-            if (kind != r::kGateUp) {
+            if (kind != r::kGateUp && kind != r::kOut) {
               expect(r::even_owner(u, units, workers) == w, "even_owner inverts",
                      workers, kind, u);
             }
@@ -82,14 +92,25 @@ int main() {
           next = range.end;
         }
         expect(next == units, "ranges cover all units", workers, kind, next);
+        if (kind == r::kOut && workers >= 2) {
+          for (uint32_t w = 0; w < workers; ++w) {
+            const r::UnitRange range = r::unit_ranges(w, workers, vocab).of[kind];
+            const uint32_t group = r::attention_group(w, workers);
+            expect(range.begin == range.end ||
+                       (range.begin / r::kOGroupUnits == group &&
+                        (range.end - 1u) / r::kOGroupUnits == group),
+                   "out units in the block's attention group", workers, w);
+          }
+        }
         expect(std::all_of(owners.begin(), owners.end(), [](uint32_t n) { return n == 1; }),
                "each unit owned once", workers, kind);
       }
     }
     // Per-block decoder bytes stay within two slots of the mean.
     const double mean =
-        (double(r::kQkvUnits + r::kOUnits + r::kGuUnits) * r::kSlotBytes +
-         double(r::kDownUnits) * r::kDownRowBytes) / workers;
+        (double(r::kQkvUnits + r::kGuUnits) * r::kSlotBytes +
+         double(r::kOUnits) * r::kOUnitBytes + double(r::kDownUnits) * r::kDownRowBytes) /
+        workers;
     for (uint32_t w = 0; w < workers; ++w) {
       const r::UnitRanges ranges = r::unit_ranges(w, workers, 4096);
       const double bytes = double(r::fixed_layer_bytes(w, workers)) +
@@ -114,7 +135,7 @@ int main() {
             r::StreamCursor c = r::start_cursor(ranges, layers, program, 0);
             const r::StreamMap map = r::make_stream_map(ranges, layers, program, 0);
             // Ring slots advance their position by the ring depth.
-            const uint32_t depth = 7;
+            const uint32_t depth = r::kSlots;
             std::vector<r::StreamPosition> slots;
             for (uint32_t k = 0; k < depth; ++k) {
               slots.push_back(r::stream_position(map, k));
@@ -130,6 +151,10 @@ int main() {
                 expect(false, "stream order", workers, w, static_cast<uint32_t>(i));
                 break;
               }
+              const r::StreamPosition direct = r::stream_position(map, static_cast<uint32_t>(i));
+              expect(direct.cycle == slot.cycle && direct.layer == slot.layer &&
+                         direct.index == slot.index,
+                     "stream position cycle", workers, w, static_cast<uint32_t>(i));
               r::advance_cursor(ranges, layers, c);
               r::advance_position(map, slot, depth);
             }
