@@ -153,6 +153,8 @@ struct alignas(16) Workspace {
   uint32_t *top1_indices;
   uint64_t *exchange;
   const void *kv_maps;
+  float *logits; // optional [vocab_size]: every LM-head row of the last step (test capture)
+  uint64_t reserved2;
 };
 
 // Bytes of one allocation holding a Workspace header followed by its arrays.
@@ -233,7 +235,7 @@ static_assert(offsetof(TailContext, workspace) == 88);
 static_assert(sizeof(StageProfile) == 240);
 static_assert(sizeof(StageProfileEntry) == 16);
 static_assert(sizeof(DecodeState) == 32);
-static_assert(sizeof(Workspace) == 64);
+static_assert(sizeof(Workspace) == 80);
 static_assert(kAttentionTaskCount <= lrrt::persistent_graph::kMaximumTasks);
 static_assert(kFfnTaskCount <= lrrt::persistent_graph::kMaximumTasks);
 static_assert(kMaximumTailTaskCount <= lrrt::persistent_graph::kMaximumTasks);

@@ -120,7 +120,8 @@ typedef enum lrq_buffer_t {
   LRQ_BUFFER_PARTIAL_INDICES = 12,
   LRQ_BUFFER_OUTPUT_TOKENS = 13,
   LRQ_BUFFER_ROPE_COS = 14,
-  LRQ_BUFFER_ROPE_SIN = 15
+  LRQ_BUFFER_ROPE_SIN = 15,
+  LRQ_BUFFER_LOGITS = 16      /* [vocab] last step's LM-head rows (logit capture) */
 } lrq_buffer_t;
 
 /* The reference task/Program table for the decode graph. Capacities in
@@ -291,6 +292,15 @@ LRRT_API lr_status_t lrq_batch_decode(lrq_batch_t *batch, uint32_t steps, uint32
  * (keys or values may be NULL). */
 LRRT_API lr_status_t lrq_batch_read_cache(lrq_batch_t *batch, uint32_t stream, uint32_t layer,
                                           uint32_t positions, float *keys, float *values);
+/* Cache rows [first_position, first_position + positions) of one stream and
+ * layer from host arrays [positions][128] (keys or values may be NULL), and a
+ * stream's next position and input token: a context set up without running
+ * its prompt (the stream's cache must then hold rows 0..position-1). */
+LRRT_API lr_status_t lrq_batch_write_cache(lrq_batch_t *batch, uint32_t stream, uint32_t layer,
+                                           uint32_t first_position, uint32_t positions,
+                                           const float *keys, const float *values);
+LRRT_API lr_status_t lrq_batch_set_next(lrq_batch_t *batch, uint32_t stream, uint32_t position,
+                                        uint32_t token);
 LRRT_API lr_status_t lrq_batch_position(lrq_batch_t *batch, uint32_t stream,
                                         uint32_t *position);
 
@@ -306,6 +316,13 @@ LRRT_API lr_status_t lrq_generate(lrq_model_t *model, const float *hidden,
 
 LRRT_API lr_status_t lrq_model_read(lrq_model_t *model, uint32_t buffer, uint32_t layer,
                                     void *destination, size_t bytes);
+
+/* Logit capture (a B200 test aid with no reference counterpart): with
+ * enable != 0 the fused path also stores every LM-head row it computes, so
+ * LRQ_BUFFER_LOGITS holds all vocab_size logits of the last decode step
+ * (the reference's resident kernel only keeps per-partition maxima). Off by
+ * default; enabling allocates vocab_size floats. */
+LRRT_API lr_status_t lrq_model_set_logit_capture(lrq_model_t *model, uint32_t enable);
 
 typedef struct lrq_model_info_t {
   uint32_t worker_count, lm_head_partitions, layer_count, vocab_size, cache_capacity,

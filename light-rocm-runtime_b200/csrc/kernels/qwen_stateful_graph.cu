@@ -555,6 +555,7 @@ struct QwenConfig {
   qd::Workspace *workspace;
   uint64_t *exchange;       // workspace exchange words
   const unsigned char *kv_maps; // [layer][K, V] tensor maps of the KV caches
+  float *logits;            // optional: every LM-head row of the step (test capture)
   const float *lm_head;
   uint32_t worker, workers, layers, vocab, lm_units;
   uint32_t limit_ms;
@@ -1979,6 +1980,9 @@ __device__ void fused_lm_head(QwenBlock &b, sg::State *state, const sg::Stage &s
         const uint32_t lane = threadIdx.x & 31u;
         const uint32_t first = u * kSlotRows;
         const uint32_t rows = min(kSlotRows, block_config.vocab - first);
+        if (block_config.logits != nullptr && valid && (lane & 3u) == 0u) {
+          block_config.logits[first + row] = value; // opt-in capture for tests
+        }
         uint32_t task_end = 0;
         if (lane == 0) {
           while (first >= task_ends[task]) {
@@ -2315,6 +2319,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
         k.lm_head = k.contexts[0].tail->lm_head_weight;
         k.exchange = k.workspace->exchange;
         k.kv_maps = static_cast<const unsigned char *>(k.workspace->kv_maps);
+        k.logits = k.workspace->logits;
         k.layers = k.contexts[0].layer_count;
         k.vocab = k.contexts[0].tail->vocab_size;
         k.lm_units = lm_units_for(k.vocab);

@@ -264,6 +264,36 @@ void BatchDecoder::decode(const ModelView &model, uint32_t steps, uint64_t weigh
   }
 }
 
+void BatchDecoder::write_cache(uint32_t stream, uint32_t layer, uint32_t first,
+                               uint32_t positions, const float *keys, const float *values) {
+  if (stream >= streams_ || layer >= layers_ || first > capacity_ ||
+      positions > capacity_ - first) {
+    throw std::invalid_argument("invalid cache write");
+  }
+  const size_t at = ((size_t{stream} * layers_ + layer) * capacity_ + first) * qd::kKvSize;
+  const size_t bytes = sizeof(float) * positions * qd::kKvSize;
+  if (keys != nullptr) {
+    check(lr_memcpy(prefill_.device_.get(), static_cast<float *>(key_cache_->data()) + at, keys,
+                    bytes, LR_MEMCPY_HOST_TO_DEVICE),
+          "lr_memcpy cache");
+  }
+  if (values != nullptr) {
+    check(lr_memcpy(prefill_.device_.get(), static_cast<float *>(value_cache_->data()) + at,
+                    values, bytes, LR_MEMCPY_HOST_TO_DEVICE),
+          "lr_memcpy cache");
+  }
+}
+
+void BatchDecoder::set_next(uint32_t stream, uint32_t position, uint32_t token, uint32_t vocab) {
+  if (stream >= streams_ || position >= capacity_ || token >= vocab) {
+    throw std::invalid_argument("invalid stream position or token");
+  }
+  positions_host_[stream] = position;
+  next_host_[stream] = token;
+  copy_to_device(*positions_, positions_host_.data(), sizeof(uint32_t) * streams_);
+  copy_to_device(*next_tokens_, next_host_.data(), sizeof(uint32_t) * streams_);
+}
+
 void BatchDecoder::read_cache(uint32_t stream, uint32_t layer, uint32_t positions, float *keys,
                               float *values) {
   if (stream >= streams_ || layer >= layers_ || positions > capacity_) {

@@ -44,6 +44,13 @@ public:
   // last_logits (optional, [streams]) receives each stream's last chosen logit.
   void decode(const ModelView &model, uint32_t steps, uint64_t weights_generation,
               uint32_t *tokens, float *last_logits);
+  // Writes cache rows [first, first + positions) of one stream and layer
+  // ([positions][128] each; keys or values may be null).
+  void write_cache(uint32_t stream, uint32_t layer, uint32_t first, uint32_t positions,
+                   const float *keys, const float *values);
+  // Sets a stream's position and the token it takes as input there (its
+  // cache must hold rows 0..position-1).
+  void set_next(uint32_t stream, uint32_t position, uint32_t token, uint32_t vocab);
   // Cache rows [0, positions) of one stream and layer, [positions][128] each.
   void read_cache(uint32_t stream, uint32_t layer, uint32_t positions, float *keys,
                   float *values);

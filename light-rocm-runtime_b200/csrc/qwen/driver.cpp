@@ -297,6 +297,7 @@ struct lrq_model_t {
       scheduler_profile_executor, stage_profile_executor;
 
   std::optional<lrrt::DeviceBuffer> trace; // StageProfileEntry array, optional
+  std::optional<lrrt::DeviceBuffer> logits; // [vocab] logit capture, optional
   // CUDA-graph comparator: one token of matched-step launches, captured once
   // and replayed per token (LRQ_PATH_GRAPH).
   cudaGraphExec_t token_graph = nullptr;
@@ -804,6 +805,11 @@ lrrt::DeviceBuffer &buffer_for(lrq_model_t &m, uint32_t which, uint32_t layer,
   case LRQ_BUFFER_OUTPUT_TOKENS: return whole(*m.output_tokens);
   case LRQ_BUFFER_ROPE_COS: return whole(*m.rope_cos);
   case LRQ_BUFFER_ROPE_SIN: return whole(*m.rope_sin);
+  case LRQ_BUFFER_LOGITS:
+    if (!m.logits) {
+      throw std::invalid_argument("logit capture is not enabled");
+    }
+    return whole(*m.logits);
   case LRQ_BUFFER_KEY_CACHE:
   case LRQ_BUFFER_VALUE_CACHE:
     if (layer >= m.config.layer_count) {
@@ -1339,6 +1345,27 @@ LRRT_API lr_status_t lrq_batch_read_cache(lrq_batch_t *batch, uint32_t stream, u
   });
 }
 
+LRRT_API lr_status_t lrq_batch_write_cache(lrq_batch_t *batch, uint32_t stream, uint32_t layer,
+                                           uint32_t first_position, uint32_t positions,
+                                           const float *keys, const float *values) {
+  return guarded("lrq_batch_write_cache", [&] {
+    if (batch == nullptr) {
+      throw std::invalid_argument("null batch");
+    }
+    batch->decoder->write_cache(stream, layer, first_position, positions, keys, values);
+  });
+}
+
+LRRT_API lr_status_t lrq_batch_set_next(lrq_batch_t *batch, uint32_t stream, uint32_t position,
+                                        uint32_t token) {
+  return guarded("lrq_batch_set_next", [&] {
+    if (batch == nullptr) {
+      throw std::invalid_argument("null batch");
+    }
+    batch->decoder->set_next(stream, position, token, batch->model->config.vocab_size);
+  });
+}
+
 LRRT_API lr_status_t lrq_batch_position(lrq_batch_t *batch, uint32_t stream, uint32_t *position) {
   return guarded("lrq_batch_position", [&] {
     if (batch == nullptr || position == nullptr || stream >= batch->decoder->streams()) {
@@ -1500,6 +1527,25 @@ LRRT_API lr_status_t lrq_model_set_trace(lrq_model_t *model, uint32_t entries) {
       model->trace.emplace(model->device, size_t{entries} * sizeof(qd::StageProfileEntry));
       model->trace_capacity = entries;
     }
+  });
+}
+
+LRRT_API lr_status_t lrq_model_set_logit_capture(lrq_model_t *model, uint32_t enable) {
+  return guarded("lrq_model_set_logit_capture", [&] {
+    if (model == nullptr) {
+      throw std::invalid_argument("null model");
+    }
+    lrrt::check(lr_synchronize(model->device.get()), "lr_synchronize");
+    if (enable != 0 && !model->logits) {
+      model->logits.emplace(model->device, sizeof(float) * size_t{model->config.vocab_size});
+      zero_fill(*model->logits);
+    }
+    float *pointer = enable != 0 ? static_cast<float *>(model->logits->data()) : nullptr;
+    auto *field = static_cast<unsigned char *>(model->workspace->data()) +
+                  offsetof(qd::Workspace, logits);
+    lrrt::check(lr_memcpy(model->device.get(), field, &pointer, sizeof(pointer),
+                          LR_MEMCPY_HOST_TO_DEVICE),
+                "lr_memcpy logit capture");
   });
 }
 

@@ -162,7 +162,18 @@ lr_status_t lm_head_top1(uint32_t device, void *stream, const float *lm_head,
     error = text;
     return LR_ERROR_INVALID_ARGUMENT;
   }
-  cudaError_t status = cudaSetDevice(static_cast<int>(device));
+  // The caller's current device is restored on every return path.
+  int previous = 0;
+  cudaError_t status = cudaGetDevice(&previous);
+  if (status != cudaSuccess) {
+    fail(error, "cudaGetDevice", status);
+    return LR_ERROR_RUNTIME;
+  }
+  struct RestoreDevice {
+    int device;
+    ~RestoreDevice() { cudaSetDevice(device); }
+  } restore{previous};
+  status = cudaSetDevice(static_cast<int>(device));
   if (status != cudaSuccess) {
     fail(error, "cudaSetDevice", status);
     return LR_ERROR_RUNTIME;

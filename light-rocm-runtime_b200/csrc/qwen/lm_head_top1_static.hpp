@@ -5,14 +5,16 @@
 #define LRQ_LM_HEAD_TOP1_STATIC_HPP_
 
 #include "lrrt/lrrt.h"
+#include "lrrt_qwen.h"
 
 #include <cstdint>
 #include <string>
 
 namespace lrq_static {
 
-// Largest grid a call may use: one candidate slot per block.
-constexpr uint32_t kMaxBlocks = 1024;
+// Largest grid a call may use: one candidate slot per block (the limit the
+// public header documents).
+constexpr uint32_t kMaxBlocks = LRQ_STATIC_TOP1_MAX_BLOCKS;
 
 // Runs the kernel on `stream` (a CUstream of the device's primary context),
 // waits for it and copies the token and logit to host memory. On failure

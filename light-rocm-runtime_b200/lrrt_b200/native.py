@@ -192,6 +192,8 @@ DRIVER_FUNCTIONS = {
     "lrq_batch_decode": (u32, [vp, u32, vp, vp]),
     "lrq_batch_read_cache": (u32, [vp, u32, u32, u32, vp, vp]),
     "lrq_batch_position": (u32, [vp, u32, P(u32)]),
+    "lrq_batch_write_cache": (u32, [vp, u32, u32, u32, u32, vp, vp]),
+    "lrq_batch_set_next": (u32, [vp, u32, u32, u32]),
     "lrq_generate": (u32, [vp, vp, u32, u32, u32, u32, P(u32), P(RunState)]),
     "lrq_model_read": (u32, [vp, u32, u32, vp, sz]),
     "lrq_model_info": (u32, [vp, P(ModelInfo)]),
@@ -199,6 +201,7 @@ DRIVER_FUNCTIONS = {
     "lrq_model_run_graph": (u32, [vp, P(Task), u32, P(Program), u32, u32, u32, u32, u32,
                                   u32, u32, P(RunState)]),
     "lrq_model_set_trace": (u32, [vp, u32]),
+    "lrq_model_set_logit_capture": (u32, [vp, u32]),
     "lrq_model_read_trace": (u32, [vp, P(u64), u32]),
     "lrq_last_error": (cp, []),
 }

@@ -49,6 +49,7 @@ BUFFERS = {
     "output_tokens": (13, None, np.uint32),
     "rope_cos": (14, None, np.float32),
     "rope_sin": (15, None, np.float32),
+    "logits": (16, None, np.float32),
 }
 
 STATUS_NAMES = {0: "ready", 1: "running", 2: "complete", 3: "max_steps", 4: "invalid_program"}
@@ -299,6 +300,8 @@ class Model:
                 count = self.info.lm_head_partitions
             elif name == "output_tokens":
                 count = self.config.max_tokens_per_run
+            elif name == "logits":
+                count = self.config.vocab_size
             elif name in ("rope_cos", "rope_sin"):
                 count = self.config.cache_capacity * HEAD_DIM // 2
             else:
@@ -314,6 +317,11 @@ class Model:
         N.check(N.driver().lrq_model_stage_profile(self.handle, ticks, counts),
                 "lrq_model_stage_profile")
         return list(ticks), list(counts)
+
+    def set_logit_capture(self, enable: bool = True) -> None:
+        """Keep every LM-head row of the last decode step (read("logits"))."""
+        N.check(N.driver().lrq_model_set_logit_capture(self.handle, 1 if enable else 0),
+                "lrq_model_set_logit_capture")
 
     def set_trace(self, entries: int) -> None:
         N.check(N.driver().lrq_model_set_trace(self.handle, entries), "lrq_model_set_trace")
@@ -394,6 +402,15 @@ class Batch:
         N.check(N.driver().lrq_batch_decode(self.handle, steps, _ptr(tokens), _ptr(logits)),
                 "lrq_batch_decode")
         return tokens, logits
+
+    def write_cache(self, stream: int, layer: int, first: int, keys, values) -> None:
+        k, v = _f32(keys), _f32(values)
+        N.check(N.driver().lrq_batch_write_cache(self.handle, stream, layer, first, len(k),
+                                                 _ptr(k), _ptr(v)), "lrq_batch_write_cache")
+
+    def set_next(self, stream: int, position: int, token: int) -> None:
+        N.check(N.driver().lrq_batch_set_next(self.handle, stream, position, token),
+                "lrq_batch_set_next")
 
     def read_cache(self, stream: int, layer: int, positions: int):
         keys = np.zeros((positions, 128), np.float32)

@@ -1,17 +1,25 @@
-"""Generates tests/golden/hf_qwen2_decode.npz: greedy decode vectors from
-Hugging Face transformers' Qwen2ForCausalLM (FP32, eager attention), the
+"""Generates the Hugging Face golden fixtures under tests/golden/: decode
+vectors from transformers' Qwen2ForCausalLM (FP32, eager attention), the
 model-level oracle light-rocm-runtime itself uses
 (tools/run_qwen_e2e.py:313-419). transformers is a third-party dependency of
-that tool, not vendored in the reference; the version used is recorded in the
-file.
+that tool, not vendored in the reference; the version used is recorded in
+each file.
 
-The model is the Qwen2.5-0.5B architecture (hidden 896, 14/2 heads, head_dim
-64, intermediate 4864, RMSNorm eps 1e-6, RoPE theta 1e6, tied embeddings)
-with a reduced depth and vocabulary so the fixture stays small; weights come
-from lrrt_b200.synthetic.model(SEED, LAYERS, VOCAB) and are regenerated
-bit-identically by the tests from the same seed.
+Every model is the Qwen2.5-0.5B architecture (hidden 896, 14/2 heads,
+head_dim 64, intermediate 4864, RMSNorm eps 1e-6, RoPE theta 1e6, tied
+embeddings); weights come from lrrt_b200.synthetic.model(seed, layers, vocab)
+and are regenerated bit-identically by the tests from the same seed.
 
-Run: python tests/golden/make_golden.py
+  hf_qwen2_decode.npz   2 layers, vocab 4096: 8 greedy tokens after a
+                        6-token prompt, last-step logits
+  hf_qwen2_config1.npz  BASELINE config 1: one layer, vocab 151936, KV cache
+                        rows 0..127 ~ N(0, 1) (seed 0), hidden ~ N(0, 1):
+                        all 151936 logits of the step at position 128
+  hf_qwen2_config2.npz  BASELINE config 2: 24 layers, vocab 151936, the
+                        32-token seed-1 prompt: the first 32 greedy tokens and
+                        the logit of each
+
+Run: python tests/golden/make_golden.py [decode|config1|config2 ...]
 """
 from __future__ import annotations
 
@@ -27,14 +35,17 @@ from lrrt_b200 import synthetic  # noqa: E402
 
 SEED, LAYERS, VOCAB, PROMPT, NEW_TOKENS = 7, 2, 4096, 6, 8
 OUT = Path(__file__).with_name("hf_qwen2_decode.npz")
+CONFIG1 = Path(__file__).with_name("hf_qwen2_config1.npz")
+CONFIG2 = Path(__file__).with_name("hf_qwen2_config2.npz")
 
 
 def build_hf(layers, tail):
     import transformers
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
-    config = Qwen2Config(vocab_size=VOCAB, hidden_size=896, intermediate_size=4864,
-                         num_hidden_layers=LAYERS, num_attention_heads=14,
+    config = Qwen2Config(vocab_size=tail["lm_head"].shape[0], hidden_size=896,
+                         intermediate_size=4864,
+                         num_hidden_layers=len(layers), num_attention_heads=14,
                          num_key_value_heads=2, rope_theta=1.0e6, rms_norm_eps=1.0e-6,
                          tie_word_embeddings=True, max_position_embeddings=4096,
                          attn_implementation="eager")
@@ -58,8 +69,7 @@ def build_hf(layers, tail):
     return model, transformers.__version__
 
 
-def main() -> None:
-    torch.set_num_threads(max(1, torch.get_num_threads()))
+def make_decode() -> None:
     layers, tail = synthetic.model(SEED, LAYERS, VOCAB)
     prompt = synthetic.prompt(SEED, PROMPT, VOCAB)
     model, version = build_hf(layers, tail)
@@ -78,6 +88,55 @@ def main() -> None:
                         max_logits=np.array(maxima, np.float32), last_logits=last,
                         transformers_version=np.array(version))
     print(f"wrote {OUT}: tokens {tokens}")
+
+
+def make_config1() -> None:
+    """One decoder step at position 128 over a cache prefilled with N(0, 1)
+    rows. The cache rows are post-RoPE keys and values ([position][2 heads x
+    64]), which is also what a transformers KV cache holds."""
+    from transformers import DynamicCache
+
+    layers, tail = synthetic.model(0, 1, 151936)
+    keys, values = synthetic.kv_prefill(0, 1, 128)[0]
+    hidden = synthetic.hidden(0)
+    model, version = build_hf(layers, tail)
+    cache = DynamicCache()
+    as_heads = lambda a: torch.from_numpy(a.reshape(128, 2, 64).transpose(1, 0, 2)[None].copy())  # noqa: E731
+    cache.update(as_heads(keys), as_heads(values), 0)
+    with torch.no_grad():
+        out = model(inputs_embeds=torch.from_numpy(hidden)[None, None],
+                    past_key_values=cache, position_ids=torch.tensor([[128]]),
+                    cache_position=torch.tensor([128]), use_cache=True)
+    logits = out.logits[0, -1].numpy().astype(np.float32)
+    np.savez_compressed(CONFIG1, logits=logits, transformers_version=np.array(version))
+    print(f"wrote {CONFIG1}: argmax {int(np.argmax(logits))}")
+
+
+def make_config2(count: int = 32) -> None:
+    layers, tail = synthetic.model(1, 24, 151936)
+    prompt = synthetic.prompt(1, 32, 151936)
+    model, version = build_hf(layers, tail)
+    tokens, maxima = [], []
+    with torch.no_grad():
+        out = model(torch.tensor([prompt.astype(np.int64)]), use_cache=True)
+        for _ in range(count):
+            logits = out.logits[0, -1]
+            token = int(torch.argmax(logits))
+            tokens.append(token)
+            maxima.append(float(logits[token]))
+            out = model(torch.tensor([[token]]), past_key_values=out.past_key_values,
+                        use_cache=True)
+    np.savez_compressed(CONFIG2, prompt=prompt, tokens=np.array(tokens, np.uint32),
+                        max_logits=np.array(maxima, np.float32),
+                        transformers_version=np.array(version))
+    print(f"wrote {CONFIG2}: tokens {tokens}")
+
+
+def main() -> None:
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    which = sys.argv[1:] or ["decode", "config1", "config2"]
+    for name in which:
+        {"decode": make_decode, "config1": make_config1, "config2": make_config2}[name]()
 
 
 if __name__ == "__main__":

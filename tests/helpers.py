@@ -21,6 +21,17 @@ def max_relative_error(actual: np.ndarray, expected: np.ndarray) -> float:
     return float(np.max(np.abs(actual - expected)) / scale)
 
 
+def elementwise_relative_error(actual: np.ndarray, expected: np.ndarray,
+                               floor: float = 1.0e-2) -> float:
+    """max |actual - expected| / max(|expected|, floor), element by element:
+    relative for every value whose magnitude exceeds `floor`, absolute
+    (scaled by floor) below it, where cancellation makes any reordered FP32
+    sum differ by more than a relative 1e-4."""
+    actual = np.asarray(actual, np.float64)
+    expected = np.asarray(expected, np.float64)
+    return float(np.max(np.abs(actual - expected) / np.maximum(np.abs(expected), floor)))
+
+
 def build_pair(seed: int, layers: int, vocab: int, capacity: int, max_tokens: int,
                partitions: int = 0, distinct_layers: bool = True, fused: bool = True,
                worker_count: int = 0):

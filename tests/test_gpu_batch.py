@@ -54,6 +54,45 @@ def test_batch_streams_match_oracle(gpu):
 
 
 @pytest.mark.gpu
+def test_config4_shape_streams_match_oracle(gpu):
+    """BASELINE config 4's shape: the 24-layer, vocab-151936 model, four
+    streams whose caches hold 1024 positions of N(0, 1) rows (written
+    directly, no prompt), 8 greedy tokens each, against the oracle's
+    single-stream decode of the same context: tokens, last logit, new KV rows."""
+    import oracle as O
+    O.set_threads(O.max_threads())
+    layers, vocab, context, steps, streams = 24, 151936, 1024, 8, 4
+    model, oracle, _, _ = build_pair(seed=1, layers=layers, vocab=vocab,
+                                     capacity=context + 16, max_tokens=steps)
+    model.enable_prefill(64)
+    first_tokens = S.prompt(2, streams, vocab)
+    contexts = [S.kv_prefill(200 + s, layers, context) for s in range(streams)]
+    with Q.Batch(model, streams, context + 16, steps) as batch:
+        for stream in range(streams):
+            for layer, (keys, values) in enumerate(contexts[stream]):
+                batch.write_cache(stream, layer, 0, keys, values)
+            batch.set_next(stream, context, int(first_tokens[stream]))
+        tokens, logits = batch.decode(steps)
+        for stream in range(streams):
+            for layer, (keys, values) in enumerate(contexts[stream]):
+                oracle.set_kv(layer, 0, keys, values)
+            oracle.decode(oracle.embedding(int(first_tokens[stream])), context, steps)
+            assert tokens[stream].tolist() == oracle.output_tokens[:steps].tolist(), stream
+            d = oracle.decode_state
+            assert abs(logits[stream] - d.sampled_logit) <= \
+                LOGIT_RTOL * max(1.0, abs(d.sampled_logit))
+            rows = context + steps
+            for layer in range(layers):
+                keys, values = batch.read_cache(stream, layer, rows)
+                assert max_relative_error(keys[context:], oracle.key_cache[layer][context:rows]) \
+                    <= KV_RTOL
+                assert max_relative_error(values[context:],
+                                          oracle.value_cache[layer][context:rows]) <= KV_RTOL
+    O.set_threads(1)
+    model.close()
+
+
+@pytest.mark.gpu
 def test_batch_argument_errors(gpu):
     model, _, _, _ = build_pair(seed=3, layers=1, vocab=1024, capacity=64, max_tokens=4)
     with pytest.raises(N.LrrtError, match="not enabled"):

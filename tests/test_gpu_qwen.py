@@ -7,7 +7,10 @@ import numpy as np
 import pytest
 
 import oracle as O
-from helpers import LOGIT_RTOL, build_pair, ingest_prompt, max_relative_error, prefill_kv
+from pathlib import Path
+
+from helpers import (LOGIT_RTOL, build_pair, elementwise_relative_error, ingest_prompt,
+                     max_relative_error, prefill_kv)
 from lrrt_b200 import native as N
 from lrrt_b200 import qwen as Q
 from lrrt_b200 import synthetic as S
@@ -168,6 +171,51 @@ def test_config1_single_layer_step(gpu):
     state, tokens = model.decode(128, 4)
     assert state.fused_path == 1
     compare_run(model, oracle, state, tokens)
+    model.close()
+
+
+@pytest.mark.gpu
+def test_config1_every_logit(gpu):
+    """BASELINE config 1 with the fused LM head's logit capture: all 151936
+    logits of the step at position 128, element by element within 1e-4 of
+    the oracle's and of Hugging Face transformers' (committed fixture)."""
+    model, oracle, _, _ = build_pair(seed=0, layers=1, vocab=151936, capacity=136,
+                                     max_tokens=1)
+    prefill_kv(model, oracle, 0, 1, 128)
+    hidden = S.hidden(0)
+    model.set_logit_capture(True)
+    model.set_hidden(hidden)
+    oracle.decode(hidden, 128, 1)
+    state, tokens = model.decode(128, 1)
+    assert state.fused_path == 1
+    compare_run(model, oracle, state, tokens)
+    logits = model.read("logits")
+    assert elementwise_relative_error(logits, oracle.logits) <= LOGIT_RTOL
+    golden = np.load(Path(__file__).parent / "golden" / "hf_qwen2_config1.npz")
+    assert elementwise_relative_error(logits, golden["logits"]) <= LOGIT_RTOL
+    assert int(np.argmax(logits)) == int(np.argmax(golden["logits"])) == int(tokens[0])
+    model.close()
+
+
+@pytest.mark.gpu
+def test_config3_full_size(gpu):
+    """BASELINE config 3 at full size: 24 layers, vocab 151936, KV rows
+    0..4095 ~ N(0, 1), 256 greedy tokens (split attention over the blocks)
+    against the oracle: tokens, DecodeState, logit, every layer's KV rows."""
+    O.set_threads(O.max_threads())
+    model, oracle, _, _ = build_pair(seed=1, layers=24, vocab=151936, capacity=4360,
+                                     max_tokens=256)
+    prefill_kv(model, oracle, 1, 24, 4096)
+    hidden = S.hidden(1)
+    model.set_hidden(hidden)
+    oracle.decode(hidden, 4096, 256)
+    state, tokens = model.decode(4096, 256)
+    assert state.fused_path == 1
+    gaps = oracle.top2_gaps[:256]
+    near_ties = [int(i) for i in np.nonzero(gaps < 1.0e-4 * np.abs(state.sampled_logit))[0]]
+    print(f"config3: near-tied steps {near_ties}, min gap {float(gaps.min()):.3e}")
+    compare_run(model, oracle, state, tokens)
+    O.set_threads(1)
     model.close()
 
 

@@ -122,6 +122,46 @@ def test_oracle_matches_transformers_golden(built):
         1.0e-4 * abs(golden["max_logits"][-1])
 
 
+def test_oracle_matches_transformers_config1_logits(built):
+    """BASELINE config 1 (one layer, vocab 151936, KV rows 0..127 ~ N(0, 1),
+    hidden ~ N(0, 1)): every logit of the step at position 128 within 1e-4
+    of transformers' (element by element, relative above 1e-2 in magnitude)."""
+    golden = np.load(GOLDEN / "hf_qwen2_config1.npz")
+    weights, tail = S.model(0, 1, 151936)
+    model = O.OracleModel(weights, tail, 136, 32, workers=148, max_tokens=1)
+    keys, values = S.kv_prefill(0, 1, 128)[0]
+    model.set_kv(0, 0, keys, values)
+    O.set_threads(O.max_threads())
+    state = model.decode(S.hidden(0), 128, 1)
+    O.set_threads(1)
+    assert state.status == 2
+    want = golden["logits"].astype(np.float64)
+    error = np.max(np.abs(model.logits - want) / np.maximum(np.abs(want), 1.0e-2))
+    assert error <= 1.0e-4, error
+    assert model.decode_state.sampled_token == int(np.argmax(want))
+
+
+def test_oracle_matches_transformers_config2_tokens(built):
+    """BASELINE config 2 (24 layers, vocab 151936, the 32-token seed-1
+    prompt): the first 32 greedy tokens equal transformers' and each chosen
+    logit is within 1e-4."""
+    golden = np.load(GOLDEN / "hf_qwen2_config2.npz")
+    weights, tail = S.model(1, 24, 151936)
+    prompt = golden["prompt"]
+    count = len(golden["tokens"])
+    model = O.OracleModel(weights, tail, 64, 32, workers=148, max_tokens=count,
+                          keep_logits=False)
+    O.set_threads(O.max_threads())
+    for i, token in enumerate(prompt[:-1]):
+        model.decode(model.embedding(int(token)), i, 1)
+    state = model.decode(model.embedding(int(prompt[-1])), len(prompt) - 1, count)
+    O.set_threads(1)
+    assert state.status == 2
+    assert model.output_tokens[:count].tolist() == golden["tokens"].tolist()
+    assert abs(model.decode_state.sampled_logit - golden["max_logits"][-1]) <= \
+        1.0e-4 * max(1.0, abs(golden["max_logits"][-1]))
+
+
 def test_wave_dot_reduction_order(built):
     """The dot product follows the lane-strided order and shfl_down tree."""
     rng = np.random.default_rng(5)

@@ -39,6 +39,16 @@ def _upload(device, array: np.ndarray) -> C.c_void_p:
     return pointer
 
 
+def _device_memory():
+    """(free device bytes, the runtime's allocation count)."""
+    import torch
+    free, _ = torch.cuda.mem_get_info(0)
+    stats = N.MemoryStats()
+    N.check(N.runtime().lr_get_memory_stats(N.Device(0), C.byref(stats)),
+            "lr_get_memory_stats")
+    return free, stats.allocation_count
+
+
 @pytest.mark.gpu
 def test_static_top1_matches_partitioned_lm_head_on_two_calls(gpu):
     vocab = 8192
@@ -53,6 +63,11 @@ def test_static_top1_matches_partitioned_lm_head_on_two_calls(gpu):
     # predicate, error code and token as the GPU parity tests do.
     assert state.predicate_value == 1 and state.error_code == 0
     assert tokens.tolist() == [state.sampled_token]
+    # ... which itself agrees with the CPU oracle's run of the same step.
+    oracle.decode(oracle.embedding(int(prompt[-1])), len(prompt) - 1, 1)
+    assert state.sampled_token == oracle.decode_state.sampled_token
+    assert abs(state.sampled_logit - oracle.decode_state.sampled_logit) <= \
+        1.0e-4 * max(1.0, abs(oracle.decode_state.sampled_logit))
     normalized = model.read("final_normalized").astype(np.float32)
     lm_head = np.ascontiguousarray(tail["lm_head"], dtype=np.float32)
     top1 = _bind()
@@ -62,6 +77,7 @@ def test_static_top1_matches_partitioned_lm_head_on_two_calls(gpu):
     hidden_device = _upload(device, normalized)
     try:
         for call in range(2):
+            before = _device_memory() if call == 1 else None
             token = C.c_uint32(NO_TOKEN)
             logit = C.c_float(float("nan"))
             N.check(top1(device, None, lm_head_device, hidden_device, vocab, 896, 0,
@@ -69,6 +85,10 @@ def test_static_top1_matches_partitioned_lm_head_on_two_calls(gpu):
             assert token.value == state.sampled_token, (call, token.value)
             assert np.float32(logit.value).tobytes() == np.float32(state.sampled_logit).tobytes(), \
                 (call, logit.value, state.sampled_logit)
+            if before is not None:
+                # The second call (set-up done) changes neither the device's
+                # free memory nor the runtime's allocation count.
+                assert _device_memory() == before
         # A grid larger than the static scratch is refused with a message.
         token = C.c_uint32(0)
         logit = C.c_float(0.0)
@@ -81,6 +101,19 @@ def test_static_top1_matches_partitioned_lm_head_on_two_calls(gpu):
         N.check(top1(device, None, lm_head_device, hidden_device, vocab, 896, 37,
                      C.byref(token), C.byref(logit)), "lrq_lm_head_top1_static")
         assert token.value == state.sampled_token
+        # On a queue the caller created; and 256 rows over 1024 blocks, so
+        # most blocks own no row and publish an empty candidate.
+        queue = C.c_void_p()
+        N.check(runtime.lr_queue_create(device, C.byref(queue)), "lr_queue_create")
+        try:
+            rows = 256
+            N.check(top1(device, queue, lm_head_device, hidden_device, rows, 896, 1024,
+                         C.byref(token), C.byref(logit)), "lrq_lm_head_top1_static")
+        finally:
+            runtime.lr_queue_destroy(queue)
+        scores = lm_head[:rows].astype(np.float64) @ normalized.astype(np.float64)
+        assert token.value == int(np.argmax(scores))
+        assert abs(logit.value - scores[token.value]) <= 1.0e-4 * max(1.0, abs(scores[token.value]))
     finally:
         runtime.lr_free(device, lm_head_device)
         runtime.lr_free(device, hidden_device)
