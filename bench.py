@@ -24,7 +24,15 @@ Reported (one JSON line, rank 0):
   batched     BASELINE config 4: 32 streams at context 1024 (seed 2),
               32/N per GPU decoded as one batch per GPU, 128 tokens each;
               aggregate tokens/s over all ranks (max-over-ranks time)
+  scheduler_floor  the control-only resident kernel (the reference's
+              scheduler-profile workload: Programs, stages and grid barriers
+              with only the state-changing tasks) on the same 128-token run:
+              microseconds per token and per grid barrier
 Weights (2 GB) exceed L2 (126 MB), so no flush is needed between steps.
+
+--profile-case prefill|batch runs one of the profiler workloads instead (the
+measured launches inside cuProfilerStart/Stop, for
+`ncu --profile-from-start off`), and prints no bench line.
 
 --impl reference times the reference's CPU implementation of the path (the
 oracle port; the reference's own code is HIP for AMD gfx1101 and cannot run
@@ -71,6 +79,15 @@ def parse_args():
                         help="tokens per step (smaller only for profiler captures)")
     parser.add_argument("--no-extra", action="store_true",
                         help="skip the config-5 prefill and config-4 batched lines")
+    parser.add_argument("--profile-case", choices=["prefill", "batch"],
+                        help="run a profiler workload instead of the bench")
+    parser.add_argument("--layers", type=int, default=LAYERS, help="profile cases only")
+    parser.add_argument("--prompt", type=int, default=PREFILL_PROMPT, help="profile cases only")
+    parser.add_argument("--streams", type=int, default=STREAMS, help="profile cases only")
+    parser.add_argument("--context", type=int, default=STREAM_CONTEXT,
+                        help="profile cases only")
+    parser.add_argument("--case-steps", type=int, default=2, help="profile cases only")
+    parser.add_argument("--vocab", type=int, default=VOCAB, help="profile cases only")
     return parser.parse_args()
 
 
@@ -177,6 +194,15 @@ def rank_seeds(rank: int):
     return SEED, SEED + rank
 
 
+def stream_slice(rank: int, world: int) -> list[int]:
+    """Config-4 streams decoded by `rank` of `world`: 32 / world consecutive
+    streams starting at rank * 32 / world (world divides 32)."""
+    if world <= 0 or STREAMS % world != 0 or not 0 <= rank < world:
+        raise ValueError(f"{world} ranks cannot split {STREAMS} streams evenly")
+    per_rank = STREAMS // world
+    return [rank * per_rank + local for local in range(per_rank)]
+
+
 def make_weights(rank: int):
     from lrrt_b200 import synthetic as S
     weight_seed, prompt_seed = rank_seeds(rank)
@@ -185,21 +211,47 @@ def make_weights(rank: int):
     return weights, tail, prompt
 
 
-def cpu_tokens_per_second(weights, tail, prompt, seconds: float, threads: int):
-    """Times the CPU oracle decoding single tokens of the same model."""
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def oracle_decoder(weights, tail, prompt, threads: int):
+    """The CPU oracle with the bench's prompt ingested (positions 0..30), and
+    a function decoding `count` greedy tokens from position 31 (the GPU arm's
+    workload: positions 31..158 for 128 tokens)."""
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle as O
     O.set_threads(threads)
     model = O.OracleModel(weights, tail, PROMPT + NEW_TOKENS, 32, workers=148,
-                          max_tokens=1, keep_logits=False)
+                          max_tokens=NEW_TOKENS, keep_logits=False)
+    for position, token in enumerate(prompt[:-1]):
+        model.decode(model.embedding(int(token)), position, 1)
+    start_hidden = model.embedding(int(prompt[-1]))
+
+    def decode(count: int) -> None:
+        model.decode(start_hidden, PROMPT - 1, count)
+
+    return decode
+
+
+def cpu_tokens_per_second(decode, seconds: float):
+    """Tokens/s of the oracle on the GPU arm's workload (positions 31..),
+    repeating decodes of up to 128 tokens for about `seconds`."""
     tokens, start = 0, time.perf_counter()
+    count = 4
     while True:
-        position = tokens % (PROMPT + NEW_TOKENS)
-        model.decode(model.embedding(int(prompt[position % PROMPT])), position, 1)
-        tokens += 1
+        decode(count)
+        tokens += count
         elapsed = time.perf_counter() - start
         if elapsed >= seconds:
             break
+        count = min(NEW_TOKENS, count * 2)
     return tokens / elapsed, tokens, elapsed
 
 
@@ -210,25 +262,23 @@ def reference_arm(args, rank: int, world: int):
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle as O
     threads = O.max_threads()
-    O.set_threads(threads)
-    model = O.OracleModel(weights, tail, PROMPT + NEW_TOKENS, 32, workers=148,
-                          max_tokens=1, keep_logits=False)
-    per_step_tokens = 2
-
-    def step(i):
-        for k in range(per_step_tokens):
-            position = (i * per_step_tokens + k) % (PROMPT + NEW_TOKENS)
-            model.decode(model.embedding(int(prompt[position % PROMPT])), position, 1)
-
-    for i in range(args.warmup):
-        step(i)
+    decode = oracle_decoder(weights, tail, prompt, threads)
+    # Each step decodes the GPU arm's workload from position 31, as many of
+    # its 128 tokens as keep the whole run to about four minutes.
+    probe = time.perf_counter()
+    decode(4)
+    rate = 4 / (time.perf_counter() - probe)
+    per_step_tokens = int(max(4, min(NEW_TOKENS, 240.0 * rate / max(1, args.steps + args.warmup))))
+    for _ in range(args.warmup):
+        decode(per_step_tokens)
     start = time.perf_counter()
-    for i in range(args.steps):
-        step(args.warmup + i)
+    for _ in range(args.steps):
+        decode(per_step_tokens)
     elapsed = time.perf_counter() - start
     value = per_step_tokens * args.steps / elapsed
-    sample = (f"{per_step_tokens} single-token decodes per step of the 24-layer model "
-              f"(positions cycling 0..159) on {threads} host threads")
+    sample = (f"greedy decode of the GPU arm's workload (prompt ingested, positions "
+              f"31..{31 + per_step_tokens - 1}, {per_step_tokens} of its 128 tokens per step) "
+              f"on {threads} host threads of {cpu_model()}")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -305,11 +355,12 @@ def extra_configs(model, Q, S, rank: int, world: int, dist, warmup: int):
     achieved = flops / prefill_s / 1e12
     # Config 4: streams [rank * per_rank, ...) of 32, each a 1025-token prompt
     # (context 1024), one batch per GPU, 128 greedy tokens per stream.
-    per_rank = STREAMS // world
+    mine = stream_slice(rank, world)
+    per_rank = len(mine)
     all_prompts = S.prompt(2, STREAMS * (STREAM_CONTEXT + 1), VOCAB).reshape(STREAMS, -1)
     with Q.Batch(model, per_rank, BATCH_CAPACITY, STREAM_TOKENS) as batch:
-        for local in range(per_rank):
-            batch.prefill(local, [int(t) for t in all_prompts[rank * per_rank + local]])
+        for local, stream in enumerate(mine):
+            batch.prefill(local, [int(t) for t in all_prompts[stream]])
         batch.decode(4)  # graph capture and warm-up
         model.synchronize()
         timer.record_start()
@@ -404,6 +455,31 @@ def our_arm(args, rank: int, world: int, local_rank: int):
     check(model.read_state())
     clock_summary = clocks.summary()
 
+    # Scheduler floor: the control-only kernel over the same 128-token run
+    # (every stage ends with a grid barrier: 9 per layer + 4 per token).
+    floor_request = model.request(start_position, NEW_TOKENS, path=Q.PATH_SCHEDULER_PROFILE)
+    model.launch(floor_request)
+    model.synchronize()
+    floor_times = []
+    for _ in range(3):
+        launch_timer.record_start()
+        model.launch(floor_request)
+        launch_timer.record_end()
+        model.synchronize()
+        floor_times.append(launch_timer.elapsed_ns())
+    floor_state = model.read_state()
+    if floor_state.status != 2 or floor_state.generated_tokens != NEW_TOKENS:
+        raise RuntimeError(f"scheduler-floor run failed: status {floor_state.status}")
+    floor_ns = statistics.median(floor_times)
+    barriers_per_token = LAYERS * 9 + 4
+    scheduler_floor = {
+        "kernel": "qwen_stateful_graph_scheduler_profile_kernel",
+        "us_per_token": floor_ns / 1e3 / NEW_TOKENS,
+        "barriers_per_token": barriers_per_token,
+        "us_per_barrier": floor_ns / 1e3 / NEW_TOKENS / barriers_per_token,
+        "workers": model.info.worker_count,
+    }
+
     # End to end through the C ABI: host hidden in, host tokens out.
     hidden_host = tail["lm_head"][int(prompt[-1])].copy()
     tokens_host = np.zeros(NEW_TOKENS, np.uint32)
@@ -453,6 +529,7 @@ def our_arm(args, rank: int, world: int, local_rank: int):
         "gpu_launches": args.steps,
         "roofline": roofline,
         "clocks": clock_summary,
+        "scheduler_floor": scheduler_floor,
     }
     if not args.no_extra:
         from lrrt_b200 import synthetic as S
@@ -461,21 +538,75 @@ def our_arm(args, rank: int, world: int, local_rank: int):
         sys.path.insert(0, str(REPO / "oracle"))
         import oracle as O
         threads = O.max_threads()
-        tps, tokens, seconds = cpu_tokens_per_second(weights, tail, prompt, args.cpu_seconds,
-                                                     threads)
+        decode = oracle_decoder(weights, tail, prompt, threads)
+        tps, tokens, seconds = cpu_tokens_per_second(decode, args.cpu_seconds)
+        O.set_threads(1)
+        tps1, tokens1, seconds1 = cpu_tokens_per_second(decode, args.cpu_seconds / 2)
         line["cpu_baseline"] = {
             "value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{tokens} single-token decodes of the same 24-layer model "
-                      f"({seconds:.1f} s, OpenMP over rows, reference reduction order)"}
+            "cpu_model": cpu_model(),
+            "sample": f"{tokens} greedy tokens of the same workload (prompt ingested, "
+                      f"decodes from position 31; {seconds:.1f} s, OpenMP over rows, "
+                      f"reference reduction order)",
+            "one_core": {"value": tps1, "unit": "tokens/s", "cores": 1,
+                         "sample": f"{tokens1} tokens in {seconds1:.1f} s"}}
     model.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def profile_case(args) -> None:
+    """Profiler workloads of the prefill and batched-decode paths: warm-up
+    outside the profiler range, the measured launches inside
+    cuProfilerStart/Stop (for `ncu --profile-from-start off`). Small sizes
+    keep `--set full` captures to a few hundred MB of device memory."""
+    import ctypes
+
+    from lrrt_b200 import qwen as Q
+    from lrrt_b200 import synthetic as S
+
+    def build(capacity: int, max_tokens: int, chunk: int):
+        weights, tail = S.model(3, args.layers, args.vocab, True)
+        model = Q.Model(Q.ModelConfig(layer_count=args.layers, vocab_size=args.vocab,
+                                      cache_capacity=capacity, max_tokens_per_run=max_tokens))
+        for i, w in enumerate(weights):
+            model.set_layer(i, w)
+        model.set_tail(tail["final_norm"], tail["lm_head"])
+        model.enable_prefill(chunk)
+        return model
+
+    cuda = ctypes.CDLL("libcuda.so.1")
+    if args.profile_case == "prefill":
+        model = build(args.prompt, 1, args.prompt)
+        prompt = S.prompt(3, args.prompt, args.vocab)
+        model.prefill(prompt, Q.PREFILL_TF32X3)  # warm-up: weight split, maps
+        model.synchronize()
+        cuda.cuProfilerStart()
+        model.prefill(prompt, Q.PREFILL_TF32X3)
+        model.synchronize()
+        cuda.cuProfilerStop()
+    else:
+        capacity = args.context + args.case_steps + 8
+        model = build(capacity, args.case_steps + 4, max(args.streams, args.context))
+        prompts = S.prompt(2, args.streams * (args.context + 1), args.vocab)
+        with Q.Batch(model, args.streams, capacity, args.case_steps + 4) as batch:
+            for s in range(args.streams):
+                batch.prefill(s, prompts[s * (args.context + 1):(s + 1) * (args.context + 1)])
+            batch.decode(4)  # graph capture, warm-up
+            cuda.cuProfilerStart()
+            batch.decode(args.case_steps)
+            cuda.cuProfilerStop()
+    model.close()
+    print("profile case done")
 
 
 def main():
     global NEW_TOKENS
     args = parse_args()
     NEW_TOKENS = args.new_tokens
+    if args.profile_case:
+        profile_case(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

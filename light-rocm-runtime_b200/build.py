@@ -6,7 +6,7 @@ Outputs (git-ignored, shipped with the working tree):
   lib/qwen_stateful_graph.cubin   sm_100a decode megakernels
   lib/qwen_prefill.cubin          sm_100a prompt prefill kernels
   lib/decoder_ops.cubin + .json   per-operation decode kernels as an lrrt::bundle
-  lib/stateful_graph_fixture.cubin  sm_100a scheduler fixture kernels
+  _build/tests/stateful_graph_fixture.cubin  sm_100a scheduler fixture kernels (tests)
   _build/tests/*                  C++ host tests (tests/cpp)
 
 Rebuilds a target only when one of its inputs is newer than it.
@@ -85,7 +85,7 @@ def build(verbose: bool = False) -> dict[str, Path]:
               "-lrt", "-ldl", "-lpthread", "-Wl,-rpath,$ORIGIN"], verbose)
     outputs["driver"] = driver
 
-    for name in ("qwen_stateful_graph", "qwen_prefill", "stateful_graph_fixture", "decoder_ops"):
+    for name in ("qwen_stateful_graph", "qwen_prefill", "decoder_ops"):
         source = csrc / "kernels" / f"{name}.cu"
         cubin = LIB / f"{name}.cubin"
         if _stale(cubin, [source] + headers):
@@ -99,6 +99,13 @@ def build(verbose: bool = False) -> dict[str, Path]:
     tests_dir = REPO / "tests" / "cpp"
     test_build = BUILD / "tests"
     test_build.mkdir(exist_ok=True)
+    # Scheduler fixture kernels (test infrastructure: the reference test's
+    # synthetic workload, replayed on both schedulers against its goldens).
+    fixture_source = tests_dir / "stateful_graph_fixture.cu"
+    fixture = test_build / "stateful_graph_fixture.cubin"
+    if _stale(fixture, [fixture_source] + headers):
+        _run([NVCC, *NVCCFLAGS, "-cubin", str(fixture_source), "-o", str(fixture)], verbose)
+    outputs["stateful_graph_fixture"] = fixture
     # Test bundle for lrrt::Bundle: manifest + sm_100a cubin side by side.
     bundle_dir = test_build / "bundle"
     bundle_dir.mkdir(exist_ok=True)

@@ -17,7 +17,7 @@ RUNTIME_PATH = LIB / "liblrrt.so"
 DRIVER_PATH = LIB / "liblrrt_qwen.so"
 QWEN_CUBIN = LIB / "qwen_stateful_graph.cubin"
 PREFILL_CUBIN = LIB / "qwen_prefill.cubin"
-FIXTURE_CUBIN = LIB / "stateful_graph_fixture.cubin"
+FIXTURE_CUBIN = PACKAGE / "_build" / "tests" / "stateful_graph_fixture.cubin"
 
 u32, u64, f32, vp, cp, sz = C.c_uint32, C.c_uint64, C.c_float, C.c_void_p, C.c_char_p, C.c_size_t
 

@@ -4,14 +4,21 @@
 // csrc/kernels/decoder_ops.cu). BASELINE config 1's shapes: hidden 896, 14
 // query heads, 2 KV heads, head_dim 64, intermediate 4864, RoPE theta 1e6,
 // RMSNorm eps 1e-6, weights N(0, 0.02), norm gains 1, KV cache prefilled with
-// 128 positions of N(0, 1), hidden N(0, 1). The reference is the same layer
-// computed in double precision on the host. Usage:
-//   decode_layer_test <decoder_ops manifest>
+// 128 positions of N(0, 1), hidden N(0, 1). Usage:
+//   decode_layer_test <decoder_ops manifest> [<io directory>]
+// Without a directory the weights and inputs come from a local generator and
+// the step is checked against the same layer computed in double precision
+// here. With one, they are read from raw float32 files in the directory
+// (attention_norm, q, k, v, q_bias, k_bias, v_bias, o, mlp_norm, gate, up,
+// down, cache_keys [128][128], cache_values, hidden) and the layer output and
+// appended key row are written to out.f32 and key.f32 for the caller to check
+// (the pytest wrapper compares them with the CPU oracle's decode step).
 #include "lrrt/executor/triton_decode_layer.hpp"
 
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <fstream>
 #include <random>
 #include <string>
 #include <vector>
@@ -144,6 +151,26 @@ Vector reference_step(const qw::DecoderLayerWeights &w, const Vector &hidden,
   return out;
 }
 
+std::vector<float> read_floats(const std::string &path, size_t count) {
+  std::vector<float> values(count);
+  std::ifstream in(path, std::ios::binary);
+  in.read(reinterpret_cast<char *>(values.data()),
+          static_cast<std::streamsize>(count * sizeof(float)));
+  if (!in || in.gcount() != static_cast<std::streamsize>(count * sizeof(float))) {
+    throw std::runtime_error("cannot read " + std::to_string(count) + " floats from " + path);
+  }
+  return values;
+}
+
+void write_floats(const std::string &path, const std::vector<float> &values) {
+  std::ofstream out(path, std::ios::binary);
+  out.write(reinterpret_cast<const char *>(values.data()),
+            static_cast<std::streamsize>(values.size() * sizeof(float)));
+  if (!out) {
+    throw std::runtime_error("cannot write " + path);
+  }
+}
+
 double relative_error(const std::vector<float> &got, const Vector &want) {
   double scale = 0.0, worst = 0.0;
   for (size_t i = 0; i < want.size(); ++i) {
@@ -156,10 +183,11 @@ double relative_error(const std::vector<float> &got, const Vector &want) {
 } // namespace
 
 int main(int argc, char **argv) {
-  if (argc != 2) {
-    std::fprintf(stderr, "usage: %s <decoder_ops manifest>\n", argv[0]);
+  if (argc != 2 && argc != 3) {
+    std::fprintf(stderr, "usage: %s <decoder_ops manifest> [<io directory>]\n", argv[0]);
     return 2;
   }
+  const std::string io = argc == 3 ? std::string(argv[2]) + "/" : std::string();
   try {
     lrrt::Runtime runtime;
     if (runtime.device_count() == 0) {
@@ -203,6 +231,36 @@ int main(int argc, char **argv) {
     w.rope_theta = theta;
     std::mt19937 rng(0);
     const auto &s = w.shape;
+    if (!io.empty()) {
+      // Weights and inputs from the caller; outputs back to it.
+      const size_t h = s.hidden, q = s.q_dim(), kv = s.kv_dim(), i = s.intermediate;
+      w.attention_norm_weight = read_floats(io + "attention_norm", h);
+      w.mlp_norm_weight = read_floats(io + "mlp_norm", h);
+      w.q_weight = read_floats(io + "q", q * h);
+      w.k_weight = read_floats(io + "k", kv * h);
+      w.v_weight = read_floats(io + "v", kv * h);
+      w.q_bias = read_floats(io + "q_bias", q);
+      w.k_bias = read_floats(io + "k_bias", kv);
+      w.v_bias = read_floats(io + "v_bias", kv);
+      w.out_weight = read_floats(io + "o", h * q);
+      w.gate_weight = read_floats(io + "gate", i * h);
+      w.up_weight = read_floats(io + "up", i * h);
+      w.down_weight = read_floats(io + "down", h * i);
+      const std::vector<float> keys = read_floats(io + "cache_keys", size_t{position} * kv);
+      const std::vector<float> values = read_floats(io + "cache_values", size_t{position} * kv);
+      const std::vector<float> input = read_floats(io + "hidden", h);
+      tr::DecodeLayer layer(device, argv[1], capacity, s, theta, eps);
+      layer.set_weights(w);
+      layer.set_kv(0, position, keys.data(), values.data());
+      std::vector<float> out;
+      layer.step(input, position, out);
+      std::vector<float> k_cache(size_t{capacity} * kv);
+      layer.buffers().copy_from(k_cache, "k_cache");
+      write_floats(io + "out.f32", out);
+      write_floats(io + "key.f32",
+                   std::vector<float>(k_cache.begin() + size_t{position} * kv,
+                                      k_cache.begin() + size_t{position + 1} * kv));
+    }
     w.attention_norm_weight.assign(s.hidden, 1.0f);
     w.mlp_norm_weight.assign(s.hidden, 1.0f);
     w.q_weight = normal(rng, s.q_dim() * s.hidden, 0.02f);

@@ -39,7 +39,8 @@ def _rank_main(rank: int, world: int, port: int, results):
         # Rank r "took" 1 + r seconds of device time and 10 - r end to end.
         elapsed, e2e = bench.max_over_ranks([1.0 + rank, 10.0 - rank], dist)
         gathered = [None] * world
-        dist.all_gather_object(gathered, (weight_seed, prompt.tolist()))
+        dist.all_gather_object(gathered, (weight_seed, prompt.tolist(),
+                                          bench.stream_slice(rank, world)))
         results[rank] = (elapsed, e2e, gathered)
     finally:
         dist.barrier()
@@ -63,7 +64,24 @@ def test_two_gloo_ranks_reduce_max_and_keep_replicas_independent():
     for rank in range(world):
         elapsed, e2e, gathered = results[rank]
         assert elapsed == 2.0 and e2e == 10.0  # max over ranks, on every rank
-        (seed0, prompt0), (seed1, prompt1) = gathered
+        (seed0, prompt0, streams0), (seed1, prompt1, streams1) = gathered
         assert seed0 == seed1                 # one model, replicated
         assert prompt0 != prompt1             # independent streams
         assert len(prompt0) == len(prompt1) == 32
+        assert sorted(streams0 + streams1) == list(range(32))  # config 4, each stream once
+
+
+def test_config4_stream_slices_cover_every_stream_once():
+    """bench.py's config-4 partition: for 1, 2, 4 and 8 ranks the ranks'
+    slices are disjoint, equal in size and together cover streams 0..31."""
+    sys.path.insert(0, str(REPO))
+    import pytest
+
+    import bench
+    for world in (1, 2, 4, 8):
+        slices = [bench.stream_slice(rank, world) for rank in range(world)]
+        assert all(len(s) == 32 // world for s in slices)
+        assert sorted(stream for s in slices for stream in s) == list(range(32))
+    for bad in ((0, 3), (2, 2), (0, 0)):
+        with pytest.raises(ValueError):
+            bench.stream_slice(*bad)
