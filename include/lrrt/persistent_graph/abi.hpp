@@ -31,6 +31,13 @@
 namespace lrrt::persistent_graph {
 
 constexpr uint32_t kAbiVersion = 10;
+// State::abi_version values the resident kernels accept: this ABI and the
+// reference's 9, whose struct layouts are the same (a State built by a
+// reference caller carries 9).
+constexpr uint32_t kReferenceAbiVersion = 9;
+LRRT_HOST_DEVICE constexpr bool accepted_abi_version(uint32_t version) {
+  return version == kAbiVersion || version == kReferenceAbiVersion;
+}
 constexpr uint32_t kWorkerThreads = 256;
 constexpr uint32_t kMaximumResidentWorkers = 256;
 constexpr uint32_t kMaximumTasks = 64;

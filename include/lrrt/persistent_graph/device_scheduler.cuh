@@ -51,7 +51,7 @@ __device__ bool validate_programs(const State *state, const Task *tasks,
                                   uint32_t total_task_count,
                                   uint32_t phase_state_count,
                                   void *opaque_context) {
-  if (state->abi_version != kAbiVersion || program_count == 0 ||
+  if (!accepted_abi_version(state->abi_version) || program_count == 0 ||
       total_task_count == 0 || program_count > kMaximumPrograms ||
       phase_program(state->phase) >= program_count ||
       phase_generation(state->phase) >= phase_state_count ||

@@ -1,7 +1,7 @@
 // sm_100a synchronisation and bulk-copy primitives used by the resident
 // schedulers and workloads: gpu-scope acquire/release accesses, %globaltimer
-// deadlines, mbarriers and 1-D TMA bulk copies (cp.async.bulk, never with
-// cluster multicast, so it is safe in multi-GPU processes).
+// deadlines, mbarriers and TMA copies into this CTA's own shared memory
+// (every copy has exactly one destination CTA).
 #ifndef LRRT_PERSISTENT_GRAPH_DEVICE_SYNC_CUH_
 #define LRRT_PERSISTENT_GRAPH_DEVICE_SYNC_CUH_
 
@@ -140,7 +140,7 @@ __device__ __forceinline__ void bulk_copy_to_shared(void *destination,
 
 // 2-D TMA tile load of the box at (x, y) of the tensor map `map` (a
 // CUtensorMap in global memory) into shared memory, completing on `barrier`.
-// No multicast. x times the element size must be a multiple of 16 bytes.
+// One destination CTA. x times the element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tensor_load_2d(void *destination, const void *map, uint32_t x,
                                                uint32_t y, uint64_t *barrier) {
   asm volatile(

@@ -317,6 +317,33 @@ LRRT_API lr_status_t lrq_generate(lrq_model_t *model, const float *hidden,
 LRRT_API lr_status_t lrq_model_read(lrq_model_t *model, uint32_t buffer, uint32_t layer,
                                     void *destination, size_t bytes);
 
+/*
+ * Fused-path workspace for callers that build the Context / TailContext
+ * arrays themselves, as the reference driver does
+ * (benchmarks/qwen_stateful_graph.cpp:730-1118), and launch through
+ * ResidentExecutor. The sm_100a compiled kernel takes its fast path only when
+ * TailContext::workspace (bytes 88-95, the reference's tail padding) points
+ * to an initialised workspace and the launch has the fused path's dynamic
+ * shared memory (ResidentConfig::dynamic_shared_memory_bytes =
+ * lrrt::qwen::stateful_graph::resident::kFusedSharedBytes, also given to
+ * admit_resident_workers); otherwise it runs the reference's per-task path.
+ *  - lrq_workspace_bytes: bytes of a workspace for `worker_count` blocks.
+ *  - lrq_workspace_init: zero-fills the device allocation `workspace`
+ *    (256-byte aligned, `bytes` from lrq_workspace_bytes) and writes its
+ *    header and the KV caches' tensor maps from `contexts`, the host copy of
+ *    the caller's Context array (layer_count entries; key_cache, value_cache
+ *    and cache_capacity as on the device). Call it again after moving a KV
+ *    cache.
+ *  - lrq_workspace_path: which path the last launch with this workspace
+ *    took: 1 fused, 2 per-task (0 none yet).
+ */
+LRRT_API lr_status_t lrq_workspace_bytes(uint32_t worker_count, uint64_t *bytes);
+LRRT_API lr_status_t lrq_workspace_init(lr_device_t device, void *workspace, uint64_t bytes,
+                                        uint32_t worker_count, const void *contexts,
+                                        uint32_t layer_count);
+LRRT_API lr_status_t lrq_workspace_path(lr_device_t device, const void *workspace,
+                                        uint32_t *path);
+
 /* Logit capture (a B200 test aid with no reference counterpart): with
  * enable != 0 the fused path also stores every LM-head row it computes, so
  * LRQ_BUFFER_LOGITS holds all vocab_size logits of the last decode step

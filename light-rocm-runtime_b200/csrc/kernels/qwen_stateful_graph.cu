@@ -17,7 +17,7 @@
 //   - Each block owns a balanced share of every weight matrix (QKV, o_proj,
 //     gate/up, down, LM head) and keeps a ring of 7 x 28 KB shared-memory
 //     slots filled by TMA (1-D bulk copies for weights, 2-D tensor copies for
-//     its KV group's cached rows; no multicast). A consumer refills the slot
+//     its KV group's cached rows; each copy has one destination). A consumer refills the slot
 //     it releases, so the stream runs ahead across stages and layers.
 //   - Values one block produces for the others inside a layer (q/k/v, the
 //     o_proj rows, silu(gate) * up, the down rows) travel as 64-bit exchange

@@ -330,6 +330,79 @@ void zero_fill(lrrt::DeviceBuffer &buffer) {
   lrrt::copy_to_device(buffer, zeros);
 }
 
+// One layer's KV caches as the fused path's tensor maps see them.
+struct KvCacheView {
+  const float *keys;
+  const float *values;
+  uint32_t capacity; // rows of [capacity][128] floats
+};
+
+// Zero-fills a workspace allocation of `bytes` (>= workspace_bytes(capacity))
+// and writes its header, array pointers and the KV caches' 2-D tensor maps
+// (boxes of 32 columns x 56 rows, 128-byte swizzle: the fused path's KV ring
+// units).
+void init_workspace(lr_device_t device, void *workspace, uint64_t bytes, uint32_t capacity,
+                    const std::vector<KvCacheView> &caches) {
+  if (workspace == nullptr || capacity < 2u || bytes < qd::workspace_bytes(capacity) ||
+      caches.size() > qd::kWorkspaceMapLayers ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
+    throw std::invalid_argument(
+        "invalid workspace: null, misaligned, too small for the worker count, or too many "
+        "layers");
+  }
+  const std::vector<unsigned char> zeros(bytes, 0);
+  lrrt::check(lr_memcpy(device, workspace, zeros.data(), bytes, LR_MEMCPY_HOST_TO_DEVICE),
+              "lr_memcpy workspace");
+  auto *base = static_cast<unsigned char *>(workspace);
+  qd::Workspace header{};
+  size_t at = 256;
+  header.magic = qd::kWorkspaceMagic;
+  header.worker_capacity = capacity;
+  header.attention_partials = reinterpret_cast<float *>(base + at);
+  at += size_t{capacity} * qd::kQueriesPerKvHead * qd::kAttentionPartialStride * sizeof(float);
+  at = (at + 255) / 256 * 256;
+  header.attention_arrivals = reinterpret_cast<uint32_t *>(base + at);
+  at += 256;
+  header.top1_values = reinterpret_cast<float *>(base + at);
+  at += (size_t{capacity} + qd::kMaximumLmHeadPartitions) * sizeof(float);
+  header.top1_indices = reinterpret_cast<uint32_t *>(base + at);
+  at += (size_t{capacity} + qd::kMaximumLmHeadPartitions) * sizeof(uint32_t);
+  at = (at + 255) / 256 * 256;
+  header.exchange = reinterpret_cast<uint64_t *>(base + at); // zero-filled above
+  at += size_t{qd::kExchangeWords} * sizeof(uint64_t);
+  at = (at + 255) / 256 * 256;
+  std::vector<unsigned char> maps(size_t{qd::kWorkspaceMapLayers} * 2u * qd::kTensorMapBytes, 0);
+  for (size_t layer = 0; layer < caches.size(); ++layer) {
+    for (uint32_t which = 0; which < 2; ++which) {
+      const float *cache = which == 0 ? caches[layer].keys : caches[layer].values;
+      if (cache == nullptr || (reinterpret_cast<uintptr_t>(cache) & 15u) != 0 ||
+          caches[layer].capacity == 0) {
+        throw std::invalid_argument("KV cache of layer " + std::to_string(layer) +
+                                    " is null, misaligned or empty");
+      }
+      CUtensorMap map{};
+      const cuuint64_t dims[2] = {qd::kKvSize, caches[layer].capacity};
+      const cuuint64_t strides[1] = {qd::kKvSize * sizeof(float)};
+      const cuuint32_t box[2] = {32, qd::resident::kKvUnitPositions};
+      const cuuint32_t element_strides[2] = {1, 1};
+      const CUresult status = lrrt::qwen::prefill::detail::encode_tiled()(
+          &map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(cache), dims, strides,
+          box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (status != CUDA_SUCCESS) {
+        throw std::runtime_error("cuTensorMapEncodeTiled failed for a KV cache map (" +
+                                 std::to_string(status) + ")");
+      }
+      std::memcpy(maps.data() + (layer * 2u + which) * qd::kTensorMapBytes, &map, sizeof(map));
+    }
+  }
+  header.kv_maps = base + at;
+  lrrt::check(lr_memcpy(device, base + at, maps.data(), maps.size(), LR_MEMCPY_HOST_TO_DEVICE),
+              "lr_memcpy KV cache maps");
+  lrrt::check(lr_memcpy(device, base, &header, sizeof(header), LR_MEMCPY_HOST_TO_DEVICE),
+              "lr_memcpy workspace header");
+}
+
 void build_model(lrq_model_t &m) {
   const lrq_model_config_t &c = m.config;
   if (c.layer_count == 0 || c.vocab_size == 0 || c.cache_capacity == 0 ||
@@ -401,58 +474,14 @@ void build_model(lrq_model_t &m) {
   // Workspace for the fused path: header followed by its arrays.
   const uint32_t capacity = std::max(m.workers, 2u);
   m.workspace.emplace(allocate(m, qd::workspace_bytes(capacity)));
-  zero_fill(*m.workspace);
-  qd::Workspace header{};
   {
-    auto *base = static_cast<unsigned char *>(m.workspace->data());
-    size_t at = 256;
-    header.magic = qd::kWorkspaceMagic;
-    header.worker_capacity = capacity;
-    header.attention_partials = reinterpret_cast<float *>(base + at);
-    at += size_t{capacity} * qd::kQueriesPerKvHead * qd::kAttentionPartialStride *
-          sizeof(float);
-    at = (at + 255) / 256 * 256;
-    header.attention_arrivals = reinterpret_cast<uint32_t *>(base + at);
-    at += 256;
-    header.top1_values = reinterpret_cast<float *>(base + at);
-    at += (size_t{capacity} + qd::kMaximumLmHeadPartitions) * sizeof(float);
-    header.top1_indices = reinterpret_cast<uint32_t *>(base + at);
-    at += (size_t{capacity} + qd::kMaximumLmHeadPartitions) * sizeof(uint32_t);
-    at = (at + 255) / 256 * 256;
-    header.exchange = reinterpret_cast<uint64_t *>(base + at); // zero-filled above
-    at += size_t{qd::kExchangeWords} * sizeof(uint64_t);
-    at = (at + 255) / 256 * 256;
-    // 2-D maps over every layer's K and V cache ([capacity][128] floats): the
-    // fused path loads a KV group's cached rows as boxes of 32 columns x 56
-    // rows with 128-byte swizzle.
-    std::vector<unsigned char> maps(size_t{qd::kWorkspaceMapLayers} * 2u * qd::kTensorMapBytes, 0);
-    for (uint32_t layer = 0; layer < c.layer_count && layer < qd::kWorkspaceMapLayers; ++layer) {
-      for (uint32_t which = 0; which < 2; ++which) {
-        const float *cache = static_cast<const float *>(
-                                 (which == 0 ? m.key_cache : m.value_cache)->data()) +
-                             layer * m.cache_floats();
-        CUtensorMap map{};
-        const cuuint64_t dims[2] = {qd::kKvSize, c.cache_capacity};
-        const cuuint64_t strides[1] = {qd::kKvSize * sizeof(float)};
-        const cuuint32_t box[2] = {32, qd::resident::kKvUnitPositions};
-        const cuuint32_t element_strides[2] = {1, 1};
-        const CUresult status = lrrt::qwen::prefill::detail::encode_tiled()(
-            &map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(cache), dims, strides,
-            box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (status != CUDA_SUCCESS) {
-          throw std::runtime_error("cuTensorMapEncodeTiled failed for a KV cache map (" +
-                                   std::to_string(status) + ")");
-        }
-        std::memcpy(maps.data() + (size_t{layer} * 2u + which) * qd::kTensorMapBytes, &map,
-                    sizeof(map));
-      }
+    std::vector<KvCacheView> caches(c.layer_count);
+    for (uint32_t layer = 0; layer < c.layer_count; ++layer) {
+      caches[layer] = {static_cast<const float *>(m.key_cache->data()) + layer * m.cache_floats(),
+                       static_cast<const float *>(m.value_cache->data()) + layer * m.cache_floats(),
+                       c.cache_capacity};
     }
-    header.kv_maps = base + at;
-    lrrt::check(lr_memcpy(m.workspace->device(), base + at, maps.data(), maps.size(),
-                          LR_MEMCPY_HOST_TO_DEVICE),
-                "lr_memcpy KV cache maps");
-    lrrt::copy_to_device(*m.workspace, &header, sizeof(header));
+    init_workspace(m.device.get(), m.workspace->data(), m.workspace->size(), capacity, caches);
   }
 
   qd::TailContext tail{};
@@ -1527,6 +1556,46 @@ LRRT_API lr_status_t lrq_model_set_trace(lrq_model_t *model, uint32_t entries) {
       model->trace.emplace(model->device, size_t{entries} * sizeof(qd::StageProfileEntry));
       model->trace_capacity = entries;
     }
+  });
+}
+
+LRRT_API lr_status_t lrq_workspace_bytes(uint32_t worker_count, uint64_t *bytes) {
+  return guarded("lrq_workspace_bytes", [&] {
+    if (bytes == nullptr || worker_count == 0 || worker_count > sg::kMaximumResidentWorkers) {
+      throw std::invalid_argument("null output or worker count out of range");
+    }
+    *bytes = qd::workspace_bytes(std::max(worker_count, 2u));
+  });
+}
+
+LRRT_API lr_status_t lrq_workspace_init(lr_device_t device, void *workspace, uint64_t bytes,
+                                        uint32_t worker_count, const void *contexts,
+                                        uint32_t layer_count) {
+  return guarded("lrq_workspace_init", [&] {
+    if (contexts == nullptr || layer_count == 0 || worker_count == 0 ||
+        worker_count > sg::kMaximumResidentWorkers) {
+      throw std::invalid_argument("null Context array, no layers or worker count out of range");
+    }
+    const auto *layers = static_cast<const qd::Context *>(contexts);
+    std::vector<KvCacheView> caches(layer_count);
+    for (uint32_t layer = 0; layer < layer_count; ++layer) {
+      caches[layer] = {layers[layer].key_cache, layers[layer].value_cache,
+                       layers[layer].cache_capacity};
+    }
+    init_workspace(device, workspace, bytes, std::max(worker_count, 2u), caches);
+  });
+}
+
+LRRT_API lr_status_t lrq_workspace_path(lr_device_t device, const void *workspace,
+                                        uint32_t *path) {
+  return guarded("lrq_workspace_path", [&] {
+    if (workspace == nullptr || path == nullptr) {
+      throw std::invalid_argument("null argument");
+    }
+    qd::Workspace header{};
+    lrrt::check(lr_memcpy(device, &header, workspace, sizeof(header), LR_MEMCPY_DEVICE_TO_HOST),
+                "lr_memcpy workspace header");
+    *path = header.reserved[0];
   });
 }
 
