@@ -173,6 +173,15 @@ __device__ __forceinline__ void exchange_store(uint64_t *word, float value, uint
                : "memory");
 }
 
+// Two consecutive words (16-byte aligned) in one access; each word is
+// single-copy atomic on its own.
+__device__ __forceinline__ void exchange_store2(uint64_t *word, float first, float second,
+                                                uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(word),
+               "l"(exchange_word(first, tag)), "l"(exchange_word(second, tag))
+               : "memory");
+}
+
 // Two consecutive words (16-byte aligned).
 __device__ __forceinline__ void exchange_load2(const uint64_t *word, uint64_t &first,
                                                uint64_t &second) {

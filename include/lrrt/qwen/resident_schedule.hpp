@@ -87,6 +87,52 @@ LRRT_HOST_DEVICE constexpr uint32_t attention_group(uint32_t worker, uint32_t wo
   return worker < attention_split(workers) ? 0u : 1u;
 }
 
+// Blocks of a KV group, and a block's index within its group.
+LRRT_HOST_DEVICE constexpr uint32_t group_size(uint32_t group, uint32_t workers) {
+  return group == 0u ? attention_split(workers) : workers - attention_split(workers);
+}
+
+LRRT_HOST_DEVICE constexpr uint32_t group_rank(uint32_t worker, uint32_t workers) {
+  return worker < attention_split(workers) ? worker : worker - attention_split(workers);
+}
+
+// How a decode step with `positions` KV positions (cached rows + the current
+// one) computes attention:
+//   local   every block attends its KV group over all positions by itself
+//           (the cached rows as its three KV units);
+//   spread  the blocks of a group split the positions into contiguous slices
+//           of at most three KV units, publish per-head partial softmax
+//           states through the exchange, and a few warps per group merge
+//           them into the attention output;
+//   split   longer contexts: items over all blocks between grid barriers.
+enum class AttentionMode : uint32_t { local = 0, spread = 1, split = 2 };
+
+LRRT_HOST_DEVICE constexpr AttentionMode attention_mode(uint32_t positions, uint32_t workers) {
+  return positions <= kLocalAttentionLimit ? AttentionMode::local
+         : positions <= kKvUnits * kKvUnitPositions * (workers / 2u) ? AttentionMode::spread
+                                                                     : AttentionMode::split;
+}
+
+// Spread attention: the slice of block `rank` of a group of `size` blocks is
+// positions [first, first + rows) read from the cache, plus the current
+// position (index positions - 1, which is not yet in the cache when the KV
+// units are issued) when `current`. rows <= kKvUnits * kKvUnitPositions
+// whenever attention_mode() is spread.
+struct SpreadSlice {
+  uint32_t first;
+  uint32_t rows;
+  bool current;
+};
+
+LRRT_HOST_DEVICE constexpr SpreadSlice spread_slice(uint32_t positions, uint32_t rank,
+                                                    uint32_t size) {
+  const uint32_t per = (positions + size - 1u) / size;
+  const uint32_t first = rank * per < positions ? rank * per : positions;
+  const uint32_t last = first + per < positions ? first + per : positions;
+  const bool current = last == positions && first < positions;
+  return {first, last - first - (current ? 1u : 0u), current};
+}
+
 LRRT_HOST_DEVICE inline UnitRange out_range(uint32_t worker, uint32_t workers) {
   if (workers == 1u) {
     return {0, kOUnits};

@@ -124,13 +124,19 @@ constexpr uint32_t kAttentionPartialStride = kHeadSize + 2u; // acc[64], max, su
 //   out  [2][kKvHeads][kHiddenSize]   o_proj split over the two KV groups
 //   act  [2][kIntermediateSize]       silu(gate) * up
 //   down [2][kHiddenSize]             down projection
+//   attention [2][kQuerySize]         attention output of a spread step
 // All words are zero when no launch is running (a launch clears the words it
 // wrote before it returns; zero never matches a tag).
 constexpr uint32_t kExchangeQkv = 0;
 constexpr uint32_t kExchangeOut = kExchangeQkv + 2u * kPackedQkvSize;
 constexpr uint32_t kExchangeAct = kExchangeOut + 2u * kKvHeads * kHiddenSize;
 constexpr uint32_t kExchangeDown = kExchangeAct + 2u * kIntermediateSize;
-constexpr uint32_t kExchangeWords = kExchangeDown + 2u * kHiddenSize;
+constexpr uint32_t kExchangeAttention = kExchangeDown + 2u * kHiddenSize;
+constexpr uint32_t kExchangeWords = kExchangeAttention + 2u * kQuerySize;
+// Spread-attention partial state of one block: per query head of its group,
+// the unnormalised weighted value sum [64], the score maximum and the sum of
+// exp(score - maximum), as exchange words.
+constexpr uint32_t kSpreadWords = kQueriesPerKvHead * kAttentionPartialStride; // 462
 
 // B200 scratch for the fused resident path (no reference counterpart). One
 // zero-filled allocation: this header, then
@@ -138,6 +144,8 @@ constexpr uint32_t kExchangeWords = kExchangeDown + 2u * kHiddenSize;
 //  attention_arrivals: [kKvHeads], zero whenever no attention stage is running
 //  top1_values/top1_indices: [worker_capacity + kMaximumLmHeadPartitions]
 //  exchange: [kExchangeWords] 64-bit words (see above)
+//  attention_words: [2][worker_capacity][kSpreadWords] exchange words, by step
+//    parity and block (spread attention partial states)
 //  kv_maps: [kWorkspaceMapLayers][2] CUtensorMap (128 B each: key cache,
 //    value cache of each layer; dims {kKvSize, cache_capacity}, box 32
 //    columns x 56 rows, 128-byte swizzle) for the fused path's KV ring units
@@ -154,7 +162,7 @@ struct alignas(16) Workspace {
   uint64_t *exchange;
   const void *kv_maps;
   float *logits; // optional [vocab_size]: every LM-head row of the last step (test capture)
-  uint64_t reserved2;
+  uint64_t *attention_words;
 };
 
 // Bytes of one allocation holding a Workspace header followed by its arrays.
@@ -165,6 +173,7 @@ constexpr size_t workspace_bytes(uint32_t worker_capacity) {
          256u + 2u * (size_t{worker_capacity} + kMaximumLmHeadPartitions) *
                     sizeof(uint32_t) +
          256u + size_t{kExchangeWords} * sizeof(uint64_t) + 256u +
+         2u * size_t{worker_capacity} * kSpreadWords * sizeof(uint64_t) + 256u +
          size_t{kWorkspaceMapLayers} * 2u * kTensorMapBytes + 256u;
 }
 

@@ -560,7 +560,10 @@ struct QwenConfig {
   uint32_t worker, workers, layers, vocab, lm_units;
   uint32_t limit_ms;
   uint32_t group;           // KV group whose attention this block computes
+  uint32_t group_rank;      // index of this block within its group
+  uint32_t group_size;      // blocks of its group
   bool group_writer;        // first block of its group: publishes the attention output
+  uint64_t *attention_words; // spread-attention partial states [2][workers][kSpreadWords]
   UnitRanges ranges;
   StreamMap map;
   uint64_t policy;
@@ -578,6 +581,21 @@ struct QwenConfig {
   uint32_t residual_argument[2];  // residual_advance task arguments
 };
 __shared__ QwenConfig block_config;
+
+// The cache rows [first, first + rows) this block attends, and whether it
+// also takes the current position, for a step with `positions` KV positions:
+// all cached rows of its group when local, its group slice when spread,
+// none when split (the split path reads the cache without the ring).
+__device__ __forceinline__ SpreadSlice attention_slice(uint32_t positions) {
+  switch (attention_mode(positions, block_config.workers)) {
+  case AttentionMode::local:
+    return {0u, positions - 1u, true};
+  case AttentionMode::spread:
+    return spread_slice(positions, block_config.group_rank, block_config.group_size);
+  default:
+    return {0u, 0u, false};
+  }
+}
 
 // Shared-memory copies of layer Contexts, double-buffered by step parity:
 // layer_cache[s & 1] holds contexts[s % layers] while step s runs. Program 1
@@ -625,6 +643,7 @@ __device__ __forceinline__ void wait_prefetched_context() {
 struct QwenBlock {
   bool fused;
   bool split_attention;     // this step's attention runs split over blocks
+  bool spread_attention;    // this step's attention is spread over its group's blocks
   bool hidden_exchanged;    // the residual's last update is the down exchange
   bool failed;              // a wait of this block gave up (block-uniform)
   uint32_t consumed;        // stream sequence number of the next unit to consume
@@ -770,17 +789,19 @@ __device__ __noinline__ void issue_unit(const QwenBlock &b, uint32_t n) {
   s->unit_tag[slot] = make_tag(c.kind, c.layer, c.unit);
   *reinterpret_cast<volatile uint32_t *>(&s->sequence[slot]) = n;
   if (c.kind == kKv) {
-    // Cached rows 56j..56j+55 of this block's KV group, for the token this
-    // layer's unit belongs to (one per stream cycle): K then V, each as two
-    // 32-column boxes. Units past the token's cached positions, and every
-    // unit of a step whose attention runs split, carry no bytes.
+    // Cached rows first + 56j .. first + 56j + 55 of this block's KV group
+    // and attention slice, for the token this layer's unit belongs to (one
+    // per stream cycle): K then V, each as two 32-column boxes. Units past
+    // the slice's cached rows, and every unit of a step whose attention runs
+    // split, carry no bytes.
     const uint32_t cached = block_config.base_position + position.cycle;
-    const bool load = cached + 1u <= kLocalAttentionLimit && c.unit * kKvUnitPositions < cached;
+    const SpreadSlice slice = attention_slice(cached + 1u);
+    const bool load = c.unit * kKvUnitPositions < slice.rows;
     dev::mbarrier_arrive_expect_tx(&s->full[slot], load ? kSlotBytes : 0u);
     if (load) {
       const unsigned char *maps = block_config.kv_maps + size_t{c.layer} * 2u * qd::kTensorMapBytes;
       const uint32_t x = block_config.group * qd::kHeadSize;
-      const uint32_t y = c.unit * kKvUnitPositions;
+      const uint32_t y = slice.first + c.unit * kKvUnitPositions;
       constexpr uint32_t kBox = kSlotBytes / 4u; // 32 columns x 56 rows
 #pragma unroll
       for (uint32_t box = 0; box < 4; ++box) {
@@ -953,7 +974,7 @@ __device__ __forceinline__ void trace_event(QwenBlock &b, uint64_t start_ns) {
 // Stage-profile runs: a point in this block's timeline, (marker id, now).
 // Ids: 20 + opcode at a stage's entry; at a stage's end 1 attention norm,
 // 2 QKV, 3 local attention, 4 o_proj, 5 MLP norm, 6 gate/up, 7 down,
-// 8 final norm, 9 LM head, 10 embedding feedback. Exchange waits record
+// 8 final norm, 9 LM head, 10 embedding feedback, 11 spread combine. Exchange waits record
 // (start, end) in the same sequence.
 __device__ __forceinline__ void trace_mark(QwenBlock &b, uint32_t id) {
   if (block_config.event_trace == nullptr) {
@@ -1279,12 +1300,8 @@ __device__ void fused_qkv(QwenBlock &b, sg::State *state, qd::Context *c, uint32
       });
 }
 
-__device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Context *c,
+__device__ void group_attention(QwenBlock &b, sg::State *state, const qd::Context *c,
                                 uint32_t layer);
-
-__device__ __forceinline__ bool use_local_attention(uint32_t positions) {
-  return positions <= kLocalAttentionLimit;
-}
 
 // o_proj split along its input over the two KV groups: this block's units
 // are rows 8v..8v+7 restricted to its group's 448 columns, each row computed
@@ -1296,8 +1313,24 @@ __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
   const uint32_t group = block_config.group;
-  if (!b.split_attention) {
-    local_attention(b, state, c, layer);
+  if (b.spread_attention) {
+    // The group's attention output from the attention exchange (thread t <
+    // 112 takes dims 4t..4t+3).
+    bool ok = true;
+    if (threadIdx.x < kGroupColumns / 4u) {
+      const uint64_t *words = exchange_words(qd::kExchangeAttention, qd::kQuerySize, b.step) +
+                              group * kGroupColumns + 4u * threadIdx.x;
+      float v[4];
+      ok = exchange_wait<2>(state, b.step + 1u, 3u, [&](uint32_t i) { return words + 2u * i; },
+                            v);
+      reinterpret_cast<float4 *>(s->input)[threadIdx.x] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    if (__syncthreads_or(ok ? 0 : 1) != 0) {
+      b.failed = true;
+      return;
+    }
+  } else if (!b.split_attention) {
+    group_attention(b, state, c, layer);
     if (b.failed) {
       return;
     }
@@ -1730,14 +1763,16 @@ __device__ void attention_item(QwenBlock &b, qd::Context *c, uint32_t group,
   __syncthreads();
 }
 
-// Local attention (contexts up to kLocalAttentionLimit positions): this block
-// computes the attention output of its KV group's seven query heads from
-// shared memory. The cached K/V rows of the earlier positions arrive as the
-// layer's three KV ring units (56 positions each: K then V, each as two
-// 32-column boxes of 56 rows, 128-byte rows swizzled by XOR of the 16-byte
-// chunk index with row % 8); the current position's K/V and the group's
-// queries come from the qkv exchange. The output, [head][dim] of the group,
-// goes to input[0, 448).
+// Attention of this block's KV group over its slice of the positions
+// (attention_slice), from shared memory: the slice's cached K/V rows arrive
+// as the layer's three KV ring units (56 positions each: K then V, each as
+// two 32-column boxes of 56 rows, 128-byte rows swizzled by XOR of the
+// 16-byte chunk index with row % 8); the current position's K/V and the
+// group's queries come from the qkv exchange. A local step's slice is every
+// position, and the output, [head][dim] of the group, goes to input[0, 448).
+// A spread step publishes the slice's partial state per query head instead:
+// the unnormalised value sums, the score maximum and the sum of
+// exp(score - maximum) (maximum -inf and zero sums for an empty slice).
 __device__ __forceinline__ const float4 *kv_chunk(const unsigned char *unit, uint32_t row,
                                                    uint32_t chunk, uint32_t part) {
   // part 0: K, 1: V; chunk = float4 index 0..15 of the 64-float row.
@@ -1746,15 +1781,23 @@ __device__ __forceinline__ const float4 *kv_chunk(const unsigned char *unit, uin
                                           (((chunk & 7u) ^ (row & 7u)) << 4));
 }
 
-__device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Context *c,
+__device__ void group_attention(QwenBlock &b, sg::State *state, const qd::Context *c,
                                 uint32_t layer) {
   FusedShared *s = block_config.shared;
   float *work = s->work;
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = threadIdx.x >> 5u;
   const uint32_t group = block_config.group;
-  const uint32_t positions = b.kv_length + 1u;
-  const uint32_t current = b.kv_length;
+  const SpreadSlice slice = attention_slice(b.kv_length + 1u);
+  // Score slot p < rows is cached row slice.first + p (unit p / 56, row
+  // p % 56); slot `rows` is the current position when the slice has it.
+  const uint32_t rows = slice.rows;
+  const uint32_t positions = rows + (slice.current ? 1u : 0u);
+  const bool spread = b.spread_attention;
+  uint64_t *partial = block_config.attention_words +
+                      (size_t{b.step & 1u} * block_config.workers + block_config.worker) *
+                          qd::kSpreadWords;
+  const uint32_t tag = b.step + 1u;
   constexpr uint32_t kHeads = qd::kQueriesPerKvHead;
   // Group entries of the qkv exchange: q [448], k [64], v [64]; thread t < 144
   // takes entries 4t..4t+3 (one region each).
@@ -1807,7 +1850,7 @@ __device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Contex
     }
 #pragma unroll 4
     for (uint32_t j = 0; j < qd::kHeadSize / 4u; ++j) {
-      const float4 k = p == current
+      const float4 k = p == rows
                            ? reinterpret_cast<const float4 *>(work + kLocalCurrent)[j]
                            : *kv_chunk(unit, row, j, 0);
 #pragma unroll
@@ -1824,7 +1867,8 @@ __device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Contex
   }
   static_assert(kLocalAttentionLimit <= kThreads, "one score row per thread");
   __syncthreads();
-  // Softmax of head h in warp h: exp(score - max), and 1 / sum.
+  // Softmax of head h in warp h: exp(score - max), and 1 / sum (local) or
+  // (max, sum) published (spread).
   if (warp < kHeads) {
     float *scores = work + kLocalScores + warp * kLocalAttentionLimit;
     float maximum = -INFINITY;
@@ -1840,7 +1884,12 @@ __device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Contex
     }
     sum = warp_all_sum(sum);
     if (lane == 0) {
-      s->reduce[warp] = 1.0f / sum;
+      if (spread) {
+        dev::exchange_store2(partial + warp * qd::kAttentionPartialStride + qd::kHeadSize,
+                             maximum, sum, tag);
+      } else {
+        s->reduce[warp] = 1.0f / sum;
+      }
     }
   }
   __syncthreads();
@@ -1857,12 +1906,12 @@ __device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Contex
     // (chunk % 8) ^ (r % 8) of the 128-byte row.
     constexpr uint32_t kBox = kSlotBytes / 4u;
     const uint32_t box = (2u + (chunk >> 3)) * kBox;
-    for (uint32_t u = 0; u * kKvUnitPositions < current; ++u) {
+    for (uint32_t u = 0; u * kKvUnitPositions < rows; ++u) {
       const unsigned char *base = units[u] + box;
-      const uint32_t rows = min(kKvUnitPositions, current - u * kKvUnitPositions);
+      const uint32_t unit_rows = min(kKvUnitPositions, rows - u * kKvUnitPositions);
       const float *weights = e + u * kKvUnitPositions;
 #pragma unroll 2
-      for (uint32_t row = half; row < rows; row += 2u) {
+      for (uint32_t row = half; row < unit_rows; row += 2u) {
         const float weight = weights[row];
         const float4 x = *reinterpret_cast<const float4 *>(base + row * 128u +
                                                            (((chunk & 7u) ^ (row & 7u)) << 4));
@@ -1872,8 +1921,8 @@ __device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Contex
         acc.w = fmaf(weight, x.w, acc.w);
       }
     }
-    if (half == (current & 1u)) { // the current position, in its parity's half
-      const float weight = e[current];
+    if (slice.current && half == (rows & 1u)) { // the current position, in its parity's half
+      const float weight = e[rows];
       const float4 x = reinterpret_cast<const float4 *>(work + kLocalCurrent + qd::kHeadSize)[chunk];
       acc.x = fmaf(weight, x.x, acc.x);
       acc.y = fmaf(weight, x.y, acc.y);
@@ -1889,7 +1938,12 @@ __device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Contex
     release_unit(b, b.consumed + warp);
   }
   b.consumed += kKvUnits;
-  if (half == 0u) {
+  if (half == 0u && spread) {
+    const float4 other = reinterpret_cast<const float4 *>(work + kLocalPartial)[item];
+    uint64_t *words = partial + h * qd::kAttentionPartialStride + 4u * chunk;
+    dev::exchange_store2(words, acc.x + other.x, acc.y + other.y, tag);
+    dev::exchange_store2(words + 2, acc.z + other.z, acc.w + other.w, tag);
+  } else if (half == 0u) {
     const float4 other = reinterpret_cast<const float4 *>(work + kLocalPartial)[item];
     const float inverse = s->reduce[h];
     const float4 out = make_float4((acc.x + other.x) * inverse, (acc.y + other.y) * inverse,
@@ -1903,10 +1957,113 @@ __device__ void local_attention(QwenBlock &b, sg::State *state, const qd::Contex
   __syncthreads();
 }
 
+// Merges the softmax partial state (m2, l2, x2, y2) into (m, l, x, y): both
+// sums rescaled to the larger maximum; an empty state (maximum -inf) adds
+// nothing.
+__device__ __forceinline__ void merge_partial(float &m, float &l, float &x, float &y, float m2,
+                                              float l2, float x2, float y2) {
+  const float top = fmaxf(m, m2);
+  const float s1 = m == -INFINITY ? 0.0f : expf(m - top);
+  const float s2 = m2 == -INFINITY ? 0.0f : expf(m2 - top);
+  l = l * s1 + l2 * s2;
+  x = x * s1 + x2 * s2;
+  y = y * s1 + y2 * s2;
+  m = top;
+}
+
+// Spread attention, second half: the group's blocks' partial states merged
+// into the attention output. Item i < 224 of a group is dims 2(i % 32),
+// 2(i % 32) + 1 of head i / 32 and belongs to warp i % 8 of the group's
+// block size - 1 - i / 8 (the group's last 28 blocks, or several items per
+// warp in smaller groups). Lane l merges the partial states of the group's
+// blocks l, l + 32, ... in order, the lanes then merge pairwise (xor
+// butterfly), and lane 0 publishes value sum / exp sum to the attention
+// exchange and, where the reference leaves the attention output, to the
+// query buffer.
+__device__ void spread_combine(QwenBlock &b, sg::State *state, qd::Context *c) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = threadIdx.x >> 5u;
+  const uint32_t size = block_config.group_size;
+  const uint32_t group = block_config.group;
+  const uint32_t workers = block_config.workers;
+  const uint64_t *partials =
+      block_config.attention_words +
+      (size_t{b.step & 1u} * workers + (group == 0u ? 0u : attention_split(workers))) *
+          qd::kSpreadWords;
+  uint64_t *outputs =
+      exchange_words(qd::kExchangeAttention, qd::kQuerySize, b.step) + group * kGroupColumns;
+  const uint32_t tag = b.step + 1u;
+  constexpr uint32_t kItems = kGroupColumns / 2u;
+  constexpr uint32_t kPerLane = 3; // partial states per lane and poll round
+  bool ok = true;
+  for (uint32_t item = (size - 1u - block_config.group_rank) * kWarps + warp; item < kItems;
+       item += kWarps * size) {
+    const uint32_t head = item / 32u, dim = 2u * (item % 32u);
+    const uint64_t *entry = partials + head * qd::kAttentionPartialStride;
+    float m = -INFINITY, l = 0.0f, x = 0.0f, y = 0.0f;
+    for (uint32_t round = 0; round < size; round += 32u * kPerLane) {
+      uint32_t mask = 0;
+      float v[4 * kPerLane];
+#pragma unroll
+      for (uint32_t k = 0; k < kPerLane; ++k) {
+        mask |= round + lane + 32u * k < size ? 3u << (2u * k) : 0u;
+        v[4 * k] = -INFINITY;
+        v[4 * k + 1] = v[4 * k + 2] = v[4 * k + 3] = 0.0f;
+      }
+      // Pair 2k: (maximum, exp sum) of block round + lane + 32k; pair
+      // 2k + 1: its value sums at dims (dim, dim + 1).
+      ok = exchange_wait<2 * kPerLane>(
+               state, tag, mask,
+               [&](uint32_t i) {
+                 return entry + size_t{round + lane + 32u * (i >> 1)} * qd::kSpreadWords +
+                        ((i & 1u) != 0u ? dim : qd::kHeadSize);
+               },
+               v) &&
+           ok;
+      if (!__all_sync(kFullMask, ok)) {
+        break;
+      }
+#pragma unroll
+      for (uint32_t k = 0; k < kPerLane; ++k) {
+        merge_partial(m, l, x, y, v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      }
+    }
+    if (!__all_sync(kFullMask, ok)) {
+      ok = false;
+      break;
+    }
+#pragma unroll
+    for (uint32_t offset = 16; offset != 0; offset >>= 1) {
+      merge_partial(m, l, x, y, __shfl_xor_sync(kFullMask, m, offset),
+                    __shfl_xor_sync(kFullMask, l, offset), __shfl_xor_sync(kFullMask, x, offset),
+                    __shfl_xor_sync(kFullMask, y, offset));
+    }
+    if (lane == 0) {
+      const float first = x / l, second = y / l;
+      dev::exchange_store2(outputs + head * qd::kHeadSize + dim, first, second, tag);
+      *reinterpret_cast<float2 *>(c->query + group * kGroupColumns + head * qd::kHeadSize +
+                                  dim) = make_float2(first, second);
+    }
+  }
+  if (__syncthreads_or(ok ? 0 : 1) != 0) {
+    b.failed = true;
+  }
+}
+
 __device__ void fused_attention(QwenBlock &b, sg::State *state, qd::Context *c,
                                 uint32_t layer) {
   issue_deferred_refills(b); // gate/up units the last down stage postponed
   const uint32_t positions = b.kv_length + 1u;
+  if (b.spread_attention) {
+    group_attention(b, state, c, layer);
+    if (b.failed) {
+      return;
+    }
+    trace_mark(b, 3);
+    spread_combine(b, state, c);
+    trace_mark(b, 11);
+    return;
+  }
   if (!b.split_attention) {
     return; // computed per block inside the o_proj stage
   }
@@ -2187,6 +2344,7 @@ __device__ bool fused_possible(const sg::ResidentArgs &args, uint32_t workers) {
   // Program 1 or 2), so the residual it starts from is in global memory.
   if (workspace == nullptr || workspace->magic != qd::kWorkspaceMagic ||
       workspace->worker_capacity < max(workers, 2u) || workspace->exchange == nullptr ||
+      workspace->attention_words == nullptr || !aligned16(workspace->attention_words) ||
       workspace->kv_maps == nullptr ||
       (reinterpret_cast<uintptr_t>(workspace->kv_maps) & 63u) != 0 ||
       !aligned16(workspace->exchange) || workers < 2u || workers > kDownUnits ||
@@ -2246,6 +2404,21 @@ __device__ void clear_exchange() {
       index = qd::kExchangeDown + parity * qd::kHiddenSize + r.of[kDown].begin + k;
     }
     x[index] = 0;
+  }
+  // Spread attention: this block's partial states and the outputs of its
+  // combine items (see spread_combine), both parities.
+  uint64_t *partial = block_config.attention_words + size_t{block_config.worker} * qd::kSpreadWords;
+  for (uint32_t i = threadIdx.x; i < qd::kSpreadWords; i += kThreads) {
+    partial[i] = 0;
+    partial[size_t{block_config.workers} * qd::kSpreadWords + i] = 0;
+  }
+  const uint32_t size = block_config.group_size;
+  const uint32_t lane = threadIdx.x & 31u;
+  for (uint32_t item = (size - 1u - block_config.group_rank) * kWarps + (threadIdx.x >> 5u);
+       lane < 4u && item < kGroupColumns / 2u; item += kWarps * size) {
+    // lane: parity * 2 + which of the item's two dims
+    x[qd::kExchangeAttention + (lane >> 1) * qd::kQuerySize + block_config.group * kGroupColumns +
+      (item / 32u) * qd::kHeadSize + 2u * (item % 32u) + (lane & 1u)] = 0;
   }
 }
 
@@ -2310,6 +2483,8 @@ template <bool kStageProfile> struct QwenWorkloadT {
       k.contexts = static_cast<const qd::Context *>(args.context);
       k.workspace = k.contexts[0].tail->workspace;
       k.group = attention_group(k.worker, k.workers);
+      k.group_rank = group_rank(k.worker, k.workers);
+      k.group_size = group_size(k.group, k.workers);
       k.group_writer = k.worker == 0 || k.worker == attention_split(k.workers);
       if (blockIdx.x == 0 && k.workspace != nullptr) {
         k.workspace->reserved[0] = fused ? 1u : 2u; // which path ran
@@ -2318,6 +2493,7 @@ template <bool kStageProfile> struct QwenWorkloadT {
         k.shared = s;
         k.lm_head = k.contexts[0].tail->lm_head_weight;
         k.exchange = k.workspace->exchange;
+        k.attention_words = k.workspace->attention_words;
         k.kv_maps = static_cast<const unsigned char *>(k.workspace->kv_maps);
         k.logits = k.workspace->logits;
         k.layers = k.contexts[0].layer_count;
@@ -2439,7 +2615,9 @@ template <bool kStageProfile> struct QwenWorkloadT {
                              block_config.base_token;
       b.position = block_config.base_position + static_cast<uint32_t>(tokens);
       b.kv_length = block_config.base_kv_length + static_cast<uint32_t>(tokens);
-      b.split_attention = !use_local_attention(b.kv_length + 1u);
+      const AttentionMode mode = attention_mode(b.kv_length + 1u, block_config.workers);
+      b.split_attention = mode == AttentionMode::split;
+      b.spread_attention = mode == AttentionMode::spread;
       if (program == 1) {
         // Completed in this Program's residual_advance stage, read after the
         // block syncs of its final barrier.

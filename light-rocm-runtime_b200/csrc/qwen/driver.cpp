@@ -371,6 +371,9 @@ void init_workspace(lr_device_t device, void *workspace, uint64_t bytes, uint32_
   header.exchange = reinterpret_cast<uint64_t *>(base + at); // zero-filled above
   at += size_t{qd::kExchangeWords} * sizeof(uint64_t);
   at = (at + 255) / 256 * 256;
+  header.attention_words = reinterpret_cast<uint64_t *>(base + at);
+  at += 2u * size_t{capacity} * qd::kSpreadWords * sizeof(uint64_t);
+  at = (at + 255) / 256 * 256;
   std::vector<unsigned char> maps(size_t{qd::kWorkspaceMapLayers} * 2u * qd::kTensorMapBytes, 0);
   for (size_t layer = 0; layer < caches.size(); ++layer) {
     for (uint32_t which = 0; which < 2; ++which) {

@@ -3,7 +3,8 @@
 // exactly one owner, gate/up balancing keeps per-block layer bytes close to the
 // mean, even_owner inverts even_range, and the producer's cyclic stream visits
 // exactly the units the compiled stages consume, in the same order (also when
-// each ring slot advances its own stream position by the ring depth).
+// each ring slot advances its own stream position by the ring depth), and
+// spread attention's position slices tile each KV group's cache.
 #include "lrrt/qwen/resident_schedule.hpp"
 
 #include <algorithm>
@@ -61,7 +62,55 @@ static std::vector<uint32_t> consumer_tags(const r::UnitRanges &ranges, uint32_t
   return tags;
 }
 
+// Spread attention: for every worker count and context length the mode
+// picks, each group's slices tile the cached rows [0, positions - 1) in block
+// order, exactly one block takes the current position, and no slice needs
+// more than the three KV units of a layer.
+static void check_spread_slices() {
+  for (uint32_t workers : {2u, 3u, 7u, 64u, 147u, 148u, 256u}) {
+    const uint32_t limit = r::kKvUnits * r::kKvUnitPositions * (workers / 2u);
+    expect(r::attention_mode(r::kLocalAttentionLimit, workers) == r::AttentionMode::local,
+           "local up to the limit", workers);
+    for (uint32_t positions = r::kLocalAttentionLimit + 1u; positions <= limit + 2u;
+         positions += positions < 400u ? 1u : 97u) {
+      const r::AttentionMode mode = r::attention_mode(positions, workers);
+      expect(mode == (positions <= limit ? r::AttentionMode::spread : r::AttentionMode::split),
+             "spread up to three units per block", workers, positions);
+      if (mode != r::AttentionMode::spread) {
+        continue;
+      }
+      for (uint32_t group = 0; group < 2; ++group) {
+        const uint32_t size = r::group_size(group, workers);
+        uint32_t next = 0, owners = 0;
+        for (uint32_t rank = 0; rank < size; ++rank) {
+          const r::SpreadSlice slice = r::spread_slice(positions, rank, size);
+          expect(slice.first == next || slice.rows == 0, "slices contiguous", workers,
+                 positions, rank);
+          expect(slice.rows <= r::kKvUnits * r::kKvUnitPositions, "three units", workers,
+                 positions, rank);
+          next = slice.rows != 0 ? slice.first + slice.rows : next;
+          owners += slice.current ? 1u : 0u;
+          expect(!slice.current || slice.first + slice.rows == positions - 1u,
+                 "current position ends the slice", workers, positions, rank);
+        }
+        expect(next == positions - 1u, "slices cover the cached rows", workers, positions);
+        expect(owners == 1u, "one block takes the current position", workers, positions);
+      }
+    }
+  }
+  for (uint32_t workers = 2; workers <= 300; ++workers) {
+    for (uint32_t worker = 0; worker < workers; ++worker) {
+      const uint32_t group = r::attention_group(worker, workers);
+      const uint32_t rank = r::group_rank(worker, workers);
+      expect(rank < r::group_size(group, workers), "rank inside its group", workers, worker);
+      expect(worker == (group == 0 ? rank : r::attention_split(workers) + rank),
+             "rank inverts", workers, worker);
+    }
+  }
+}
+
 int main() {
+  check_spread_slices();
   const uint32_t worker_counts[] = {1, 2, 3, 7, 64, 147, 148, 256};
   const uint32_t vocabs[] = {1, 7, 64, 4096, 151936};
   for (uint32_t workers : worker_counts) {

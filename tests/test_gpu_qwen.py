@@ -200,8 +200,9 @@ def test_config1_every_logit(gpu):
 @pytest.mark.gpu
 def test_config3_full_size(gpu):
     """BASELINE config 3 at full size: 24 layers, vocab 151936, KV rows
-    0..4095 ~ N(0, 1), 256 greedy tokens (split attention over the blocks)
-    against the oracle: tokens, DecodeState, logit, every layer's KV rows."""
+    0..4095 ~ N(0, 1), 256 greedy tokens (attention spread over each KV
+    group's blocks) against the oracle: tokens, DecodeState, logit, every
+    layer's KV rows."""
     O.set_threads(O.max_threads())
     model, oracle, _, _ = build_pair(seed=1, layers=24, vocab=151936, capacity=4360,
                                      max_tokens=256)
@@ -220,16 +221,40 @@ def test_config3_full_size(gpu):
 
 
 @pytest.mark.gpu
-def test_long_context_split_attention(gpu):
-    """4096 pre-filled positions: the attention stage runs split over the
-    resident blocks and combines partial softmax states."""
+@pytest.mark.parametrize("workers", [0, 16], ids=["spread", "split"])
+def test_long_context_attention(gpu, workers):
+    """4096 pre-filled positions. With one block per SM each KV group's
+    blocks take a slice of the positions each and merge their partial
+    softmax states through the exchange (spread); with 16 blocks a slice
+    would exceed three KV units, so the attention stage runs split over the
+    blocks between grid barriers."""
     model, oracle, _, _ = build_pair(seed=5, layers=2, vocab=2048, capacity=4104,
-                                     max_tokens=8)
+                                     max_tokens=8, worker_count=workers)
     prefill_kv(model, oracle, 5, 2, 4096)
     hidden = S.hidden(5)
     model.set_hidden(hidden)
     oracle.decode(hidden, 4096, 8)
     state, tokens = model.decode(4096, 8)
+    assert state.fused_path == 1
+    compare_run(model, oracle, state, tokens)
+    model.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("workers,start", [(0, 160), (4, 330)],
+                         ids=["local-to-spread", "spread-to-split"])
+def test_attention_mode_changes_within_a_run(gpu, workers, start):
+    """One launch whose context grows across an attention-mode boundary:
+    local to spread at 170 positions (one block per SM), spread to split
+    past 336 positions (4 blocks, two per KV group). Every step matches the
+    oracle."""
+    model, oracle, _, _ = build_pair(seed=11, layers=2, vocab=2048, capacity=start + 24,
+                                     max_tokens=16, worker_count=workers)
+    prefill_kv(model, oracle, 11, 2, start)
+    hidden = S.hidden(11)
+    model.set_hidden(hidden)
+    oracle.decode(hidden, start, 16)
+    state, tokens = model.decode(start, 16)
     assert state.fused_path == 1
     compare_run(model, oracle, state, tokens)
     model.close()
