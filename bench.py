@@ -30,7 +30,7 @@ Reported (one JSON line, rank 0):
               microseconds per token and per grid barrier
 Weights (2 GB) exceed L2 (126 MB), so no flush is needed between steps.
 
---profile-case prefill|batch runs one of the profiler workloads instead (the
+--profile-case prefill|batch|long runs one of the profiler workloads instead (the
 measured launches inside cuProfilerStart/Stop, for
 `ncu --profile-from-start off`), and prints no bench line.
 
@@ -79,7 +79,7 @@ def parse_args():
                         help="tokens per step (smaller only for profiler captures)")
     parser.add_argument("--no-extra", action="store_true",
                         help="skip the config-5 prefill and config-4 batched lines")
-    parser.add_argument("--profile-case", choices=["prefill", "batch"],
+    parser.add_argument("--profile-case", choices=["prefill", "batch", "long"],
                         help="run a profiler workload instead of the bench")
     parser.add_argument("--layers", type=int, default=LAYERS, help="profile cases only")
     parser.add_argument("--prompt", type=int, default=PREFILL_PROMPT, help="profile cases only")
@@ -576,7 +576,27 @@ def profile_case(args) -> None:
         return model
 
     cuda = ctypes.CDLL("libcuda.so.1")
-    if args.profile_case == "prefill":
+    if args.profile_case == "long":
+        # Config 3's resident decode: KV rows 0..context-1 pre-filled, one
+        # warm-up launch, then --case-steps tokens at positions context...
+        weights, tail = S.model(SEED, args.layers, args.vocab, True)
+        model = Q.Model(Q.ModelConfig(layer_count=args.layers, vocab_size=args.vocab,
+                                      cache_capacity=args.context + 2 * args.case_steps + 8,
+                                      max_tokens_per_run=args.case_steps))
+        for i, w in enumerate(weights):
+            model.set_layer(i, w)
+        model.set_tail(tail["final_norm"], tail["lm_head"])
+        for layer, (keys, values) in enumerate(S.kv_prefill(SEED, args.layers, args.context)):
+            model.set_kv(layer, 0, keys, values)
+        model.set_hidden(S.hidden(SEED))
+        model.decode(args.context, args.case_steps)
+        model.set_hidden(S.hidden(SEED))
+        cuda.cuProfilerStart()
+        state, _ = model.decode(args.context, args.case_steps)
+        cuda.cuProfilerStop()
+        if state.status != 2 or state.fused_path != 1:
+            raise RuntimeError(f"long-context case: status {state.status}")
+    elif args.profile_case == "prefill":
         model = build(args.prompt, 1, args.prompt)
         prompt = S.prompt(3, args.prompt, args.vocab)
         model.prefill(prompt, Q.PREFILL_TF32X3)  # warm-up: weight split, maps

@@ -1175,10 +1175,6 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
       const float c = row_dot(slot + (pair + 4u) * qd::kHiddenSize, x, lane);
       valid = row == pair || row == pair + 4u;
       value = row == pair ? a : c;
-      if (lane == 0 && (atomicAdd(&block_config.shared->pair_done[n % kSlots], 1u) &
-                        (kPairWarps - 1u)) == kPairWarps - 1u) {
-        release_unit(b, n); // the unit's last warp refills the slot
-      }
     } else {
       // Rows past `rows` (the LM head's last unit) hold stale bytes; their
       // sums stay in their own lanes and are flagged invalid.
@@ -1202,11 +1198,14 @@ __device__ bool consume_units(QwenBlock &b, sg::State *state, uint32_t kind,
       // The shuffles complete every lane's shared-memory reads of the slot.
       value = reduce_rows8(a, lane);
       valid = row < rows;
-      if (lane == 0) {
-        release_unit(b, n);
-      }
     }
+    // The epilogue's exchange stores go first: the refill's copy issue can
+    // hold its lane for several hundred nanoseconds.
     epilogue(u, row, value, valid, extra);
+    if (lane == 0 && (!split || (atomicAdd(&block_config.shared->pair_done[n % kSlots], 1u) &
+                                 (kPairWarps - 1u)) == kPairWarps - 1u)) {
+      release_unit(b, n); // (split: the unit's last warp) refills the slot
+    }
     if (lane == 0 && block_config.unit_trace != nullptr) {
       trace_unit(b, n, t_before, t_ready, dev::global_timer_ns());
     }
