@@ -760,12 +760,17 @@ __device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
 // consumer of the slot's previous unit.
 __shared__ StreamPosition slot_position[kSlots];
 
-// Gate/up refills the down stage postpones: deferred_unit[s] is the sequence
-// number slot s is still to receive (UINT32_MAX: none). Gate/up units are
-// first needed in the next gate/up stage; issued at the end of the down
-// stage, their bytes would sit in front of the next layer's first exchanges
-// in the memory queues, so they are issued in the attention stage instead
-// (issue_deferred_refills).
+// Postponed refills: deferred_unit[s] is the sequence number slot s is still
+// to receive (UINT32_MAX: none).
+//  - Gate/up units the down stage would refill are first needed in the next
+//    gate/up stage; issued at the end of the down stage, their bytes would
+//    sit in front of the next layer's first exchanges in the memory queues,
+//    so they are issued in the attention stage instead
+//    (issue_deferred_refills).
+//  - o_proj units' refills (not needed by a later unit of the same stage)
+//    are issued by the MLP norm's last warp, which has no hidden values to
+//    wait for: a copy issue holds its lane for up to a microsecond, and the
+//    o_proj warps go on to the stage's final block sync.
 __shared__ uint32_t deferred_unit[kSlots];
 
 // Issues the copies of stream unit `n` into its ring slot (one lane). The
@@ -1035,6 +1040,14 @@ __device__ void fused_norm(QwenBlock &b, sg::State *state, const qd::Context *c,
                       (h.w + v[3]) + v[7]);
     }
     reinterpret_cast<float4 *>(s->hidden)[t] = h;
+  }
+  if (source == HiddenSource::attention && threadIdx.x == kContextCopyThread) {
+    for (uint32_t slot = 0; slot < kSlots; ++slot) {
+      if (deferred_unit[slot] != UINT32_MAX) {
+        issue_unit(b, deferred_unit[slot]);
+        deferred_unit[slot] = UINT32_MAX;
+      }
+    }
   }
   if (source == HiddenSource::attention && threadIdx.x >= kContextCopyThread) {
     wait_prefetched_context(); // the next step's Context (Program 1's begin)
@@ -1379,9 +1392,14 @@ __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32
     if (lane == 0) {
       const uint32_t out_row = (u % kOGroupUnits) * kSlotRows + warp;
       dev::exchange_store(words + (u / kOGroupUnits) * qd::kHiddenSize + out_row, a, tag);
-      // The unit's eighth warp refills the slot.
+      // The unit's eighth warp hands the slot's refill to the MLP norm's
+      // last warp, which waits for the o_proj exchange meanwhile.
       if ((atomicAdd(&s->rows_done[n % kSlots], 1u) & (kWarps - 1u)) == kWarps - 1u) {
-        release_unit(b, n);
+        if (n + kSlots < b.consumed + (range.end - range.begin)) {
+          release_unit(b, n); // a later unit of this stage takes the slot
+        } else {
+          deferred_unit[n % kSlots] = n + kSlots;
+        }
       }
     }
   }
