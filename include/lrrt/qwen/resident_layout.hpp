@@ -18,6 +18,8 @@ constexpr uint32_t kSlotBytes = kSlotRows * kRowBytes;               // 28672
 constexpr uint32_t kDownRowBytes = kIntermediateSize * sizeof(float); // 19456
 constexpr uint32_t kGroupColumns = kQueriesPerKvHead * kHeadSize;    // 448
 constexpr uint32_t kHalfRowBytes = kGroupColumns * sizeof(float);    // 1792
+constexpr uint32_t kORows = kSlotBytes / kHalfRowBytes;              // 16 o_proj rows per unit
+constexpr uint32_t kOBoxColumns = kGroupColumns / 2u;                // 224: two boxes per unit
 constexpr uint32_t kRingBytes = kSlots * kSlotBytes;
 constexpr uint32_t kBlockThreads = lrrt::persistent_graph::kWorkerThreads;
 

@@ -8,9 +8,10 @@
 //   KV      3 units per block (not partitioned: every block reads its own
 //                    KV group): cached K and V rows of positions 56j..56j+55,
 //                    loaded only for the positions the step attends to
-//   OUT   224 units: 8 consecutive o_proj rows restricted to the 448 input
-//                    columns of one KV group (units 0-111 group 0, 112-223
-//                    group 1); o_proj is split along its input over the groups
+//   OUT   112 units: 16 consecutive o_proj rows restricted to the 448 input
+//                    columns of one KV group (units 0-55 group 0, 56-111
+//                    group 1), copied as two 224-column 2-D tensor boxes;
+//                    o_proj is split along its input over the groups
 //   GU   1216 units: gate rows 4u..4u+3 followed by up rows 4u..4u+3
 //   DOWN  896 units: one 4864-float down_proj row
 //   LM   ceil(V/8) units: 8 LM-head rows (the last may be shorter)
@@ -48,9 +49,10 @@ static_assert(kKvUnits * kKvUnitPositions + 1u >= kLocalAttentionLimit,
 constexpr uint32_t kQkvUnits = kPackedQkvSize / kSlotRows;     // 144
 constexpr uint32_t kQUnits = kQuerySize / kSlotRows;           // 112
 constexpr uint32_t kKUnits = kKvSize / kSlotRows;              // 16
-constexpr uint32_t kOGroupUnits = kHiddenSize / kSlotRows;     // 112 per KV group
-constexpr uint32_t kOUnits = kKvHeads * kOGroupUnits;          // 224
-constexpr uint32_t kOUnitBytes = kSlotRows * kHalfRowBytes;    // 14336
+constexpr uint32_t kOGroupUnits = kHiddenSize / kORows;        // 56 per KV group
+constexpr uint32_t kOUnits = kKvHeads * kOGroupUnits;          // 112
+constexpr uint32_t kOUnitBytes = kORows * kHalfRowBytes;       // 28672
+static_assert(kHiddenSize % kORows == 0 && kOUnitBytes <= kSlotBytes);
 constexpr uint32_t kGuRowsPerUnit = kSlotRows / 2u;            // 4
 constexpr uint32_t kGuUnits = kIntermediateSize / kGuRowsPerUnit; // 1216
 constexpr uint32_t kDownUnits = kHiddenSize;                   // 896

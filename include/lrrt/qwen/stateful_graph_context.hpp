@@ -146,10 +146,13 @@ constexpr uint32_t kSpreadWords = kQueriesPerKvHead * kAttentionPartialStride; /
 //  exchange: [kExchangeWords] 64-bit words (see above)
 //  attention_words: [2][worker_capacity][kSpreadWords] exchange words, by step
 //    parity and block (spread attention partial states)
-//  kv_maps: [kWorkspaceMapLayers][2] CUtensorMap (128 B each: key cache,
-//    value cache of each layer; dims {kKvSize, cache_capacity}, box 32
-//    columns x 56 rows, 128-byte swizzle) for the fused path's KV ring units
+//  kv_maps: [kWorkspaceMapLayers][3] CUtensorMap (128 B each: key cache,
+//    value cache of each layer, dims {kKvSize, cache_capacity}, box 32
+//    columns x 56 rows, 128-byte swizzle, for the fused path's KV ring
+//    units; o_proj weight, dims {kHiddenSize, kHiddenSize}, box 224 columns x
+//    16 rows, no swizzle, for its OUT units)
 constexpr uint32_t kWorkspaceMapLayers = 48;
+constexpr uint32_t kWorkspaceMapsPerLayer = 3; // key cache, value cache, o_proj
 constexpr uint32_t kTensorMapBytes = 128;
 struct alignas(16) Workspace {
   uint32_t magic;
@@ -174,7 +177,7 @@ constexpr size_t workspace_bytes(uint32_t worker_capacity) {
                     sizeof(uint32_t) +
          256u + size_t{kExchangeWords} * sizeof(uint64_t) + 256u +
          2u * size_t{worker_capacity} * kSpreadWords * sizeof(uint64_t) + 256u +
-         size_t{kWorkspaceMapLayers} * 2u * kTensorMapBytes + 256u;
+         size_t{kWorkspaceMapLayers} * kWorkspaceMapsPerLayer * kTensorMapBytes + 256u;
 }
 
 // Model tail shared by every layer Context.

@@ -554,7 +554,7 @@ struct QwenConfig {
   const qd::Context *contexts;
   qd::Workspace *workspace;
   uint64_t *exchange;       // workspace exchange words
-  const unsigned char *kv_maps; // [layer][K, V] tensor maps of the KV caches
+  const unsigned char *kv_maps; // [layer][K cache, V cache, o_proj] tensor maps
   float *logits;            // optional: every LM-head row of the step (test capture)
   const float *lm_head;
   uint32_t worker, workers, layers, vocab, lm_units;
@@ -731,14 +731,8 @@ __device__ UnitSource unit_source(const QwenBlock &b, const StreamCursor &c) {
     return {first, first + size_t{qd::kRotarySize} * qd::kHiddenSize, 4u * kRowBytes,
             4u * kRowBytes, 1, 0};
   }
-  case kOut: {
-    // Rows 8v..8v+7 of o_proj, input columns of KV group u / 112 only.
-    const uint32_t group = u / kOGroupUnits;
-    const uint32_t row = (u % kOGroupUnits) * kSlotRows;
-    return {w[kMo] + size_t{row} * qd::kHiddenSize + group * kGroupColumns, nullptr,
-            kHalfRowBytes, 0, kSlotRows, qd::kHiddenSize};
-  }
-  case kKv: // filled by tensor copies in issue_unit
+  case kOut: // filled by tensor copies in issue_unit
+  case kKv:
     return {nullptr, nullptr, 0, 0, 1, 0};
   case kGateUp:
     return {w[kMgate] + size_t{u} * kGuRowsPerUnit * qd::kHiddenSize,
@@ -793,6 +787,20 @@ __device__ __noinline__ void issue_unit(const QwenBlock &b, uint32_t n) {
   slot_position[slot] = next;
   s->unit_tag[slot] = make_tag(c.kind, c.layer, c.unit);
   *reinterpret_cast<volatile uint32_t *>(&s->sequence[slot]) = n;
+  if (c.kind == kOut) {
+    // o_proj rows 16v..16v+15 (v = unit % 56), input columns of KV group
+    // unit / 56: two 224-column boxes of the layer's o_proj tensor map,
+    // landing as [box][16 rows][224 floats].
+    dev::mbarrier_arrive_expect_tx(&s->full[slot], kOUnitBytes);
+    const unsigned char *map = block_config.kv_maps +
+                               (size_t{c.layer} * qd::kWorkspaceMapsPerLayer + 2u) *
+                                   qd::kTensorMapBytes;
+    const uint32_t x = (c.unit / kOGroupUnits) * kGroupColumns;
+    const uint32_t y = (c.unit % kOGroupUnits) * kORows;
+    dev::tensor_load_2d(destination, map, x, y, &s->full[slot]);
+    dev::tensor_load_2d(destination + kOUnitBytes / 2u, map, x + kOBoxColumns, y, &s->full[slot]);
+    return;
+  }
   if (c.kind == kKv) {
     // Cached rows first + 56j .. first + 56j + 55 of this block's KV group
     // and attention slice, for the token this layer's unit belongs to (one
@@ -804,7 +812,8 @@ __device__ __noinline__ void issue_unit(const QwenBlock &b, uint32_t n) {
     const bool load = c.unit * kKvUnitPositions < slice.rows;
     dev::mbarrier_arrive_expect_tx(&s->full[slot], load ? kSlotBytes : 0u);
     if (load) {
-      const unsigned char *maps = block_config.kv_maps + size_t{c.layer} * 2u * qd::kTensorMapBytes;
+      const unsigned char *maps =
+          block_config.kv_maps + size_t{c.layer} * qd::kWorkspaceMapsPerLayer * qd::kTensorMapBytes;
       const uint32_t x = block_config.group * qd::kHeadSize;
       const uint32_t y = slice.first + c.unit * kKvUnitPositions;
       constexpr uint32_t kBox = kSlotBytes / 4u; // 32 columns x 56 rows
@@ -1355,13 +1364,17 @@ __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32
     }
     __syncthreads();
   }
-  constexpr uint32_t kVectors = kGroupColumns / 4u; // 112 float4 per half row
+  constexpr uint32_t kVectors = kGroupColumns / 4u;   // 112 float4 per half row
+  constexpr uint32_t kBoxVectors = kOBoxColumns / 4u; // 56 per tensor box row
   float4 x[4];
+  uint32_t offset[4]; // float4 offset of input vector v = lane + 32j in a unit's row 0
 #pragma unroll
   for (uint32_t j = 0; j < 4; ++j) {
     const uint32_t v = lane + 32u * j;
     x[j] = v < kVectors ? reinterpret_cast<const float4 *>(s->input)[v]
                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    offset[j] = v < kBoxVectors ? v : kORows * kBoxVectors + (v - kBoxVectors);
+    static_assert(kORows % kWarps == 0, "every warp takes the same o_proj rows");
   }
   const UnitRange range = block_config.ranges.of[kOut];
   const uint32_t tag = b.step + 1u;
@@ -1375,23 +1388,37 @@ __device__ void fused_out(QwenBlock &b, sg::State *state, qd::Context *c, uint32
       ok = false;
       break;
     }
-    const float4 *row = reinterpret_cast<const float4 *>(slot + warp * kGroupColumns);
-    float a = 0.0f;
+    // Warp w computes rows w, w + 8, ... of the unit ([box][kORows][56 float4]).
+    constexpr uint32_t kRowsPerWarp = kORows / kWarps;
+    float a[kRowsPerWarp];
+#pragma unroll
+    for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+      a[r] = 0.0f;
+    }
 #pragma unroll
     for (uint32_t j = 0; j < 4; ++j) {
-      const uint32_t v = lane + 32u * j;
-      if (v < kVectors) {
-        const float4 w = row[v];
-        a = fmaf(w.x, x[j].x, a);
-        a = fmaf(w.y, x[j].y, a);
-        a = fmaf(w.z, x[j].z, a);
-        a = fmaf(w.w, x[j].w, a);
+      if (lane + 32u * j < kVectors) {
+#pragma unroll
+        for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+          const float4 w = reinterpret_cast<const float4 *>(slot)[(warp + kWarps * r) * kBoxVectors + offset[j]];
+          a[r] = fmaf(w.x, x[j].x, a[r]);
+          a[r] = fmaf(w.y, x[j].y, a[r]);
+          a[r] = fmaf(w.z, x[j].z, a[r]);
+          a[r] = fmaf(w.w, x[j].w, a[r]);
+        }
       }
     }
-    a = warp_all_sum(a); // completes the warp's reads of the slot
+#pragma unroll
+    for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+      a[r] = warp_all_sum(a[r]); // the shuffles complete the warp's reads of the slot
+    }
     if (lane == 0) {
-      const uint32_t out_row = (u % kOGroupUnits) * kSlotRows + warp;
-      dev::exchange_store(words + (u / kOGroupUnits) * qd::kHiddenSize + out_row, a, tag);
+      uint64_t *group_words = words + (u / kOGroupUnits) * qd::kHiddenSize;
+#pragma unroll
+      for (uint32_t r = 0; r < kRowsPerWarp; ++r) {
+        dev::exchange_store(group_words + (u % kOGroupUnits) * kORows + warp + kWarps * r, a[r],
+                            tag);
+      }
       // The unit's eighth warp hands the slot's refill to the MLP norm's
       // last warp, which waits for the o_proj exchange meanwhile.
       if ((atomicAdd(&s->rows_done[n % kSlots], 1u) & (kWarps - 1u)) == kWarps - 1u) {
@@ -2393,10 +2420,10 @@ __device__ void clear_exchange() {
   uint64_t *x = block_config.exchange;
   const UnitRanges &r = block_config.ranges;
   const uint32_t qkv = r.of[kQkv].end - r.of[kQkv].begin;   // 8 rows each
-  const uint32_t out = r.of[kOut].end - r.of[kOut].begin;   // 8 rows each
+  const uint32_t out = r.of[kOut].end - r.of[kOut].begin;   // kORows rows each
   const uint32_t gu = r.of[kGateUp].end - r.of[kGateUp].begin; // 4 rows each
   const uint32_t down = r.of[kDown].end - r.of[kDown].begin;
-  const uint32_t words = 8u * qkv + 8u * out + 4u * gu + down;
+  const uint32_t words = 8u * qkv + kORows * out + 4u * gu + down;
   for (uint32_t i = threadIdx.x; i < 2u * words; i += kThreads) {
     const uint32_t parity = i / words;
     uint32_t k = i % words;
@@ -2409,11 +2436,11 @@ __device__ void clear_exchange() {
                                               : qd::kQuerySize + qd::kKvSize;
       index = qd::kExchangeQkv + parity * qd::kPackedQkvSize + base +
               (row < 4u ? rows.first : rows.second);
-    } else if ((k -= 8u * qkv) < 8u * out) {
-      const uint32_t u = r.of[kOut].begin + k / 8u;
+    } else if ((k -= 8u * qkv) < kORows * out) {
+      const uint32_t u = r.of[kOut].begin + k / kORows;
       index = qd::kExchangeOut + parity * qd::kKvHeads * qd::kHiddenSize +
-              (u / kOGroupUnits) * qd::kHiddenSize + (u % kOGroupUnits) * kSlotRows + k % 8u;
-    } else if ((k -= 8u * out) < 4u * gu) {
+              (u / kOGroupUnits) * qd::kHiddenSize + (u % kOGroupUnits) * kORows + k % kORows;
+    } else if ((k -= kORows * out) < 4u * gu) {
       index = qd::kExchangeAct + parity * qd::kIntermediateSize +
               (r.of[kGateUp].begin + k / 4u) * kGuRowsPerUnit + k % 4u;
     } else {

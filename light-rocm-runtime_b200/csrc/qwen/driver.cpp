@@ -330,17 +330,20 @@ void zero_fill(lrrt::DeviceBuffer &buffer) {
   lrrt::copy_to_device(buffer, zeros);
 }
 
-// One layer's KV caches as the fused path's tensor maps see them.
+// One layer's KV caches and o_proj weight as the fused path's tensor maps
+// see them.
 struct KvCacheView {
   const float *keys;
   const float *values;
-  uint32_t capacity; // rows of [capacity][128] floats
+  uint32_t capacity;       // rows of [capacity][128] floats
+  const float *out_weight; // [896][896]
 };
 
 // Zero-fills a workspace allocation of `bytes` (>= workspace_bytes(capacity))
-// and writes its header, array pointers and the KV caches' 2-D tensor maps
-// (boxes of 32 columns x 56 rows, 128-byte swizzle: the fused path's KV ring
-// units).
+// and writes its header, array pointers and each layer's 2-D tensor maps: the
+// KV caches (boxes of 32 columns x 56 rows, 128-byte swizzle: the fused
+// path's KV ring units) and the o_proj weight (boxes of 224 columns x 16
+// rows: an OUT unit is two of them).
 void init_workspace(lr_device_t device, void *workspace, uint64_t bytes, uint32_t capacity,
                     const std::vector<KvCacheView> &caches) {
   if (workspace == nullptr || capacity < 2u || bytes < qd::workspace_bytes(capacity) ||
@@ -374,7 +377,8 @@ void init_workspace(lr_device_t device, void *workspace, uint64_t bytes, uint32_
   header.attention_words = reinterpret_cast<uint64_t *>(base + at);
   at += 2u * size_t{capacity} * qd::kSpreadWords * sizeof(uint64_t);
   at = (at + 255) / 256 * 256;
-  std::vector<unsigned char> maps(size_t{qd::kWorkspaceMapLayers} * 2u * qd::kTensorMapBytes, 0);
+  std::vector<unsigned char> maps(
+      size_t{qd::kWorkspaceMapLayers} * qd::kWorkspaceMapsPerLayer * qd::kTensorMapBytes, 0);
   for (size_t layer = 0; layer < caches.size(); ++layer) {
     for (uint32_t which = 0; which < 2; ++which) {
       const float *cache = which == 0 ? caches[layer].keys : caches[layer].values;
@@ -396,8 +400,29 @@ void init_workspace(lr_device_t device, void *workspace, uint64_t bytes, uint32_
         throw std::runtime_error("cuTensorMapEncodeTiled failed for a KV cache map (" +
                                  std::to_string(status) + ")");
       }
-      std::memcpy(maps.data() + (layer * 2u + which) * qd::kTensorMapBytes, &map, sizeof(map));
+      std::memcpy(maps.data() + (layer * qd::kWorkspaceMapsPerLayer + which) * qd::kTensorMapBytes,
+                  &map, sizeof(map));
     }
+    const float *out = caches[layer].out_weight;
+    if (out == nullptr || (reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
+      throw std::invalid_argument("o_proj weight of layer " + std::to_string(layer) +
+                                  " is null or misaligned");
+    }
+    CUtensorMap map{};
+    const cuuint64_t dims[2] = {qd::kHiddenSize, qd::kHiddenSize};
+    const cuuint64_t strides[1] = {qd::kHiddenSize * sizeof(float)};
+    const cuuint32_t box[2] = {qd::resident::kOBoxColumns, qd::resident::kORows};
+    const cuuint32_t element_strides[2] = {1, 1};
+    const CUresult status = lrrt::qwen::prefill::detail::encode_tiled()(
+        &map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(out), dims, strides, box,
+        element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (status != CUDA_SUCCESS) {
+      throw std::runtime_error("cuTensorMapEncodeTiled failed for an o_proj map (" +
+                               std::to_string(status) + ")");
+    }
+    std::memcpy(maps.data() + (layer * qd::kWorkspaceMapsPerLayer + 2u) * qd::kTensorMapBytes,
+                &map, sizeof(map));
   }
   header.kv_maps = base + at;
   lrrt::check(lr_memcpy(device, base + at, maps.data(), maps.size(), LR_MEMCPY_HOST_TO_DEVICE),
@@ -482,7 +507,7 @@ void build_model(lrq_model_t &m) {
     for (uint32_t layer = 0; layer < c.layer_count; ++layer) {
       caches[layer] = {static_cast<const float *>(m.key_cache->data()) + layer * m.cache_floats(),
                        static_cast<const float *>(m.value_cache->data()) + layer * m.cache_floats(),
-                       c.cache_capacity};
+                       c.cache_capacity, m.layer_weight(layer, m.layout.o)};
     }
     init_workspace(m.device.get(), m.workspace->data(), m.workspace->size(), capacity, caches);
   }
@@ -1583,7 +1608,7 @@ LRRT_API lr_status_t lrq_workspace_init(lr_device_t device, void *workspace, uin
     std::vector<KvCacheView> caches(layer_count);
     for (uint32_t layer = 0; layer < layer_count; ++layer) {
       caches[layer] = {layers[layer].key_cache, layers[layer].value_cache,
-                       layers[layer].cache_capacity};
+                       layers[layer].cache_capacity, layers[layer].out_weight};
     }
     init_workspace(device, workspace, bytes, std::max(worker_count, 2u), caches);
   });
