@@ -377,22 +377,30 @@ __device__ void embedding_feedback(qd::Context *c, sg::State *state) {
   __shared__ uint32_t continue_with;
   qd::DecodeState *decode = c->tail->decode_state;
   if (threadIdx.x == 0) {
+    // Every field is read before any is written, so the loads are in flight
+    // together (one round trip instead of one per field).
     const uint32_t index = decode_field(&decode->generated_tokens);
     const uint32_t token = decode_field(&decode->sampled_token);
+    const uint32_t eos_token = decode_field(&decode->eos_token);
+    const uint32_t maximum = decode_field(&decode->maximum_tokens);
+    const uint32_t position = decode_field(&decode->token_position);
+    const uint32_t kv_length = decode_field(&decode->kv_length);
+    uint32_t predicate = state->predicate_value;
     c->tail->output_tokens[index] = token;
     const uint32_t generated = index + 1u;
     decode->generated_tokens = generated;
-    const bool eos = token == decode_field(&decode->eos_token);
-    const bool limit = generated >= decode_field(&decode->maximum_tokens);
+    const bool eos = token == eos_token;
+    const bool limit = generated >= maximum;
     if (eos || limit) {
       decode->stop_reason = static_cast<uint32_t>(
           eos ? qd::StopReason::eos_token : qd::StopReason::maximum_tokens);
       state->predicate_value = 1;
+      predicate = 1;
     } else {
-      decode->token_position = decode_field(&decode->token_position) + 1u;
-      decode->kv_length = decode_field(&decode->kv_length) + 1u;
+      decode->token_position = position + 1u;
+      decode->kv_length = kv_length + 1u;
     }
-    continue_with = state->predicate_value == 0 ? token : UINT32_MAX;
+    continue_with = predicate == 0 ? token : UINT32_MAX;
   }
   __syncthreads();
   if (continue_with != UINT32_MAX) {
