@@ -60,13 +60,20 @@ __device__ __forceinline__ void add_release(uint32_t *address, uint32_t value) {
 }
 
 // Wait limit helper: every spin in the resident kernels compares against a
-// deadline taken from the launch's wait limit.
+// deadline taken from the launch's wait limit. The clock starts at the first
+// check: a wait that never has to check (the common case) reads no timer, and
+// constructing one stalls no warp on a special-register read.
 struct Deadline {
-  uint64_t end_ns;
-  __device__ __forceinline__ explicit Deadline(uint32_t limit_ms)
-      : end_ns(global_timer_ns() + uint64_t{limit_ms} * 1000000ull) {}
+  mutable uint64_t end_ns;
+  uint32_t limit_ms;
+  __device__ __forceinline__ explicit Deadline(uint32_t limit) : end_ns(0), limit_ms(limit) {}
   __device__ __forceinline__ bool expired() const {
-    return global_timer_ns() > end_ns;
+    const uint64_t now = global_timer_ns();
+    if (end_ns == 0) {
+      end_ns = now + uint64_t{limit_ms} * 1000000ull;
+      return false;
+    }
+    return now > end_ns;
   }
 };
 
