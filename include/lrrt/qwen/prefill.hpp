@@ -248,16 +248,29 @@ struct TcGemmArgs {
 constexpr uint32_t kTcTileM = 128;
 constexpr uint32_t kTcTileK = 16;   // one 64-byte swizzle row of fp32
 constexpr uint32_t kTcThreads = 128;
-constexpr uint32_t kTcMaximumN = 256;
+constexpr uint32_t kTcMaximumN = 256;     // one MMA's N
 constexpr uint32_t kTcTmemColumns = 256;
+// Gate/up pair tiles wider than one MMA: kTcPairN accumulator columns (gate
+// then up, kTcPairN / 2 each, two MMAs per product), 512 TMEM columns. 4864
+// gate/up columns make 34 such tiles per 128-row band: the 511 rows of a
+// 512-token chunk fit one wave of 148 SMs (136 tiles) where 128 + 128 tiles
+// need 152.
+constexpr uint32_t kTcPairN = 288;
+constexpr uint32_t kTcPairTmemColumns = 512;
 
 LRRT_PREFILL_HD constexpr uint32_t tc_stage_bytes(uint32_t n) { return 2u * (kTcTileM + n) * kTcTileK * 4u; }
+// Up to 200 KB of stages (213 KB for the pair tiles: four 52 KB stages).
+LRRT_PREFILL_HD constexpr uint32_t tc_stage_budget(uint32_t n) {
+  return (n > kTcMaximumN ? 213u : 200u) * 1024u;
+}
 LRRT_PREFILL_HD constexpr uint32_t tc_stages(uint32_t n) {
-  return (200u * 1024u) / tc_stage_bytes(n) > 8u ? 8u : (200u * 1024u) / tc_stage_bytes(n);
+  return tc_stage_budget(n) / tc_stage_bytes(n) > 8u ? 8u : tc_stage_budget(n) / tc_stage_bytes(n);
 }
 LRRT_PREFILL_HD constexpr uint32_t tc_shared_bytes(uint32_t n) {
   return tc_stages(n) * tc_stage_bytes(n) + 1024u /* alignment */ + 256u /* barriers */;
 }
+static_assert(tc_stages(kTcPairN) == 4 && tc_shared_bytes(kTcPairN) <= 227u * 1024u,
+              "pair tiles: four stages within one block's shared memory");
 
 // Narrow GEMMs (at most kNarrowRows rows: batched decode, short chunks) swap
 // the operands: a tile is kNarrowTileN weight rows (the MMA's M) times the

@@ -244,9 +244,10 @@ LRRT_API lr_status_t lrq_model_prefill_at(lrq_model_t *model, const uint32_t *to
  * read and written (mode 0: c = acc + bias; 1: c += acc; 2: c = silu(gate) *
  * up). tile_columns 0 runs the FP32 SIMT kernels; 192, 224 or 256 runs the
  * 3xTF32 tensor-core kernel of that accumulator width (k a multiple of 16,
- * n of 32; swiglu: tile_columns 192 or 256 and n a multiple of half of it),
- * except that m <= 32 rows run the narrow swapped-operand kernels whatever
- * the tensor-core width (swiglu then takes any n).
+ * n of 32; swiglu: tile_columns 192 or 256 and n a multiple of half of it,
+ * or 288, the prefill's 144 + 144 gate/up pairs, for any n), except that
+ * m <= 32 rows run the narrow swapped-operand kernels whatever the
+ * tensor-core width (swiglu then takes any n).
  * Needs
  * lrq_model_enable_prefill; waits for the device.
  */

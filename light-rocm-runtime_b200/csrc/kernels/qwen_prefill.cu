@@ -254,6 +254,23 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
+// 16 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_load16(uint32_t address, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(address));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (uint32_t i = 0; i < 16; ++i) {
+    v[i] = __uint_as_float(r[i]);
+  }
+}
+
 // 32 consecutive accumulator columns of this thread's TMEM lane.
 __device__ __forceinline__ void tc_load32(uint32_t address, float (&v)[32]) {
   uint32_t r[32];
@@ -888,14 +905,22 @@ extern "C" __global__ void __launch_bounds__(256) prefill_split(pf::SplitArgs p)
 // epilogue, one accumulator row per thread. Every mbarrier wait is bounded;
 // on expiry the kernel records kTcErrorWaitTimeout, skips its stores, waits
 // (bounded) for its copies and MMAs in flight, frees TMEM and returns.
+// Pair tiles wider than one MMA (kN = kTcPairN, gate/up pairs only) issue
+// each product as two MMAs of N = kN / 2 into the two halves of the
+// accumulator.
 template <uint32_t kN>
 __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
+  constexpr bool kSplitMma = kN > pf::kTcMaximumN;
+  constexpr uint32_t kMmaN = kSplitMma ? kN / 2u : kN;
+  constexpr uint32_t kTmemColumns = kSplitMma ? pf::kTcPairTmemColumns : pf::kTcTmemColumns;
   constexpr uint32_t kStages = pf::tc_stages(kN);
   constexpr uint32_t kStageBytes = pf::tc_stage_bytes(kN);
   constexpr uint32_t kBytesA = pf::kTcTileM * pf::kTcTileK * 4u;
   constexpr uint32_t kBytesB = kN * pf::kTcTileK * 4u;
-  constexpr uint32_t kInstruction = tc_instruction<kN>();
-  static_assert(kN % 32 == 0 && kN <= pf::kTcMaximumN, "accumulator width");
+  constexpr uint32_t kInstruction = tc_instruction<kMmaN>();
+  static_assert(kN % 32 == 0 && kMmaN % 16 == 0 && kMmaN <= pf::kTcMaximumN &&
+                    kN <= kTmemColumns,
+                "accumulator width");
   // The swiglu epilogue reads gate/up column pairs in chunks of 32; widths
   // whose halves are not multiples of 32 (224) serve only the other modes.
   static_assert(kBytesA % 512 == 0 && (kBytesB / 2) % 512 == 0, "swizzle atom alignment");
@@ -930,7 +955,7 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      dev::shared_address(&s.tmem)),
-                 "r"(pf::kTcTmemColumns)
+                 "r"(kTmemColumns)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -992,9 +1017,18 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
 #pragma unroll
       for (uint32_t kk = 0; kk < pf::kTcTileK / 8u; ++kk) {
         const uint64_t step = kk * 2u; // 32 bytes, in 16-byte descriptor units
-        tc_mma(tmem, ah + step, bh + step, kInstruction, (i | kk) != 0 ? 1u : 0u);
+        const uint32_t first = (i | kk) != 0 ? 1u : 0u;
+        tc_mma(tmem, ah + step, bh + step, kInstruction, first);
         tc_mma(tmem, ah + step, bl + step, kInstruction, 1u);
         tc_mma(tmem, al + step, bh + step, kInstruction, 1u);
+        if constexpr (kSplitMma) {
+          // The second half of B (the up rows, 512-byte aligned) into
+          // accumulator columns kMmaN..kN - 1.
+          constexpr uint64_t kHalf = (kBytesB / 2u) >> 4u; // descriptor units
+          tc_mma(tmem + kMmaN, ah + step, bh + kHalf + step, kInstruction, first);
+          tc_mma(tmem + kMmaN, ah + step, bl + kHalf + step, kInstruction, 1u);
+          tc_mma(tmem + kMmaN, al + step, bh + kHalf + step, kInstruction, 1u);
+        }
       }
       tc_commit(&s.empty[st]);
     }
@@ -1061,6 +1095,8 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
       }
     }
   } else if (swiglu) {
+    // Gate columns [0, kN / 2), up columns [kN / 2, kN): whole 32-column
+    // chunks, then (kN / 2 = 144) a 16-column tail.
 #pragma unroll 1
     for (uint32_t chunk = 0; chunk < kN / 64u; ++chunk) {
       float gate[32], up[32];
@@ -1073,7 +1109,7 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
           gate[j] = silu_times(gate[j], up[j]);
         }
         staged(gate, [&](uint32_t r, uint32_t c, float4 x) {
-          if (row_base + r < p.m) {
+          if (row_base + r < p.m && column + c < p.n) {
             const size_t at = size_t{row_base + r} * p.ldc + column + c;
             if (p.c_lo == nullptr) {
               *reinterpret_cast<float4 *>(p.c + at) = x;
@@ -1086,6 +1122,35 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
             }
           }
         });
+      }
+    }
+    if constexpr ((kN / 2u) % 32u != 0u) {
+      static_assert((kN / 2u) % 32u == 16u, "a 16-column tail");
+      constexpr uint32_t kTail = kN / 2u - 16u;
+      float gate[16], up[16];
+      tc_load16(lane_address + kTail, gate);
+      tc_load16(lane_address + kN / 2u + kTail, up);
+      const uint32_t row = row_base + lane;
+      const uint32_t column = n_tile * (kN / 2u) + kTail;
+      if (store && row < p.m) {
+#pragma unroll
+        for (uint32_t c = 0; c < 16u; c += 4u) {
+          if (column + c < p.n) {
+            const size_t at = size_t{row} * p.ldc + column + c;
+            const float4 x = make_float4(silu_times(gate[c], up[c]), silu_times(gate[c + 1u], up[c + 1u]),
+                                         silu_times(gate[c + 2u], up[c + 2u]),
+                                         silu_times(gate[c + 3u], up[c + 3u]));
+            if (p.c_lo == nullptr) {
+              *reinterpret_cast<float4 *>(p.c + at) = x;
+            } else {
+              const float4 hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+              *reinterpret_cast<float4 *>(p.c + at) = hi;
+              *reinterpret_cast<float4 *>(p.c_lo + at) =
+                  make_float4(to_tf32(x.x - hi.x), to_tf32(x.y - hi.y), to_tf32(x.z - hi.z),
+                              to_tf32(x.w - hi.w));
+            }
+          }
+        }
       }
     }
   } else {
@@ -1114,7 +1179,7 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(pf::kTcTmemColumns)
+                 "r"(kTmemColumns)
                  : "memory");
   }
 }
@@ -1132,6 +1197,12 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
     prefill_tc_gemm_n256(const __grid_constant__ pf::TcGemmArgs p) {
   tc_gemm<256>(p);
+}
+
+// Gate/up pairs of 144 + 144 columns (swiglu, or its split-K partials).
+extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
+    prefill_tc_gemm_pair288(const __grid_constant__ pf::TcGemmArgs p) {
+  tc_gemm<pf::kTcPairN>(p);
 }
 
 // Narrow 3xTF32 GEMM (m <= kNarrowRows rows) with the operands swapped:

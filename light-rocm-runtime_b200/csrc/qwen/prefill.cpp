@@ -20,6 +20,7 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
       tc_n192_(module_.kernel("prefill_tc_gemm_n192")),
       tc_n224_(module_.kernel("prefill_tc_gemm_n224")),
       tc_n256_(module_.kernel("prefill_tc_gemm_n256")),
+      tc_pair288_(module_.kernel("prefill_tc_gemm_pair288")),
       tc_narrow_(module_.kernel("prefill_tc_narrow")),
       tc_narrow_pair_(module_.kernel("prefill_tc_narrow_pair")),
       finish_rows_(module_.kernel("prefill_finish_rows")),
@@ -34,7 +35,8 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   // previous kernel drains.
   for (const Kernel *kernel :
        {&embed_, &rmsnorm_, &rope_kv_, &attend_, &reduce_, &split_, &gemm_bias_, &gemm_residual_,
-        &gemm_swiglu_, &tc_n192_, &tc_n224_, &tc_n256_, &tc_narrow_, &tc_narrow_pair_,
+        &gemm_swiglu_, &tc_n192_, &tc_n224_, &tc_n256_, &tc_pair288_, &tc_narrow_,
+        &tc_narrow_pair_,
         &finish_rows_, &batch_attention_, &batch_argmax_}) {
     check(lr_kernel_set_overlapped(kernel->get(), 1), "lr_kernel_set_overlapped");
   }
@@ -48,7 +50,7 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   activated_.emplace(allocate(sizeof(float) * c * kIntermediate));
   activated_lo_.emplace(allocate(sizeof(float) * c * kIntermediate));
   // Split-K partials: at most one 128 x 256 tile per SM in flight.
-  partials_.emplace(allocate(sizeof(float) * kSms * kTcTileM * kTcMaximumN));
+  partials_.emplace(allocate(sizeof(float) * kSms * kTcTileM * kTcPairN));
   error_.emplace(allocate(sizeof(uint32_t)));
   // Attention: per (row tile, head) the key chunks' softmax states, and the
   // arrival counters (zero; the last chunk block resets its counter).
@@ -143,6 +145,8 @@ void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_gene
     maps.qkv = weight_maps(hi, lo, kQkv, kHidden, kQkvTile);
     maps.o = weight_maps(hi + kQkvFloats, lo + kQkvFloats, kHidden, kHidden, kHiddenTile);
     maps.gate_up = weight_maps(hi + gate_up, lo + gate_up, 2 * kIntermediate, kHidden, kGateUpTile);
+    maps.gate_up_pair =
+        weight_maps(hi + gate_up, lo + gate_up, 2 * kIntermediate, kHidden, kTcPairN);
     maps.down = weight_maps(hi + down, lo + down, kHidden, kIntermediate, kHiddenTile);
   }
   split_generation_ = weights_generation;
@@ -195,10 +199,14 @@ PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const OperandMaps &a, const
   const uint32_t n_tiles = ceil_div(n, out_columns);
   const uint32_t tiles = n_tiles * ceil_div(m, tile_rows);
   const uint32_t k_tiles = k / kTcTileK;
+  if (!narrow && tile_columns == kTcPairN && !swiglu) {
+    throw std::invalid_argument("288-column tiles are gate/up pairs");
+  }
   const Kernel &kernel = narrow ? (swiglu ? tc_narrow_pair_ : tc_narrow_)
-                         : tile_columns == 192 ? tc_n192_
-                         : tile_columns == 224 ? tc_n224_
-                                               : tc_n256_;
+                         : tile_columns == 192      ? tc_n192_
+                         : tile_columns == 224      ? tc_n224_
+                         : tile_columns == kTcPairN ? tc_pair288_
+                                                    : tc_n256_;
   const uint32_t shared = narrow ? tc_narrow_shared_bytes(swiglu) : tc_shared_bytes(tile_columns);
   TcGemmArgs args{};
   // The narrow kernels take the weights as the MMA's A operand.
@@ -327,9 +335,11 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
       finish(tc_gemm(kHiddenTile, attention_maps_, layer_maps_[layer].o, count, kHidden, kHidden,
                      GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr, true),
              w.mlp_norm);
-      tc_gemm(kGateUpTile, normalized_maps_, layer_maps_[layer].gate_up, count, kIntermediate,
-              kHidden, GemmEpilogue::swiglu, activated, activated_lo, kIntermediate, nullptr,
-              false);
+      // 144 + 144-column pair tiles: a 512-token chunk's gate/up is one wave.
+      tc_gemm(count <= kNarrowRows ? kGateUpTile : kTcPairN, normalized_maps_,
+              count <= kNarrowRows ? layer_maps_[layer].gate_up : layer_maps_[layer].gate_up_pair,
+              count, kIntermediate, kHidden, GemmEpilogue::swiglu, activated, activated_lo,
+              kIntermediate, nullptr, false);
       finish(tc_gemm(kHiddenTile, activated_maps_, layer_maps_[layer].down, count, kHidden,
                      kIntermediate, GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr,
                      true),
@@ -361,8 +371,10 @@ void Prefill::gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, u
                          float *c) {
   const bool swiglu = mode == GemmEpilogue::swiglu;
   if (m == 0 || n == 0 || k == 0 || k % kTcTileK != 0 || n % 32 != 0 || mode == GemmEpilogue::partial ||
-      (tile_columns != 0 && tile_columns != 192 && tile_columns != 224 && tile_columns != 256) ||
-      (swiglu && tile_columns != 0 && m > kNarrowRows &&
+      (tile_columns != 0 && tile_columns != 192 && tile_columns != 224 && tile_columns != 256 &&
+       tile_columns != kTcPairN) ||
+      (tile_columns == kTcPairN && !swiglu) ||
+      (swiglu && tile_columns != 0 && tile_columns != kTcPairN && m > kNarrowRows &&
        (n % (tile_columns / 2u) != 0 || (tile_columns / 2u) % 32u != 0))) {
     throw std::invalid_argument("unsupported GEMM check shape");
   }

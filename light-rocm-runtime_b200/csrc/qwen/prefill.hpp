@@ -67,7 +67,7 @@ public:
   // scheduler and kernels as the prefill (numerics checks): A [m][k],
   // B [rows][k] (swiglu: gate rows [0, n), up rows [n, 2n)), c [m][n] in/out.
   // tile_columns 0 runs the SIMT kernels, else 192, 224 or 256 picks the
-  // tensor-core tile width.
+  // tensor-core tile width (288: gate/up pairs of 144 + 144, swiglu only).
   void gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, uint32_t n, uint32_t k,
                   const float *a, const float *b, const float *bias, float *c);
 
@@ -77,9 +77,10 @@ public:
 private:
   friend class BatchDecoder;
 
-  // One layer's weights.
+  // One layer's weights (gate_up_pair: the same rows in boxes of
+  // kTcPairN / 2 for the prefill's pair tiles).
   struct LayerMaps {
-    OperandMaps qkv, o, gate_up, down;
+    OperandMaps qkv, o, gate_up, gate_up_pair, down;
   };
 
   DeviceBuffer allocate(size_t bytes);
@@ -94,8 +95,8 @@ private:
   Device device_;
   Module module_;
   Kernel embed_, rmsnorm_, rope_kv_, attend_, reduce_, split_, gemm_bias_, gemm_residual_,
-      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, tc_narrow_, tc_narrow_pair_, finish_rows_,
-      batch_attention_, batch_argmax_;
+      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, tc_pair288_, tc_narrow_, tc_narrow_pair_,
+      finish_rows_, batch_attention_, batch_argmax_;
   uint32_t chunk_;
   uint64_t device_bytes_ = 0;
 
