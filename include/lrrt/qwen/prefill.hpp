@@ -144,8 +144,10 @@ struct AttentionArgs {
   uint32_t first_position;
   uint32_t chunk_keys;   // key positions per block (a multiple of 64)
   uint32_t max_chunks;   // partial-state slots per (row tile, head)
-  float *partials;       // [row tile][14][max_chunks][rows][kAttentionPartialStride]
+  float *partials;       // per (row tile, head, chunk): rows x kAttentionPartialStride floats
   uint32_t *arrivals;    // [row tile][14], zero between launches
+  uint32_t wait_limit_ms; // prefill_attention_tc: per mbarrier wait
+  uint32_t *error;        // prefill_attention_tc: kTcErrorWaitTimeout when a wait gives up
 };
 
 // Batched decode attention: one query row per stream. Block (s, g, b)
@@ -212,6 +214,19 @@ constexpr uint32_t kAttentionThreads = 256;
 constexpr uint32_t kAttentionSharedBytes = 4u * (64u * 68u + 2u * 64u * 68u + 2u * 64u * 64u + 64u * 68u);
 constexpr uint32_t kAttentionPartialStride = 68; // acc[64], maximum, sum, 2 pad: 16-byte rows
 constexpr uint32_t kAttentionMaximumChunks = 16;
+// prefill_attention_tc (the 3xTF32 path): kTcAttentionRows query rows per
+// block, keys in sub-tiles of kTcAttentionKeys on the tensor cores; the same
+// arguments and (row tile, key chunk) enumeration as prefill_attention.
+// Shared memory: Q, K, V^T and the softmax weights P as TF32 (hi, lo) pairs
+// in 64-byte-swizzled slabs (Q [2][128][64], K [2][64][64], V^T [2][64][64],
+// P [2][128][64] floats), the row maxima and sums of both column halves
+// [2][2][128], two mbarriers and flags, and 1 KB to align the slabs.
+constexpr uint32_t kTcAttentionRows = 128;
+constexpr uint32_t kTcAttentionKeys = 64;
+constexpr uint32_t kTcAttentionThreads = 256;
+constexpr uint32_t kTcAttentionSharedBytes =
+    1024u + 4u * (2u * 128u * 64u + 2u * 64u * 64u + 2u * 64u * 64u + 2u * 128u * 64u) +
+    4u * 4u * 128u + 64u;
 
 // hi[i] = tf32(x[i]), lo[i] = tf32(x[i] - hi[i]) for i < count.
 struct SplitArgs {

@@ -834,6 +834,451 @@ extern "C" __global__ void __launch_bounds__(pf::kAttentionThreads)
   }
 }
 
+// ------------------------------------------------ tensor-core attention --
+
+// The same causal GQA attention on the tensor cores (3xTF32), for the
+// tf32x3 path. Block (x, h) serves query rows t0 = 128r .. t0 + 127 of head
+// h against key positions [c * chunk_keys, (c + 1) * chunk_keys) for the
+// x-th (row tile r, key chunk c) pair with work (the last row tile first, as
+// prefill_attention), in sub-tiles of 64 keys:
+//   S = Q.K^T (M = 128 rows, N = 64 keys, K = 64 dims) into TMEM columns
+//   [0, 64), then P = exp(S / 8 - running maximum) into shared memory and
+//   O = P.V (N = 64 dims, K = 64 keys) into TMEM columns [64, 128); the
+//   running output stays in registers, rescaled per sub-tile (the decode
+//   step's online softmax, expf).
+// Every product is hi.hi + hi.lo + lo.hi of TF32 pairs that the block splits
+// while staging Q, K and V^T (transposed on the way) from global memory into
+// K-major slabs of 16 fp32 (64-byte rows, 64-byte swizzle; the layout the
+// GEMMs' TMA boxes write). Thread (warp w, lane l) owns query row
+// 32 (w % 4) + l, its TMEM lane, and column half w / 4 of S and O; the two
+// threads of a row combine maxima and sums through shared memory. The key
+// and value rows of sub-tile j + 1 are loaded into registers while sub-tile
+// j is on the tensor cores. A row tile split over several chunks merges
+// their partial states in the last chunk block to finish, in chunk order.
+// Every mbarrier wait is bounded; on expiry the block records
+// kTcErrorWaitTimeout, stores nothing and frees its TMEM.
+constexpr uint32_t kTaRows = pf::kTcAttentionRows, kTaKeys = pf::kTcAttentionKeys;
+constexpr uint32_t kTaSlabs = qd::kHeadSize / 16u; // 16-fp32 slabs along the head dims
+constexpr uint32_t kTaKeySlabs = kTaKeys / 16u;    // 16-fp32 slabs along the keys
+constexpr uint32_t kTaTmemColumns = 128;           // S [0, 64), O [64, 128)
+static_assert(pf::kTcAttentionThreads == 2u * kTaRows && kTaRows == pf::kTcTileM,
+              "two threads per row, one 128-lane accumulator");
+static_assert(kTaKeys == 64u && qd::kHeadSize == 64u, "32-column halves of S and O");
+
+struct TcAttentionShared {
+  float q[2][kTaSlabs][kTaRows][16];           // [hi / lo][dim slab][row]
+  float k[2][kTaSlabs][kTaKeys][16];           // [hi / lo][dim slab][key]
+  float vt[2][kTaKeySlabs][qd::kHeadSize][16]; // [hi / lo][key slab][dim]
+  float p[2][kTaKeySlabs][kTaRows][16];        // [hi / lo][key slab][row]
+  float maximum[2][kTaRows];                   // [column half][row]
+  float sum[2][kTaRows];
+  uint64_t s_done, o_done;
+  uint32_t tmem;
+  uint32_t finisher;
+};
+static_assert(sizeof(TcAttentionShared) + 1024u <= pf::kTcAttentionSharedBytes, "shared layout");
+static_assert(offsetof(TcAttentionShared, k) % 1024u == 0 &&
+                  offsetof(TcAttentionShared, vt) % 1024u == 0 &&
+                  offsetof(TcAttentionShared, p) % 1024u == 0,
+              "slabs on swizzle-pattern boundaries");
+
+// Byte offset of 16-byte chunk `chunk` (0..3) of row `row` in a
+// 64-byte-swizzled slab: address bits [4, 6) XOR bits [7, 9).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t row, uint32_t chunk) {
+  return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
+}
+
+// TF32 pair by truncation: hi keeps the sign, exponent and top 10 mantissa
+// bits, lo = x - hi is exact, and the MMA reads lo's top 10 mantissa bits
+// (relative error of hi + lo below 2^-20, no conversion instructions).
+__device__ __forceinline__ float tf32_high(float x) {
+  return __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+}
+
+__device__ __forceinline__ void store_pair4(float *hi_slab, float *lo_slab, uint32_t offset,
+                                            float4 x) {
+  const float4 hi = make_float4(tf32_high(x.x), tf32_high(x.y), tf32_high(x.z), tf32_high(x.w));
+  *reinterpret_cast<float4 *>(reinterpret_cast<unsigned char *>(hi_slab) + offset) = hi;
+  *reinterpret_cast<float4 *>(reinterpret_cast<unsigned char *>(lo_slab) + offset) =
+      make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+}
+
+__device__ __forceinline__ void proxy_fence_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+extern "C" __global__ void __launch_bounds__(pf::kTcAttentionThreads, 1)
+    prefill_attention_tc(pf::AttentionArgs p) {
+  extern __shared__ __align__(1024) unsigned char ta_raw[];
+  TcAttentionShared &sh = *reinterpret_cast<TcAttentionShared *>(
+      (reinterpret_cast<uintptr_t>(ta_raw) + 1023u) & ~uintptr_t{1023});
+  const uint32_t tid = threadIdx.x, warp = tid >> 5u, lane = tid & 31u;
+  const uint32_t quadrant = warp & 3u, half = warp >> 2u;
+  const uint32_t row = quadrant * 32u + lane; // this thread's query row and TMEM lane
+  const uint32_t head = blockIdx.y;
+  const uint32_t row_tiles = (p.count + kTaRows - 1u) / kTaRows;
+  auto chunks_of = [&](uint32_t tile) {
+    const uint32_t tile_last = p.first_position + min(p.count, (tile + 1u) * kTaRows) - 1u;
+    return tile_last / p.chunk_keys + 1u;
+  };
+  uint32_t r = row_tiles, chunk = blockIdx.x;
+  while (r > 0u) {
+    --r;
+    const uint32_t n = chunks_of(r);
+    if (chunk < n) {
+      break;
+    }
+    chunk -= n;
+  }
+  const uint32_t t0 = r * kTaRows;
+  const uint32_t chunks = chunks_of(r);
+  if (t0 >= p.count || chunk >= chunks) {
+    return; // past the enumeration (not launched by the host)
+  }
+  const uint32_t rows = min(kTaRows, p.count - t0);
+  const uint32_t last = p.first_position + t0 + rows - 1u;
+  const uint32_t begin = chunk * p.chunk_keys;
+  const uint32_t end = min(begin + p.chunk_keys, last + 1u);
+  const uint32_t tiles = (end - begin + kTaKeys - 1u) / kTaKeys;
+  const size_t kv_offset = size_t{head / qd::kQueriesPerKvHead} * qd::kHeadSize;
+
+  if (tid == 0) {
+    dev::mbarrier_init(&sh.s_done, 1);
+    dev::mbarrier_init(&sh.o_done, 1);
+    dev::mbarrier_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     dev::shared_address(&sh.tmem)),
+                 "r"(kTaTmemColumns)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+  const uint32_t lane_address = tmem + ((quadrant * 32u) << 16);
+  dependent_launch_entry(); // barriers and TMEM are ready; qkv and the cache come next
+
+  // Q and K rows are copied two rows per warp instruction (coalesced): lane
+  // l takes chunk 4 (l / 8) + l % 4 of row 2 i + (l / 4) % 2, so that each
+  // quarter-warp stores both rows' 64-byte piece of one slab (all 32 banks).
+  const uint32_t pair_row = (lane >> 2u) & 1u, pair_chunk = (lane >> 3u) * 4u + (lane & 3u);
+  // V: thread (key 16 (w % 4) + l % 16, chunks 8 (w / 4) + 4 (l / 16) ..)
+  // loads four chunks and writes them down the columns of V^T; lanes 16..31
+  // take the elements in the order 1, 0, 3, 2 so that the two half-warps
+  // write rows of opposite parity (other banks).
+  const uint32_t v_key = (warp & 3u) * 16u + (lane & 15u);
+  const uint32_t v_chunk = (warp >> 2u) * 8u + (lane >> 4u) * 4u;
+  const uint32_t v_swap = lane >> 4u;
+  float4 k_next[4], v_next[4];
+  auto load_tile = [&](uint32_t base) {
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      const uint32_t key = 2u * (warp + 8u * j) + pair_row;
+      k_next[j] = base + key < end
+                      ? reinterpret_cast<const float4 *>(p.key_cache + size_t{base + key} * qd::kKvSize +
+                                                         kv_offset)[pair_chunk]
+                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    const bool v_valid = base + v_key < end;
+    const float4 *v_source = reinterpret_cast<const float4 *>(
+        p.value_cache + size_t{v_valid ? base + v_key : begin} * qd::kKvSize + kv_offset +
+        v_chunk * 4u);
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      v_next[j] = v_valid ? v_source[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  };
+  load_tile(begin); // in flight while Q is staged
+  {
+    float4 x[8];
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      const uint32_t q_row = 2u * (warp + 8u * j) + pair_row;
+      x[j] = q_row < rows ? reinterpret_cast<const float4 *>(
+                                p.qkv + size_t{t0 + q_row} * qd::kPackedQkvSize +
+                                head * qd::kHeadSize)[pair_chunk]
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      const uint32_t q_row = 2u * (warp + 8u * j) + pair_row;
+      store_pair4(&sh.q[0][pair_chunk / 4u][0][0], &sh.q[1][pair_chunk / 4u][0][0],
+                  sw64_offset(q_row, pair_chunk % 4u), x[j]);
+    }
+  }
+  auto stage_tile = [&]() {
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      store_pair4(&sh.k[0][pair_chunk / 4u][0][0], &sh.k[1][pair_chunk / 4u][0][0],
+                  sw64_offset(2u * (warp + 8u * j) + pair_row, pair_chunk % 4u), k_next[j]);
+    }
+    const uint32_t slab = v_key / 16u, column = v_key % 16u;
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      const float4 v = v_next[j];
+      const float in_order[4] = {v.x, v.y, v.z, v.w};
+      const float swapped[4] = {v.y, v.x, v.w, v.z};
+#pragma unroll
+      for (uint32_t e = 0; e < 4; ++e) {
+        const uint32_t dim = (v_chunk + j) * 4u + (e ^ v_swap);
+        const float x = v_swap != 0u ? swapped[e] : in_order[e];
+        const uint32_t offset = sw64_offset(dim, column / 4u) + (column % 4u) * 4u;
+        const float hi = tf32_high(x);
+        *reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(&sh.vt[0][slab][0][0]) +
+                                   offset) = hi;
+        *reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(&sh.vt[1][slab][0][0]) +
+                                   offset) = x - hi;
+      }
+    }
+  };
+
+  constexpr uint32_t kInstruction = tc_instruction<kTaKeys>(); // M = 128, N = 64
+  static_assert(kTaKeys == qd::kHeadSize, "one instruction for S and O");
+  // Descriptor units (16 bytes) between consecutive slabs.
+  constexpr uint64_t kRowSlab = kTaRows * 64u / 16u, kKeySlab = kTaKeys * 64u / 16u;
+  auto issue = [&](uint32_t accumulator, const float *a_hi, const float *a_lo, uint64_t a_slab,
+                   const float *b_hi, const float *b_lo, uint64_t b_slab, uint64_t *done) {
+    tc_fence_after();
+    const uint64_t ah = sw64_descriptor(a_hi), al = sw64_descriptor(a_lo);
+    const uint64_t bh = sw64_descriptor(b_hi), bl = sw64_descriptor(b_lo);
+#pragma unroll
+    for (uint32_t s = 0; s < 4u; ++s) {
+#pragma unroll
+      for (uint32_t kk = 0; kk < 2u; ++kk) {
+        const uint64_t a = s * a_slab + kk * 2u, b = s * b_slab + kk * 2u;
+        tc_mma(accumulator, ah + a, bh + b, kInstruction, (s | kk) != 0u ? 1u : 0u);
+        tc_mma(accumulator, ah + a, bl + b, kInstruction, 1u);
+        tc_mma(accumulator, al + a, bh + b, kInstruction, 1u);
+      }
+    }
+    tc_commit(done);
+  };
+
+  const uint32_t position = p.first_position + t0 + row;
+  float maximum = -INFINITY, denominator = 0.0f, acc[32];
+#pragma unroll
+  for (uint32_t i = 0; i < 32; ++i) {
+    acc[i] = 0.0f;
+  }
+  const dev::Deadline deadline(p.wait_limit_ms);
+  bool failed = false;
+  for (uint32_t t = 0; t < tiles; ++t) {
+    const uint32_t base = begin + t * kTaKeys;
+    stage_tile();
+    proxy_fence_shared();
+    tc_fence_before();
+    failed = __syncthreads_or(failed); // also: the previous sub-tile's O is read
+    if (failed) {
+      break;
+    }
+    if (tid == 0) {
+      issue(tmem, &sh.q[0][0][0][0], &sh.q[1][0][0][0], kRowSlab, &sh.k[0][0][0][0],
+            &sh.k[1][0][0][0], kKeySlab, &sh.s_done);
+    }
+    if (t + 1u < tiles) {
+      load_tile(base + kTaKeys);
+    }
+    failed |= !dev::mbarrier_wait(&sh.s_done, t & 1u, deadline);
+    tc_fence_after();
+    float s[32];
+    tc_load32(lane_address + half * 32u, s);
+    float tile_maximum = -INFINITY;
+#pragma unroll
+    for (uint32_t i = 0; i < 32; ++i) {
+      const uint32_t key = base + half * 32u + i;
+      s[i] = key <= position && key < end ? s[i] * 0.125f : -INFINITY;
+      tile_maximum = fmaxf(tile_maximum, s[i]);
+    }
+    sh.maximum[half][row] = tile_maximum;
+    asm volatile("bar.sync %0, 64;" ::"r"(1u + quadrant) : "memory"); // warps q and q + 4
+    tile_maximum = fmaxf(tile_maximum, sh.maximum[half ^ 1u][row]);
+    // Rows whose positions all precede this sub-tile's keys keep their
+    // state: scale 1, weights 0 (also while their maximum is still -inf).
+    const float next = fmaxf(maximum, tile_maximum);
+    const bool live = next != -INFINITY;
+    const float scale = live ? expf(maximum - next) : 1.0f;
+    float sum = 0.0f;
+#pragma unroll
+    for (uint32_t i = 0; i < 32; ++i) {
+      s[i] = live ? expf(s[i] - next) : 0.0f;
+      sum += s[i];
+    }
+#pragma unroll
+    for (uint32_t c = 0; c < 8; ++c) {
+      const uint32_t slab = half * 2u + c / 4u;
+      store_pair4(&sh.p[0][slab][0][0], &sh.p[1][slab][0][0], sw64_offset(row, c % 4u),
+                  make_float4(s[4u * c], s[4u * c + 1u], s[4u * c + 2u], s[4u * c + 3u]));
+    }
+    sh.sum[half][row] = sum;
+    proxy_fence_shared();
+    tc_fence_before();
+    failed = __syncthreads_or(failed); // P complete; S read by every warp
+    denominator = denominator * scale + sum + sh.sum[half ^ 1u][row];
+    maximum = next;
+    if (failed) {
+      break;
+    }
+    if (tid == 0) {
+      issue(tmem + kTaKeys, &sh.p[0][0][0][0], &sh.p[1][0][0][0], kRowSlab, &sh.vt[0][0][0][0],
+            &sh.vt[1][0][0][0], kKeySlab, &sh.o_done);
+    }
+    failed |= !dev::mbarrier_wait(&sh.o_done, t & 1u, deadline);
+    tc_fence_after();
+    float o[32];
+    tc_load32(lane_address + kTaKeys + half * 32u, o);
+#pragma unroll
+    for (uint32_t i = 0; i < 32; ++i) {
+      acc[i] = fmaf(acc[i], scale, o[i]);
+    }
+    tc_fence_before();
+  }
+  failed = __syncthreads_or(failed);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTaTmemColumns)
+                 : "memory");
+  }
+  if (failed) {
+    if (tid == 0) {
+      atomicExch(p.error, pf::kTcErrorWaitTimeout);
+    }
+    return;
+  }
+
+  // Output rows o * scale go through shared memory (the Q slabs are free
+  // now): each warp transposes its 32 rows x 32 columns so that eight lanes
+  // store one row's 128 contiguous bytes.
+  float *stage = &sh.q[0][0][0][0] + warp * 32u * 33u;
+  auto store_rows = [&](const float (&o)[32], float scale) {
+#pragma unroll
+    for (uint32_t j = 0; j < 32u; ++j) {
+      stage[lane * 33u + j] = o[j] * scale;
+    }
+    __syncwarp();
+#pragma unroll
+    for (uint32_t it = 0; it < 8u; ++it) {
+      const uint32_t r_in = it * 4u + lane / 8u, c = (lane % 8u) * 4u;
+      const uint32_t out_row = quadrant * 32u + r_in;
+      const float4 x = make_float4(stage[r_in * 33u + c], stage[r_in * 33u + c + 1u],
+                                   stage[r_in * 33u + c + 2u], stage[r_in * 33u + c + 3u]);
+      if (out_row < rows) {
+        const size_t at =
+            size_t{t0 + out_row} * qd::kQuerySize + head * qd::kHeadSize + half * 32u + c;
+        if (p.out_lo == nullptr) {
+          *reinterpret_cast<float4 *>(p.out + at) = x;
+        } else {
+          const float4 hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+          *reinterpret_cast<float4 *>(p.out + at) = hi;
+          *reinterpret_cast<float4 *>(p.out_lo + at) =
+              make_float4(to_tf32(x.x - hi.x), to_tf32(x.y - hi.y), to_tf32(x.z - hi.z),
+                          to_tf32(x.w - hi.w));
+        }
+      }
+    }
+  };
+  if (chunks == 1u) {
+    store_rows(acc, 1.0f / denominator);
+    return;
+  }
+  // Partial state of this chunk, in column quads so that a warp's 32 rows
+  // are 512 contiguous bytes: [r][head][chunk] then acc [16][128 rows][4],
+  // maximum [128], sum [128] (within kAttentionPartialStride x 128 floats).
+  const size_t tile_state = size_t{r} * qd::kAttentionHeads + head;
+  const size_t chunk_stride = size_t{kTaRows} * pf::kAttentionPartialStride;
+  static_assert(pf::kAttentionPartialStride >= qd::kHeadSize + 2u, "acc, maximum, sum");
+  float *states = p.partials + tile_state * p.max_chunks * chunk_stride;
+  {
+    float *state = states + chunk * chunk_stride;
+#pragma unroll
+    for (uint32_t i = 0; i < 8u; ++i) {
+      *reinterpret_cast<float4 *>(state + ((half * 8u + i) * kTaRows + row) * 4u) =
+          make_float4(acc[4u * i], acc[4u * i + 1u], acc[4u * i + 2u], acc[4u * i + 3u]);
+    }
+    if (half == 0u) {
+      state[64u * kTaRows + row] = maximum;     // -inf: no key of this chunk precedes the row
+      state[65u * kTaRows + row] = denominator; // 0 then
+    }
+  }
+  // The block's stores, then one release-acquire count per block: the CTA
+  // barrier orders every thread's stores before thread 0's release, and the
+  // finisher's acquire (with the barrier after it) orders its loads after
+  // the other blocks' stores.
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t previous;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                 : "=r"(previous)
+                 : "l"(p.arrivals + tile_state)
+                 : "memory");
+    sh.finisher = previous == chunks - 1u ? 1u : 0u;
+  }
+  __syncthreads();
+  if (sh.finisher == 0u) {
+    return;
+  }
+  // Merge in chunk order: the common maximum, then the rescaled sums and
+  // accumulators. All chunks' maxima and sums are loaded at once, the
+  // accumulators four chunks at a time.
+  constexpr uint32_t kChunks = pf::kAttentionMaximumChunks;
+  float weight[kChunks], chunk_sum[kChunks];
+#pragma unroll
+  for (uint32_t c = 0; c < kChunks; ++c) {
+    const float *state = states + c * chunk_stride + row;
+    weight[c] = c < chunks ? __ldcg(state + 64u * kTaRows) : -INFINITY;
+    chunk_sum[c] = c < chunks ? __ldcg(state + 65u * kTaRows) : 0.0f;
+  }
+  float common = -INFINITY;
+#pragma unroll
+  for (uint32_t c = 0; c < kChunks; ++c) {
+    common = fmaxf(common, weight[c]);
+  }
+  float total = 0.0f;
+#pragma unroll
+  for (uint32_t c = 0; c < kChunks; ++c) {
+    // A chunk without keys before the row (maximum -inf) adds nothing.
+    weight[c] = weight[c] == -INFINITY ? 0.0f : expf(weight[c] - common);
+    total += chunk_sum[c] * weight[c];
+  }
+#pragma unroll
+  for (uint32_t i = 0; i < 32; ++i) {
+    acc[i] = 0.0f;
+  }
+#pragma unroll
+  for (uint32_t c0 = 0; c0 < kChunks; c0 += 4u) {
+    if (c0 < chunks) {
+      float4 a[4][8];
+#pragma unroll
+      for (uint32_t cc = 0; cc < 4u; ++cc) {
+        const float4 *state = reinterpret_cast<const float4 *>(states + (c0 + cc) * chunk_stride);
+#pragma unroll
+        for (uint32_t i = 0; i < 8u; ++i) {
+          a[cc][i] = c0 + cc < chunks ? __ldcg(state + (half * 8u + i) * kTaRows + row)
+                                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+      }
+#pragma unroll
+      for (uint32_t cc = 0; cc < 4u; ++cc) {
+#pragma unroll
+        for (uint32_t i = 0; i < 8u; ++i) {
+          acc[4u * i] += a[cc][i].x * weight[c0 + cc];
+          acc[4u * i + 1u] += a[cc][i].y * weight[c0 + cc];
+          acc[4u * i + 2u] += a[cc][i].z * weight[c0 + cc];
+          acc[4u * i + 3u] += a[cc][i].w * weight[c0 + cc];
+        }
+      }
+    }
+  }
+  store_rows(acc, 1.0f / total);
+  __syncthreads();
+  if (tid == 0) {
+    p.arrivals[tile_state] = 0; // ready for the next layer
+  }
+}
+
 // Finishes split-K tiles: one thread per output element of tiles
 // [tile_offset, tile_offset + tile_count); partial sums are added in split
 // order, so the result does not depend on which CTA finished first.

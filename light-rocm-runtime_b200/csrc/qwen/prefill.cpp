@@ -13,7 +13,8 @@ using namespace detail;
 Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t max_chunk_tokens)
     : device_(device), module_(device, image, image_size), embed_(module_.kernel("prefill_embed")),
       rmsnorm_(module_.kernel("prefill_rmsnorm")), rope_kv_(module_.kernel("prefill_rope_kv")),
-      attend_(module_.kernel("prefill_attention")), reduce_(module_.kernel("prefill_reduce")),
+      attend_(module_.kernel("prefill_attention")),
+      attend_tc_(module_.kernel("prefill_attention_tc")), reduce_(module_.kernel("prefill_reduce")),
       split_(module_.kernel("prefill_split")), gemm_bias_(module_.kernel("prefill_gemm_bias")),
       gemm_residual_(module_.kernel("prefill_gemm_residual")),
       gemm_swiglu_(module_.kernel("prefill_gemm_swiglu")),
@@ -34,7 +35,7 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   // a kernel's prologue (barrier setup, TMEM allocation) runs while the
   // previous kernel drains.
   for (const Kernel *kernel :
-       {&embed_, &rmsnorm_, &rope_kv_, &attend_, &reduce_, &split_, &gemm_bias_, &gemm_residual_,
+       {&embed_, &rmsnorm_, &rope_kv_, &attend_, &attend_tc_, &reduce_, &split_, &gemm_bias_, &gemm_residual_,
         &gemm_swiglu_, &tc_n192_, &tc_n224_, &tc_n256_, &tc_pair288_, &tc_narrow_,
         &tc_narrow_pair_,
         &finish_rows_, &batch_attention_, &batch_argmax_}) {
@@ -54,10 +55,13 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   error_.emplace(allocate(sizeof(uint32_t)));
   // Attention: per (row tile, head) the key chunks' softmax states, and the
   // arrival counters (zero; the last chunk block resets its counter).
+  // Sized for the larger of the two row tilings (64-row SIMT tiles,
+  // 128-row tensor-core tiles); counters for the finer one.
   const size_t row_tiles = ceil_div(chunk_, kAttentionTileRows);
-  attention_partials_.emplace(allocate(sizeof(float) * row_tiles * qd::kAttentionHeads *
-                                       kAttentionMaximumChunks * kAttentionTileRows *
-                                       kAttentionPartialStride));
+  const size_t tiled_rows = std::max<size_t>(row_tiles * kAttentionTileRows,
+                                             ceil_div(chunk_, kTcAttentionRows) * kTcAttentionRows);
+  attention_partials_.emplace(allocate(sizeof(float) * tiled_rows * qd::kAttentionHeads *
+                                       kAttentionMaximumChunks * kAttentionPartialStride));
   attention_arrivals_.emplace(allocate(sizeof(uint32_t) * row_tiles * qd::kAttentionHeads));
   const std::vector<uint32_t> no_arrivals(row_tiles * qd::kAttentionHeads, 0u);
   check(lr_memcpy(device_.get(), attention_arrivals_->data(), no_arrivals.data(),
@@ -277,7 +281,7 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
   auto *activated = static_cast<float *>(activated_->data());
   auto *activated_lo = tc ? static_cast<float *>(activated_lo_->data()) : nullptr;
   const uint32_t m_tiles = ceil_div(count, 128);
-  const PartialTiles direct{nullptr, 0, 0, 0, 0};
+  const PartialTiles direct{nullptr, 0, 0, 0, 0, 0};
   auto simt = [&](const Kernel &kernel, const GemmArgs &args, uint32_t n_tiles) {
     const lr_launch_config_t config{{n_tiles * 256u, m_tiles, 1}, {256, 1, 1}, 0};
     launch(kernel.get(), config, args);
@@ -317,20 +321,24 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
     const uint32_t keys = first_position + count;
     const uint32_t chunk_keys =
         128u * std::max(1u, ceil_div(keys, 128u * kAttentionMaximumChunks));
+    // The tf32x3 path runs the tensor-core kernel (128-row tiles).
+    const uint32_t tile_rows = tc ? kTcAttentionRows : kAttentionTileRows;
+    const uint32_t attention_threads = tc ? kTcAttentionThreads : kAttentionThreads;
     uint32_t attention_blocks = 0; // (row tile, key chunk) pairs with work
-    for (uint32_t t0 = 0; t0 < count; t0 += kAttentionTileRows) {
-      const uint32_t tile_last = first_position + std::min(count, t0 + kAttentionTileRows) - 1u;
+    for (uint32_t t0 = 0; t0 < count; t0 += tile_rows) {
+      const uint32_t tile_last = first_position + std::min(count, t0 + tile_rows) - 1u;
       attention_blocks += tile_last / chunk_keys + 1u;
     }
     const lr_launch_config_t attention_config{
-        {attention_blocks * kAttentionThreads, qd::kAttentionHeads, 1},
-        {kAttentionThreads, 1, 1},
-        kAttentionSharedBytes};
-    launch(attend_.get(), attention_config,
+        {attention_blocks * attention_threads, qd::kAttentionHeads, 1},
+        {attention_threads, 1, 1},
+        tc ? kTcAttentionSharedBytes : kAttentionSharedBytes};
+    launch(tc ? attend_tc_.get() : attend_.get(), attention_config,
            AttentionArgs{qkv, w.key_cache, w.value_cache, attention, attention_lo, count,
                          first_position, chunk_keys, kAttentionMaximumChunks,
                          static_cast<float *>(attention_partials_->data()),
-                         static_cast<uint32_t *>(attention_arrivals_->data())});
+                         static_cast<uint32_t *>(attention_arrivals_->data()), kWaitLimitMs,
+                         static_cast<uint32_t *>(error_->data())});
     if (tc) {
       finish(tc_gemm(kHiddenTile, attention_maps_, layer_maps_[layer].o, count, kHidden, kHidden,
                      GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr, true),
@@ -425,7 +433,7 @@ void Prefill::gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, u
   check(lr_memcpy(device_.get(), &error, error_->data(), sizeof(error), LR_MEMCPY_DEVICE_TO_HOST),
         "lr_memcpy gemm error");
   if (error != 0) {
-    throw std::runtime_error("prefill tensor-core GEMM gave up waiting (code " +
+    throw std::runtime_error("prefill tensor-core kernel gave up waiting (code " +
                              std::to_string(error) + ")");
   }
 }
@@ -473,7 +481,7 @@ void Prefill::run(const ModelView &model, const uint32_t *tokens, uint32_t count
   check(lr_memcpy(device_.get(), &error, error_->data(), sizeof(error), LR_MEMCPY_DEVICE_TO_HOST),
         "lr_memcpy prefill error");
   if (error != 0) {
-    throw std::runtime_error("prefill tensor-core GEMM gave up waiting (code " +
+    throw std::runtime_error("prefill tensor-core kernel gave up waiting (code " +
                              std::to_string(error) + ")");
   }
 }

@@ -63,23 +63,29 @@ def test_prefill_matches_oracle_ingest(gpu, path, prompt_length, chunk):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("path", PATHS)
-def test_prefill_at_continues_a_cached_context(gpu, path):
-    """prefill_at on top of 64 cache rows written by set_kv: rows 64..99 from
-    tokens, rows before 64 untouched, decode continues from position 100."""
-    model, oracle, _, _ = build_pair(seed=12, layers=2, vocab=4096, capacity=128, max_tokens=4)
+@pytest.mark.parametrize("cached", [64, 2100])
+def test_prefill_at_continues_a_cached_context(gpu, path, cached):
+    """prefill_at on top of `cached` cache rows written by set_kv: the next 36
+    rows from tokens, earlier rows untouched, decode continues after them.
+    Past 2048 keys the attention chunks grow to 256 keys (four 64-key
+    sub-tiles per block on the tensor-core path)."""
+    model, oracle, _, _ = build_pair(seed=12, layers=2, vocab=4096, capacity=cached + 64,
+                                     max_tokens=4)
     model.enable_prefill(512)
-    prefill_kv(model, oracle, seed=12, layers=2, positions=64)
-    before = [model.read("key_cache", layer).reshape(-1, 128)[:64].copy() for layer in range(2)]
+    prefill_kv(model, oracle, seed=12, layers=2, positions=cached)
+    before = [model.read("key_cache", layer).reshape(-1, 128)[:cached].copy()
+              for layer in range(2)]
     tokens = S.prompt(13, 37, 4096)
-    model.prefill_at(tokens[:-1], 64, path)
+    model.prefill_at(tokens[:-1], cached, path)
     for i, token in enumerate(tokens[:-1]):
-        oracle.decode(oracle.embedding(int(token)), 64 + i, 1)
+        oracle.decode(oracle.embedding(int(token)), cached + i, 1)
     for layer in range(2):
-        assert np.array_equal(model.read("key_cache", layer).reshape(-1, 128)[:64], before[layer])
-    compare_kv(model, oracle, 100, first=64)
+        assert np.array_equal(model.read("key_cache", layer).reshape(-1, 128)[:cached],
+                              before[layer])
+    compare_kv(model, oracle, cached + 36, first=cached)
     model.set_hidden_from_token(int(tokens[-1]))
-    oracle.decode(oracle.embedding(int(tokens[-1])), 100, 4)
-    decode_matches(model, oracle, 100, 4)
+    oracle.decode(oracle.embedding(int(tokens[-1])), cached + 36, 4)
+    decode_matches(model, oracle, cached + 36, 4)
     model.close()
 
 
