@@ -127,6 +127,11 @@ struct FinishArgs {
   float *out_lo;
 };
 
+// An encoded CUtensorMap, passed by value in kernel arguments.
+struct alignas(64) TensorMap {
+  uint64_t opaque[16];
+};
+
 // Causal GQA attention: query row t attends to cache positions
 // 0..first_position + t. out [count][896] (hi part when out_lo is set).
 // Launch: blocks of kAttentionThreads threads over (the (row tile, key
@@ -148,6 +153,9 @@ struct AttentionArgs {
   uint32_t *arrivals;    // [row tile][14], zero between launches
   uint32_t wait_limit_ms; // prefill_attention_tc: per mbarrier wait
   uint32_t *error;        // prefill_attention_tc: kTcErrorWaitTimeout when a wait gives up
+  // prefill_attention_tc: tensor maps of out and out_lo ([rows][896], boxes
+  // of 16 columns x 128 rows, 64-byte swizzle) for its TMA stores.
+  TensorMap out_map, out_lo_map;
 };
 
 // Batched decode attention: one query row per stream. Block (s, g, b)
@@ -243,10 +251,6 @@ struct SplitArgs {
 // are 2-D fp32 maps with 64-byte swizzle and boxes of 16 columns x 128 rows
 // (A) or N / 2 rows (B: each B tile loads as two half boxes, so swiglu takes
 // N / 2 gate rows and N / 2 up rows starting at n_gate_offset).
-struct alignas(64) TensorMap {
-  uint64_t opaque[16];
-};
-
 struct TcGemmArgs {
   TensorMap a_hi, a_lo, b_hi, b_lo;
   const float *bias;

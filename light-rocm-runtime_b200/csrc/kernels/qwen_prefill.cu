@@ -907,8 +907,16 @@ __device__ __forceinline__ void proxy_fence_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+__device__ __forceinline__ void tma_store_2d(const pf::TensorMap *map, const void *source,
+                                             uint32_t x, uint32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(dev::shared_address(source)), "r"(x), "r"(y)
+               : "memory");
+}
+
 extern "C" __global__ void __launch_bounds__(pf::kTcAttentionThreads, 1)
-    prefill_attention_tc(pf::AttentionArgs p) {
+    prefill_attention_tc(const __grid_constant__ pf::AttentionArgs p) {
   extern __shared__ __align__(1024) unsigned char ta_raw[];
   TcAttentionShared &sh = *reinterpret_cast<TcAttentionShared *>(
       (reinterpret_cast<uintptr_t>(ta_raw) + 1023u) & ~uintptr_t{1023});
@@ -1082,6 +1090,7 @@ extern "C" __global__ void __launch_bounds__(pf::kTcAttentionThreads, 1)
       load_tile(base + kTaKeys);
     }
     failed |= !dev::mbarrier_wait(&sh.s_done, t & 1u, deadline);
+    __syncwarp(); // the warp-collective TMEM load below runs converged
     tc_fence_after();
     float s[32];
     tc_load32(lane_address + half * 32u, s);
@@ -1126,6 +1135,7 @@ extern "C" __global__ void __launch_bounds__(pf::kTcAttentionThreads, 1)
             &sh.vt[1][0][0][0], kKeySlab, &sh.o_done);
     }
     failed |= !dev::mbarrier_wait(&sh.o_done, t & 1u, deadline);
+    __syncwarp();
     tc_fence_after();
     float o[32];
     tc_load32(lane_address + kTaKeys + half * 32u, o);
@@ -1149,35 +1159,35 @@ extern "C" __global__ void __launch_bounds__(pf::kTcAttentionThreads, 1)
     return;
   }
 
-  // Output rows o * scale go through shared memory (the Q slabs are free
-  // now): each warp transposes its 32 rows x 32 columns so that eight lanes
-  // store one row's 128 contiguous bytes.
-  float *stage = &sh.q[0][0][0][0] + warp * 32u * 33u;
+  // Output rows o * scale as TF32 pairs into the Q slabs (free now, the
+  // layout of the out maps' 16-column boxes), then thread 0 stores the
+  // head's four boxes per buffer with TMA (rows past the chunk's count land
+  // in unused rows of the buffer; the box is clipped at its end).
   auto store_rows = [&](const float (&o)[32], float scale) {
 #pragma unroll
-    for (uint32_t j = 0; j < 32u; ++j) {
-      stage[lane * 33u + j] = o[j] * scale;
+    for (uint32_t c = 0; c < 8u; ++c) {
+      const uint32_t slab = half * 2u + c / 4u;
+      const float4 x = make_float4(o[4u * c] * scale, o[4u * c + 1u] * scale,
+                                   o[4u * c + 2u] * scale, o[4u * c + 3u] * scale);
+      const float4 hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+      const uint32_t offset = sw64_offset(row, c % 4u);
+      *reinterpret_cast<float4 *>(reinterpret_cast<unsigned char *>(&sh.q[0][slab][0][0]) +
+                                  offset) = hi;
+      *reinterpret_cast<float4 *>(reinterpret_cast<unsigned char *>(&sh.q[1][slab][0][0]) +
+                                  offset) =
+          make_float4(to_tf32(x.x - hi.x), to_tf32(x.y - hi.y), to_tf32(x.z - hi.z),
+                      to_tf32(x.w - hi.w));
     }
-    __syncwarp();
+    proxy_fence_shared();
+    __syncthreads();
+    if (tid == 0) {
 #pragma unroll
-    for (uint32_t it = 0; it < 8u; ++it) {
-      const uint32_t r_in = it * 4u + lane / 8u, c = (lane % 8u) * 4u;
-      const uint32_t out_row = quadrant * 32u + r_in;
-      const float4 x = make_float4(stage[r_in * 33u + c], stage[r_in * 33u + c + 1u],
-                                   stage[r_in * 33u + c + 2u], stage[r_in * 33u + c + 3u]);
-      if (out_row < rows) {
-        const size_t at =
-            size_t{t0 + out_row} * qd::kQuerySize + head * qd::kHeadSize + half * 32u + c;
-        if (p.out_lo == nullptr) {
-          *reinterpret_cast<float4 *>(p.out + at) = x;
-        } else {
-          const float4 hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
-          *reinterpret_cast<float4 *>(p.out + at) = hi;
-          *reinterpret_cast<float4 *>(p.out_lo + at) =
-              make_float4(to_tf32(x.x - hi.x), to_tf32(x.y - hi.y), to_tf32(x.z - hi.z),
-                          to_tf32(x.w - hi.w));
-        }
+      for (uint32_t s = 0; s < kTaSlabs; ++s) {
+        tma_store_2d(&p.out_map, &sh.q[0][s][0][0], head * qd::kHeadSize + 16u * s, t0);
+        tma_store_2d(&p.out_lo_map, &sh.q[1][s][0][0], head * qd::kHeadSize + 16u * s, t0);
       }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
   };
   if (chunks == 1u) {
@@ -1490,6 +1500,7 @@ __device__ __forceinline__ void tc_gemm(const pf::TcGemmArgs &p) {
   if (!ready) {
     fail();
   }
+  __syncwarp(); // the warp-collective TMEM loads below run converged
   tc_fence_after();
   const uint32_t lane_address = tmem + ((warp * 32u) << 16);
   const uint32_t row_base = m0 + warp * 32u;
@@ -1776,6 +1787,7 @@ __device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
   if (!ready) {
     fail();
   }
+  __syncwarp(); // the warp-collective TMEM loads below run converged
   tc_fence_after();
   const uint32_t lane_address = tmem + ((warp * 32u) << 16);
   const uint32_t local = warp * 32u + lane; // column within the tile

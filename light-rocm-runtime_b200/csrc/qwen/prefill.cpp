@@ -338,7 +338,9 @@ void Prefill::run_chunk(const ModelView &model, uint32_t count, uint32_t first_p
                          first_position, chunk_keys, kAttentionMaximumChunks,
                          static_cast<float *>(attention_partials_->data()),
                          static_cast<uint32_t *>(attention_arrivals_->data()), kWaitLimitMs,
-                         static_cast<uint32_t *>(error_->data())});
+                         static_cast<uint32_t *>(error_->data()),
+                         tc ? attention_maps_.wide[0] : TensorMap{},
+                         tc ? attention_maps_.wide[1] : TensorMap{}});
     if (tc) {
       finish(tc_gemm(kHiddenTile, attention_maps_, layer_maps_[layer].o, count, kHidden, kHidden,
                      GemmEpilogue::residual, hidden, nullptr, kHidden, nullptr, true),
