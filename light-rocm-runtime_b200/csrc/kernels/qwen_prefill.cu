@@ -1664,15 +1664,28 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 // Narrow 3xTF32 GEMM (m <= kNarrowRows rows) with the operands swapped:
 // CTA (x, 0, z) computes output columns [n0, n0 + 128), n0 = 128 *
 // (tile_offset + x), over K slice z as D^T = W . X^T: the 128 weight rows
-// (TMA maps a_hi / a_lo, box 16 x 128) are the MMA's A operand (M = 128) and
-// the 32 activation rows (b_hi / b_lo, box 16 x 32; rows past m are never
-// stored) its B operand (N = 32), so the tensor cores spend nothing on
-// padding rows and each weight byte is read once per step. kPaired
+// (TMA map a_hi over the FP32 weights, box 16 x 128) are the MMA's A
+// operand (M = 128) and the 32 activation rows (b_hi / b_lo, box 16 x 32;
+// rows past m are never stored) its B operand (N = 32), so the tensor cores
+// spend nothing on padding rows and each weight byte is read from HBM once
+// per step, as FP32: warps 2 and 3 split every landed weight tile in place
+// into its TF32 pair (hi = the top 10 mantissa bits, lo = w - hi exactly,
+// written beside it) and release the stage to the MMA warp. kPaired
 // (swiglu): a second accumulator takes the up rows n_gate_offset + n0...;
-// the gate/up pair lands on the same thread. Same ring, roles and bounded
-// waits as tc_gemm; thread (warp, lane) owns output column n0 + 32 * warp +
-// lane and walks the rows, so each row's 32 columns per warp are one
-// 128-byte store. Partial tiles: [split][tile][kNarrowRows][128 or 256].
+// the gate/up pair lands on the same thread. Same ring and bounded waits as
+// tc_gemm; thread (warp, lane) owns output column n0 + 32 * warp + lane and
+// walks the rows, so each row's 32 columns per warp are one 128-byte store.
+// Partial tiles: [split][tile][kNarrowRows][128 or 256].
+template <uint32_t kStages> struct NarrowShared {
+  uint64_t full[kStages];      // TMA landed
+  uint64_t converted[kStages]; // weight tiles split (64 converter arrivals)
+  uint64_t empty[kStages];     // MMAs done
+  uint64_t done;
+  uint32_t tmem;
+  uint32_t abort;
+};
+static_assert(sizeof(NarrowShared<8>) <= 256u, "within the 256 bytes the host adds");
+
 template <bool kPaired>
 __device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
   constexpr uint32_t kStages = pf::tc_narrow_stages(kPaired);
@@ -1682,12 +1695,17 @@ __device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
   constexpr uint32_t kWeights = kPaired ? 2u : 1u;
   constexpr uint32_t kTileColumns = kWeights * pf::kNarrowTileN;
   constexpr uint32_t kInstruction = tc_instruction<pf::kNarrowRows>();
+  constexpr uint32_t kConverters = 64;                         // warps 2 and 3
+  constexpr uint32_t kLoadBytes = kStageBytes - kWeights * kWeightBytes; // no W_lo
+  static_assert(pf::kTcThreads == 128u && kWeightBytes % (16u * kConverters) == 0,
+                "two converter warps, whole float4s each");
   static_assert(kWeightBytes % 512 == 0 && kRowBytes % 512 == 0, "swizzle atom alignment");
   extern __shared__ __align__(1024) unsigned char raw_shared[];
   unsigned char *tiles = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(raw_shared) + 1023u) & ~uintptr_t{1023});
-  auto &s = *reinterpret_cast<TcShared<kStages> *>(tiles + kStages * kStageBytes);
-  // Stage: W_hi, W_lo (then the up rows' W_hi, W_lo), X_hi, X_lo.
+  auto &s = *reinterpret_cast<NarrowShared<kStages> *>(tiles + kStages * kStageBytes);
+  // Stage: W_hi, W_lo (then the up rows' W_hi, W_lo), X_hi, X_lo. TMA fills
+  // W_hi with the FP32 weights; the converters rewrite it as hi and fill W_lo.
   auto w_hi = [&](uint32_t st, uint32_t w) { return tiles + st * kStageBytes + 2u * w * kWeightBytes; };
   auto w_lo = [&](uint32_t st, uint32_t w) { return w_hi(st, w) + kWeightBytes; };
   auto x_hi = [&](uint32_t st) { return tiles + st * kStageBytes + 2u * kWeights * kWeightBytes; };
@@ -1704,6 +1722,7 @@ __device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kStages; ++i) {
       dev::mbarrier_init(&s.full[i], 1);
+      dev::mbarrier_init(&s.converted[i], kConverters);
       dev::mbarrier_init(&s.empty[i], 1);
     }
     dev::mbarrier_init(&s.done, 1);
@@ -1737,12 +1756,11 @@ __device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
         break;
       }
       const uint32_t k0 = (first_tile + i) * pf::kTcTileK;
-      dev::mbarrier_arrive_expect_tx(&s.full[st], kStageBytes);
+      dev::mbarrier_arrive_expect_tx(&s.full[st], kLoadBytes);
 #pragma unroll
       for (uint32_t w = 0; w < kWeights; ++w) {
         const uint32_t row = w == 0 ? n0 : p.n_gate_offset + n0;
         tma_load_2d(w_hi(st, w), &p.a_hi, k0, row, &s.full[st]);
-        tma_load_2d(w_lo(st, w), &p.a_lo, k0, row, &s.full[st]);
       }
       tma_load_2d(x_hi(st), &p.b_hi, k0, 0, &s.full[st]);
       tma_load_2d(x_lo(st), &p.b_lo, k0, 0, &s.full[st]);
@@ -1754,11 +1772,39 @@ __device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
         fail();
       }
     }
+  } else if (warp >= 2) {
+    // Converters: per landed stage, w -> (hi, lo) for every weight tile
+    // (elementwise, so the swizzled layout is kept), then release it.
+    const uint32_t t = threadIdx.x - 64u;
+    for (uint32_t i = 0; i < count; ++i) {
+      const uint32_t st = i % kStages;
+      if (!dev::mbarrier_wait(&s.full[st], (i / kStages) & 1u, deadline)) {
+        fail();
+        break;
+      }
+#pragma unroll
+      for (uint32_t w = 0; w < kWeights; ++w) {
+        float4 *hi = reinterpret_cast<float4 *>(w_hi(st, w));
+        float4 *lo = reinterpret_cast<float4 *>(w_lo(st, w));
+#pragma unroll
+        for (uint32_t j = 0; j < kWeightBytes / (16u * kConverters); ++j) {
+          const float4 x = hi[t + kConverters * j];
+          const float4 h =
+              make_float4(tf32_high(x.x), tf32_high(x.y), tf32_high(x.z), tf32_high(x.w));
+          hi[t + kConverters * j] = h;
+          lo[t + kConverters * j] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+        }
+      }
+      proxy_fence_shared();
+      asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(
+                       dev::shared_address(&s.converted[st]))
+                   : "memory");
+    }
   } else if (warp == 1 && lane == 0) {
     // Per stage two K = 8 steps, three products per accumulator each.
     for (uint32_t i = 0; i < count; ++i) {
       const uint32_t st = i % kStages;
-      if (!dev::mbarrier_wait(&s.full[st], (i / kStages) & 1u, deadline)) {
+      if (!dev::mbarrier_wait(&s.converted[st], (i / kStages) & 1u, deadline)) {
         fail();
         break;
       }

@@ -88,16 +88,16 @@ OperandMaps activation_maps(const float *hi, const float *lo, uint64_t rows,
   return maps;
 }
 
-// Maps of a (hi, lo) weight pair [rows][columns]: boxes of half a
-// tile_columns-wide tile (the wide kernels' B operand) and kNarrowTileN-row
-// boxes (the narrow kernels' A).
-OperandMaps weight_maps(const float *hi, const float *lo, uint64_t rows, uint64_t columns,
-                                 uint32_t tile_columns) {
+// Maps of a weight matrix [rows][columns]: over its (hi, lo) pair, boxes of
+// half a tile_columns-wide tile (the wide kernels' B operand); over the FP32
+// weights themselves, kNarrowTileN-row boxes (the narrow kernels' A, which
+// they split into the TF32 pair in shared memory).
+OperandMaps weight_maps(const float *hi, const float *lo, const float *weights, uint64_t rows,
+                        uint64_t columns, uint32_t tile_columns) {
   OperandMaps maps;
   maps.wide[0] = map_2d(hi, rows, columns, tile_columns / 2u);
   maps.wide[1] = map_2d(lo, rows, columns, tile_columns / 2u);
-  maps.narrow[0] = map_2d(hi, rows, columns, kNarrowTileN);
-  maps.narrow[1] = map_2d(lo, rows, columns, kNarrowTileN);
+  maps.narrow[0] = map_2d(weights, rows, columns, kNarrowTileN);
   return maps;
 }
 
@@ -146,12 +146,13 @@ void Prefill::prepare_tensor_cores(const ModelView &model, uint64_t weights_gene
     }
     LayerMaps &maps = layer_maps_[layer];
     const size_t gate_up = kQkvFloats + kOFloats, down = gate_up + kGateUpFloats;
-    maps.qkv = weight_maps(hi, lo, kQkv, kHidden, kQkvTile);
-    maps.o = weight_maps(hi + kQkvFloats, lo + kQkvFloats, kHidden, kHidden, kHiddenTile);
-    maps.gate_up = weight_maps(hi + gate_up, lo + gate_up, 2 * kIntermediate, kHidden, kGateUpTile);
+    maps.qkv = weight_maps(hi, lo, w.qkv, kQkv, kHidden, kQkvTile);
+    maps.o = weight_maps(hi + kQkvFloats, lo + kQkvFloats, w.o, kHidden, kHidden, kHiddenTile);
+    maps.gate_up = weight_maps(hi + gate_up, lo + gate_up, w.gate_up, 2 * kIntermediate, kHidden,
+                               kGateUpTile);
     maps.gate_up_pair =
-        weight_maps(hi + gate_up, lo + gate_up, 2 * kIntermediate, kHidden, kTcPairN);
-    maps.down = weight_maps(hi + down, lo + down, kHidden, kIntermediate, kHiddenTile);
+        weight_maps(hi + gate_up, lo + gate_up, w.gate_up, 2 * kIntermediate, kHidden, kTcPairN);
+    maps.down = weight_maps(hi + down, lo + down, w.down, kHidden, kIntermediate, kHiddenTile);
   }
   split_generation_ = weights_generation;
   split_source_ = model.layers[0].qkv;
@@ -173,7 +174,7 @@ void Prefill::prepare_tail(const ModelView &model, uint64_t weights_generation) 
   auto *hi = static_cast<float *>(tail_split_->data());
   launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(floats, 256), kSms * 8), 256),
          SplitArgs{model.lm_head, hi, hi + floats, floats});
-  tail_maps_ = weight_maps(hi, hi + floats, model.vocab, kHidden, kGateUpTile);
+  tail_maps_ = weight_maps(hi, hi + floats, model.lm_head, model.vocab, kHidden, kGateUpTile);
   tail_generation_ = weights_generation;
   tail_source_ = model.lm_head;
 }
@@ -215,7 +216,7 @@ PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const OperandMaps &a, const
   TcGemmArgs args{};
   // The narrow kernels take the weights as the MMA's A operand.
   args.a_hi = narrow ? b.narrow[0] : a.wide[0];
-  args.a_lo = narrow ? b.narrow[1] : a.wide[1];
+  args.a_lo = narrow ? TensorMap{} : a.wide[1]; // narrow: the kernel splits the weights
   args.b_hi = narrow ? a.narrow[0] : b.wide[0];
   args.b_lo = narrow ? a.narrow[1] : b.wide[1];
   args.m = m;
@@ -426,7 +427,9 @@ void Prefill::gemm_check(uint32_t tile_columns, GemmEpilogue mode, uint32_t m, u
     launch(split_.get(), rows_config(std::min<uint32_t>(ceil_div(b_floats, 256), kSms * 8), 256),
            SplitArgs{static_cast<const float *>(b_dev.data()), bh, bh + b_floats, b_floats});
     tc_gemm(tile_columns, activation_maps(ah, ah + a_floats, m, k),
-            weight_maps(bh, bh + b_floats, rows_b, k, tile_columns), m, n, k, mode, cd, nullptr,
+            weight_maps(bh, bh + b_floats, static_cast<const float *>(b_dev.data()), rows_b, k,
+                        tile_columns),
+            m, n, k, mode, cd, nullptr,
             n, bias_ptr, false);
   }
   device_.synchronize();

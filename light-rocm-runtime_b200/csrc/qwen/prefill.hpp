@@ -48,7 +48,8 @@ class BatchDecoder;
 // (hi, lo) tensor maps of one GEMM operand: `wide` boxes for the
 // 128-row-band kernels (activations: 128 rows; weights: half a tile), and
 // `narrow` boxes for the swapped-operand kernels of at most kNarrowRows rows
-// (activations: kNarrowRows rows; weights: kNarrowTileN rows).
+// (activations: kNarrowRows rows of the pair; weights: kNarrowTileN rows of
+// the FP32 weights in narrow[0], which those kernels split themselves).
 struct OperandMaps {
   TensorMap wide[2]{}, narrow[2]{};
 };
