@@ -215,7 +215,9 @@ LRRT_API lr_status_t lrq_model_ingest_prompt(lrq_model_t *model, const uint32_t 
  * The projections run as GEMMs over all prompt rows:
  *   LRQ_PREFILL_SIMT    FP32 FMA tiles on the CUDA cores;
  *   LRQ_PREFILL_TF32X3  3xTF32 on the tcgen05 tensor cores (FP32 accuracy:
- *                       each operand split into TF32 hi + lo, three products).
+ *                       each operand split into TF32 hi + lo, three products;
+ *                       the causal attention too). GEMMs of at most 32 rows
+ *                       read the FP32 weights and split them on chip.
  * Results match single-token ingestion to FP32 rounding (summation order
  * differs), not bit for bit. Waits for the device before returning.
  *
