@@ -301,14 +301,20 @@ constexpr uint32_t kNarrowTmemColumns = 64;
 LRRT_PREFILL_HD constexpr uint32_t tc_narrow_stage_bytes(bool paired) {
   return 2u * ((paired ? 2u : 1u) * kNarrowTileN + kNarrowRows) * kTcTileK * 4u;
 }
-LRRT_PREFILL_HD constexpr uint32_t tc_narrow_stages(bool paired) {
-  return (200u * 1024u) / tc_narrow_stage_bytes(paired) > 8u
+// Up to 200 KB of stages (one CTA per SM); `shared_sm` narrow launches of
+// more than one wave of tiles (prefill_tc_narrow_shared_sm: the LM head of
+// a batched step) take 100 KB, so that two CTAs share an SM and one's
+// pipeline fill and epilogue overlap the other's weight stream.
+LRRT_PREFILL_HD constexpr uint32_t tc_narrow_stages(bool paired, bool shared_sm = false) {
+  return ((shared_sm ? 100u : 200u) * 1024u) / tc_narrow_stage_bytes(paired) > 8u
              ? 8u
-             : (200u * 1024u) / tc_narrow_stage_bytes(paired);
+             : ((shared_sm ? 100u : 200u) * 1024u) / tc_narrow_stage_bytes(paired);
 }
-LRRT_PREFILL_HD constexpr uint32_t tc_narrow_shared_bytes(bool paired) {
-  return tc_narrow_stages(paired) * tc_narrow_stage_bytes(paired) + 1024u + 256u;
+LRRT_PREFILL_HD constexpr uint32_t tc_narrow_shared_bytes(bool paired, bool shared_sm = false) {
+  return tc_narrow_stages(paired, shared_sm) * tc_narrow_stage_bytes(paired) + 1024u + 256u;
 }
+static_assert(2u * tc_narrow_shared_bytes(false, true) <= 227u * 1024u,
+              "two shared-SM narrow CTAs per SM");
 
 constexpr uint32_t kTcErrorWaitTimeout = 1;
 

@@ -1686,9 +1686,9 @@ template <uint32_t kStages> struct NarrowShared {
 };
 static_assert(sizeof(NarrowShared<8>) <= 256u, "within the 256 bytes the host adds");
 
-template <bool kPaired>
+template <bool kPaired, bool kSharedSm = false>
 __device__ __forceinline__ void tc_narrow(const pf::TcGemmArgs &p) {
-  constexpr uint32_t kStages = pf::tc_narrow_stages(kPaired);
+  constexpr uint32_t kStages = pf::tc_narrow_stages(kPaired, kSharedSm);
   constexpr uint32_t kStageBytes = pf::tc_narrow_stage_bytes(kPaired);
   constexpr uint32_t kWeightBytes = pf::kNarrowTileN * pf::kTcTileK * 4u;
   constexpr uint32_t kRowBytes = pf::kNarrowRows * pf::kTcTileK * 4u;
@@ -1891,6 +1891,13 @@ extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
 extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 1)
     prefill_tc_narrow_pair(const __grid_constant__ pf::TcGemmArgs p) {
   tc_narrow<true>(p);
+}
+
+// The same with a half-size ring, two CTAs per SM (launches of more than
+// one wave of tiles).
+extern "C" __global__ void __launch_bounds__(pf::kTcThreads, 2)
+    prefill_tc_narrow_shared_sm(const __grid_constant__ pf::TcGemmArgs p) {
+  tc_narrow<false, true>(p);
 }
 
 // ------------------------------------------------------- batched decode --

@@ -24,6 +24,7 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
       tc_pair288_(module_.kernel("prefill_tc_gemm_pair288")),
       tc_narrow_(module_.kernel("prefill_tc_narrow")),
       tc_narrow_pair_(module_.kernel("prefill_tc_narrow_pair")),
+      tc_narrow_shared_sm_(module_.kernel("prefill_tc_narrow_shared_sm")),
       finish_rows_(module_.kernel("prefill_finish_rows")),
       batch_attention_(module_.kernel("batch_attention")),
       batch_argmax_(module_.kernel("batch_argmax")), chunk_(max_chunk_tokens) {
@@ -37,7 +38,7 @@ Prefill::Prefill(Device device, const void *image, size_t image_size, uint32_t m
   for (const Kernel *kernel :
        {&embed_, &rmsnorm_, &rope_kv_, &attend_, &attend_tc_, &reduce_, &split_, &gemm_bias_, &gemm_residual_,
         &gemm_swiglu_, &tc_n192_, &tc_n224_, &tc_n256_, &tc_pair288_, &tc_narrow_,
-        &tc_narrow_pair_,
+        &tc_narrow_pair_, &tc_narrow_shared_sm_,
         &finish_rows_, &batch_attention_, &batch_argmax_}) {
     check(lr_kernel_set_overlapped(kernel->get(), 1), "lr_kernel_set_overlapped");
   }
@@ -207,12 +208,15 @@ PartialTiles Prefill::tc_gemm(uint32_t tile_columns, const OperandMaps &a, const
   if (!narrow && tile_columns == kTcPairN && !swiglu) {
     throw std::invalid_argument("288-column tiles are gate/up pairs");
   }
-  const Kernel &kernel = narrow ? (swiglu ? tc_narrow_pair_ : tc_narrow_)
+  // Narrow launches of more than one wave of tiles (not swiglu) share SMs.
+  const bool shared_sm = narrow && !swiglu && tiles > kSms;
+  const Kernel &kernel = narrow ? (swiglu ? tc_narrow_pair_ : shared_sm ? tc_narrow_shared_sm_ : tc_narrow_)
                          : tile_columns == 192      ? tc_n192_
                          : tile_columns == 224      ? tc_n224_
                          : tile_columns == kTcPairN ? tc_pair288_
                                                     : tc_n256_;
-  const uint32_t shared = narrow ? tc_narrow_shared_bytes(swiglu) : tc_shared_bytes(tile_columns);
+  const uint32_t shared =
+      narrow ? tc_narrow_shared_bytes(swiglu, shared_sm) : tc_shared_bytes(tile_columns);
   TcGemmArgs args{};
   // The narrow kernels take the weights as the MMA's A operand.
   args.a_hi = narrow ? b.narrow[0] : a.wide[0];

@@ -96,7 +96,7 @@ private:
   Device device_;
   Module module_;
   Kernel embed_, rmsnorm_, rope_kv_, attend_, attend_tc_, reduce_, split_, gemm_bias_, gemm_residual_,
-      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, tc_pair288_, tc_narrow_, tc_narrow_pair_,
+      gemm_swiglu_, tc_n192_, tc_n224_, tc_n256_, tc_pair288_, tc_narrow_, tc_narrow_pair_, tc_narrow_shared_sm_,
       finish_rows_, batch_attention_, batch_argmax_;
   uint32_t chunk_;
   uint64_t device_bytes_ = 0;

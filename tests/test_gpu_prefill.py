@@ -202,13 +202,14 @@ def test_prefill_gemm_matches_float64(gemm_model, tile, mode, m, n, k):
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode", [0, 1, 2], ids=["bias", "residual", "swiglu"])
 @pytest.mark.parametrize("m,n,k", [(1, 1152, 896), (17, 480, 4864), (32, 4864, 896),
-                                   (32, 896, 4864)])
+                                   (32, 896, 4864), (32, 19072, 896)])
 def test_narrow_gemm_matches_float64(gemm_model, mode, m, n, k):
     """At most 32 rows run the swapped-operand kernels (weights as the MMA's
     A operand, 128 output columns per tile, gate/up pairs in two
     accumulators) under the same split-K schedule: one row, a ragged last
     column tile (480 = 3.75 x 128) with a long K, a 32-row swiglu of
-    Qwen2-0.5B's MLP width, and the down projection's shape."""
+    Qwen2-0.5B's MLP width, the down projection's shape, and 149 tiles (more
+    than one wave: the two-CTAs-per-SM kernel, then a split-K remainder)."""
     _check_gemm(gemm_model, 256, mode, m, n, k)
 
 
