@@ -18,9 +18,13 @@
 //    (exact FP32 products, the comparator);
 //  * prefill_tc_gemm: 3xTF32 on the tcgen05 tensor cores. Operands are stored
 //    as TF32 (hi, lo) pairs (include/lrrt/qwen/prefill.hpp), TMA moves
-//    128-byte-swizzled tiles into shared memory, one thread issues
+//    64-byte-swizzled tiles into shared memory, one thread issues
 //    tcgen05.mma into a TMEM accumulator (hi.hi + hi.lo + lo.hi per K step)
-//    and four warps read it back with tcgen05.ld for the epilogue.
+//    and four warps read it back with tcgen05.ld for the epilogue. GEMMs of
+//    at most 32 rows (prefill_tc_narrow*) swap the operands and stream the
+//    FP32 weights, splitting them into TF32 pairs in shared memory.
+// The causal attention has a CUDA-core kernel (prefill_attention, the SIMT
+// path) and a tensor-core one (prefill_attention_tc, the 3xTF32 path).
 #include "lrrt/persistent_graph/device_sync.cuh"
 #include "lrrt/qwen/prefill.hpp"
 #include "lrrt/qwen/stateful_graph_context.hpp"
